@@ -1,0 +1,31 @@
+// Python bindings of the koochak_b200 native library (module koochak_b200_C).
+#include <torch/extension.h>
+
+#include "host_utils.h"
+
+namespace kb {
+void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
+                 const c10::optional<at::Tensor>& d, double alpha, double beta, const c10::optional<at::Tensor>& bias,
+                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n);
+void register_norm_ops(pybind11::module& m);
+void register_elementwise_ops(pybind11::module& m);
+void register_attention_ops(pybind11::module& m);
+void register_optim_ops(pybind11::module& m);
+void register_comm_ops(pybind11::module& m);
+}  // namespace kb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "koochak_b200 sm_100a kernels";
+  m.def("gemm", &kb::gemm_launch, "tcgen05 GEMM: c = epilogue(alpha * op(a) @ op(b)^T)", pybind11::arg("a"),
+        pybind11::arg("a_mn_major"), pybind11::arg("b"), pybind11::arg("b_mn_major"), pybind11::arg("c"),
+        pybind11::arg("d") = pybind11::none(), pybind11::arg("alpha") = 1.0, pybind11::arg("beta") = 0.0,
+        pybind11::arg("bias") = pybind11::none(), pybind11::arg("aux") = pybind11::none(),
+        pybind11::arg("act") = 0, pybind11::arg("block_n") = 0);
+  m.def("read_and_clear_status", &kb::read_and_clear_status, "read and clear the device status word");
+  m.def("num_sms", &kb::num_sms, "streaming multiprocessor count of a device");
+  kb::register_norm_ops(m);
+  kb::register_elementwise_ops(m);
+  kb::register_attention_ops(m);
+  kb::register_optim_ops(m);
+  kb::register_comm_ops(m);
+}

@@ -1,0 +1,515 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[b] = epilogue( alpha * A[b] . B[b]^T )        (A: M x K, B: N x K logically)
+//
+// Each operand is given either K-major (K contiguous) or MN-major (M or N
+// contiguous), so forward (x W^T), data-gradient (dy W) and weight-gradient
+// (dy^T x) products, and the Newton-Schulz products of the Muon optimizer,
+// all run without a transpose copy.
+//
+// Roles inside one CTA (192 threads, one CTA per SM, grid = #SMs):
+//   warp 0      TMA producer: 128-byte-swizzled tiles into a STAGES-deep ring
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld from TMEM, fused math, global stores
+// The fp32 accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Epilogue, in order:  v = alpha*acc (+ bias[n])
+//   ACT_GELU      : aux = bf16(v); v = gelu_tanh(v)
+//   ACT_GELU_BWD  : v = v * gelu_tanh'(D[m,n])           (D = saved pre-activation)
+//   otherwise     : v = v + beta * D[m,n]                 (residual add / accumulate)
+//   C[m,n] = v  (bf16, fp16 or fp32)
+//
+// There is no TMA multicast here: every CTA loads its own tiles.
+#include "host_utils.h"
+#include "sm100.cuh"
+
+#include <torch/extension.h>
+
+namespace kb {
+
+enum GemmAct : int { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
+
+struct GemmParams {
+  int M, N, K, batch;
+  int a_mn_major, b_mn_major;
+  int fp16_inputs;
+  void* C;
+  long long ldc, strideC;
+  const void* D;
+  long long ldd, strideD;
+  float alpha, beta;
+  const float* bias;
+  void* aux;
+  long long ldaux, strideAux;
+  int vec_ok;  // C/D/aux rows 16-byte aligned for vector access
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // 256 or 512: power of two
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <typename OutT>
+__device__ __forceinline__ void store_row32(OutT* dst, const float (&v)[32], int valid, bool vec);
+
+template <>
+__device__ __forceinline__ void store_row32<float>(float* dst, const float (&v)[32], int valid, bool vec) {
+  if (vec && valid == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+    for (int j = 0; j < valid; ++j) dst[j] = v[j];
+  }
+}
+
+template <>
+__device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* dst, const float (&v)[32], int valid,
+                                                          bool vec) {
+  if (vec && valid == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 p;
+      p.x = pack_bf16(v[j], v[j + 1]);
+      p.y = pack_bf16(v[j + 2], v[j + 3]);
+      p.z = pack_bf16(v[j + 4], v[j + 5]);
+      p.w = pack_bf16(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(dst + j) = p;
+    }
+  } else {
+    for (int j = 0; j < valid; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+template <>
+__device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v)[32], int valid, bool vec) {
+  if (vec && valid == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      uint4 p;
+      p.x = pack_f16(v[j], v[j + 1]);
+      p.y = pack_f16(v[j + 2], v[j + 3]);
+      p.z = pack_f16(v[j + 4], v[j + 5]);
+      p.w = pack_f16(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(dst + j) = p;
+    }
+  } else {
+    for (int j = 0; j < valid; ++j) dst[j] = __float2half_rn(v[j]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_row32(const T* src, float (&v)[32], int valid, bool vec) {
+  if (vec && valid == 32) {
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 q = *reinterpret_cast<const float4*>(src + j);
+        v[j] = q.x; v[j + 1] = q.y; v[j + 2] = q.z; v[j + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 q = *reinterpret_cast<const uint4*>(src + j);
+        const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[j + t] = to_f32<T>(e[t]);
+      }
+    }
+  } else {
+    for (int j = 0; j < 32; ++j) v[j] = (j < valid) ? to_f32<T>(src[j]) : 0.f;
+  }
+}
+
+template <int BN, typename OutT, int ACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int tiles_per_batch = num_m * num_n;
+  const int total_tiles = tiles_per_batch * p.batch;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_parity[S];
+      bool armed[S];
+      for (int s = 0; s < S; ++s) armed[s] = false;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const int b = t / tiles_per_batch;
+        const int r = t - b * tiles_per_batch;
+        const int n_blk = r / num_m;
+        const int m_blk = r - n_blk * num_m;
+        const int m0 = m_blk * kBM;
+        const int n0 = n_blk * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          armed[stage] = true;
+          armed_parity[stage] = phase;
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          const int k0 = kb * kBK;
+          if (!p.a_mn_major) {
+            tma_load_3d(&tmA, &full[stage], a_dst, k0, m0, b);
+          } else {
+            tma_load_3d(&tmA, &full[stage], a_dst, m0, k0, b);
+            tma_load_3d(&tmA, &full[stage], a_dst + 8192, m0 + 64, k0, b);
+          }
+          if (!p.b_mn_major) {
+            tma_load_3d(&tmB, &full[stage], b_dst, k0, n0, b);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_3d(&tmB, &full[stage], b_dst + c * 8192, n0 + c * 64, k0, b);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every armed stage must have landed before this CTA may exit.
+      for (int s = 0; s < S; ++s) {
+        if (armed[s]) {
+          volatile int never = 0;
+          if (!mbar_wait(&full[s], armed_parity[s], &never, p.status, kStatusTimeoutDrain)) break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_f16(kBM, BN, p.fp16_inputs != 0, p.a_mn_major != 0, p.b_mn_major != 0);
+      // K-major: rows are 128 B, 8-row groups 1024 B apart, K step of 16 = +32 B.
+      // MN-major: 64-wide chunks 8192 B apart (LBO), 8-row K groups 1024 B apart,
+      // K step of 16 rows = +2048 B.
+      const uint32_t a_lbo = p.a_mn_major ? 8192u : 16u;
+      const uint32_t b_lbo = p.b_mn_major ? 8192u : 16u;
+      const uint32_t a_kstep = p.a_mn_major ? 2048u : 32u;
+      const uint32_t b_kstep = p.b_mn_major ? 2048u : 32u;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sw128_desc(a_addr + k * a_kstep, a_lbo, 1024);
+            const uint64_t bd = sw128_desc(b_addr + k * b_kstep, b_lbo, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      // Drain: wait until every MMA this thread issued has completed.
+      if (issued_any) {
+        umma_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool vec = p.vec_ok != 0;
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int b = t / tiles_per_batch;
+      const int r = t - b * tiles_per_batch;
+      const int n_blk = r / num_m;
+      const int m_blk = r - n_blk * num_m;
+      const int row = m_blk * kBM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      OutT* crow = reinterpret_cast<OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc;
+      const OutT* drow = p.D ? reinterpret_cast<const OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd
+                             : nullptr;
+      __nv_bfloat16* arow =
+          p.aux ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux
+                : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t raw[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c, raw);
+        tmem_wait_ld();
+        const int col0 = n_blk * BN + c;
+        if (!row_ok || col0 >= p.N) continue;
+        const int valid = min(32, p.N - col0);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * p.alpha;
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += (j < valid) ? p.bias[col0 + j] : 0.f;
+        }
+        if constexpr (ACT == ACT_GELU) {
+          if (arow) store_row32<__nv_bfloat16>(arow + col0, v, valid, vec);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+        } else if constexpr (ACT == ACT_GELU_BWD) {
+          float h[32];
+          load_row32<OutT>(drow + col0, h, valid, vec);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad(h[j]);
+        } else {
+          if (drow != nullptr && p.beta != 0.f) {
+            float d[32];
+            load_row32<OutT>(drow + col0, d, valid, vec);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += p.beta * d[j];
+          }
+        }
+        store_row32<OutT>(crow + col0, v, valid, vec);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------- host
+
+static bool is_mn_major_2d(const at::Tensor& t) {
+  // For a [rows, cols] view: K-major means cols (K) contiguous.
+  return t.stride(-1) != 1;
+}
+
+template <int BN, typename OutT, int ACT>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                        cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tcgen05_kernel<BN, OutT, ACT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  KB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int BN, typename OutT>
+static void dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+                         cudaStream_t s) {
+  switch (act) {
+    case ACT_NONE: launch_gemm<BN, OutT, ACT_NONE>(ta, tb, p, grid, s); break;
+    case ACT_GELU: launch_gemm<BN, OutT, ACT_GELU>(ta, tb, p, grid, s); break;
+    case ACT_GELU_BWD: launch_gemm<BN, OutT, ACT_GELU_BWD>(ta, tb, p, grid, s); break;
+    default: KB_CHECK(false, "bad activation");
+  }
+}
+
+// Operand description: `t` is a 2-D [rows, cols] or 3-D [batch, rows, cols] view.
+// For A: logical (M x K). If K-major, t is [.., M, K] with stride(-1)==1. If
+// M-major, t is [.., K, M] with stride(-1)==1 (flag mn_major=true).
+static CUtensorMap operand_map(const at::Tensor& t, bool mn_major, int mn_extent, int k_extent, int box_rows) {
+  const int64_t batch = t.dim() == 3 ? t.size(0) : 1;
+  const int64_t bstride = t.dim() == 3 ? t.stride(0) : 0;
+  const int64_t ld = t.stride(-2);
+  const int64_t esz = t.element_size();
+  uint64_t dims[3];
+  uint64_t strides[2];
+  uint32_t box[3];
+  if (!mn_major) {
+    dims[0] = (uint64_t)k_extent;
+    dims[1] = (uint64_t)mn_extent;
+    box[0] = 64;
+    box[1] = (uint32_t)box_rows;
+  } else {
+    dims[0] = (uint64_t)mn_extent;
+    dims[1] = (uint64_t)k_extent;
+    box[0] = 64;
+    box[1] = 64;
+  }
+  dims[2] = (uint64_t)batch;
+  box[2] = 1;
+  strides[0] = (uint64_t)(ld * esz);
+  strides[1] = (uint64_t)((batch > 1 ? bstride : ld * (mn_major ? k_extent : mn_extent)) * esz);
+  if (strides[1] % 16 != 0) strides[1] = ((strides[1] + 15) / 16) * 16;  // unused when batch == 1
+  return make_tma(t.data_ptr(), t.scalar_type(), 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Public entry: see gemm() in bindings for argument meaning.
+void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
+                 const c10::optional<at::Tensor>& d, double alpha, double beta, const c10::optional<at::Tensor>& bias,
+                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n) {
+  check_cuda_tensor(a, "a");
+  check_cuda_tensor(b, "b");
+  check_cuda_tensor(c, "c");
+  KB_CHECK(a.scalar_type() == b.scalar_type(), "A and B must have the same dtype");
+  KB_CHECK(a.scalar_type() == at::kBFloat16 || a.scalar_type() == at::kHalf, "A/B must be bf16 or fp16");
+  KB_CHECK(a.dim() == b.dim() && (a.dim() == 2 || a.dim() == 3), "A and B must both be 2-D or 3-D");
+  KB_CHECK(a.stride(-1) == 1 && b.stride(-1) == 1, "A and B must have unit inner stride");
+  const bool batched = a.dim() == 3;
+  const int64_t batch = batched ? a.size(0) : 1;
+  const int64_t M = a_mn_major ? a.size(-1) : a.size(-2);
+  const int64_t K = a_mn_major ? a.size(-2) : a.size(-1);
+  const int64_t N = b_mn_major ? b.size(-1) : b.size(-2);
+  const int64_t Kb = b_mn_major ? b.size(-2) : b.size(-1);
+  KB_CHECK(K == Kb, "inner dimensions differ");
+  KB_CHECK(c.size(-2) == M && c.size(-1) == N && c.stride(-1) == 1, "C shape mismatch");
+  KB_CHECK(!batched || (b.size(0) == batch && c.dim() == 3 && c.size(0) == batch), "batch mismatch");
+  KB_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
+  const auto ct = c.scalar_type();
+  KB_CHECK(ct == at::kFloat || ct == at::kBFloat16 || ct == at::kHalf, "C must be fp32, bf16 or fp16");
+  KB_CHECK(ct == at::kFloat || ct == a.scalar_type(), "reduced-precision C must match the input dtype");
+
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int dev = a.get_device();
+  int bn = (int)block_n;
+  if (bn != 128 && bn != 256) {
+    // Pick the tile width that wastes the least of the final wave.
+    const int sms = num_sms(dev);
+    auto waste = [&](int w) {
+      const int64_t tiles = batch * ((M + 127) / 128) * ((N + w - 1) / w);
+      const int64_t waves = (tiles + sms - 1) / sms;
+      const double work = double(batch) * double((M + 127) / 128 * 128) * double(N);
+      return double(waves) * sms * 128.0 * w / work;  // >= 1, smaller is better
+    };
+    bn = (N <= 128 || waste(128) + 0.03 < waste(256)) ? 128 : 256;
+  }
+  const CUtensorMap ta = operand_map(a, a_mn_major, (int)M, (int)K, 128);
+  const CUtensorMap tb = operand_map(b, b_mn_major, (int)N, (int)K, bn);
+
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.batch = (int)batch;
+  p.a_mn_major = a_mn_major;
+  p.b_mn_major = b_mn_major;
+  p.fp16_inputs = a.scalar_type() == at::kHalf;
+  p.C = c.data_ptr();
+  p.ldc = c.stride(-2);
+  p.strideC = batched ? c.stride(0) : 0;
+  p.alpha = (float)alpha;
+  p.beta = (float)beta;
+  bool vec = (p.ldc % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) && (!batched || p.strideC % 8 == 0);
+  if (d.has_value() && d->defined()) {
+    KB_CHECK(d->scalar_type() == ct && d->size(-2) == M && d->size(-1) == N && d->stride(-1) == 1, "D mismatch");
+    p.D = d->data_ptr();
+    p.ldd = d->stride(-2);
+    p.strideD = batched ? d->stride(0) : 0;
+    vec = vec && (p.ldd % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.D) & 15) == 0) && (!batched || p.strideD % 8 == 0);
+  }
+  if (bias.has_value() && bias->defined()) {
+    KB_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N && bias->is_contiguous(), "bias must be fp32 [N]");
+    p.bias = bias->data_ptr<float>();
+  }
+  if (aux.has_value() && aux->defined()) {
+    KB_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(-2) == M && aux->size(-1) == N, "aux mismatch");
+    p.aux = aux->data_ptr();
+    p.ldaux = aux->stride(-2);
+    p.strideAux = batched ? aux->stride(0) : 0;
+    vec = vec && (p.ldaux % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.aux) & 15) == 0);
+  }
+  KB_CHECK(act != ACT_GELU_BWD || p.D != nullptr, "GELU backward needs the pre-activation as D");
+  p.vec_ok = vec;
+  p.status = device_status_ptr(dev);
+
+  const int64_t tiles = batch * ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int grid = (int)std::min<int64_t>(tiles, num_sms(dev));
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  if (bn == 256) {
+    if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, grid, stream);
+    else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, grid, stream);
+    else dispatch_act<256, __half>((int)act, ta, tb, p, grid, stream);
+  } else {
+    if (ct == at::kFloat) dispatch_act<128, float>((int)act, ta, tb, p, grid, stream);
+    else if (ct == at::kBFloat16) dispatch_act<128, __nv_bfloat16>((int)act, ta, tb, p, grid, stream);
+    else dispatch_act<128, __half>((int)act, ta, tb, p, grid, stream);
+  }
+}
+
+}  // namespace kb
