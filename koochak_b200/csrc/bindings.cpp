@@ -23,6 +23,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("act") = 0, pybind11::arg("block_n") = 0);
   m.def("read_and_clear_status", &kb::read_and_clear_status, "read and clear the device status word");
   m.def("num_sms", &kb::num_sms, "streaming multiprocessor count of a device");
+  m.def("launch_count", []() { return kb::launch_counter().load(); }, "kernels launched by this library so far");
   kb::register_norm_ops(m);
   kb::register_elementwise_ops(m);
   kb::register_attention_ops(m);

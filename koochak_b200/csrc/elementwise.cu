@@ -1,3 +1,439 @@
-// placeholder, filled in below
+// Memory-bound kernels for sm_100a: token+position embedding (fwd/bwd),
+// fused softmax cross-entropy (fwd saves the log-sum-exp; bwd overwrites the
+// logits with their gradient in place), bias gradients (column sums), a
+// multi-tensor fp32 -> bf16/fp16 cast, SwiGLU and rotary embedding.
+#include "host_utils.h"
+#include "sm100.cuh"
+
 #include <torch/extension.h>
-namespace kb { void register_elementwise_ops(pybind11::module& m) {} }
+
+#include <vector>
+
+namespace kb {
+
+// ------------------------------------------------------------ embedding
+
+// out[t, :] = wte[idx[t], :] + wpe[t % S, :]   (fp32 out; wpe optional)
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
+                                     const float* __restrict__ wpe, float* __restrict__ out, int T, int S, int C,
+                                     int V, int* status) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  int64_t tok = idx[t];
+  if (tok < 0 || tok >= V) {
+    record_status(status, kStatusBadArgs);
+    tok = 0;
+  }
+  const float4* we = reinterpret_cast<const float4*>(wte + tok * (int64_t)C);
+  const float4* pe = wpe ? reinterpret_cast<const float4*>(wpe + (int64_t)(t % S) * C) : nullptr;
+  float4* o = reinterpret_cast<float4*>(out + (int64_t)t * C);
+  for (int i = threadIdx.x; i < C / 4; i += blockDim.x) {
+    float4 a = we[i];
+    if (pe) {
+      const float4 b = pe[i];
+      a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+    }
+    o[i] = a;
+  }
+}
+
+// dwte[idx[t]] += dout[t];  dwpe[t % S] += dout[t]   (fp32 atomics)
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ dout,
+                                     float* __restrict__ dwte, float* __restrict__ dwpe, int T, int S, int C, int V) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  int64_t tok = idx[t];
+  if (tok < 0 || tok >= V) return;
+  const float* g = dout + (int64_t)t * C;
+  float* dw = dwte + tok * (int64_t)C;
+  float* dp = dwpe ? dwpe + (int64_t)(t % S) * C : nullptr;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float v = g[i];
+    atomicAdd(dw + i, v);
+    if (dp) atomicAdd(dp + i, v);
+  }
+}
+
+void embedding_forward(const at::Tensor& idx, const at::Tensor& wte, const c10::optional<at::Tensor>& wpe,
+                       at::Tensor& out, int64_t seq_len) {
+  check_cuda_tensor(idx, "idx");
+  KB_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous(), "idx must be contiguous int64");
+  KB_CHECK(wte.scalar_type() == at::kFloat && wte.is_contiguous() && out.scalar_type() == at::kFloat, "fp32 tables");
+  const int C = (int)wte.size(1);
+  KB_CHECK(C % 4 == 0, "embedding width must be a multiple of 4");
+  const int T = (int)idx.numel();
+  const c10::cuda::CUDAGuard guard(idx.device());
+  const float* pe = (wpe.has_value() && wpe->defined()) ? wpe->data_ptr<float>() : nullptr;
+  embedding_fwd_kernel<<<T, 128, 0, c10::cuda::getCurrentCUDAStream().stream()>>>(
+      idx.data_ptr<int64_t>(), wte.data_ptr<float>(), pe, out.data_ptr<float>(), T, (int)seq_len, C,
+      (int)wte.size(0), device_status_ptr(idx.get_device()));
+  KB_LAUNCHED();
+}
+
+void embedding_backward(const at::Tensor& idx, const at::Tensor& dout, at::Tensor& dwte,
+                        const c10::optional<at::Tensor>& dwpe, int64_t seq_len) {
+  const int C = (int)dwte.size(1);
+  const int T = (int)idx.numel();
+  KB_CHECK(dout.scalar_type() == at::kFloat && dout.is_contiguous(), "dout must be contiguous fp32");
+  const c10::cuda::CUDAGuard guard(idx.device());
+  float* dp = (dwpe.has_value() && dwpe->defined()) ? dwpe->data_ptr<float>() : nullptr;
+  embedding_bwd_kernel<<<T, 256, 0, c10::cuda::getCurrentCUDAStream().stream()>>>(
+      idx.data_ptr<int64_t>(), dout.data_ptr<float>(), dwte.data_ptr<float>(), dp, T, (int)seq_len, C,
+      (int)dwte.size(0));
+  KB_LAUNCHED();
+}
+
+// ------------------------------------------------------------ cross-entropy
+
+// Per row: lse = log(sum exp(z)), loss = lse - z[target] (0 for ignored rows).
+// One CTA per row, logits in bf16/fp16/fp32 with row stride ld, V valid columns.
+template <typename T>
+__global__ void __launch_bounds__(256) ce_fwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ tgt,
+                                                     float* __restrict__ loss, float* __restrict__ lse_out, int V,
+                                                     long long ld, int64_t ignore_index) {
+  const int row = blockIdx.x;
+  const T* z = logits + (long long)row * ld;
+  float m = -INFINITY, s = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = to_f32<T>(z[i]);
+    if (v > m) {
+      s = s * __expf(m - v) + 1.f;
+      m = v;
+    } else {
+      s += __expf(v - m);
+    }
+  }
+  // warp combine
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+    m = mm;
+  }
+  __shared__ float sm[32], ss[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[warp] = m;
+    ss[warp] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mm = fmaxf(m, m2);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+      m = mm;
+    }
+    if (lane == 0) {
+      const float l = m + logf(s);
+      lse_out[row] = l;
+      const int64_t t = tgt[row];
+      if (t == ignore_index || t < 0 || t >= V) loss[row] = 0.f;
+      else loss[row] = l - to_f32<T>(z[t]);
+    }
+  }
+}
+
+// dz = (softmax(z) - onehot(target)) * scale_row, written over z in place.
+// scale_row = grad_scale for counted rows, 0 for ignored rows.
+template <typename T>
+__global__ void __launch_bounds__(256) ce_bwd_kernel(T* __restrict__ logits, const int64_t* __restrict__ tgt,
+                                                     const float* __restrict__ lse, const float* __restrict__ gscale,
+                                                     int V, long long ld, int64_t ignore_index) {
+  const int row = blockIdx.x;
+  T* z = logits + (long long)row * ld;
+  const int64_t t = tgt[row];
+  const bool ignored = (t == ignore_index || t < 0 || t >= V);
+  const float g = ignored ? 0.f : gscale[0];
+  const float l = lse[row];
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float p = __expf(to_f32<T>(z[i]) - l);
+    z[i] = from_f32<T>((p - (i == t ? 1.f : 0.f)) * g);
+  }
+}
+
+void cross_entropy_forward(const at::Tensor& logits, const at::Tensor& target, at::Tensor& loss, at::Tensor& lse,
+                           int64_t V, int64_t ignore_index) {
+  check_cuda_tensor(logits, "logits");
+  KB_CHECK(logits.stride(-1) == 1, "logits must have unit inner stride");
+  const int rows = (int)target.numel();
+  const long long ld = logits.stride(-2);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  if (rows == 0) return;
+  switch (logits.scalar_type()) {
+    case at::kBFloat16:
+      ce_fwd_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>((const __nv_bfloat16*)logits.data_ptr(),
+                                                        target.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                                                        lse.data_ptr<float>(), (int)V, ld, ignore_index);
+      break;
+    case at::kHalf:
+      ce_fwd_kernel<__half><<<rows, 256, 0, s>>>((const __half*)logits.data_ptr(), target.data_ptr<int64_t>(),
+                                                 loss.data_ptr<float>(), lse.data_ptr<float>(), (int)V, ld,
+                                                 ignore_index);
+      break;
+    case at::kFloat:
+      ce_fwd_kernel<float><<<rows, 256, 0, s>>>(logits.data_ptr<float>(), target.data_ptr<int64_t>(),
+                                                loss.data_ptr<float>(), lse.data_ptr<float>(), (int)V, ld, ignore_index);
+      break;
+    default: KB_CHECK(false, "cross_entropy: unsupported dtype");
+  }
+  KB_LAUNCHED();
+}
+
+void cross_entropy_backward(at::Tensor& logits, const at::Tensor& target, const at::Tensor& lse,
+                            const at::Tensor& gscale, int64_t V, int64_t ignore_index) {
+  const int rows = (int)target.numel();
+  const long long ld = logits.stride(-2);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  if (rows == 0) return;
+  KB_CHECK(gscale.scalar_type() == at::kFloat && gscale.is_cuda(), "gscale must be a CUDA fp32 scalar");
+  switch (logits.scalar_type()) {
+    case at::kBFloat16:
+      ce_bwd_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>((__nv_bfloat16*)logits.data_ptr(), target.data_ptr<int64_t>(),
+                                                        lse.data_ptr<float>(), gscale.data_ptr<float>(), (int)V, ld,
+                                                        ignore_index);
+      break;
+    case at::kHalf:
+      ce_bwd_kernel<__half><<<rows, 256, 0, s>>>((__half*)logits.data_ptr(), target.data_ptr<int64_t>(),
+                                                 lse.data_ptr<float>(), gscale.data_ptr<float>(), (int)V, ld,
+                                                 ignore_index);
+      break;
+    case at::kFloat:
+      ce_bwd_kernel<float><<<rows, 256, 0, s>>>(logits.data_ptr<float>(), target.data_ptr<int64_t>(),
+                                                lse.data_ptr<float>(), gscale.data_ptr<float>(), (int)V, ld,
+                                                ignore_index);
+      break;
+    default: KB_CHECK(false, "cross_entropy: unsupported dtype");
+  }
+  KB_LAUNCHED();
+}
+
+// ------------------------------------------------------------ bias gradient
+
+// out[n] (+)= sum_m g[m, n]; each CTA covers 64 columns x a slice of rows.
+template <typename T>
+__global__ void __launch_bounds__(256) bias_grad_kernel(const T* __restrict__ g, float* __restrict__ out, int M,
+                                                        int N, int rows_per_cta) {
+  const int col = blockIdx.x * 64 + (threadIdx.x & 63);
+  const int r0 = blockIdx.y * rows_per_cta;
+  const int r1 = min(M, r0 + rows_per_cta);
+  float s = 0.f;
+  if (col < N)
+    for (int r = r0 + (threadIdx.x >> 6); r < r1; r += 4) s += to_f32<T>(g[(long long)r * N + col]);
+  __shared__ float red[4][64];
+  red[threadIdx.x >> 6][threadIdx.x & 63] = s;
+  __syncthreads();
+  if (threadIdx.x < 64 && col < N) {
+    const float t = red[0][threadIdx.x] + red[1][threadIdx.x] + red[2][threadIdx.x] + red[3][threadIdx.x];
+    atomicAdd(out + col, t);
+  }
+}
+
+// out must be zeroed by the caller unless accumulating.
+void bias_grad(const at::Tensor& g, at::Tensor& out) {
+  KB_CHECK(g.is_contiguous() && out.scalar_type() == at::kFloat, "bias_grad: contiguous g, fp32 out");
+  const int N = (int)g.size(-1);
+  const int M = (int)(g.numel() / N);
+  const c10::cuda::CUDAGuard guard(g.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int col_blocks = (N + 63) / 64;
+  const int target_ctas = num_sms(g.get_device()) * 8;
+  int row_blocks = std::max(1, std::min((M + 255) / 256, target_ctas / std::max(1, col_blocks)));
+  const int rows_per = (M + row_blocks - 1) / row_blocks;
+  row_blocks = (M + rows_per - 1) / rows_per;
+  dim3 grid(col_blocks, row_blocks);
+  if (g.scalar_type() == at::kBFloat16)
+    bias_grad_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)g.data_ptr(), out.data_ptr<float>(), M, N, rows_per);
+  else if (g.scalar_type() == at::kHalf)
+    bias_grad_kernel<__half><<<grid, 256, 0, s>>>((const __half*)g.data_ptr(), out.data_ptr<float>(), M, N, rows_per);
+  else
+    bias_grad_kernel<float><<<grid, 256, 0, s>>>(g.data_ptr<float>(), out.data_ptr<float>(), M, N, rows_per);
+  KB_LAUNCHED();
+}
+
+// ------------------------------------------------------------ multi-tensor cast
+
+constexpr int kCastMaxTensors = 128;
+struct CastArgs {
+  int n;
+  const float* src[kCastMaxTensors];
+  void* dst[kCastMaxTensors];
+  long long start[kCastMaxTensors + 1];  // cumulative element offsets
+};
+
+template <typename TOut>
+__global__ void cast_multi_kernel(const __grid_constant__ CastArgs a) {
+  const long long total = a.start[a.n];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  int ti = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    while (i >= a.start[ti + 1]) ++ti;
+    const long long j = i - a.start[ti];
+    reinterpret_cast<TOut*>(a.dst[ti])[j] = from_f32<TOut>(a.src[ti][j]);
+  }
+}
+
+void cast_multi(const std::vector<at::Tensor>& src, const std::vector<at::Tensor>& dst) {
+  KB_CHECK(src.size() == dst.size(), "cast_multi: list lengths differ");
+  if (src.empty()) return;
+  const c10::cuda::CUDAGuard guard(src[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const auto out_t = dst[0].scalar_type();
+  for (size_t base = 0; base < src.size(); base += kCastMaxTensors) {
+    CastArgs a{};
+    a.n = (int)std::min<size_t>(kCastMaxTensors, src.size() - base);
+    a.start[0] = 0;
+    for (int i = 0; i < a.n; ++i) {
+      const auto& x = src[base + i];
+      const auto& y = dst[base + i];
+      KB_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel() &&
+                   y.scalar_type() == out_t,
+               "cast_multi: fp32 contiguous sources and matching contiguous destinations required");
+      a.src[i] = x.data_ptr<float>();
+      a.dst[i] = y.data_ptr();
+      a.start[i + 1] = a.start[i] + x.numel();
+    }
+    if (a.start[a.n] == 0) continue;
+    const int blocks = (int)std::min<long long>((a.start[a.n] + 255) / 256, num_sms(src[0].get_device()) * 8LL);
+    if (out_t == at::kBFloat16) cast_multi_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a);
+    else if (out_t == at::kHalf) cast_multi_kernel<__half><<<blocks, 256, 0, s>>>(a);
+    else KB_CHECK(false, "cast_multi: destination must be bf16 or fp16");
+    KB_LAUNCHED();
+  }
+}
+
+// ------------------------------------------------------------ SwiGLU
+
+// h[m, j] = silu(gu[m, j]) * gu[m, F + j]  (gate and up packed side by side)
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, long long M, int F) {
+  const long long total = M * F;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / F;
+    const int j = (int)(i - m * F);
+    const float g = to_f32<T>(gu[m * 2 * F + j]);
+    const float u = to_f32<T>(gu[m * 2 * F + F + j]);
+    const float sg = g / (1.f + __expf(-g));
+    h[i] = from_f32<T>(sg * u);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ gu, const T* __restrict__ dh, T* __restrict__ dgu,
+                                  long long M, int F) {
+  const long long total = M * F;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / F;
+    const int j = (int)(i - m * F);
+    const float g = to_f32<T>(gu[m * 2 * F + j]);
+    const float u = to_f32<T>(gu[m * 2 * F + F + j]);
+    const float d = to_f32<T>(dh[i]);
+    const float sig = 1.f / (1.f + __expf(-g));
+    const float silu = g * sig;
+    dgu[m * 2 * F + j] = from_f32<T>(d * u * (sig + silu * (1.f - sig)));
+    dgu[m * 2 * F + F + j] = from_f32<T>(d * silu);
+  }
+}
+
+void swiglu_forward(const at::Tensor& gu, at::Tensor& h) {
+  const int F = (int)h.size(-1);
+  const long long M = h.numel() / F;
+  const c10::cuda::CUDAGuard guard(gu.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int blocks = (int)std::min<long long>((M * F + 255) / 256, num_sms(gu.get_device()) * 16LL);
+  KB_CHECK(gu.scalar_type() == h.scalar_type(), "swiglu dtype mismatch");
+  if (gu.scalar_type() == at::kBFloat16)
+    swiglu_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)h.data_ptr(), M, F);
+  else if (gu.scalar_type() == at::kHalf)
+    swiglu_fwd_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)gu.data_ptr(), (__half*)h.data_ptr(), M, F);
+  else
+    swiglu_fwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
+  KB_LAUNCHED();
+}
+
+void swiglu_backward(const at::Tensor& gu, const at::Tensor& dh, at::Tensor& dgu) {
+  const int F = (int)dh.size(-1);
+  const long long M = dh.numel() / F;
+  const c10::cuda::CUDAGuard guard(gu.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int blocks = (int)std::min<long long>((M * F + 255) / 256, num_sms(gu.get_device()) * 16LL);
+  if (gu.scalar_type() == at::kBFloat16)
+    swiglu_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)gu.data_ptr(), (const __nv_bfloat16*)dh.data_ptr(),
+                                                            (__nv_bfloat16*)dgu.data_ptr(), M, F);
+  else if (gu.scalar_type() == at::kHalf)
+    swiglu_bwd_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)gu.data_ptr(), (const __half*)dh.data_ptr(),
+                                                     (__half*)dgu.data_ptr(), M, F);
+  else
+    swiglu_bwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(), dgu.data_ptr<float>(), M, F);
+  KB_LAUNCHED();
+}
+
+// ------------------------------------------------------------ rotary embedding
+
+// In place on x[B, S, H, D] (row stride given), rotate-half convention:
+// x1' = x1*cos - x2*sin ; x2' = x2*cos + x1*sin with x1 = x[..., :D/2].
+// inverse=1 applies the transpose rotation (used for the backward pass).
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ x, const float* __restrict__ cosb, const float* __restrict__ sinb,
+                            long long tokens, int S, int H, int D, long long row_stride, int inverse) {
+  const int half = D / 2;
+  const long long total = tokens * H * half;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % half);
+    const long long th = i / half;
+    const int h = (int)(th % H);
+    const long long t = th / H;
+    const int pos = (int)(t % S);
+    T* p = x + t * row_stride + (long long)h * D;
+    const float c = cosb[(long long)pos * half + j];
+    const float sn = inverse ? -sinb[(long long)pos * half + j] : sinb[(long long)pos * half + j];
+    const float a = to_f32<T>(p[j]);
+    const float b = to_f32<T>(p[j + half]);
+    p[j] = from_f32<T>(a * c - b * sn);
+    p[j + half] = from_f32<T>(b * c + a * sn);
+  }
+}
+
+void rope_apply(at::Tensor& x, const at::Tensor& cosb, const at::Tensor& sinb, int64_t S, int64_t H, int64_t D,
+                bool inverse) {
+  const long long row_stride = x.stride(-3);
+  const long long tokens = x.numel() / x.size(-3) / x.size(-2) / x.size(-1) * x.size(-3);
+  (void)tokens;
+  const long long T = x.size(0) * x.size(1);
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int blocks = (int)std::min<long long>((T * H * (D / 2) + 255) / 256, num_sms(x.get_device()) * 16LL);
+  if (x.scalar_type() == at::kBFloat16)
+    rope_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((__nv_bfloat16*)x.data_ptr(), cosb.data_ptr<float>(),
+                                                      sinb.data_ptr<float>(), T, (int)S, (int)H, (int)D, row_stride, inverse);
+  else if (x.scalar_type() == at::kHalf)
+    rope_kernel<__half><<<blocks, 256, 0, s>>>((__half*)x.data_ptr(), cosb.data_ptr<float>(), sinb.data_ptr<float>(), T,
+                                               (int)S, (int)H, (int)D, row_stride, inverse);
+  else
+    rope_kernel<float><<<blocks, 256, 0, s>>>(x.data_ptr<float>(), cosb.data_ptr<float>(), sinb.data_ptr<float>(), T,
+                                              (int)S, (int)H, (int)D, row_stride, inverse);
+  KB_LAUNCHED();
+}
+
+void register_elementwise_ops(pybind11::module& m) {
+  m.def("embedding_forward", &embedding_forward);
+  m.def("embedding_backward", &embedding_backward);
+  m.def("cross_entropy_forward", &cross_entropy_forward);
+  m.def("cross_entropy_backward", &cross_entropy_backward);
+  m.def("bias_grad", &bias_grad);
+  m.def("cast_multi", &cast_multi);
+  m.def("swiglu_forward", &swiglu_forward);
+  m.def("swiglu_backward", &swiglu_backward);
+  m.def("rope_apply", &rope_apply);
+}
+
+}  // namespace kb

@@ -376,7 +376,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     attr_set = true;
   }
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
-  KB_CUDA_CHECK(cudaGetLastError());
+  KB_LAUNCHED();
 }
 
 template <int BN, typename OutT>

@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <array>
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -129,6 +130,19 @@ inline CUtensorMap make_tma(const void* base, at::ScalarType dtype, int rank, co
   }
   return map;
 }
+
+// Host-side count of kernels launched by this library (a benchmark reads it
+// before and after a timed region).
+inline std::atomic<long long>& launch_counter() {
+  static std::atomic<long long> n{0};
+  return n;
+}
+
+#define KB_LAUNCHED()                      \
+  do {                                     \
+    ::kb::launch_counter().fetch_add(1);   \
+    KB_CUDA_CHECK(cudaGetLastError());     \
+  } while (0)
 
 // Device status word: one int per device, allocated once and kept alive for
 // the life of the process. Kernels with bounded waits record timeouts here.

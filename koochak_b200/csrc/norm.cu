@@ -1,3 +1,363 @@
-// placeholder, filled in below
+// LayerNorm and RMSNorm forward/backward for sm_100a.
+//
+// One warp owns one row; each lane keeps VPT values of the row in registers
+// (rows up to 32*VPT wide, VPT chosen per call). Inputs may be fp32 (a
+// residual stream kept in fp32, as autocast does) or bf16/fp16; the normalised
+// output is written in the compute dtype for the next GEMM. Statistics are
+// fp32 and saved for the backward pass.
+//
+// Backward writes dx (optionally adding an incoming residual gradient in the
+// same pass) and accumulates dgamma/dbeta per CTA in registers; a persistent
+// grid keeps the partial buffer at (#CTAs x C) and a second kernel reduces it.
+#include "host_utils.h"
+#include "sm100.cuh"
+
 #include <torch/extension.h>
-namespace kb { void register_norm_ops(pybind11::module& m) {} }
+
+namespace kb {
+
+constexpr int kNormWarps = 8;
+
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  float4 q = *reinterpret_cast<const float4*>(p);
+  v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  uint2 q = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&q);
+  for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(e[i]);
+}
+template <>
+__device__ __forceinline__ void load4<__half>(const __half* p, float (&v)[4]) {
+  uint2 q = *reinterpret_cast<const uint2*>(p);
+  const __half* e = reinterpret_cast<const __half*>(&q);
+  for (int i = 0; i < 4; ++i) v[i] = __half2float(e[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void store4(T* p, const float (&v)[4]);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[4]) {
+  uint2 q;
+  q.x = pack_bf16(v[0], v[1]);
+  q.y = pack_bf16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = q;
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* p, const float (&v)[4]) {
+  uint2 q;
+  q.x = pack_f16(v[0], v[1]);
+  q.y = pack_f16(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = q;
+}
+
+// Column layout: lane l owns columns {4*l + 128*j + t : j < VPT/4, t < 4}.
+template <int VPT, typename TIn, typename TOut, bool RMS>
+__global__ void __launch_bounds__(32 * kNormWarps)
+    norm_fwd_kernel(const TIn* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                    TOut* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out, int M, int C,
+                    float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kNormWarps + warp;
+  if (row >= M) return;
+  const TIn* xr = x + (long long)row * C;
+  float v[VPT];
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT / 4; ++j) {
+    const int col = 4 * lane + 128 * j;
+    float q[4] = {0.f, 0.f, 0.f, 0.f};
+    if (col < C) load4<TIn>(xr + col, q);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      v[4 * j + t] = q[t];
+      sum += q[t];
+    }
+  }
+  float mean = 0.f;
+  if (!RMS) mean = warp_sum(sum) / C;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT / 4; ++j) {
+    const int col = 4 * lane + 128 * j;
+    if (col < C) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float d = v[4 * j + t] - mean;
+        ss += d * d;
+      }
+    }
+  }
+  const float var = warp_sum(ss) / C;
+  const float rstd = rsqrtf(var + eps);
+  if (lane == 0) {
+    if (!RMS) mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+  TOut* yr = y + (long long)row * C;
+#pragma unroll
+  for (int j = 0; j < VPT / 4; ++j) {
+    const int col = 4 * lane + 128 * j;
+    if (col < C) {
+      float wq[4], o[4];
+      load4<float>(w + col, wq);
+      float bq[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!RMS && b != nullptr) load4<float>(b + col, bq);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) o[t] = (v[4 * j + t] - mean) * rstd * wq[t] + bq[t];
+      store4<TOut>(yr + col, o);
+    }
+  }
+}
+
+// dx = rstd * (w*dy - mean(w*dy) - xhat*mean(w*dy*xhat))     (LayerNorm)
+// dx = rstd * (w*dy - xhat*mean(w*dy*xhat))                   (RMSNorm)
+template <int VPT, typename TIn, typename TG, typename TDx, bool RMS>
+__global__ void __launch_bounds__(32 * kNormWarps)
+    norm_bwd_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
+                    const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                    const TDx* __restrict__ dres, TDx* __restrict__ dx, float* __restrict__ dw_part,
+                    float* __restrict__ db_part, int M, int C) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float dw_acc[VPT];
+  float db_acc[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    dw_acc[i] = 0.f;
+    db_acc[i] = 0.f;
+  }
+  float wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT / 4; ++j) {
+    const int col = 4 * lane + 128 * j;
+    float q[4] = {0.f, 0.f, 0.f, 0.f};
+    if (col < C) load4<float>(w + col, q);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) wv[4 * j + t] = q[t];
+  }
+  for (int row = blockIdx.x * kNormWarps + warp; row < M; row += gridDim.x * kNormWarps) {
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
+    const TIn* xr = x + (long long)row * C;
+    const TG* gr = dy + (long long)row * C;
+    float xh[VPT], g[VPT];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT / 4; ++j) {
+      const int col = 4 * lane + 128 * j;
+      float xq[4] = {0.f, 0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
+      if (col < C) {
+        load4<TIn>(xr + col, xq);
+        load4<TG>(gr + col, gq);
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int i = 4 * j + t;
+        xh[i] = (col < C) ? (xq[t] - mean) * rstd : 0.f;
+        g[i] = gq[t];
+        const float wg = wv[i] * g[i];
+        s1 += wg;
+        s2 += wg * xh[i];
+        dw_acc[i] += g[i] * xh[i];
+        db_acc[i] += g[i];
+      }
+    }
+    s1 = warp_sum(s1) / C;
+    s2 = warp_sum(s2) / C;
+    TDx* dxr = dx + (long long)row * C;
+    const TDx* drr = dres ? dres + (long long)row * C : nullptr;
+#pragma unroll
+    for (int j = 0; j < VPT / 4; ++j) {
+      const int col = 4 * lane + 128 * j;
+      if (col < C) {
+        float o[4];
+        float rq[4] = {0.f, 0.f, 0.f, 0.f};
+        if (drr) load4<TDx>(drr + col, rq);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int i = 4 * j + t;
+          const float wg = wv[i] * g[i];
+          o[t] = rstd * (wg - (RMS ? 0.f : s1) - xh[i] * s2) + rq[t];
+        }
+        store4<TDx>(dxr + col, o);
+      }
+    }
+  }
+  // Per-warp partials -> shared -> one row of partials per CTA.
+  __shared__ float red[kNormWarps][32];
+#pragma unroll
+  for (int j = 0; j < VPT / 4; ++j) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int i = 4 * j + t;
+      const int col = 4 * lane + 128 * j + t;
+      red[warp][lane] = dw_acc[i];
+      __syncthreads();
+      if (warp == 0) {
+        float s = 0.f;
+        for (int k = 0; k < kNormWarps; ++k) s += red[k][lane];
+        if (col < C) dw_part[(long long)blockIdx.x * C + col] = s;
+      }
+      __syncthreads();
+      if (!RMS && db_part != nullptr) {
+        red[warp][lane] = db_acc[i];
+        __syncthreads();
+        if (warp == 0) {
+          float s = 0.f;
+          for (int k = 0; k < kNormWarps; ++k) s += red[k][lane];
+          if (col < C) db_part[(long long)blockIdx.x * C + col] = s;
+        }
+        __syncthreads();
+      }
+    }
+  }
+}
+
+// out[c] (+)= sum_r part[r, c]
+__global__ void column_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, int R, int C,
+                                     int accumulate) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= C) return;
+  float s = 0.f;
+  for (int r = 0; r < R; ++r) s += part[(long long)r * C + col];
+  out[col] = accumulate ? out[col] + s : s;
+}
+
+// ---------------------------------------------------------------------- host
+
+template <typename F>
+static void with_vpt(int C, F&& f) {
+  if (C <= 256) f(std::integral_constant<int, 8>{});
+  else if (C <= 512) f(std::integral_constant<int, 16>{});
+  else if (C <= 768) f(std::integral_constant<int, 24>{});
+  else if (C <= 1024) f(std::integral_constant<int, 32>{});
+  else if (C <= 2048) f(std::integral_constant<int, 64>{});
+  else if (C <= 4096) f(std::integral_constant<int, 128>{});
+  else KB_CHECK(false, "norm: rows wider than 4096 are not supported");
+}
+
+template <typename F>
+static void with_lp_type(at::ScalarType t, F&& f) {
+  if (t == at::kBFloat16) f(__nv_bfloat16{});
+  else if (t == at::kHalf) f(__half{});
+  else KB_CHECK(false, "norm backward: dy must be bf16 or fp16");
+}
+
+template <typename F>
+static void with_type(at::ScalarType t, F&& f) {
+  if (t == at::kFloat) f(float{});
+  else if (t == at::kBFloat16) f(__nv_bfloat16{});
+  else if (t == at::kHalf) f(__half{});
+  else KB_CHECK(false, "norm: unsupported dtype");
+}
+
+// y = norm(x) * w + b ; returns nothing, writes y, mean (LayerNorm only), rstd.
+void norm_forward(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& b, at::Tensor& y,
+                  const c10::optional<at::Tensor>& mean, at::Tensor& rstd, double eps, bool rms) {
+  check_cuda_tensor(x, "x");
+  KB_CHECK(x.is_contiguous() && y.is_contiguous(), "norm: x and y must be contiguous");
+  const int C = (int)x.size(-1);
+  const int M = (int)(x.numel() / C);
+  KB_CHECK(C % 4 == 0, "norm: row width must be a multiple of 4");
+  KB_CHECK(w.scalar_type() == at::kFloat && w.numel() == C, "norm: weight must be fp32 [C]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
+  const float* bp = (b.has_value() && b->defined()) ? b->data_ptr<float>() : nullptr;
+  float* mp = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
+  KB_CHECK(rms || mp != nullptr, "LayerNorm needs a mean buffer");
+  const int grid = (M + kNormWarps - 1) / kNormWarps;
+  with_vpt(C, [&](auto vpt) {
+    constexpr int V = decltype(vpt)::value;
+    with_type(x.scalar_type(), [&](auto tin) {
+      using TIn = decltype(tin);
+      with_type(y.scalar_type(), [&](auto tout) {
+        using TOut = decltype(tout);
+        if (rms)
+          norm_fwd_kernel<V, TIn, TOut, true><<<grid, 32 * kNormWarps, 0, stream>>>(
+              (const TIn*)x.data_ptr(), w.data_ptr<float>(), nullptr, (TOut*)y.data_ptr(), nullptr,
+              rstd.data_ptr<float>(), M, C, (float)eps);
+        else
+          norm_fwd_kernel<V, TIn, TOut, false><<<grid, 32 * kNormWarps, 0, stream>>>(
+              (const TIn*)x.data_ptr(), w.data_ptr<float>(), bp, (TOut*)y.data_ptr(), mp, rstd.data_ptr<float>(), M,
+              C, (float)eps);
+      });
+    });
+  });
+  KB_LAUNCHED();
+}
+
+// Writes dx (= norm backward + optional dres) and dw (and db for LayerNorm),
+// accumulating into dw/db when `accumulate` is set. `workspace` is fp32 scratch
+// of at least (2 * grid * C) elements, grid = min(#SMs * 4, ceil(M / 8)).
+void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                   const c10::optional<at::Tensor>& mean, const at::Tensor& rstd, const c10::optional<at::Tensor>& dres,
+                   at::Tensor& dx, at::Tensor& dw, const c10::optional<at::Tensor>& db, at::Tensor& workspace,
+                   bool rms, bool accumulate) {
+  check_cuda_tensor(dy, "dy");
+  KB_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous(), "norm bwd: contiguous tensors required");
+  const int C = (int)x.size(-1);
+  const int M = (int)(x.numel() / C);
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
+  const int dev = x.get_device();
+  const int grid = std::max(1, std::min(num_sms(dev) * 4, (M + kNormWarps - 1) / kNormWarps));
+  KB_CHECK(workspace.scalar_type() == at::kFloat && workspace.numel() >= 2LL * grid * C, "norm bwd: workspace too small");
+  float* dw_part = workspace.data_ptr<float>();
+  float* db_part = rms ? nullptr : dw_part + (long long)grid * C;
+  const float* mp = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
+  KB_CHECK(rms || mp, "LayerNorm backward needs mean");
+  const bool has_res = dres.has_value() && dres->defined();
+  KB_CHECK(dx.scalar_type() == x.scalar_type(), "norm bwd: dx must have the dtype of x");
+  if (has_res) KB_CHECK(dres->scalar_type() == dx.scalar_type() && dres->is_contiguous(), "dres must match dx");
+  with_vpt(C, [&](auto vpt) {
+    constexpr int V = decltype(vpt)::value;
+    with_type(x.scalar_type(), [&](auto tin) {
+      using TIn = decltype(tin);
+      with_lp_type(dy.scalar_type(), [&](auto tg) {
+        using TG = decltype(tg);
+        {
+          using TDx = TIn;
+          const TDx* rp = has_res ? (const TDx*)dres->data_ptr() : nullptr;
+          if (rms)
+            norm_bwd_kernel<V, TIn, TG, TDx, true><<<grid, 32 * kNormWarps, 0, stream>>>(
+                (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), nullptr,
+                rstd.data_ptr<float>(), rp, (TDx*)dx.data_ptr(), dw_part, nullptr, M, C);
+          else
+            norm_bwd_kernel<V, TIn, TG, TDx, false><<<grid, 32 * kNormWarps, 0, stream>>>(
+                (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), mp, rstd.data_ptr<float>(),
+                rp, (TDx*)dx.data_ptr(), dw_part, db_part, M, C);
+        }
+      });
+    });
+  });
+  KB_LAUNCHED();
+  KB_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == C, "dw must be fp32 [C]");
+  column_reduce_kernel<<<(C + 255) / 256, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), grid, C, accumulate);
+  KB_LAUNCHED();
+  if (!rms && db.has_value() && db->defined()) {
+    KB_CHECK(db->scalar_type() == at::kFloat && db->numel() == C, "db must be fp32 [C]");
+    column_reduce_kernel<<<(C + 255) / 256, 256, 0, stream>>>(db_part, db->data_ptr<float>(), grid, C, accumulate);
+    KB_LAUNCHED();
+  }
+}
+
+int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
+  const int grid = std::max<int64_t>(1, std::min<int64_t>(num_sms((int)device) * 4, (M + kNormWarps - 1) / kNormWarps));
+  return 2LL * grid * C;
+}
+
+void register_norm_ops(pybind11::module& m) {
+  m.def("norm_forward", &norm_forward, "LayerNorm/RMSNorm forward");
+  m.def("norm_backward", &norm_backward, "LayerNorm/RMSNorm backward");
+  m.def("norm_backward_workspace_elems", &norm_backward_workspace_elems, "scratch size for norm_backward");
+}
+
+}  // namespace kb

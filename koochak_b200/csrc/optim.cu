@@ -1,3 +1,496 @@
-// placeholder, filled in below
+// Optimizer-side kernels for sm_100a.
+//
+//  * grad_stats: one pass over every gradient that (optionally) unscales it in
+//    place (GradScaler), flags any non-finite entry, and accumulates per-tensor
+//    sums of squares in fp64; a one-thread finalize turns them into the global
+//    L2 norm and the clip coefficient min(1, max_norm / (norm + 1e-6)) on the
+//    device, so the host needs one small read per step.
+//  * adamw_step: the Adam update of the aux-Adam groups (bias-corrected,
+//    decoupled weight decay) with the clip coefficient applied on read, and
+//    optionally the EMA update of the new parameter and its bf16 shadow copy,
+//    all in one pass.
+//  * muon_prologue / muon_scale / muon_epilogue: the per-matrix parts of Muon
+//    around the Newton-Schulz GEMMs (momentum + Nesterov + bf16 cast with an
+//    optional transpose + Frobenius sum of squares; normalisation; parameter
+//    update with weight decay, fused EMA and bf16 shadow).
+//  * ema_update: shadow = d * shadow + (1 - d) * param for a tensor list.
+//
+// Tensor lists are passed by value in the kernel parameter block (<= 32 KB)
+// together with a block table, so a call is one launch and no host-to-device
+// copy.
+#include "host_utils.h"
+#include "sm100.cuh"
+
 #include <torch/extension.h>
-namespace kb { void register_optim_ops(pybind11::module& m) {} }
+
+#include <cmath>
+#include <vector>
+
+namespace kb {
+
+constexpr int kChunk = 8192;      // elements per block-table entry
+constexpr int kMaxT = 96;         // tensors per launch
+constexpr int kMaxBlocks = 1024;  // block-table entries per launch
+
+struct BlockTable {
+  int n_blocks;
+  int tensor[kMaxBlocks];
+  int chunk[kMaxBlocks];
+};
+
+template <typename F>
+static void for_each_launch(const std::vector<int64_t>& numels, F&& launch) {
+  // Splits the tensor list into launches that respect kMaxT and kMaxBlocks.
+  size_t t = 0;
+  int64_t chunk_in_t = 0;
+  while (t < numels.size()) {
+    std::vector<int> tensors;
+    BlockTable bt;
+    bt.n_blocks = 0;
+    while (t < numels.size() && (int)tensors.size() < kMaxT && bt.n_blocks < kMaxBlocks) {
+      const int64_t nch = (numels[t] + kChunk - 1) / kChunk;
+      if (tensors.empty() || tensors.back() != (int)t) tensors.push_back((int)t);
+      const int local = (int)tensors.size() - 1;
+      while (chunk_in_t < nch && bt.n_blocks < kMaxBlocks) {
+        bt.tensor[bt.n_blocks] = local;
+        bt.chunk[bt.n_blocks] = (int)chunk_in_t;
+        ++bt.n_blocks;
+        ++chunk_in_t;
+      }
+      if (chunk_in_t >= nch) {
+        ++t;
+        chunk_in_t = 0;
+      }
+    }
+    if (bt.n_blocks > 0) launch(tensors, bt);
+  }
+}
+
+// ------------------------------------------------------------ grad stats
+
+struct GradStatsArgs {
+  int n;
+  float* g[kMaxT];
+  long long numel[kMaxT];
+  int global_index[kMaxT];  // index into the per-tensor accumulator array
+};
+
+__global__ void __launch_bounds__(256)
+    grad_stats_kernel(const __grid_constant__ GradStatsArgs a, const __grid_constant__ BlockTable bt,
+                      const float* __restrict__ inv_scale, double* __restrict__ sumsq, int* __restrict__ nonfinite) {
+  const int ti = bt.tensor[blockIdx.x];
+  float* g = a.g[ti];
+  const long long n = a.numel[ti];
+  const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
+  const long long end = min(n, start + kChunk);
+  const float s = inv_scale ? *inv_scale : 1.f;
+  float acc = 0.f;
+  bool bad = false;
+  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) {
+    float x = g[i];
+    if (inv_scale) {
+      x *= s;
+      g[i] = x;
+    }
+    bad |= !isfinite(x);
+    acc += x * x;
+  }
+  acc = warp_sum(acc);
+  __shared__ float red[8];
+  __shared__ int any_bad;
+  if (threadIdx.x == 0) any_bad = 0;
+  __syncthreads();
+  if (bad) any_bad = 1;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    atomicAdd(&sumsq[a.global_index[ti]], (double)t);
+    if (any_bad) atomicExch(nonfinite, 1);
+  }
+}
+
+// out[0] = global norm, out[1] = clip coefficient, out[2] = non-finite flag (0/1)
+__global__ void grad_stats_finalize_kernel(const double* __restrict__ sumsq, int n, const int* __restrict__ nonfinite,
+                                           float max_norm, int clip, float* __restrict__ out,
+                                           float* __restrict__ per_tensor_norm) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double total = 0.0;
+  for (int i = 0; i < n; ++i) {
+    const double v = sumsq[i];
+    // Per-tensor norms are rounded to fp32 first, as a foreach norm would.
+    const float nt = (float)sqrt(v);
+    if (per_tensor_norm) per_tensor_norm[i] = nt;
+    total += (double)nt * (double)nt;
+  }
+  const double norm = sqrt(total);
+  float coef = 1.f;
+  if (clip) {
+    const double c = (double)max_norm / (norm + 1e-6);
+    coef = (float)(c < 1.0 ? c : 1.0);
+  }
+  out[0] = (float)norm;
+  out[1] = coef;
+  out[2] = (*nonfinite || !isfinite(norm)) ? 1.f : 0.f;
+}
+
+// grads: fp32 tensors. scratch: fp64 [n] + int flag (caller supplies, zeroed here).
+// out: fp32 [3] as above. per_tensor: optional fp32 [n].
+void grad_stats(const std::vector<at::Tensor>& grads, const c10::optional<at::Tensor>& inv_scale, double max_norm,
+                bool clip, at::Tensor& scratch, at::Tensor& out, const c10::optional<at::Tensor>& per_tensor) {
+  KB_CHECK(!grads.empty(), "grad_stats: empty gradient list");
+  const int n = (int)grads.size();
+  KB_CHECK(scratch.scalar_type() == at::kDouble && scratch.numel() >= n + 1, "grad_stats: scratch must be fp64 [n+1]");
+  const c10::cuda::CUDAGuard guard(grads[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  double* sumsq = scratch.data_ptr<double>();
+  int* flag = reinterpret_cast<int*>(sumsq + n);
+  KB_CUDA_CHECK(cudaMemsetAsync(sumsq, 0, (n + 1) * sizeof(double), s));
+  std::vector<int64_t> numels;
+  for (auto& g : grads) {
+    KB_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && g.is_cuda(), "grad_stats: fp32 contiguous CUDA grads");
+    numels.push_back(g.numel());
+  }
+  const float* isp = (inv_scale.has_value() && inv_scale->defined()) ? inv_scale->data_ptr<float>() : nullptr;
+  int base = 0;
+  for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
+    GradStatsArgs a{};
+    a.n = (int)tensors.size();
+    for (int i = 0; i < a.n; ++i) {
+      const int gi = tensors[i];
+      a.g[i] = grads[gi].data_ptr<float>();
+      a.numel[i] = grads[gi].numel();
+      a.global_index[i] = gi;
+    }
+    grad_stats_kernel<<<bt.n_blocks, 256, 0, s>>>(a, bt, isp, sumsq, flag);
+    KB_LAUNCHED();
+    base += a.n;
+  });
+  float* ptn = (per_tensor.has_value() && per_tensor->defined()) ? per_tensor->data_ptr<float>() : nullptr;
+  grad_stats_finalize_kernel<<<1, 32, 0, s>>>(sumsq, n, flag, (float)max_norm, clip ? 1 : 0, out.data_ptr<float>(), ptn);
+  KB_LAUNCHED();
+}
+
+// ------------------------------------------------------------ AdamW
+
+struct AdamArgs {
+  int n;
+  float* p[kMaxT];
+  const float* g[kMaxT];
+  float* m[kMaxT];
+  float* v[kMaxT];
+  float* ema[kMaxT];       // may be null
+  void* shadow[kMaxT];     // bf16 copy, may be null
+  long long numel[kMaxT];
+  float bc1[kMaxT];        // 1 - beta1^step
+  float bc2[kMaxT];        // 1 - beta2^step
+};
+
+__global__ void __launch_bounds__(256)
+    adamw_kernel(const __grid_constant__ AdamArgs a, const __grid_constant__ BlockTable bt,
+                 const float* __restrict__ coef_ptr, float lr, float beta1, float beta2, float eps, float wd,
+                 float ema_decay) {
+  const int ti = bt.tensor[blockIdx.x];
+  const long long n = a.numel[ti];
+  const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
+  const long long end = min(n, start + kChunk);
+  float* p = a.p[ti];
+  const float* g = a.g[ti];
+  float* m = a.m[ti];
+  float* v = a.v[ti];
+  float* e = a.ema[ti];
+  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(a.shadow[ti]);
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  const float inv_bc1 = 1.f / a.bc1[ti];
+  const float inv_bc2 = 1.f / a.bc2[ti];
+  const float decay = 1.f - lr * wd;
+  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) {
+    const float gi = g[i] * coef;
+    float mi = m[i];
+    float vi = v[i];
+    mi = mi + (1.f - beta1) * (gi - mi);
+    vi = vi + (1.f - beta2) * (gi * gi - vi);
+    m[i] = mi;
+    v[i] = vi;
+    const float upd = (mi * inv_bc1) / (sqrtf(vi * inv_bc2) + eps);
+    const float pn = p[i] * decay - lr * upd;
+    p[i] = pn;
+    if (e) e[i] = e[i] * ema_decay + (1.f - ema_decay) * pn;
+    if (sh) sh[i] = __float2bfloat16_rn(pn);
+  }
+}
+
+void adamw_step(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
+                const std::vector<at::Tensor>& exp_avg, const std::vector<at::Tensor>& exp_avg_sq,
+                const std::vector<int64_t>& steps, const std::vector<at::Tensor>& ema,
+                const std::vector<at::Tensor>& shadow, const c10::optional<at::Tensor>& coef, double lr, double beta1,
+                double beta2, double eps, double weight_decay, double ema_decay) {
+  const size_t n = params.size();
+  KB_CHECK(grads.size() == n && exp_avg.size() == n && exp_avg_sq.size() == n && steps.size() == n,
+           "adamw_step: list lengths differ");
+  KB_CHECK(ema.empty() || ema.size() == n, "adamw_step: ema list length");
+  KB_CHECK(shadow.empty() || shadow.size() == n, "adamw_step: shadow list length");
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  std::vector<int64_t> numels;
+  for (size_t i = 0; i < n; ++i) {
+    KB_CHECK(params[i].scalar_type() == at::kFloat && params[i].is_contiguous() && grads[i].is_contiguous() &&
+                 grads[i].scalar_type() == at::kFloat && exp_avg[i].is_contiguous() && exp_avg_sq[i].is_contiguous(),
+             "adamw_step: fp32 contiguous tensors required");
+    numels.push_back(params[i].numel());
+  }
+  const float* cp = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
+  for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
+    AdamArgs a{};
+    a.n = (int)tensors.size();
+    for (int i = 0; i < a.n; ++i) {
+      const int k = tensors[i];
+      a.p[i] = params[k].data_ptr<float>();
+      a.g[i] = grads[k].data_ptr<float>();
+      a.m[i] = exp_avg[k].data_ptr<float>();
+      a.v[i] = exp_avg_sq[k].data_ptr<float>();
+      a.ema[i] = (ema.empty() || ema[k].numel() == 0) ? nullptr : ema[k].data_ptr<float>();
+      a.shadow[i] = (shadow.empty() || shadow[k].numel() == 0) ? nullptr : shadow[k].data_ptr();
+      a.numel[i] = params[k].numel();
+      a.bc1[i] = (float)(1.0 - std::pow(beta1, (double)steps[k]));
+      a.bc2[i] = (float)(1.0 - std::pow(beta2, (double)steps[k]));
+    }
+    adamw_kernel<<<bt.n_blocks, 256, 0, s>>>(a, bt, cp, (float)lr, (float)beta1, (float)beta2, (float)eps,
+                                             (float)weight_decay, (float)ema_decay);
+    KB_LAUNCHED();
+  });
+}
+
+// ------------------------------------------------------------ EMA
+
+struct EmaArgs {
+  int n;
+  float* shadow[kMaxT];
+  const float* param[kMaxT];
+  long long numel[kMaxT];
+};
+
+__global__ void __launch_bounds__(256) ema_kernel(const __grid_constant__ EmaArgs a, const __grid_constant__ BlockTable bt,
+                                                  float d) {
+  const int ti = bt.tensor[blockIdx.x];
+  const long long n = a.numel[ti];
+  const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
+  const long long end = min(n, start + kChunk);
+  float* sh = a.shadow[ti];
+  const float* p = a.param[ti];
+  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) sh[i] = sh[i] * d + (1.f - d) * p[i];
+}
+
+void ema_update(const std::vector<at::Tensor>& shadow, const std::vector<at::Tensor>& params, double decay) {
+  KB_CHECK(shadow.size() == params.size(), "ema_update: list lengths differ");
+  if (shadow.empty()) return;
+  const c10::cuda::CUDAGuard guard(shadow[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  std::vector<int64_t> numels;
+  for (size_t i = 0; i < shadow.size(); ++i) {
+    KB_CHECK(shadow[i].scalar_type() == at::kFloat && params[i].scalar_type() == at::kFloat &&
+                 shadow[i].is_contiguous() && params[i].is_contiguous() && shadow[i].numel() == params[i].numel(),
+             "ema_update: fp32 contiguous tensors of equal size required");
+    numels.push_back(shadow[i].numel());
+  }
+  for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
+    EmaArgs a{};
+    a.n = (int)tensors.size();
+    for (int i = 0; i < a.n; ++i) {
+      a.shadow[i] = shadow[tensors[i]].data_ptr<float>();
+      a.param[i] = params[tensors[i]].data_ptr<float>();
+      a.numel[i] = shadow[tensors[i]].numel();
+    }
+    ema_kernel<<<bt.n_blocks, 256, 0, s>>>(a, bt, (float)decay);
+    KB_LAUNCHED();
+  });
+}
+
+// ------------------------------------------------------------ Muon
+
+constexpr int kMuonMax = 64;
+struct MuonMats {
+  int n;
+  int R, C;  // parameter shape (rows, cols)
+  const float* g[kMuonMax];
+  float* mom[kMuonMax];
+  float* p[kMuonMax];
+  float* ema[kMuonMax];
+  void* shadow[kMuonMax];
+};
+
+// X[i] = bf16(nesterov(momentum update)) stored [R, C] or transposed [C, R];
+// sumsq[i] += sum X^2 (of the bf16 values).
+__global__ void __launch_bounds__(256)
+    muon_prologue_kernel(const __grid_constant__ MuonMats mm, __nv_bfloat16* __restrict__ X, float* __restrict__ sumsq,
+                         const float* __restrict__ coef_ptr, float beta, int nesterov, int transpose) {
+  const int i = blockIdx.z;
+  const int R = mm.R, C = mm.C;
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const float* g = mm.g[i];
+  float* m = mm.mom[i];
+  float local = 0.f;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = r0 + ty + 8 * k, c = c0 + tx;
+    float u = 0.f;
+    if (r < R && c < C) {
+      const long long idx = (long long)r * C + c;
+      const float gi = g[idx] * coef;
+      float mi = m[idx];
+      mi = mi + (1.f - beta) * (gi - mi);
+      m[idx] = mi;
+      u = nesterov ? gi + beta * (mi - gi) : mi;
+      u = __bfloat162float(__float2bfloat16_rn(u));
+      local += u * u;
+      if (!transpose) X[(long long)i * R * C + idx] = __float2bfloat16_rn(u);
+    }
+    tile[ty + 8 * k][tx] = u;
+  }
+  if (transpose) {
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + ty + 8 * k, r = r0 + tx;  // output row = c, col = r
+      if (r < R && c < C) X[(long long)i * R * C + (long long)c * R + r] = __float2bfloat16_rn(tile[tx][ty + 8 * k]);
+    }
+  }
+  local = warp_sum(local);
+  if (tx == 0) atomicAdd(&sumsq[i], local);
+}
+
+// X[i] *= 1 / (sqrt(sumsq[i]) + 1e-7)
+__global__ void muon_scale_kernel(__nv_bfloat16* __restrict__ X, const float* __restrict__ sumsq, long long per_mat) {
+  const int i = blockIdx.y;
+  const float inv = 1.f / (sqrtf(sumsq[i]) + 1e-7f);
+  __nv_bfloat16* x = X + (long long)i * per_mat;
+  for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < per_mat; j += (long long)gridDim.x * blockDim.x)
+    x[j] = __float2bfloat16_rn(__bfloat162float(x[j]) * inv);
+}
+
+// p = p * (1 - lr*wd) - lr * scale * U  (U = X or X^T), then EMA and bf16 shadow.
+__global__ void __launch_bounds__(256)
+    muon_epilogue_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr, float wd,
+                         float scale, int transpose, float ema_decay) {
+  const int i = blockIdx.z;
+  const int R = mm.R, C = mm.C;
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const __nv_bfloat16* x = X + (long long)i * R * C;
+  if (transpose) {
+    // X is [C, R]: read a 32x32 block coalesced along R, transpose through smem.
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + ty + 8 * k, r = r0 + tx;
+      tile[ty + 8 * k][tx] = (r < R && c < C) ? __bfloat162float(x[(long long)c * R + r]) : 0.f;
+    }
+    __syncthreads();
+  }
+  float* p = mm.p[i];
+  float* e = mm.ema[i];
+  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(mm.shadow[i]);
+  const float decay = 1.f - lr * wd;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = r0 + ty + 8 * k, c = c0 + tx;
+    if (r < R && c < C) {
+      const long long idx = (long long)r * C + c;
+      const float u = transpose ? tile[tx][ty + 8 * k] : __bfloat162float(x[idx]);
+      const float pn = p[idx] * decay - lr * (scale * u);
+      p[idx] = pn;
+      if (e) e[idx] = e[idx] * ema_decay + (1.f - ema_decay) * pn;
+      if (sh) sh[idx] = __float2bfloat16_rn(pn);
+    }
+  }
+}
+
+static MuonMats make_mats(const std::vector<at::Tensor>& grads, const std::vector<at::Tensor>& moms,
+                          const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& ema,
+                          const std::vector<at::Tensor>& shadow, size_t base, int count) {
+  MuonMats mm{};
+  mm.n = count;
+  const auto& p0 = params.empty() ? grads[base] : params[base];
+  mm.R = (int)p0.size(0);
+  mm.C = (int)(p0.numel() / p0.size(0));
+  for (int j = 0; j < count; ++j) {
+    const size_t k = base + j;
+    if (!grads.empty()) mm.g[j] = grads[k].data_ptr<float>();
+    if (!moms.empty()) mm.mom[j] = moms[k].data_ptr<float>();
+    if (!params.empty()) mm.p[j] = params[k].data_ptr<float>();
+    mm.ema[j] = (ema.empty() || ema[k].numel() == 0) ? nullptr : ema[k].data_ptr<float>();
+    mm.shadow[j] = (shadow.empty() || shadow[k].numel() == 0) ? nullptr : shadow[k].data_ptr();
+  }
+  return mm;
+}
+
+// X: bf16 [n, r, c] workspace (r <= c after the optional transpose), sumsq: fp32 [n] scratch.
+void muon_prologue(const std::vector<at::Tensor>& grads, const std::vector<at::Tensor>& moms, at::Tensor& X,
+                   at::Tensor& sumsq, const c10::optional<at::Tensor>& coef, double beta, bool nesterov, bool transpose) {
+  const size_t n = grads.size();
+  KB_CHECK(n > 0 && moms.size() == n, "muon_prologue: list lengths");
+  const c10::cuda::CUDAGuard guard(grads[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int R = (int)grads[0].size(0);
+  const int C = (int)(grads[0].numel() / R);
+  for (size_t i = 0; i < n; ++i)
+    KB_CHECK(grads[i].is_contiguous() && moms[i].is_contiguous() && grads[i].numel() == (int64_t)R * C &&
+                 grads[i].scalar_type() == at::kFloat,
+             "muon_prologue: same-shape fp32 contiguous matrices required");
+  KB_CHECK(X.scalar_type() == at::kBFloat16 && X.numel() >= (int64_t)n * R * C, "muon_prologue: X too small");
+  KB_CUDA_CHECK(cudaMemsetAsync(sumsq.data_ptr<float>(), 0, n * sizeof(float), s));
+  const float* cp = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
+  for (size_t base = 0; base < n; base += kMuonMax) {
+    const int count = (int)std::min<size_t>(kMuonMax, n - base);
+    MuonMats mm = make_mats(grads, moms, {}, {}, {}, base, count);
+    dim3 grid((C + 31) / 32, (R + 31) / 32, count);
+    muon_prologue_kernel<<<grid, 256, 0, s>>>(mm, (__nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C,
+                                              sumsq.data_ptr<float>() + base, cp, (float)beta, nesterov ? 1 : 0,
+                                              transpose ? 1 : 0);
+    KB_LAUNCHED();
+  }
+}
+
+void muon_scale(at::Tensor& X, const at::Tensor& sumsq, int64_t n) {
+  const c10::cuda::CUDAGuard guard(X.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const long long per = X.numel() / X.size(0);
+  dim3 grid((unsigned)std::min<long long>((per + 255) / 256, 256), (unsigned)n);
+  muon_scale_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)X.data_ptr(), sumsq.data_ptr<float>(), per);
+  KB_LAUNCHED();
+}
+
+void muon_epilogue(const std::vector<at::Tensor>& params, const at::Tensor& X, const std::vector<at::Tensor>& ema,
+                   const std::vector<at::Tensor>& shadow, double lr, double wd, double scale, bool transpose,
+                   double ema_decay) {
+  const size_t n = params.size();
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int R = (int)params[0].size(0);
+  const int C = (int)(params[0].numel() / R);
+  for (size_t base = 0; base < n; base += kMuonMax) {
+    const int count = (int)std::min<size_t>(kMuonMax, n - base);
+    MuonMats mm = make_mats({}, {}, params, ema, shadow, base, count);
+    dim3 grid((C + 31) / 32, (R + 31) / 32, count);
+    muon_epilogue_kernel<<<grid, 256, 0, s>>>(mm, (const __nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C,
+                                              (float)lr, (float)wd, (float)scale, transpose ? 1 : 0, (float)ema_decay);
+    KB_LAUNCHED();
+  }
+}
+
+void register_optim_ops(pybind11::module& m) {
+  m.def("grad_stats", &grad_stats);
+  m.def("adamw_step", &adamw_step);
+  m.def("ema_update", &ema_update);
+  m.def("muon_prologue", &muon_prologue);
+  m.def("muon_scale", &muon_scale);
+  m.def("muon_epilogue", &muon_epilogue);
+}
+
+}  // namespace kb

@@ -1,0 +1,624 @@
+"""Muon / NorMuon / Hyperball optimizers with auxiliary Adam (reference: koochak/optim/muon.py:13-573).
+
+Semantics follow the reference exactly (momentum lerp, Nesterov, quintic
+Newton-Schulz with (a, b, c) = (3.4445, -4.7750, 2.0315) in bf16 after
+Frobenius normalisation, Moonlight scale 0.2*sqrt(max(rows, cols)), decoupled
+weight decay; bias-corrected Adam for the aux groups; per-parameter state
+``momentum_buffer`` / ``exp_avg``, ``exp_avg_sq`` and an int ``step``), so
+optimizer state dicts are interchangeable with the reference's.
+
+Execution:
+
+* CPU or non-fp32 parameters run the plain-PyTorch functions below (they are
+  also the oracle of the tests).
+* CUDA fp32 parameters run the native path. Muon matrices are bucketed by
+  shape; per bucket one kernel applies the clip coefficient, momentum and
+  Nesterov and writes bf16 (transposed when rows > cols) while accumulating
+  the Frobenius norms, one kernel normalises, the 5 Newton-Schulz iterations
+  are 15 batched tcgen05 GEMMs with the ``b*A + c*A@A`` and ``a*X + B@X``
+  combinations fused into their epilogues, and one kernel applies the update
+  with weight decay, the EMA of the new parameter and its bf16 copy. Aux Adam
+  groups are one multi-tensor kernel (clip coefficient, moments, bias
+  correction, decoupled weight decay, EMA and bf16 copy).
+* Distributed classes (chosen when a process group exists) shard the Muon
+  work: within each shape bucket, matrix k is owned by rank k % world (its
+  momentum lives only there); owners update their matrices and one
+  all-gather per bucket publishes the new values. Adam groups run on every
+  rank, as in the reference.
+
+The training loop passes the gradient-clip coefficient as a device scalar
+(``optimizer.kb_grad_scale``) so gradients are scaled on read instead of being
+rewritten, and may hand over a GPU EMA (``optimizer.kb_ema``) to be fused.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+import os
+from typing import Any, Callable, Dict, Iterable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..utils import flags
+
+__all__ = ["zeropower_via_newtonschulz5", "muon_update", "normuon_update", "adam_update", "HyperballOptimizer",
+           "Muon", "SingleDeviceMuon", "NorMuon", "SingleDeviceNorMuon", "MuonWithAuxAdam",
+           "SingleDeviceMuonWithAuxAdam", "NorMuonWithAuxAdam", "SingleDeviceNorMuonWithAuxAdam", "NS_COEFFS"]
+
+NS_COEFFS = (3.4445, -4.7750, 2.0315)
+
+
+# ----------------------------------------------------------------------------- reference math
+
+
+@flags.compile_wrap
+def zeropower_via_newtonschulz5(G, steps: int):
+    """Quintic Newton-Schulz orthogonalisation in bf16 (approximately U S' V^T)."""
+
+    assert G.ndim >= 2
+    a, b, c = NS_COEFFS
+    X = G.bfloat16()
+    tall = G.size(-2) > G.size(-1)
+    if tall:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
+    for _ in range(steps):
+        A = X @ X.mT
+        B = b * A + c * A @ A
+        X = a * X + B @ X
+    return X.mT if tall else X
+
+
+@flags.compile_wrap
+def muon_update(grad, momentum, beta=0.95, ns_steps=5, nesterov=True):
+    momentum.lerp_(grad, 1 - beta)
+    update = grad.lerp_(momentum, beta) if nesterov else momentum
+    if update.ndim > 2:
+        update = update.reshape(len(update), -1)
+    rows, cols = update.size(-2), update.size(-1)
+    update = zeropower_via_newtonschulz5(update, steps=ns_steps)
+    update *= 0.2 * max(rows, cols) ** 0.5
+    return update
+
+
+@flags.compile_wrap
+def normuon_update(grad, momentum, second_momentum, beta=0.95, beta2=0.95, ns_steps=5, nesterov=True):
+    momentum.lerp_(grad, 1 - beta)
+    update = grad.lerp_(momentum, beta) if nesterov else momentum
+    if update.ndim > 2:
+        update = update.reshape(len(update), -1)
+    rows, cols = update.size(-2), update.size(-1)
+    update = zeropower_via_newtonschulz5(update, steps=ns_steps).float()
+    vnorm = update.norm(dim=(-2, -1), keepdim=True)
+    v_mean = torch.mean(update * update, dim=-1, keepdim=True)
+    second_momentum.lerp_(v_mean, 1 - beta2)
+    update.mul_(1 / second_momentum.sqrt().add_(1e-10))
+    vnorm_new = update.norm(dim=(-2, -1), keepdim=True)
+    update.mul_(vnorm / vnorm_new.add_(1e-10))
+    update *= max(1, rows / cols) ** 0.5
+    return update
+
+
+@flags.compile_wrap
+def adam_update(grad, buf1, buf2, step, betas, eps):
+    buf1.lerp_(grad, 1 - betas[0])
+    buf2.lerp_(grad.square(), 1 - betas[1])
+    return (buf1 / (1 - betas[0] ** step)) / ((buf2 / (1 - betas[1] ** step)).sqrt() + eps)
+
+
+def _profile_ranges_on() -> bool:
+    return os.environ.get("KAVEH_PROFILE_RANGES", "").lower() in {"1", "true", "yes", "on"}
+
+
+@contextlib.contextmanager
+def _profile_range(name: str):
+    if not _profile_ranges_on():
+        yield
+        return
+    with torch.autograd.profiler.record_function(name):
+        yield
+
+
+class HyperballOptimizer:
+    """Wraps an optimizer; after each step projects selected matrices back to their initial Frobenius radii."""
+
+    def __init__(self, inner: torch.optim.Optimizer, params: Iterable[torch.nn.Parameter], *, eps: float = 1.0e-8,
+                 radius_scale: float = 1.0, projection: str = "sphere") -> None:
+        self.inner = inner
+        self.eps = float(eps)
+        self.radius_scale = float(radius_scale)
+        if self.radius_scale <= 0.0:
+            raise ValueError("radius_scale must be positive")
+        self.projection = str(projection).lower()
+        if self.projection not in {"sphere", "ball"}:
+            raise ValueError("projection must be 'sphere' or 'ball'")
+        self.params: List[torch.nn.Parameter] = []
+        self.radii: List[torch.Tensor] = []
+        seen = set()
+        for p in params:
+            if id(p) in seen or not p.requires_grad or p.ndim < 2:
+                continue
+            seen.add(id(p))
+            r = p.detach().float().norm()
+            if float(r) <= self.eps:
+                continue
+            self.params.append(p)
+            self.radii.append((r * self.radius_scale).detach())
+
+    @property
+    def param_groups(self):
+        return self.inner.param_groups
+
+    @property
+    def state(self):
+        return self.inner.state
+
+    def zero_grad(self, *args, **kwargs):
+        return self.inner.zero_grad(*args, **kwargs)
+
+    def __getattr__(self, name: str) -> Any:
+        if name.startswith("kb_"):
+            return getattr(self.inner, name)
+        raise AttributeError(name)
+
+    def __setattr__(self, name: str, value: Any) -> None:
+        if name.startswith("kb_") and "inner" in self.__dict__:
+            setattr(self.inner, name, value)
+        else:
+            object.__setattr__(self, name, value)
+
+    @torch.no_grad()
+    def _project(self) -> None:
+        for i, (p, r) in enumerate(zip(self.params, self.radii)):
+            norm = p.detach().float().norm()
+            if r.device != p.device or r.dtype != torch.float32:
+                r = r.to(device=p.device, dtype=torch.float32)
+                self.radii[i] = r.detach()
+            scale = r / norm.clamp_min(self.eps)
+            if self.projection == "ball":
+                scale = torch.minimum(scale, torch.ones_like(scale))
+            p.mul_(scale.to(dtype=p.dtype))
+
+    def step(self, closure=None):
+        with _profile_range("optimizer.hyperball.inner_step"):
+            loss = self.inner.step(closure)
+        with _profile_range("optimizer.hyperball.project"):
+            self._project()
+        return loss
+
+    def state_dict(self) -> dict[str, Any]:
+        return {"inner": self.inner.state_dict(),
+                "hyperball_radii": [r.detach().cpu().clone() for r in self.radii],
+                "hyperball_radius_scale": self.radius_scale, "hyperball_projection": self.projection}
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        if "inner" not in state_dict:
+            self.inner.load_state_dict(state_dict)
+            return
+        self.inner.load_state_dict(state_dict["inner"])
+        radii = state_dict.get("hyperball_radii")
+        if radii is not None and len(radii) == len(self.radii):
+            self.radii = [torch.as_tensor(r).detach().clone() for r in radii]
+
+
+# ----------------------------------------------------------------------------- reference-path group steps
+
+
+def _foreach_adam_enabled(group: Dict[str, Any]) -> bool:
+    if "foreach_adam_update" in group:
+        return bool(group["foreach_adam_update"])
+    return os.environ.get("KAVEH_ADAM_FOREACH_UPDATE", "").lower() in {"1", "true", "yes", "on"}
+
+
+def _ensure_grad(p: torch.nn.Parameter) -> None:
+    if p.grad is None:
+        p.grad = torch.zeros_like(p)
+
+
+def _apply_update(p: torch.nn.Parameter, update: torch.Tensor, group: Dict[str, Any]) -> None:
+    p.mul_(1 - group["lr"] * group["weight_decay"])
+    p.add_(update.reshape(p.shape), alpha=-group["lr"])
+
+
+def _muon_param_update(p, group, state):
+    if "momentum_buffer" not in state:
+        state["momentum_buffer"] = torch.zeros_like(p)
+    return muon_update(p.grad, state["momentum_buffer"], beta=group["momentum"])
+
+
+def _normuon_param_update(p, group, state):
+    if "momentum_buffer" not in state:
+        state["momentum_buffer"] = torch.zeros_like(p)
+        shape = (p.shape[0], 1) if p.ndim > 2 else (*p.shape[:-1], 1)
+        state["second_momentum_buffer"] = torch.zeros(shape, dtype=p.dtype, device=p.device)
+    return normuon_update(p.grad, state["momentum_buffer"], state["second_momentum_buffer"], beta=group["momentum"],
+                          beta2=group["beta2"])
+
+
+def _adam_param_update(p, group, state):
+    if "exp_avg" not in state:
+        state["exp_avg"] = torch.zeros_like(p)
+        state["exp_avg_sq"] = torch.zeros_like(p)
+        state["step"] = 0
+    state["step"] += 1
+    return adam_update(p.grad, state["exp_avg"], state["exp_avg_sq"], state["step"], group["betas"], group["eps"])
+
+
+def _clip_scale(optimizer) -> Optional[torch.Tensor]:
+    return getattr(optimizer, "kb_grad_scale", None)
+
+
+def _scaled_grad_inplace(optimizer, p) -> None:
+    """Reference path: apply a pending clip coefficient to ``p.grad`` in place."""
+
+    s = _clip_scale(optimizer)
+    if s is not None and p.grad is not None:
+        p.grad.mul_(s.to(device=p.grad.device, dtype=p.grad.dtype))
+
+
+def _ref_muon_group(optimizer, group, update_fn, distributed: bool) -> None:
+    params: List[torch.nn.Parameter] = group["params"]
+    if not params:
+        return
+    if not distributed:
+        for p in params:
+            _ensure_grad(p)
+            _scaled_grad_inplace(optimizer, p)
+            _apply_update(p, update_fn(p, group, optimizer.state[p]), group)
+        return
+    world, rank = dist.get_world_size(), dist.get_rank()
+    padded = params + [torch.empty_like(params[-1])] * (world - len(params) % world)
+    for base in range(0, len(params), world):
+        i = base + rank
+        if i < len(params):
+            p = params[i]
+            _ensure_grad(p)
+            _scaled_grad_inplace(optimizer, p)
+            _apply_update(p, update_fn(p, group, optimizer.state[p]), group)
+        dist.all_gather(padded[base:base + world], padded[base + rank])
+
+
+def _ref_adam_group(optimizer, group) -> None:
+    for p in group["params"]:
+        _ensure_grad(p)
+        _scaled_grad_inplace(optimizer, p)
+    if _foreach_adam_enabled(group) and _foreach_adam_group(optimizer, group):
+        return
+    for p in group["params"]:
+        _apply_update(p, _adam_param_update(p, group, optimizer.state[p]), group)
+
+
+def _foreach_adam_group(optimizer, group) -> bool:
+    params = list(group["params"])
+    if not params:
+        return True
+    if len({p.device for p in params}) != 1 or len({p.dtype for p in params}) != 1:
+        return False
+    states = []
+    for p in params:
+        st = optimizer.state[p]
+        if "exp_avg" not in st:
+            st["exp_avg"] = torch.zeros_like(p)
+            st["exp_avg_sq"] = torch.zeros_like(p)
+            st["step"] = 0
+        states.append(st)
+    if len({int(st["step"]) for st in states}) != 1:
+        return False
+    step = int(states[0]["step"]) + 1
+    for st in states:
+        st["step"] = step
+    grads = [p.grad for p in params]
+    m = [st["exp_avg"] for st in states]
+    v = [st["exp_avg_sq"] for st in states]
+    b1, b2 = group["betas"]
+    sq_bc2 = (1 - b2 ** step) ** 0.5
+    step_size = group["lr"] * sq_bc2 / (1 - b1 ** step)
+    torch._foreach_lerp_(m, grads, 1 - b1)
+    torch._foreach_lerp_(v, torch._foreach_mul(grads, grads), 1 - b2)
+    denom = torch._foreach_sqrt(v)
+    torch._foreach_add_(denom, group["eps"] * sq_bc2)
+    if float(group["weight_decay"]) != 0.0:
+        torch._foreach_mul_(params, 1 - group["lr"] * float(group["weight_decay"]))
+    torch._foreach_addcdiv_(params, m, denom, value=-step_size)
+    return True
+
+
+# ----------------------------------------------------------------------------- native path
+
+_EMPTY_CACHE: Dict[torch.device, torch.Tensor] = {}
+
+
+def _empty(device: torch.device) -> torch.Tensor:
+    t = _EMPTY_CACHE.get(device)
+    if t is None:
+        t = torch.empty(0, device=device, dtype=torch.float32)
+        _EMPTY_CACHE[device] = t
+    return t
+
+
+def _native_ready(params: Sequence[torch.Tensor]) -> bool:
+    if not params:
+        return False
+    if not all(p.is_cuda and p.dtype == torch.float32 and p.is_contiguous() for p in params):
+        return False
+    from ..ops._ext import available
+
+    return available()
+
+
+def _shadow_list(params: Sequence[torch.Tensor]) -> List[torch.Tensor]:
+    """bf16 copies kept by the models (updated in the same pass), or empty placeholders."""
+
+    out = []
+    for p in params:
+        sh = getattr(p, "_kb_shadow", None)
+        ok = sh is not None and sh.shape == p.shape and sh.device == p.device and sh.dtype == torch.bfloat16
+        out.append(sh if ok else _empty(p.device))
+    return out
+
+
+def _mark_shadows(params: Sequence[torch.Tensor]) -> None:
+    for p in params:
+        if getattr(p, "_kb_shadow", None) is not None and p._kb_shadow.dtype == torch.bfloat16:  # type: ignore
+            p._kb_shadow_version = p._version  # type: ignore[attr-defined]
+
+
+def _ema_list(optimizer, params: Sequence[torch.Tensor]) -> Tuple[List[torch.Tensor], float]:
+    fused = getattr(optimizer, "kb_ema", None)
+    if not fused:
+        return [], 0.0
+    d, by_id = fused
+    return [by_id.get(id(p), _empty(p.device)) for p in params], float(d)
+
+
+def _native_adam_group(optimizer, group) -> None:
+    from ..ops._ext import native
+
+    params = list(group["params"])
+    grads, m, v, steps = [], [], [], []
+    for p in params:
+        _ensure_grad(p)
+        st = optimizer.state[p]
+        if "exp_avg" not in st:
+            st["exp_avg"] = torch.zeros_like(p)
+            st["exp_avg_sq"] = torch.zeros_like(p)
+            st["step"] = 0
+        st["step"] = int(st["step"]) + 1
+        g = p.grad
+        if g.dtype != torch.float32 or not g.is_contiguous():
+            g = g.float().contiguous()
+        grads.append(g)
+        m.append(st["exp_avg"])
+        v.append(st["exp_avg_sq"])
+        steps.append(int(st["step"]))
+    ema, d = _ema_list(optimizer, params)
+    b1, b2 = group["betas"]
+    native().adamw_step(params, grads, m, v, steps, ema, _shadow_list(params), _clip_scale(optimizer),
+                        float(group["lr"]), float(b1), float(b2), float(group["eps"]), float(group["weight_decay"]), d)
+    _mark_shadows(params)
+
+
+def newton_schulz_batched(X: torch.Tensor, steps: int = 5) -> torch.Tensor:
+    """In-place-style NS5 on a normalised bf16 batch [n, r, c] (r <= c) with tcgen05 GEMMs."""
+
+    from ..ops import functional as kf
+
+    a, b, c = NS_COEFFS
+    n, r, cols = X.shape
+    A = torch.empty((n, r, r), device=X.device, dtype=torch.bfloat16)
+    B = torch.empty_like(A)
+    Y = torch.empty_like(X)
+    for _ in range(steps):
+        kf.gemm(X, X, out=A)                                 # A = X X^T
+        kf.gemm(A, A, out=B, d=A, alpha=c, beta=b)           # B = b A + c A A   (A symmetric)
+        kf.gemm(B, X, b_mn_major=True, out=Y, d=X, beta=a)   # X' = a X + B X
+        X, Y = Y, X
+    return X
+
+
+def _muon_buckets(params: Sequence[torch.nn.Parameter]) -> Dict[Tuple[int, int], List[int]]:
+    buckets: Dict[Tuple[int, int], List[int]] = {}
+    for i, p in enumerate(params):
+        R = p.shape[0]
+        C = p.numel() // R
+        buckets.setdefault((R, C), []).append(i)
+    return buckets
+
+
+def _native_muon_bucket(optimizer, group, params: List[torch.nn.Parameter], R: int, C: int) -> None:
+    from ..ops._ext import native
+
+    n = len(params)
+    dev = params[0].device
+    transpose = R > C
+    r, c = (C, R) if transpose else (R, C)
+    grads, moms = [], []
+    for p in params:
+        _ensure_grad(p)
+        st = optimizer.state[p]
+        if "momentum_buffer" not in st:
+            st["momentum_buffer"] = torch.zeros_like(p)
+        g = p.grad
+        if g.dtype != torch.float32 or not g.is_contiguous():
+            g = g.float().contiguous()
+        grads.append(g)
+        moms.append(st["momentum_buffer"])
+    X = torch.empty((n, r, c), device=dev, dtype=torch.bfloat16)
+    ss = torch.empty(n, device=dev, dtype=torch.float32)
+    native().muon_prologue(grads, moms, X, ss, _clip_scale(optimizer), float(group["momentum"]), True, transpose)
+    native().muon_scale(X, ss, n)
+    X = newton_schulz_batched(X, 5)
+    ema, d = _ema_list(optimizer, params)
+    native().muon_epilogue(params, X, ema, _shadow_list(params), float(group["lr"]), float(group["weight_decay"]),
+                           0.2 * math.sqrt(max(R, C)), transpose, d)
+    _mark_shadows(params)
+
+
+def _native_muon_group(optimizer, group, distributed: bool) -> None:
+    params: List[torch.nn.Parameter] = list(group["params"])
+    if not params:
+        return
+    buckets = _muon_buckets(params)
+    if not distributed:
+        for (R, C), idx in buckets.items():
+            _native_muon_bucket(optimizer, group, [params[i] for i in idx], R, C)
+        return
+    world, rank = dist.get_world_size(), dist.get_rank()
+    for (R, C), idx in buckets.items():
+        owned = [params[i] for k, i in enumerate(idx) if k % world == rank]
+        if owned:
+            _native_muon_bucket(optimizer, group, owned, R, C)
+        per_rank = (len(idx) + world - 1) // world
+        send = torch.zeros((per_rank, R * C), device=params[0].device, dtype=torch.float32)
+        for j, p in enumerate(owned):
+            send[j].copy_(p.detach().reshape(-1))
+        recv = torch.empty((world * per_rank, R * C), device=send.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(recv, send)
+        for k, i in enumerate(idx):
+            if k % world == rank:
+                continue
+            params[i].detach().view(-1).copy_(recv[(k % world) * per_rank + k // world])
+
+
+def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) -> None:
+    for group in optimizer.param_groups:
+        params = group["params"]
+        if group.get("use_muon", True):
+            with _profile_range("optimizer.muon.update"):
+                if not normuon and _native_ready(params):
+                    _native_muon_group(optimizer, group, distributed)
+                else:
+                    _ref_muon_group(optimizer, group, muon_fn, distributed)
+        else:
+            with _profile_range("optimizer.adam.update"):
+                if _native_ready(params) and not _foreach_adam_enabled(group):
+                    _native_adam_group(optimizer, group)
+                else:
+                    _ref_adam_group(optimizer, group)
+
+
+def _sorted_desc(params: Iterable[torch.nn.Parameter]) -> List[torch.nn.Parameter]:
+    return sorted(list(params), key=lambda x: x.size(), reverse=True)
+
+
+def _muon_defaults(group: Dict[str, Any], with_beta2: bool = False) -> None:
+    group.setdefault("lr", 0.02)
+    group.setdefault("momentum", 0.95)
+    group.setdefault("weight_decay", 0)
+    if with_beta2:
+        group.setdefault("beta2", 0.95)
+
+
+def _adam_defaults(group: Dict[str, Any]) -> None:
+    group.setdefault("lr", 3e-4)
+    group.setdefault("betas", (0.9, 0.95))
+    group.setdefault("eps", 1e-10)
+    group.setdefault("weight_decay", 0)
+
+
+def _closure(closure):
+    if closure is None:
+        return None
+    with torch.enable_grad():
+        return closure()
+
+
+class _KbOptimizer(torch.optim.Optimizer):
+    """Base: fused-path hooks (clip coefficient, fused EMA) consumed by one step."""
+
+    kb_fused = True
+    _normuon = False
+    _distributed = False
+
+    def _distributed_now(self) -> bool:
+        return self._distributed and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = _closure(closure)
+        fn = _normuon_param_update if self._normuon else _muon_param_update
+        try:
+            _run_groups(self, fn, self._normuon, self._distributed_now())
+        finally:
+            self.kb_grad_scale = None
+            self.kb_ema = None
+        return loss
+
+
+class Muon(_KbOptimizer):
+    """Distributed Muon for hidden matrices (``lr`` in spectral-norm units)."""
+
+    _distributed = True
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95):
+        params = list(params)
+        assert len(params) >= 1 and isinstance(params[0], torch.nn.Parameter)
+        super().__init__(_sorted_desc(params), dict(lr=lr, weight_decay=weight_decay, momentum=momentum))
+
+
+class SingleDeviceMuon(_KbOptimizer):
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95):
+        super().__init__(params, dict(lr=lr, weight_decay=weight_decay, momentum=momentum))
+
+
+class NorMuon(_KbOptimizer):
+    _distributed = True
+    _normuon = True
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95, beta2=0.95):
+        params = list(params)
+        assert len(params) >= 1 and isinstance(params[0], torch.nn.Parameter)
+        super().__init__(_sorted_desc(params), dict(lr=lr, weight_decay=weight_decay, momentum=momentum, beta2=beta2))
+
+
+class SingleDeviceNorMuon(_KbOptimizer):
+    _normuon = True
+
+    def __init__(self, params, lr=0.02, weight_decay=0, momentum=0.95, beta2=0.95):
+        super().__init__(params, dict(lr=lr, weight_decay=weight_decay, momentum=momentum, beta2=beta2))
+
+
+def _init_groups(groups: Sequence[Dict[str, Any]], *, with_beta2: bool, sort_muon: bool) -> None:
+    for g in groups:
+        assert "use_muon" in g
+        if g["use_muon"]:
+            if sort_muon:
+                g["params"] = _sorted_desc(g["params"])
+            _muon_defaults(g, with_beta2)
+        else:
+            _adam_defaults(g)
+
+
+class MuonWithAuxAdam(_KbOptimizer):
+    """Muon on ``use_muon`` groups and Adam on the rest (distributed Muon sharding)."""
+
+    _distributed = True
+
+    def __init__(self, param_groups):
+        _init_groups(param_groups, with_beta2=False, sort_muon=True)
+        super().__init__(param_groups, dict())
+
+
+class SingleDeviceMuonWithAuxAdam(_KbOptimizer):
+    def __init__(self, param_groups):
+        _init_groups(param_groups, with_beta2=False, sort_muon=False)
+        super().__init__(param_groups, dict())
+
+
+class NorMuonWithAuxAdam(_KbOptimizer):
+    _distributed = True
+    _normuon = True
+
+    def __init__(self, param_groups):
+        _init_groups(param_groups, with_beta2=True, sort_muon=True)
+        super().__init__(param_groups, dict())
+
+
+class SingleDeviceNorMuonWithAuxAdam(_KbOptimizer):
+    _normuon = True
+
+    def __init__(self, param_groups):
+        _init_groups(param_groups, with_beta2=True, sort_muon=False)
+        super().__init__(param_groups, dict())

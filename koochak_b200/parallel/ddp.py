@@ -1,0 +1,211 @@
+"""Data-parallel gradient synchronisation, overlapped with backward.
+
+(replaces torch DDP at reference koochak/loop.py:705-723)
+
+``DataParallel`` wraps a module the way ``DistributedDataParallel`` does
+(``.module``, ``no_sync()``, parameters broadcast from rank 0 at wrap time,
+buffers broadcast before every forward when ``broadcast_buffers``), with its
+own bucketing:
+
+* parameters are grouped into buckets of ``bucket_cap_mb`` in reverse
+  registration order (the order backward produces gradients), identically on
+  every rank;
+* a post-accumulate-grad hook copies each finished gradient into its bucket's
+  flat fp32 buffer; when a bucket is complete its reduction is launched on a
+  dedicated communication stream while backward keeps running;
+* at the end of backward the compute stream waits for every bucket and each
+  ``param.grad`` becomes a view of the averaged bucket.
+
+Reduction transports (``transport``):
+
+* ``"nccl"`` / ``"gloo"``: one averaging all-reduce per bucket (baseline);
+* ``"p2p"``: the native single-node path: every rank exposes its bucket in
+  CUDA IPC-shared memory, one kernel per bucket reduces this rank's shard by
+  reading all peers over NVLink (no NCCL in the data path) and another
+  gathers the reduced shards back, with bounded cross-GPU flag waits
+  (see ``parallel/symm.py``).
+"""
+
+from __future__ import annotations
+
+import contextlib
+from typing import Callable, Dict, List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+__all__ = ["DataParallel", "Bucket"]
+
+
+class Bucket:
+    def __init__(self, index: int, params: List[nn.Parameter], device: torch.device) -> None:
+        self.index = index
+        self.params = params
+        self.offsets: List[int] = []
+        total = 0
+        for p in params:
+            self.offsets.append(total)
+            total += p.numel()
+        self.numel = total
+        self.buffer = torch.zeros(total, device=device, dtype=torch.float32)
+        self.pending = 0
+        self.work = None
+        self.ready_event: Optional[torch.cuda.Event] = None
+
+    def view_of(self, i: int) -> torch.Tensor:
+        p = self.params[i]
+        return self.buffer.narrow(0, self.offsets[i], p.numel()).view_as(p)
+
+
+class DataParallel(nn.Module):
+    def __init__(self, module: nn.Module, *, bucket_cap_mb: float = 25.0, broadcast_buffers: bool = True,
+                 transport: str = "auto", process_group=None, find_unused_parameters: bool = False) -> None:
+        super().__init__()
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("DataParallel needs an initialised process group")
+        self.module = module
+        self.group = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        self.broadcast_buffers = broadcast_buffers
+        self.find_unused_parameters = find_unused_parameters
+        self.require_sync = True
+        params = [p for p in module.parameters() if p.requires_grad]
+        self.device = params[0].device if params else torch.device("cpu")
+        backend = str(dist.get_backend(process_group)).lower()
+        self.transport = self._pick_transport(transport, backend)
+        self._sync_module_states()
+        cap = max(1, int(bucket_cap_mb * 1024 * 1024 / 4))
+        self.buckets: List[Bucket] = []
+        current: List[nn.Parameter] = []
+        size = 0
+        for p in reversed(params):
+            current.append(p)
+            size += p.numel()
+            if size >= cap:
+                self.buckets.append(Bucket(len(self.buckets), current, self.device))
+                current, size = [], 0
+        if current:
+            self.buckets.append(Bucket(len(self.buckets), current, self.device))
+        self._where: Dict[int, tuple] = {}
+        for b in self.buckets:
+            for i, p in enumerate(b.params):
+                self._where[id(p)] = (b, i)
+        self._comm_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+        self._p2p = None
+        if self.transport == "p2p":
+            from .symm import P2PReducer
+
+            self._p2p = P2PReducer([b.numel for b in self.buckets], self.device, process_group)
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in params]
+        self._armed = False
+        self._callback_queued = False
+
+    # ------------------------------------------------------------------ setup
+    def _pick_transport(self, transport: str, backend: str) -> str:
+        t = (transport or "auto").lower()
+        if backend != "nccl":
+            return "gloo"
+        if t == "auto":
+            return "nccl"
+        if t not in ("nccl", "p2p"):
+            raise ValueError(f"unknown gradient-sync transport {transport!r}")
+        return t
+
+    @torch.no_grad()
+    def _sync_module_states(self) -> None:
+        for t in list(self.module.parameters()) + list(self.module.buffers()):
+            dist.broadcast(t.data, src=0, group=self.group)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, *args, **kwargs):
+        if self.broadcast_buffers and self.world > 1:
+            with torch.no_grad():
+                for b in self.module.buffers():
+                    dist.broadcast(b, src=0, group=self.group)
+        if torch.is_grad_enabled() and self.require_sync:
+            self._arm()
+        return self.module(*args, **kwargs)
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        prev = self.require_sync
+        self.require_sync = False
+        try:
+            yield
+        finally:
+            self.require_sync = prev
+
+    def _arm(self) -> None:
+        self._armed = True
+        self._callback_queued = False
+        for b in self.buckets:
+            b.pending = len(b.params)
+            b.work = None
+            b.ready_event = None
+
+    # ------------------------------------------------------------------ backward
+    def _on_grad(self, p: nn.Parameter) -> None:
+        if not self._armed:
+            return
+        if not self._callback_queued:
+            torch.autograd.Variable._execution_engine.queue_callback(self._finish)
+            self._callback_queued = True
+        b, i = self._where[id(p)]
+        with torch.no_grad():
+            b.view_of(i).copy_(p.grad)
+        b.pending -= 1
+        if b.pending == 0:
+            self._launch(b)
+
+    def _launch(self, b: Bucket) -> None:
+        if self._comm_stream is None:
+            self._reduce_now(b)
+            return
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self._comm_stream):
+            self._comm_stream.wait_event(ev)
+            self._reduce_now(b)
+            b.buffer.record_stream(self._comm_stream)
+            done = torch.cuda.Event()
+            done.record(self._comm_stream)
+            b.ready_event = done
+
+    def _reduce_now(self, b: Bucket) -> None:
+        if self.transport == "p2p":
+            assert self._p2p is not None
+            self._p2p.all_reduce_mean(b.index, b.buffer)
+        elif self.transport == "nccl":
+            dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
+        else:
+            dist.all_reduce(b.buffer, group=self.group)
+            b.buffer.div_(self.world)
+
+    def _finish(self) -> None:
+        # Buckets that never completed (unused parameters) are reduced now so
+        # every rank issues the same collectives in the same order.
+        for b in self.buckets:
+            if b.pending > 0:
+                for i, p in enumerate(b.params):
+                    if p.grad is None:
+                        b.view_of(i).zero_()
+                    b.pending = 0
+                self._launch(b)
+        cur = torch.cuda.current_stream(self.device) if self._comm_stream is not None else None
+        for b in self.buckets:
+            if cur is not None and b.ready_event is not None:
+                cur.wait_event(b.ready_event)
+            for i, p in enumerate(b.params):
+                p.grad = b.view_of(i)
+        if self._p2p is not None:
+            self._p2p.check()
+        self._armed = False
+
+    def state_dict(self, *args, **kwargs):
+        return {f"module.{k}": v for k, v in self.module.state_dict(*args, **kwargs).items()}
+
+    def load_state_dict(self, state_dict, strict: bool = True):
+        stripped = {(k[7:] if k.startswith("module.") else k): v for k, v in state_dict.items()}
+        return self.module.load_state_dict(stripped, strict=strict)
