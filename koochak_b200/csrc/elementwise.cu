@@ -7,6 +7,7 @@
 
 #include <torch/extension.h>
 
+#include <type_traits>
 #include <vector>
 
 namespace kb {
@@ -88,13 +89,48 @@ void embedding_backward(const at::Tensor& idx, const at::Tensor& dout, at::Tenso
 // Per row: lse = log(sum exp(z)), loss = lse - z[target] (0 for ignored rows).
 // One CTA per row, logits in bf16/fp16/fp32 with row stride ld, V valid columns.
 template <typename T>
+__device__ __forceinline__ void online_add8(const T* p, float& m, float& s) {
+  const uint4 q = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&q);
+  float v[8];
+  float lm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j] = to_f32<T>(e[j]);
+    lm = fmaxf(lm, v[j]);
+  }
+  if (lm > m) {
+    s *= __expf(m - lm);
+    m = lm;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += __expf(v[j] - m);
+}
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
+  m = mm;
+}
+
+// Per row: lse = log(sum exp(z)), loss = lse - z[target] (0 for ignored rows).
+// One CTA per row; 16-byte vector loads when the row is 16-byte aligned.
+template <typename T>
 __global__ void __launch_bounds__(256) ce_fwd_kernel(const T* __restrict__ logits, const int64_t* __restrict__ tgt,
                                                      float* __restrict__ loss, float* __restrict__ lse_out, int V,
                                                      long long ld, int64_t ignore_index) {
   const int row = blockIdx.x;
   const T* z = logits + (long long)row * ld;
   float m = -INFINITY, s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  constexpr int VEC = 16 / sizeof(T);
+  const bool aligned = (reinterpret_cast<uintptr_t>(z) & 15) == 0;
+  int done = 0;
+  if (aligned && VEC == 8) {
+    const int nvec = V / 8;
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) online_add8<T>(z + 8 * i, m, s);
+    done = nvec * 8;
+  }
+  for (int i = done + threadIdx.x; i < V; i += blockDim.x) {
     const float v = to_f32<T>(z[i]);
     if (v > m) {
       s = s * __expf(m - v) + 1.f;
@@ -103,14 +139,11 @@ __global__ void __launch_bounds__(256) ce_fwd_kernel(const T* __restrict__ logit
       s += __expf(v - m);
     }
   }
-  // warp combine
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
     const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float mm = fmaxf(m, m2);
-    s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
-    m = mm;
+    online_merge(m, s, m2, s2);
   }
   __shared__ float sm[32], ss[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,9 +160,7 @@ __global__ void __launch_bounds__(256) ce_fwd_kernel(const T* __restrict__ logit
     for (int o = 16; o > 0; o >>= 1) {
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
       const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      const float mm = fmaxf(m, m2);
-      s = (m == -INFINITY ? 0.f : s * __expf(m - mm)) + (m2 == -INFINITY ? 0.f : s2 * __expf(m2 - mm));
-      m = mm;
+      online_merge(m, s, m2, s2);
     }
     if (lane == 0) {
       const float l = m + logf(s);
@@ -153,7 +184,23 @@ __global__ void __launch_bounds__(256) ce_bwd_kernel(T* __restrict__ logits, con
   const bool ignored = (t == ignore_index || t < 0 || t >= V);
   const float g = ignored ? 0.f : gscale[0];
   const float l = lse[row];
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  int done = 0;
+  if ((reinterpret_cast<uintptr_t>(z) & 15) == 0 && sizeof(T) == 2) {
+    const int nvec = V / 8;
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+      uint4 q = *reinterpret_cast<const uint4*>(z + 8 * i);
+      T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = 8 * i + j;
+        const float p = __expf(to_f32<T>(e[j]) - l);
+        e[j] = from_f32<T>((p - (col == t ? 1.f : 0.f)) * g);
+      }
+      *reinterpret_cast<uint4*>(z + 8 * i) = q;
+    }
+    done = nvec * 8;
+  }
+  for (int i = done + threadIdx.x; i < V; i += blockDim.x) {
     const float p = __expf(to_f32<T>(z[i]) - l);
     z[i] = from_f32<T>((p - (i == t ? 1.f : 0.f)) * g);
   }
@@ -219,23 +266,38 @@ void cross_entropy_backward(at::Tensor& logits, const at::Tensor& target, const 
 
 // ------------------------------------------------------------ bias gradient
 
-// out[n] (+)= sum_m g[m, n]; each CTA covers 64 columns x a slice of rows.
+// out[n] += sum_m g[m, n]. A CTA covers 256 columns (32 threads x 8 columns,
+// 16-byte loads) x 8 row groups over a slice of rows; one atomic per column per CTA.
 template <typename T>
 __global__ void __launch_bounds__(256) bias_grad_kernel(const T* __restrict__ g, float* __restrict__ out, int M,
                                                         int N, int rows_per_cta) {
-  const int col = blockIdx.x * 64 + (threadIdx.x & 63);
+  const int cg = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int col0 = blockIdx.x * 256 + cg * 8;
   const int r0 = blockIdx.y * rows_per_cta;
   const int r1 = min(M, r0 + rows_per_cta);
-  float s = 0.f;
-  if (col < N)
-    for (int r = r0 + (threadIdx.x >> 6); r < r1; r += 4) s += to_f32<T>(g[(long long)r * N + col]);
-  __shared__ float red[4][64];
-  red[threadIdx.x >> 6][threadIdx.x & 63] = s;
-  __syncthreads();
-  if (threadIdx.x < 64 && col < N) {
-    const float t = red[0][threadIdx.x] + red[1][threadIdx.x] + red[2][threadIdx.x] + red[3][threadIdx.x];
-    atomicAdd(out + col, t);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const bool vec = (col0 + 8 <= N) && (N % 8 == 0) && sizeof(T) == 2;
+  for (int r = r0 + rg; r < r1; r += 8) {
+    const T* p = g + (long long)r * N + col0;
+    if (vec) {
+      const uint4 q = *reinterpret_cast<const uint4*>(p);
+      const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += to_f32<T>(e[j]);
+    } else {
+      for (int j = 0; j < 8; ++j)
+        if (col0 + j < N) acc[j] += to_f32<T>(p[j]);
+    }
   }
+  __shared__ float red[8][257];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[rg][cg * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = threadIdx.x;  // 256 columns, one per thread
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += red[k][c];
+  if (blockIdx.x * 256 + c < N) atomicAdd(out + blockIdx.x * 256 + c, t);
 }
 
 // out must be zeroed by the caller unless accumulating.
@@ -245,9 +307,9 @@ void bias_grad(const at::Tensor& g, at::Tensor& out) {
   const int M = (int)(g.numel() / N);
   const c10::cuda::CUDAGuard guard(g.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
-  const int col_blocks = (N + 63) / 64;
-  const int target_ctas = num_sms(g.get_device()) * 8;
-  int row_blocks = std::max(1, std::min((M + 255) / 256, target_ctas / std::max(1, col_blocks)));
+  const int col_blocks = (N + 255) / 256;
+  const int target_ctas = num_sms(g.get_device()) * 4;
+  int row_blocks = std::max(1, std::min((M + 63) / 64, target_ctas / std::max(1, col_blocks)));
   const int rows_per = (M + row_blocks - 1) / row_blocks;
   row_blocks = (M + rows_per - 1) / rows_per;
   dim3 grid(col_blocks, row_blocks);
@@ -272,13 +334,28 @@ struct CastArgs {
 
 template <typename TOut>
 __global__ void cast_multi_kernel(const __grid_constant__ CastArgs a) {
-  const long long total = a.start[a.n];
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  int ti = 0;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
-    while (i >= a.start[ti + 1]) ++ti;
-    const long long j = i - a.start[ti];
-    reinterpret_cast<TOut*>(a.dst[ti])[j] = from_f32<TOut>(a.src[ti][j]);
+  // Each CTA walks its share of every tensor with 4-wide loads (tensors are
+  // 16-byte aligned allocations; the tail is scalar).
+  for (int ti = 0; ti < a.n; ++ti) {
+    const long long n = a.start[ti + 1] - a.start[ti];
+    const float* src = a.src[ti];
+    TOut* dst = reinterpret_cast<TOut*>(a.dst[ti]);
+    const long long n4 = ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 7) == 0)
+                             ? n / 4 : 0;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(src)[i];
+      uint2 o;
+      if constexpr (sizeof(TOut) == 2 && std::is_same<TOut, __nv_bfloat16>::value) {
+        o.x = pack_bf16(v.x, v.y);
+        o.y = pack_bf16(v.z, v.w);
+      } else {
+        o.x = pack_f16(v.x, v.y);
+        o.y = pack_f16(v.z, v.w);
+      }
+      reinterpret_cast<uint2*>(dst)[i] = o;
+    }
+    for (long long i = n4 * 4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+      dst[i] = from_f32<TOut>(src[i]);
   }
 }
 
@@ -303,7 +380,7 @@ void cast_multi(const std::vector<at::Tensor>& src, const std::vector<at::Tensor
       a.start[i + 1] = a.start[i] + x.numel();
     }
     if (a.start[a.n] == 0) continue;
-    const int blocks = (int)std::min<long long>((a.start[a.n] + 255) / 256, num_sms(src[0].get_device()) * 8LL);
+    const int blocks = (int)std::min<long long>((a.start[a.n] / 4 + 255) / 256 + 1, num_sms(src[0].get_device()) * 8LL);
     if (out_t == at::kBFloat16) cast_multi_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(a);
     else if (out_t == at::kHalf) cast_multi_kernel<__half><<<blocks, 256, 0, s>>>(a);
     else KB_CHECK(false, "cast_multi: destination must be bf16 or fp16");

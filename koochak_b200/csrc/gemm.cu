@@ -26,6 +26,8 @@
 
 #include <torch/extension.h>
 
+#include <type_traits>
+
 namespace kb {
 
 enum GemmAct : int { ACT_NONE = 0, ACT_GELU = 1, ACT_GELU_BWD = 2 };
@@ -43,6 +45,8 @@ struct GemmParams {
   void* aux;
   long long ldaux, strideAux;
   int vec_ok;  // C/D/aux rows 16-byte aligned for vector access
+  int splits;  // split-K factor; > 1 means fp32 C is accumulated with atomics
+  int kb_per_split;  // 64-wide K blocks per split (every split non-empty)
   int* status;
 };
 
@@ -176,8 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_n = (p.N + BN - 1) / BN;
   const int tiles_per_batch = num_m * num_n;
-  const int total_tiles = tiles_per_batch * p.batch;
-  const int num_kb = (p.K + kBK - 1) / kBK;
+  const int tiles_per_split = tiles_per_batch * p.batch;
+  const int total_tiles = tiles_per_split * p.splits;
+  const int num_kb_total = (p.K + kBK - 1) / kBK;
+  const int kb_per_split = p.kb_per_split;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -189,13 +195,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < S; ++s) armed[s] = false;
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-        const int b = t / tiles_per_batch;
-        const int r = t - b * tiles_per_batch;
+        const int split = t / tiles_per_split;
+        const int ts = t - split * tiles_per_split;
+        const int b = ts / tiles_per_batch;
+        const int r = ts - b * tiles_per_batch;
         const int n_blk = r / num_m;
         const int m_blk = r - n_blk * num_m;
         const int m0 = m_blk * kBM;
         const int n0 = n_blk * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = split * kb_per_split;
+        const int kb1 = min(num_kb_total, kb0 + kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -257,7 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int split = t / tiles_per_split;
+        const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
+        for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
@@ -298,8 +310,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
-      const int b = t / tiles_per_batch;
-      const int r = t - b * tiles_per_batch;
+      const int split = t / tiles_per_split;
+      const int ts = t - split * tiles_per_split;
+      const int b = ts / tiles_per_batch;
+      const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
       const int row = m_blk * kBM + q * 32 + lane;
@@ -321,9 +335,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * p.alpha;
-        if (p.bias) {
+        if (p.bias && split == 0) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] += (j < valid) ? p.bias[col0 + j] : 0.f;
+        }
+        if constexpr (std::is_same<OutT, float>::value && ACT == ACT_NONE) {
+          if (p.splits > 1) {
+            // Split-K: accumulate partial sums into C (pre-initialised by the host).
+            float* dst = reinterpret_cast<float*>(crow) + col0;
+            if (vec && valid == 32) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            } else {
+              for (int j = 0; j < valid; ++j) atomicAdd(dst + j, v[j]);
+            }
+            continue;
+          }
         }
         if constexpr (ACT == ACT_GELU) {
           if (arow) store_row32<__nv_bfloat16>(arow + col0, v, valid, vec);
@@ -499,8 +527,35 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   p.status = device_status_ptr(dev);
 
   const int64_t tiles = batch * ((M + 127) / 128) * ((N + bn - 1) / bn);
-  const int grid = (int)std::min<int64_t>(tiles, num_sms(dev));
+  const int sms = num_sms(dev);
+  const int64_t num_kb = (K + 63) / 64;
+  // Split K when the output has too few tiles to fill the GPU and K is long
+  // (weight gradients): partial tiles are summed into C with fp32 atomics.
+  int splits = 1;
+  if (ct == at::kFloat && act == ACT_NONE && tiles < sms && num_kb >= 16) {
+    splits = (int)std::min<int64_t>({(2 * sms + tiles - 1) / tiles, num_kb / 8, (int64_t)16});
+    splits = std::max(1, splits);
+  }
+  const int64_t kb_per = (num_kb + splits - 1) / splits;
+  splits = (int)((num_kb + kb_per - 1) / kb_per);
+  p.splits = splits;
+  p.kb_per_split = (int)kb_per;
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
+  if (splits > 1) {
+    // C = beta * D (or 0); every split then adds its partial product.
+    if (p.D != nullptr && p.beta != 0.f) {
+      if (p.D != p.C || p.beta != 1.f) {
+        at::Tensor cv = c;
+        cv.copy_(*d);
+        if (p.beta != 1.f) cv.mul_(p.beta);
+      }
+    } else {
+      c.zero_();
+    }
+    p.D = nullptr;
+    p.beta = 0.f;
+  }
+  const int grid = (int)std::min<int64_t>(tiles * splits, sms);
   if (bn == 256) {
     if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, grid, stream);
     else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, grid, stream);

@@ -124,8 +124,8 @@ template <int VPT, typename TIn, typename TG, typename TDx, bool RMS>
 __global__ void __launch_bounds__(32 * kNormWarps)
     norm_bwd_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
-                    const TDx* __restrict__ dres, TDx* __restrict__ dx, float* __restrict__ dw_part,
-                    float* __restrict__ db_part, int M, int C) {
+                    const TDx* __restrict__ dres, TDx* __restrict__ dx, TG* __restrict__ dx_lp,
+                    float* __restrict__ dw_part, float* __restrict__ db_part, int M, int C) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float dw_acc[VPT];
   float db_acc[VPT];
@@ -188,47 +188,64 @@ __global__ void __launch_bounds__(32 * kNormWarps)
           o[t] = rstd * (wg - (RMS ? 0.f : s1) - xh[i] * s2) + rq[t];
         }
         store4<TDx>(dxr + col, o);
+        if (dx_lp) store4<TG>(dx_lp + (long long)row * C + col, o);
       }
     }
   }
-  // Per-warp partials -> shared -> one row of partials per CTA.
-  __shared__ float red[kNormWarps][32];
+  // Per-warp partials -> shared memory -> one row of partials per CTA.
+  extern __shared__ float red[];  // [kNormWarps][C]
 #pragma unroll
   for (int j = 0; j < VPT / 4; ++j) {
+    const int col = 4 * lane + 128 * j;
+    if (col < C) {
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int i = 4 * j + t;
-      const int col = 4 * lane + 128 * j + t;
-      red[warp][lane] = dw_acc[i];
-      __syncthreads();
-      if (warp == 0) {
-        float s = 0.f;
-        for (int k = 0; k < kNormWarps; ++k) s += red[k][lane];
-        if (col < C) dw_part[(long long)blockIdx.x * C + col] = s;
+      for (int t = 0; t < 4; ++t) red[warp * C + col + t] = dw_acc[4 * j + t];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormWarps; ++k) s += red[k * C + c];
+    dw_part[(long long)blockIdx.x * C + c] = s;
+  }
+  if (!RMS && db_part != nullptr) {
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < VPT / 4; ++j) {
+      const int col = 4 * lane + 128 * j;
+      if (col < C) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) red[warp * C + col + t] = db_acc[4 * j + t];
       }
-      __syncthreads();
-      if (!RMS && db_part != nullptr) {
-        red[warp][lane] = db_acc[i];
-        __syncthreads();
-        if (warp == 0) {
-          float s = 0.f;
-          for (int k = 0; k < kNormWarps; ++k) s += red[k][lane];
-          if (col < C) db_part[(long long)blockIdx.x * C + col] = s;
-        }
-        __syncthreads();
-      }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < kNormWarps; ++k) s += red[k * C + c];
+      db_part[(long long)blockIdx.x * C + c] = s;
     }
   }
 }
 
-// out[c] (+)= sum_r part[r, c]
-__global__ void column_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, int R, int C,
-                                     int accumulate) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= C) return;
+// out[c] (+)= sum_r part[r, c]; a CTA owns 32 columns, 8 row groups per column.
+__global__ void __launch_bounds__(256) column_reduce_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                            int R, int C, int accumulate) {
+  const int col = blockIdx.x * 32 + (threadIdx.x & 31);
+  const int rg = threadIdx.x >> 5;
   float s = 0.f;
-  for (int r = 0; r < R; ++r) s += part[(long long)r * C + col];
-  out[col] = accumulate ? out[col] + s : s;
+  if (col < C)
+    for (int r = rg; r < R; r += 8) s += part[(long long)r * C + col];
+  __shared__ float red[8][33];
+  red[rg][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (rg == 0 && col < C) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x & 31];
+    out[col] = accumulate ? out[col] + t : t;
+  }
 }
 
 // ---------------------------------------------------------------------- host
@@ -300,7 +317,7 @@ void norm_forward(const at::Tensor& x, const at::Tensor& w, const c10::optional<
 void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                    const c10::optional<at::Tensor>& mean, const at::Tensor& rstd, const c10::optional<at::Tensor>& dres,
                    at::Tensor& dx, at::Tensor& dw, const c10::optional<at::Tensor>& db, at::Tensor& workspace,
-                   bool rms, bool accumulate) {
+                   bool rms, bool accumulate, const c10::optional<at::Tensor>& dx_lp) {
   check_cuda_tensor(dy, "dy");
   KB_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous(), "norm bwd: contiguous tensors required");
   const int C = (int)x.size(-1);
@@ -317,6 +334,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const bool has_res = dres.has_value() && dres->defined();
   KB_CHECK(dx.scalar_type() == x.scalar_type(), "norm bwd: dx must have the dtype of x");
   if (has_res) KB_CHECK(dres->scalar_type() == dx.scalar_type() && dres->is_contiguous(), "dres must match dx");
+  const int smem = kNormWarps * C * (int)sizeof(float);
   with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
     with_type(x.scalar_type(), [&](auto tin) {
@@ -326,25 +344,37 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
         {
           using TDx = TIn;
           const TDx* rp = has_res ? (const TDx*)dres->data_ptr() : nullptr;
+          TG* lp = nullptr;
+          if (dx_lp.has_value() && dx_lp->defined()) {
+            KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
+                     "dx_lp must be contiguous, of dy's dtype and dx's size");
+            lp = (TG*)dx_lp->data_ptr();
+          }
+          if (smem > 48 * 1024) {
+            KB_CUDA_CHECK(cudaFuncSetAttribute(norm_bwd_kernel<V, TIn, TG, TDx, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            KB_CUDA_CHECK(cudaFuncSetAttribute(norm_bwd_kernel<V, TIn, TG, TDx, false>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+          }
           if (rms)
-            norm_bwd_kernel<V, TIn, TG, TDx, true><<<grid, 32 * kNormWarps, 0, stream>>>(
+            norm_bwd_kernel<V, TIn, TG, TDx, true><<<grid, 32 * kNormWarps, smem, stream>>>(
                 (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), nullptr,
-                rstd.data_ptr<float>(), rp, (TDx*)dx.data_ptr(), dw_part, nullptr, M, C);
+                rstd.data_ptr<float>(), rp, (TDx*)dx.data_ptr(), lp, dw_part, nullptr, M, C);
           else
-            norm_bwd_kernel<V, TIn, TG, TDx, false><<<grid, 32 * kNormWarps, 0, stream>>>(
+            norm_bwd_kernel<V, TIn, TG, TDx, false><<<grid, 32 * kNormWarps, smem, stream>>>(
                 (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), mp, rstd.data_ptr<float>(),
-                rp, (TDx*)dx.data_ptr(), dw_part, db_part, M, C);
+                rp, (TDx*)dx.data_ptr(), lp, dw_part, db_part, M, C);
         }
       });
     });
   });
   KB_LAUNCHED();
   KB_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == C, "dw must be fp32 [C]");
-  column_reduce_kernel<<<(C + 255) / 256, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), grid, C, accumulate);
+  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), grid, C, accumulate);
   KB_LAUNCHED();
   if (!rms && db.has_value() && db->defined()) {
     KB_CHECK(db->scalar_type() == at::kFloat && db->numel() == C, "db must be fp32 [C]");
-    column_reduce_kernel<<<(C + 255) / 256, 256, 0, stream>>>(db_part, db->data_ptr<float>(), grid, C, accumulate);
+    column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(db_part, db->data_ptr<float>(), grid, C, accumulate);
     KB_LAUNCHED();
   }
 }
@@ -356,7 +386,10 @@ int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
 
 void register_norm_ops(pybind11::module& m) {
   m.def("norm_forward", &norm_forward, "LayerNorm/RMSNorm forward");
-  m.def("norm_backward", &norm_backward, "LayerNorm/RMSNorm backward");
+  m.def("norm_backward", &norm_backward, "LayerNorm/RMSNorm backward", pybind11::arg("dy"), pybind11::arg("x"),
+        pybind11::arg("w"), pybind11::arg("mean"), pybind11::arg("rstd"), pybind11::arg("dres"), pybind11::arg("dx"),
+        pybind11::arg("dw"), pybind11::arg("db"), pybind11::arg("workspace"), pybind11::arg("rms"),
+        pybind11::arg("accumulate"), pybind11::arg("dx_lp") = pybind11::none());
   m.def("norm_backward_workspace_elems", &norm_backward_workspace_elems, "scratch size for norm_backward");
 }
 

@@ -361,7 +361,15 @@ __global__ void __launch_bounds__(256)
     }
   }
   local = warp_sum(local);
-  if (tx == 0) atomicAdd(&sumsq[i], local);
+  __shared__ float part[8];
+  if (tx == 0) part[ty] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k];
+    atomicAdd(&sumsq[i], t);
+  }
 }
 
 // X[i] *= 1 / (sqrt(sumsq[i]) + 1e-7)

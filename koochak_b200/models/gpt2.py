@@ -86,6 +86,24 @@ class Block(nn.Module):
         return [self.attn.c_attn.weight, self.attn.c_proj.weight, self.mlp.c_fc.weight, self.mlp.c_proj.weight]
 
 
+def _with_lp_copy(grad: torch.Tensor, lp: torch.Tensor) -> torch.Tensor:
+    """Attach the low-precision copy of an fp32 residual-stream gradient.
+
+    The LayerNorm backward kernel writes both copies in one pass; the next
+    block's backward reuses the bf16 copy for its GEMMs instead of casting.
+    """
+
+    grad._kb_lp = lp  # type: ignore[attr-defined]
+    return grad
+
+
+def _lp_copy_of(grad: torch.Tensor, dtype: torch.dtype):
+    lp = getattr(grad, "_kb_lp", None)
+    if lp is None or lp.dtype != dtype or lp.numel() != grad.numel():
+        return None
+    return lp
+
+
 class _BlockFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, ln1_w, ln1_b, attn_w, attn_b, proj_w, proj_b, ln2_w, ln2_b, fc_w, fc_b, fcp_w, fcp_b,
@@ -118,7 +136,8 @@ class _BlockFn(torch.autograd.Function):
         M = B * S
         cdt = attn_w16.dtype
         dout2 = dout.reshape(M, C).float().contiguous()
-        dy = to_lp(dout2, cdt)
+        dy = _lp_copy_of(dout, cdt)
+        dy = dy.reshape(M, C) if dy is not None else to_lp(dout2, cdt)
         # MLP
         dpre = kf.gemm(dy, fcp_w16, b_mn_major=True, d=pre, act=kf.ACT_GELU_BWD)
         d_fcp_w = kf.gemm(dy, g, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
@@ -126,10 +145,9 @@ class _BlockFn(torch.autograd.Function):
         dh2 = kf.gemm(dpre, fc_w16, b_mn_major=True)
         d_fc_w = kf.gemm(dpre, h2, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
         d_fc_b = kf.bias_grad(dpre)
-        dx_mid, d_ln2_w, d_ln2_b = kf.norm_backward(dh2, x_mid, ln2_w, m2, r2, rms=False, dres=dout2,
-                                                    dx_dtype=torch.float32)
+        dx_mid, d_ln2_w, d_ln2_b, dmid = kf.norm_backward(dh2, x_mid, ln2_w, m2, r2, rms=False, dres=dout2,
+                                                          dx_dtype=torch.float32, want_lp=True)
         # attention output projection
-        dmid = to_lp(dx_mid, cdt)
         da = kf.gemm(dmid, proj_w16, b_mn_major=True)
         d_proj_w = kf.gemm(dmid, a2, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
         d_proj_b = kf.bias_grad(dmid)
@@ -142,9 +160,9 @@ class _BlockFn(torch.autograd.Function):
         dh1 = kf.gemm(dqkv2, attn_w16, b_mn_major=True)
         d_attn_w = kf.gemm(dqkv2, h1, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
         d_attn_b = kf.bias_grad(dqkv2)
-        dx, d_ln1_w, d_ln1_b = kf.norm_backward(dh1, x2, ln1_w, m1, r1, rms=False, dres=dx_mid,
-                                                dx_dtype=torch.float32)
-        return (dx.view(B, S, C), d_ln1_w, d_ln1_b, d_attn_w, d_attn_b, d_proj_w, d_proj_b, d_ln2_w, d_ln2_b,
+        dx, d_ln1_w, d_ln1_b, dx_lp = kf.norm_backward(dh1, x2, ln1_w, m1, r1, rms=False, dres=dx_mid,
+                                                       dx_dtype=torch.float32, want_lp=True)
+        return (_with_lp_copy(dx.view(B, S, C), dx_lp), d_ln1_w, d_ln1_b, d_attn_w, d_attn_b, d_proj_w, d_proj_b, d_ln2_w, d_ln2_b,
                 d_fc_w, d_fc_b, d_fcp_w, d_fcp_b, None, None, None)
 
 
@@ -196,8 +214,9 @@ class _HeadLossFn(torch.autograd.Function):
         dlog = logits[:, :V]
         dh = kf.gemm(dlog, wte16, b_mn_major=True)
         dwte = kf.gemm(dlog, h, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
-        dx, dlnf_w, dlnf_b = kf.norm_backward(dh, x2, lnf_w, m, r, rms=False, dx_dtype=torch.float32)
-        return dx.view(B, S, C), dlnf_w, dlnf_b, dwte, None, None, None, None
+        dx, dlnf_w, dlnf_b, dx_lp = kf.norm_backward(dh, x2, lnf_w, m, r, rms=False, dx_dtype=torch.float32,
+                                                     want_lp=True)
+        return _with_lp_copy(dx.view(B, S, C), dx_lp), dlnf_w, dlnf_b, dwte, None, None, None, None
 
 
 class GPT2(nn.Module):

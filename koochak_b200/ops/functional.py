@@ -88,7 +88,9 @@ def norm_forward(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Ten
 
 
 def norm_backward(dy, x, weight, mean, rstd, *, rms: bool, dres: Optional[torch.Tensor] = None,
-                  dx_dtype: Optional[torch.dtype] = None, need_bias_grad: bool = True):
+                  dx_dtype: Optional[torch.dtype] = None, need_bias_grad: bool = True, want_lp: bool = False):
+    """Returns (dx, dweight, dbias[, dx in dy's dtype when ``want_lp``])."""
+
     C = x.shape[-1]
     rows = x.numel() // C
     dx = torch.empty(x.shape, device=x.device, dtype=dx_dtype or (dres.dtype if dres is not None else x.dtype))
@@ -96,7 +98,10 @@ def norm_backward(dy, x, weight, mean, rstd, *, rms: bool, dres: Optional[torch.
     db = None if (rms or not need_bias_grad) else torch.empty(C, device=x.device, dtype=torch.float32)
     ws = torch.empty(native().norm_backward_workspace_elems(rows, C, x.device.index or 0), device=x.device,
                      dtype=torch.float32)
-    native().norm_backward(dy, x, weight, mean, rstd, dres, dx, dw, db, ws, bool(rms), False)
+    lp = torch.empty(x.shape, device=x.device, dtype=dy.dtype) if want_lp else None
+    native().norm_backward(dy, x, weight, mean, rstd, dres, dx, dw, db, ws, bool(rms), False, lp)
+    if want_lp:
+        return dx, dw, db, lp
     return dx, dw, db
 
 
