@@ -7,10 +7,11 @@
 // (dy^T x) products, and the Newton-Schulz products of the Muon optimizer,
 // all run without a transpose copy.
 //
-// Roles inside one CTA (192 threads, one CTA per SM, grid = #SMs):
+// Roles inside one CTA (320 threads, one CTA per SM, grid = #SMs):
 //   warp 0      TMA producer: 128-byte-swizzled tiles into a STAGES-deep ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld from TMEM, fused math, global stores
+//   warps 2..9  epilogue: two warps per TMEM lane quarter, each taking half the
+//               columns; tcgen05.ld double-buffered against the math and stores
 // The fp32 accumulator is double-buffered in TMEM (2 x BN columns), so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -26,6 +27,7 @@
 
 #include <torch/extension.h>
 
+#include <cstring>
 #include <type_traits>
 
 namespace kb {
@@ -47,21 +49,28 @@ struct GemmParams {
   int vec_ok;  // C/D/aux rows 16-byte aligned for vector access
   int splits;  // split-K factor; > 1 means fp32 C is accumulated with atomics
   int kb_per_split;  // 64-wide K blocks per split (every split non-empty)
+  int tma_store;     // epilogue writes C (and aux) through staged TMA stores
   int* status;
 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+// Per-warp epilogue staging for TMA stores: two ping-pong 32 x 32 tiles of the
+// output type, plus two bf16 tiles for the pre-activation when the output is
+// 16-bit and GELU is fused (8 KB per warp either way).
+constexpr int kWarpStageBytes = 8192;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiStageBytes = kEpiWarps * kWarpStageBytes;  // 64 KB
+constexpr int kThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (BN == 256) ? 3 : 5;
   static constexpr int kTmemCols = 2 * BN;  // 256 or 512: power of two
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
 };
 
 template <typename OutT>
@@ -135,17 +144,178 @@ __device__ __forceinline__ void load_row32(const T* src, float (&v)[32], int val
   }
 }
 
+// Epilogue math for 32 consecutive accumulator columns of one row (one thread):
+// pre = alpha*acc (+ bias), v = the value to store (activation / D term applied).
+template <typename OutT, int ACT>
+__device__ __forceinline__ void epi_values(const GemmParams& p, const uint32_t (&raw)[32], const OutT* drow, int col0,
+                                           int valid, int split, bool vec, float (&v)[32], float (&pre)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) pre[j] = __uint_as_float(raw[j]) * p.alpha;
+  if (p.bias && split == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) pre[j] += (j < valid) ? p.bias[col0 + j] : 0.f;
+  }
+  if constexpr (ACT == ACT_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(pre[j]);
+  } else if constexpr (ACT == ACT_GELU_BWD) {
+    float h[32];
+    load_row32<OutT>(drow + col0, h, valid, vec);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = pre[j] * gelu_tanh_grad(h[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = pre[j];
+    if (drow != nullptr && p.beta != 0.f) {
+      float d[32];
+      load_row32<OutT>(drow + col0, d, valid, vec);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += p.beta * d[j];
+    }
+  }
+}
+
+// Writes one thread's 32 values (its row) into a warp staging tile laid out as
+// the TMA store expects: 32 rows x 32 elements, 128-byte rows (fp32, 128-byte
+// swizzle) or 64-byte rows (16-bit types, 64-byte swizzle), so the 16-byte
+// writes of a warp are bank-conflict free.
+template <typename T>
+__device__ __forceinline__ void stage_row32(uint8_t* tile, int r, const float (&v)[32]) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int pc = c ^ (r & 7);
+      *reinterpret_cast<float4*>(tile + r * 128 + pc * 16) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int pc = c ^ ((r >> 1) & 3);
+      uint4 q;
+      if constexpr (std::is_same<T, __half>::value) {
+        q.x = pack_f16(v[8 * c], v[8 * c + 1]);
+        q.y = pack_f16(v[8 * c + 2], v[8 * c + 3]);
+        q.z = pack_f16(v[8 * c + 4], v[8 * c + 5]);
+        q.w = pack_f16(v[8 * c + 6], v[8 * c + 7]);
+      } else {
+        q.x = pack_bf16(v[8 * c], v[8 * c + 1]);
+        q.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+        q.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+        q.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+      }
+      *reinterpret_cast<uint4*>(tile + r * 64 + pc * 16) = q;
+    }
+  }
+}
+
+struct EpiMaps {
+  CUtensorMap c;    // C: dims {N, M, batch}, box {32, 32, 1}
+  CUtensorMap aux;  // pre-activation, bf16
+};
+
+// One warp's share of a tile's epilogue: its 32 accumulator rows (TMEM lane
+// quarter) x columns [c_begin, c_end). TMEM loads are double-buffered so the
+// load of chunk i+1 overlaps the math of chunk i. With `use_tma`, each 32 x 32
+// chunk is staged in shared memory and written by one TMA store (full-line
+// writes instead of 32 scattered row segments per warp instruction).
+template <typename OutT, int ACT>
+__device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps& maps, uint8_t* wstage,
+                                              int& stage_pp, uint32_t tmem_row, int row0, int b, int n0, int split,
+                                              int c_begin, int c_end, bool vec, bool use_tma) {
+  const int lane = threadIdx.x & 31;
+  const int row = row0 + lane;
+  const bool row_ok = row < p.M;
+  OutT* crow = reinterpret_cast<OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc;
+  const OutT* drow =
+      p.D ? reinterpret_cast<const OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd : nullptr;
+  __nv_bfloat16* arow =
+      p.aux ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux : nullptr;
+  const bool atomic_out = std::is_same<OutT, float>::value && ACT == ACT_NONE && p.splits > 1;
+  uint32_t r0[32], r1[32];
+
+  auto handle = [&](const uint32_t (&raw)[32], int c) {
+    const int col0 = n0 + c;
+    if (col0 >= p.N) return;
+    const int valid = min(32, p.N - col0);
+    float v[32], pre[32];
+    if (row_ok) {
+      epi_values<OutT, ACT>(p, raw, drow, col0, valid, split, vec, v, pre);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = pre[j] = 0.f;  // rows past M: clipped by the TMA store
+    }
+    if (atomic_out) {
+      if (!row_ok) return;
+      float* dst = reinterpret_cast<float*>(crow) + col0;
+      if (vec && valid == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      } else {
+        for (int j = 0; j < valid; ++j) atomicAdd(dst + j, v[j]);
+      }
+      return;
+    }
+    if (!use_tma) {
+      if (!row_ok) return;
+      if constexpr (ACT == ACT_GELU) {
+        if (arow) store_row32<__nv_bfloat16>(arow + col0, pre, valid, vec);
+      }
+      store_row32<OutT>(crow + col0, v, valid, vec);
+      return;
+    }
+    // TMA path: make sure the store that used this buffer two chunks ago has
+    // finished reading shared memory, stage, then issue one bulk store.
+    constexpr int kCTile = 32 * 32 * (int)sizeof(OutT);
+    uint8_t* ctile = wstage + stage_pp * kCTile;
+    uint8_t* atile = wstage + 2 * kCTile + stage_pp * 2048;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    stage_row32<OutT>(ctile, lane, v);
+    if constexpr (ACT == ACT_GELU) {
+      if (p.aux) stage_row32<__nv_bfloat16>(atile, lane, pre);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(&maps.c, ctile, col0, row0, b);
+      if constexpr (ACT == ACT_GELU) {
+        if (p.aux) tma_store_3d(&maps.aux, atile, col0, row0, b);
+      }
+      bulk_commit();
+    }
+    stage_pp ^= 1;
+  };
+
+  tmem_ld_32x32b_x32(tmem_row + c_begin, r0);
+  tmem_wait_ld_dep(r0);
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; c += 64) {
+    const bool second = c + 32 < c_end;
+    if (second) tmem_ld_32x32b_x32(tmem_row + c + 32, r1);
+    handle(r0, c);
+    if (second) {
+      tmem_wait_ld_dep(r1);
+      const bool third = c + 64 < c_end;
+      if (third) tmem_ld_32x32b_x32(tmem_row + c + 64, r0);
+      handle(r1, c + 32);
+      if (third) tmem_wait_ld_dep(r0);
+    }
+  }
+}
 template <int BN, typename OutT, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const GemmParams p) {
+                        const GemmParams p, const __grid_constant__ EpiMaps maps) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
+  uint8_t* sEpi = sB + S * Cfg::kBBytes;  // 1024-aligned: stage sizes are multiples of 8 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -163,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -302,8 +472,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // two warps per quarter split the columns
     const bool vec = p.vec_ok != 0;
+    const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
+    uint8_t* wstage = sEpi + (warp - 2) * kWarpStageBytes;
+    int stage_pp = 0;
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -316,66 +490,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
-      const int row = m_blk * kBM + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      OutT* crow = reinterpret_cast<OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc;
-      const OutT* drow = p.D ? reinterpret_cast<const OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd
-                             : nullptr;
-      __nv_bfloat16* arow =
-          p.aux ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux
-                : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t raw[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c, raw);
-        tmem_wait_ld();
-        const int col0 = n_blk * BN + c;
-        if (!row_ok || col0 >= p.N) continue;
-        const int valid = min(32, p.N - col0);
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * p.alpha;
-        if (p.bias && split == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += (j < valid) ? p.bias[col0 + j] : 0.f;
-        }
-        if constexpr (std::is_same<OutT, float>::value && ACT == ACT_NONE) {
-          if (p.splits > 1) {
-            // Split-K: accumulate partial sums into C (pre-initialised by the host).
-            float* dst = reinterpret_cast<float*>(crow) + col0;
-            if (vec && valid == 32) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-            } else {
-              for (int j = 0; j < valid; ++j) atomicAdd(dst + j, v[j]);
-            }
-            continue;
-          }
-        }
-        if constexpr (ACT == ACT_GELU) {
-          if (arow) store_row32<__nv_bfloat16>(arow + col0, v, valid, vec);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-        } else if constexpr (ACT == ACT_GELU_BWD) {
-          float h[32];
-          load_row32<OutT>(drow + col0, h, valid, vec);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= gelu_tanh_grad(h[j]);
-        } else {
-          if (drow != nullptr && p.beta != 0.f) {
-            float d[32];
-            load_row32<OutT>(drow + col0, d, valid, vec);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += p.beta * d[j];
-          }
-        }
-        store_row32<OutT>(crow + col0, v, valid, vec);
-      }
+      epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
+                               m_blk * kBM + q * 32, b, n_blk * BN, split, half * (BN / 2), (half + 1) * (BN / 2), vec,
+                               use_tma);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (use_tma && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -383,6 +505,239 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------- 2-SM variant
+//
+// A cluster of two CTAs computes a 256 x BN tile with tcgen05.mma.cta_group::2:
+// each CTA stages its own 128 rows of A and its own BN/2 rows of B (halving the
+// operand traffic per SM against the 1-SM kernel), the even CTA issues the
+// MMAs, and each CTA's TMEM receives the 128 x BN fp32 accumulator of its rows.
+// Both CTAs' TMA loads signal the even CTA's "full" barrier; the MMA commit
+// signals the "empty"/"tmem full" barriers of both CTAs; both CTAs' epilogues
+// signal the even CTA's "tmem empty" barrier. No load uses cluster multicast.
+
+template <int BN>
+struct Gemm2Cfg {
+  static constexpr int kABytes = 128 * kBK * 2;
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (192 * 1024 - kEpiStageBytes) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+};
+
+template <int BN, typename OutT, int ACT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p, const __grid_constant__ EpiMaps maps) {
+  using Cfg = Gemm2Cfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int BHALF = BN / 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint8_t* sEpi = sB + S * Cfg::kBBytes;  // 1024-aligned: stage sizes are multiples of 8 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 16);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int num_m = (p.M + 255) / 256;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int tiles_per_batch = num_m * num_n;
+  const int tiles_per_split = tiles_per_batch * p.batch;
+  const int total_tiles = tiles_per_split * p.splits;
+  const int num_kb_total = (p.K + kBK - 1) / kBK;
+  const int kb_per_split = p.kb_per_split;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producers (both CTAs)
+      const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_parity[S];
+      bool armed[S];
+      for (int s = 0; s < S; ++s) armed[s] = false;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
+        const int split = t / tiles_per_split;
+        const int ts = t - split * tiles_per_split;
+        const int b = ts / tiles_per_batch;
+        const int r = ts - b * tiles_per_batch;
+        const int n_blk = r / num_m;
+        const int m_blk = r - n_blk * num_m;
+        const int m0 = m_blk * 256 + (int)rank * 128;
+        const int n0 = n_blk * BN + (int)rank * BHALF;
+        const int kb0 = split * kb_per_split;
+        const int kb1 = min(num_kb_total, kb0 + kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+            armed[stage] = true;
+            armed_parity[stage] = phase;
+          }
+          const uint32_t fb = full0 + stage * 8;
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          const int k0 = kb * kBK;
+          if (!p.a_mn_major) {
+            tma_load_3d_pair(&tmA, fb, a_dst, k0, m0, b);
+          } else {
+            tma_load_3d_pair(&tmA, fb, a_dst, m0, k0, b);
+            tma_load_3d_pair(&tmA, fb, a_dst + 8192, m0 + 64, k0, b);
+          }
+          if (!p.b_mn_major) {
+            tma_load_3d_pair(&tmB, fb, b_dst, k0, n0, b);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BHALF / 64; ++c) tma_load_3d_pair(&tmB, fb, b_dst + c * 8192, n0 + c * 64, k0, b);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (leader) {
+        // The leader's full barriers account for both CTAs' copies.
+        for (int s = 0; s < S; ++s) {
+          if (armed[s]) {
+            volatile int never = 0;
+            if (!mbar_wait(&full[s], armed_parity[s], &never, p.status, kStatusTimeoutDrain)) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (even CTA)
+      const uint32_t idesc = idesc_f16(256, BN, p.fp16_inputs != 0, p.a_mn_major != 0, p.b_mn_major != 0);
+      const uint32_t a_lbo = p.a_mn_major ? 8192u : 16u;
+      const uint32_t b_lbo = p.b_mn_major ? 8192u : 16u;
+      const uint32_t a_kstep = p.a_mn_major ? 2048u : 32u;
+      const uint32_t b_kstep = p.b_mn_major ? 2048u : 32u;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = pair; t < total_tiles && ok; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        const int split = t / tiles_per_split;
+        const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sw128_desc(a_addr + k * a_kstep, a_lbo, 1024);
+            const uint64_t bd = sw128_desc(b_addr + k * b_kstep, b_lbo, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tfull[acc], 0x3);
+      }
+      if (issued_any) {
+        umma_commit_pair(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const bool vec = p.vec_ok != 0;
+    const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
+    uint8_t* wstage = sEpi + (warp - 2) * kWarpStageBytes;
+    int stage_pp = 0;
+    const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
+    int local = 0;
+    for (int t = pair; t < total_tiles; t += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int split = t / tiles_per_split;
+      const int ts = t - split * tiles_per_split;
+      const int b = ts / tiles_per_batch;
+      const int r = ts - b * tiles_per_batch;
+      const int n_blk = r / num_m;
+      const int m_blk = r - n_blk * num_m;
+      epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
+                               m_blk * 256 + (int)rank * 128 + q * 32, b, n_blk * BN, split, half * (BN / 2),
+                               (half + 1) * (BN / 2), vec, use_tma);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
+    }
+    if (use_tma && lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -394,8 +749,8 @@ static bool is_mn_major_2d(const at::Tensor& t) {
 }
 
 template <int BN, typename OutT, int ACT>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
-                        cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps,
+                        int grid, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tcgen05_kernel<BN, OutT, ACT>;
   static bool attr_set = false;
@@ -403,17 +758,42 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_set = true;
   }
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p, maps);
   KB_LAUNCHED();
 }
 
 template <int BN, typename OutT>
-static void dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+static void dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps, int grid,
                          cudaStream_t s) {
   switch (act) {
-    case ACT_NONE: launch_gemm<BN, OutT, ACT_NONE>(ta, tb, p, grid, s); break;
-    case ACT_GELU: launch_gemm<BN, OutT, ACT_GELU>(ta, tb, p, grid, s); break;
-    case ACT_GELU_BWD: launch_gemm<BN, OutT, ACT_GELU_BWD>(ta, tb, p, grid, s); break;
+    case ACT_NONE: launch_gemm<BN, OutT, ACT_NONE>(ta, tb, p, maps, grid, s); break;
+    case ACT_GELU: launch_gemm<BN, OutT, ACT_GELU>(ta, tb, p, maps, grid, s); break;
+    case ACT_GELU_BWD: launch_gemm<BN, OutT, ACT_GELU_BWD>(ta, tb, p, maps, grid, s); break;
+    default: KB_CHECK(false, "bad activation");
+  }
+}
+
+template <int BN, typename OutT, int ACT>
+static void launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps,
+                         int grid, cudaStream_t stream) {
+  using Cfg = Gemm2Cfg<BN>;
+  auto kern = gemm_2sm_kernel<BN, OutT, ACT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p, maps);
+  KB_LAUNCHED();
+}
+
+template <int BN, typename OutT>
+static void dispatch_act2(int act, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps, int grid,
+                          cudaStream_t s) {
+  switch (act) {
+    case ACT_NONE: launch_gemm2<BN, OutT, ACT_NONE>(ta, tb, p, maps, grid, s); break;
+    case ACT_GELU: launch_gemm2<BN, OutT, ACT_GELU>(ta, tb, p, maps, grid, s); break;
+    case ACT_GELU_BWD: launch_gemm2<BN, OutT, ACT_GELU_BWD>(ta, tb, p, maps, grid, s); break;
     default: KB_CHECK(false, "bad activation");
   }
 }
@@ -475,20 +855,41 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
 
   const c10::cuda::CUDAGuard guard(a.device());
   const int dev = a.get_device();
-  int bn = (int)block_n;
-  if (bn != 128 && bn != 256) {
-    // Pick the tile width that wastes the least of the final wave.
-    const int sms = num_sms(dev);
-    auto waste = [&](int w) {
-      const int64_t tiles = batch * ((M + 127) / 128) * ((N + w - 1) / w);
-      const int64_t waves = (tiles + sms - 1) / sms;
-      const double work = double(batch) * double((M + 127) / 128 * 128) * double(N);
-      return double(waves) * sms * 128.0 * w / work;  // >= 1, smaller is better
-    };
-    bn = (N <= 128 || waste(128) + 0.03 < waste(256)) ? 128 : 256;
+  // Tile configuration: 1-SM 128 x {128, 256} or 2-SM 256 x {128, 256}.
+  // block_n > 0 forces a 1-SM width, block_n < 0 forces a 2-SM width |block_n|;
+  // 0 picks the configuration with the lowest estimated time (waves x tile work,
+  // weighted by each configuration's measured relative efficiency).
+  const int sms_all = num_sms(dev);
+  int bn = 0;
+  bool pair_mode = false;
+  if (block_n == 128 || block_n == 256) {
+    bn = (int)block_n;
+  } else if (block_n == -128 || block_n == -256) {
+    bn = (int)-block_n;
+    pair_mode = true;
+  } else {
+    double best = 1e30;
+    const int cand_bn[4] = {128, 256, 128, 256};
+    const bool cand_pair[4] = {false, false, true, true};
+    const double factor[4] = {1.15, 1.0, 0.9, 0.8};
+    for (int i = 0; i < 4; ++i) {
+      const int w = cand_bn[i];
+      const bool pm = cand_pair[i];
+      if (pm && M < 256) continue;
+      const int rows = pm ? 256 : 128;
+      const int64_t t = batch * ((M + rows - 1) / rows) * ((N + w - 1) / w);
+      const int64_t slots = pm ? sms_all / 2 : sms_all;
+      const int64_t waves = (t + slots - 1) / slots;
+      const double cost = double(waves) * (double(w) / 256.0) * factor[i];
+      if (cost < best - 1e-9) {
+        best = cost;
+        bn = w;
+        pair_mode = pm;
+      }
+    }
   }
   const CUtensorMap ta = operand_map(a, a_mn_major, (int)M, (int)K, 128);
-  const CUtensorMap tb = operand_map(b, b_mn_major, (int)N, (int)K, bn);
+  const CUtensorMap tb = operand_map(b, b_mn_major, (int)N, (int)K, pair_mode ? bn / 2 : bn);
 
   GemmParams p{};
   p.M = (int)M;
@@ -526,8 +927,9 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   p.vec_ok = vec;
   p.status = device_status_ptr(dev);
 
-  const int64_t tiles = batch * ((M + 127) / 128) * ((N + bn - 1) / bn);
-  const int sms = num_sms(dev);
+  const int rows_per_tile = pair_mode ? 256 : 128;
+  const int64_t tiles = batch * ((M + rows_per_tile - 1) / rows_per_tile) * ((N + bn - 1) / bn);
+  const int sms = pair_mode ? (sms_all / 2) : sms_all;  // concurrent tile slots
   const int64_t num_kb = (K + 63) / 64;
   // Split K when the output has too few tiles to fill the GPU and K is long
   // (weight gradients): partial tiles are summed into C with fp32 atomics.
@@ -555,15 +957,50 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     p.D = nullptr;
     p.beta = 0.f;
   }
+  // Staged TMA stores need 16-byte aligned rows (and batch strides) for C and aux.
+  EpiMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  {
+    const int64_t esz = c.element_size();
+    bool ok = splits == 1 && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+              (!batched || (p.strideC * esz) % 16 == 0);
+    if (ok && p.aux != nullptr)
+      ok = (p.ldaux * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15) == 0 && (!batched || (p.strideAux * 2) % 16 == 0);
+    if (ok) {
+      auto make = [&](void* base, at::ScalarType t, int64_t ld, int64_t bstride, int64_t es) {
+        uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)batch};
+        uint64_t strides[2] = {(uint64_t)(ld * es), (uint64_t)((batched ? bstride : ld * M) * es)};
+        if (strides[1] % 16) strides[1] = (strides[1] + 15) / 16 * 16;
+        uint32_t box[3] = {32, 32, 1};
+        return make_tma(base, t, 3, dims, strides, box, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+      };
+      maps.c = make(p.C, ct, p.ldc, p.strideC, esz);
+      if (p.aux != nullptr) maps.aux = make(p.aux, at::kBFloat16, p.ldaux, p.strideAux, 2);
+      p.tma_store = 1;
+    }
+  }
+  if (pair_mode) {
+    const int grid2 = 2 * (int)std::min<int64_t>(tiles * splits, sms);
+    if (bn == 256) {
+      if (ct == at::kFloat) dispatch_act2<256, float>((int)act, ta, tb, p, maps, grid2, stream);
+      else if (ct == at::kBFloat16) dispatch_act2<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid2, stream);
+      else dispatch_act2<256, __half>((int)act, ta, tb, p, maps, grid2, stream);
+    } else {
+      if (ct == at::kFloat) dispatch_act2<128, float>((int)act, ta, tb, p, maps, grid2, stream);
+      else if (ct == at::kBFloat16) dispatch_act2<128, __nv_bfloat16>((int)act, ta, tb, p, maps, grid2, stream);
+      else dispatch_act2<128, __half>((int)act, ta, tb, p, maps, grid2, stream);
+    }
+    return;
+  }
   const int grid = (int)std::min<int64_t>(tiles * splits, sms);
   if (bn == 256) {
-    if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, grid, stream);
-    else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, grid, stream);
-    else dispatch_act<256, __half>((int)act, ta, tb, p, grid, stream);
+    if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, maps, grid, stream);
+    else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid, stream);
+    else dispatch_act<256, __half>((int)act, ta, tb, p, maps, grid, stream);
   } else {
-    if (ct == at::kFloat) dispatch_act<128, float>((int)act, ta, tb, p, grid, stream);
-    else if (ct == at::kBFloat16) dispatch_act<128, __nv_bfloat16>((int)act, ta, tb, p, grid, stream);
-    else dispatch_act<128, __half>((int)act, ta, tb, p, grid, stream);
+    if (ct == at::kFloat) dispatch_act<128, float>((int)act, ta, tb, p, maps, grid, stream);
+    else if (ct == at::kBFloat16) dispatch_act<128, __nv_bfloat16>((int)act, ta, tb, p, maps, grid, stream);
+    else dispatch_act<128, __half>((int)act, ta, tb, p, maps, grid, stream);
   }
 }
 

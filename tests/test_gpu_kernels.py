@@ -249,3 +249,23 @@ def test_gpt2_native_matches_reference_path():
     assert abs(loss.item() - ref.item()) < 2e-2
     for n, p in model.named_parameters():
         assert _rel(g_native[n], p.grad) < 0.08, n
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (520, 384, 200), (2048, 2304, 768), (1000, 776, 1024)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("block_n", [-128, -256])
+def test_gemm_two_sm(M, N, K, a_mn, b_mn, block_n):
+    """2-SM (cta_group::2) tiles against the fp32 reference, including epilogues and split-K."""
+    kf = _kf()
+    torch.manual_seed(11)
+    if (a_mn and M % 8) or (b_mn and N % 8):
+        pytest.skip("MN-major operands need 16-byte aligned rows")
+    a = (torch.randn(K, M) if a_mn else torch.randn(M, K)).to(DEV, torch.bfloat16)
+    b = (torch.randn(K, N) if b_mn else torch.randn(N, K)).to(DEV, torch.bfloat16)
+    out = kf.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, out_dtype=torch.float32, block_n=block_n)
+    assert _rel(out, kf.gemm_ref(a, b, a_mn_major=a_mn, b_mn_major=b_mn)) < 1e-4
+    bias = torch.randn(N, device=DEV)
+    aux = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    g = kf.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, aux=aux, act=kf.ACT_GELU, block_n=block_n)
+    rg, rpre = kf.gemm_ref(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, act=kf.ACT_GELU)
+    assert _rel(g, rg) < 1e-2 and _rel(aux, rpre) < 1e-2
