@@ -11,6 +11,7 @@
 // grid keeps the partial buffer at (#CTAs x C) and a second kernel reduces it.
 #include "host_utils.h"
 #include "sm100.cuh"
+#include "noalloc.h"
 
 #include <torch/extension.h>
 
@@ -382,6 +383,103 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
 int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
   const int grid = std::max<int64_t>(1, std::min<int64_t>(num_sms((int)device) * 4, (M + kNormWarps - 1) / kNormWarps));
   return 2LL * grid * C;
+}
+
+// ---------------------------------------------------------------------------
+// kb_layernorm_backward_noalloc: LayerNorm backward that allocates nothing.
+//
+// This entry point has no counterpart in the reference framework.
+//
+// The regular norm_backward above takes its partial-sum scratch from the
+// caller (the Python layer allocates it through PyTorch's caching allocator).
+// Some callers cannot allocate device memory at the point where they need
+// this op: code running while a stream is being captured into a CUDA graph
+// (an allocation made there is not part of the graph and breaks replay),
+// engines that own a fixed device-memory arena and forbid any other
+// allocation, and plain C callers that link this library without PyTorch and
+// therefore have no allocator to hand over. For them this variant keeps its
+// scratch in a file-scope device array of fixed size:
+//
+//   * limit: kNoAllocScratchFloats fp32 values (4 MiB). A call needs
+//     2 * grid * C values, where the grid is shrunk (down to one CTA) to fit;
+//     rows wider than kNoAllocMaxC = 4096 are rejected with an error code.
+//   * every GPU that loads this library holds the 4 MiB until process exit.
+//   * all calls share the one array, which keeps the previous call's
+//     contents; every partial that is read is first written in the same
+//     call, so nothing has to start at zero. Calls whose kernels overlap on
+//     the GPU (different streams, or concurrent host threads) race on the
+//     array and must be serialised by the caller.
+//   * the first call on each device resolves the array's device address with
+//     cudaGetSymbolAddress (the host-side name of a __device__ array is not a
+//     device address); make that first call before any stream capture.
+//   * no cudaMalloc, cudaFree or allocating library routine is called.
+//
+// Types: dy bf16 [M, C]; x, w, mean, rstd, dx, dw, db fp32; all contiguous,
+// x/dy/dx rows 16-byte aligned. dx = LayerNorm backward (no residual term);
+// dw, db are overwritten. Returns 0 on success, or a cudaError_t value / -1
+// (bad arguments) / -2 (row width over the limit).
+
+constexpr long long kNoAllocScratchFloats = 1ll << 20;  // 4 MiB of fp32
+constexpr int kNoAllocMaxC = 4096;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+static float* noalloc_scratch_ptr(int device, cudaError_t* err) {
+  static std::mutex mu;
+  static float* ptrs[64] = {nullptr};
+  if (device < 0 || device >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[device] == nullptr) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // `device` is current here
+    if (*err != cudaSuccess) return nullptr;
+    ptrs[device] = static_cast<float*>(p);
+  }
+  *err = cudaSuccess;
+  return ptrs[device];
+}
+
+extern "C" __attribute__((visibility("default"))) int kb_layernorm_backward_noalloc(
+    const void* dy, const float* x, const float* w, const float* mean, const float* rstd, float* dx, float* dw,
+    float* db, int M, int C, cudaStream_t stream) {
+  if (dy == nullptr || x == nullptr || w == nullptr || mean == nullptr || rstd == nullptr || dx == nullptr ||
+      dw == nullptr || db == nullptr || M <= 0 || C <= 0 || C % 4 != 0)
+    return -1;
+  if (C > kNoAllocMaxC) return -2;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return (int)err;
+  float* scratch = noalloc_scratch_ptr(device, &err);
+  if (scratch == nullptr) return (int)err;
+  int sms = 0;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err != cudaSuccess) return (int)err;
+  long long grid = std::min<long long>((long long)sms * 4, (M + kNormWarps - 1) / kNormWarps);
+  grid = std::min<long long>(grid, kNoAllocScratchFloats / (2LL * C));
+  grid = std::max<long long>(grid, 1);
+  float* dw_part = scratch;
+  float* db_part = scratch + grid * C;
+  const int smem = kNormWarps * C * (int)sizeof(float);
+  bool launched = false;
+  with_vpt(C, [&](auto vpt) {
+    constexpr int V = decltype(vpt)::value;
+    auto kern = norm_bwd_kernel<V, float, __nv_bfloat16, float, false>;
+    if (smem > 48 * 1024) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
+    }
+    kern<<<(unsigned)grid, 32 * kNormWarps, smem, stream>>>(static_cast<const __nv_bfloat16*>(dy), x, w, mean, rstd,
+                                                             nullptr, dx, nullptr, dw_part, db_part, M, C);
+    launched = true;
+  });
+  if (!launched) return (int)cudaErrorInvalidConfiguration;
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return (int)err;
+  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw, (int)grid, C, 0);
+  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(db_part, db, (int)grid, C, 0);
+  err = cudaGetLastError();
+  return (int)err;
 }
 
 void register_norm_ops(pybind11::module& m) {
