@@ -1,0 +1,102 @@
+"""GEMM benchmark: the native tcgen05 GEMM against cuBLAS on the model shapes.
+
+Shapes are the linear layers of GPT-2 124M at 16 x 1024 tokens per GPU
+(M = 16384; d = 768, FFN 3072, vocab 50304 padded) and the Newton-Schulz
+GEMMs of Muon on 12 stacked 768 x c matrices. Each case is timed with CUDA
+events after warm-up; the inputs of the linear cases stay resident in L2
+(this measures the kernels, not DRAM).
+
+    python -m koochak_b200.benchmarks.gemm                 # every case
+    python -m koochak_b200.benchmarks.gemm --case fc --op fwd --iters 4 --no-compare
+"""
+
+from __future__ import annotations
+
+import argparse
+from typing import Callable, Dict, List, Tuple
+
+import torch
+
+LINEAR: Dict[str, Tuple[int, int]] = {  # name -> (N out, K in)
+    "qkv": (2304, 768),
+    "attn_proj": (768, 768),
+    "fc": (3072, 768),
+    "mlp_proj": (768, 3072),
+    "lm_head": (50304, 768),
+}
+
+
+def time_ms(fn: Callable[[], object], iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def linear_cases(name: str, M: int, block_n: int):
+    from koochak_b200.ops import functional as kf
+
+    N, K = LINEAR[name]
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(N, K, device="cuda").bfloat16()
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    flops = 2.0 * M * N * K
+    return flops, {
+        "fwd": (lambda: kf.gemm(x, w, block_n=block_n), lambda: torch.matmul(x, w.t())),
+        "dgrad": (lambda: kf.gemm(dy, w, b_mn_major=True, block_n=block_n), lambda: torch.matmul(dy, w)),
+        "wgrad": (lambda: kf.gemm(dy, x, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32, block_n=block_n),
+                  lambda: torch.matmul(dy.t(), x)),
+    }
+
+
+def ns_cases(c: int, batch: int = 12, r: int = 768):
+    from koochak_b200.ops import functional as kf
+
+    X = torch.randn(batch, r, c, device="cuda").bfloat16()
+    A = torch.randn(batch, r, r, device="cuda").bfloat16()
+    return {
+        "XXt": (2.0 * batch * r * r * c, lambda: kf.gemm(X, X), lambda: torch.bmm(X, X.transpose(1, 2))),
+        "AA": (2.0 * batch * r ** 3, lambda: kf.gemm(A, A, d=A, alpha=2.0, beta=-4.0), lambda: torch.bmm(A, A)),
+        "BX": (2.0 * batch * r * r * c, lambda: kf.gemm(A, X, b_mn_major=True, d=X, beta=3.0),
+               lambda: torch.bmm(A, X)),
+    }
+
+
+def main(argv: List[str] | None = None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--case", default="all", help="linear layer name, 'ns<c>' (e.g. ns768) or 'all'")
+    ap.add_argument("--op", default="all", help="fwd | dgrad | wgrad | XXt | AA | BX | all")
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--block-n", type=int, default=0, help="0 auto; 128/256 one-SM tiles; -128/-256 two-SM tiles")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS comparison")
+    args = ap.parse_args(argv)
+    torch.manual_seed(0)
+    names = list(LINEAR) + ["ns768", "ns2304", "ns3072"] if args.case == "all" else [args.case]
+    for name in names:
+        if name.startswith("ns"):
+            cases = ns_cases(int(name[2:]))
+            items = [(op, fl, a, b) for op, (fl, a, b) in cases.items()]
+        else:
+            fl, cases = linear_cases(name, args.tokens, args.block_n)
+            items = [(op, fl, a, b) for op, (a, b) in cases.items()]
+        for op, fl, ours, ref in items:
+            if args.op != "all" and op != args.op:
+                continue
+            t = time_ms(ours, args.iters)
+            line = f"{name:10s} {op:6s} ours {t * 1e3:8.1f} us {fl / t / 1e9:6.0f} TF/s"
+            if not args.no_compare:
+                tr = time_ms(ref, args.iters)
+                line += f" | cublas {tr * 1e3:8.1f} us {fl / tr / 1e9:6.0f} TF/s | ratio {tr / t:.2f}"
+            print(line, flush=True)
+
+
+if __name__ == "__main__":
+    main()

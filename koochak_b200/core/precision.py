@@ -144,6 +144,27 @@ class FusedGradScaler(GradScaler):
         self.last_stats = stats
 
 
+    def mark_unscaled(self, optimizer, stats: torch.Tensor) -> None:
+        """Record gradients that were already unscaled elsewhere (the fused all-reduce).
+
+        ``stats`` is the device vector [norm, coefficient, found_inf, ...] of
+        that pass; its found_inf decides whether ``step`` is skipped.
+        """
+
+        from torch.amp.grad_scaler import OptState
+
+        if not self._enabled:
+            return
+        self._check_scale_growth_tracker("unscale_")
+        state = self._per_optimizer_states[id(optimizer)]
+        if state["stage"] is not OptState.READY:
+            raise RuntimeError("mark_unscaled() must come before unscale_() / step() of this update.")
+        dev = stats.device
+        state["found_inf_per_device"] = {dev: stats[2:3].clone()}
+        state["stage"] = OptState.UNSCALED
+        self.last_stats = stats
+
+
 def Scaler(mode: Optional[str]):
     """GradScaler for fp16 on CUDA, a no-op scaler otherwise."""
 

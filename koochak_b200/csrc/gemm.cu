@@ -55,22 +55,32 @@ struct GemmParams {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-// Per-warp epilogue staging for TMA stores: two ping-pong 32 x 32 tiles of the
-// output type, plus two bf16 tiles for the pre-activation when the output is
-// 16-bit and GELU is fused (8 KB per warp either way).
-constexpr int kWarpStageBytes = 8192;
 constexpr int kEpiWarps = 8;
-constexpr int kEpiStageBytes = kEpiWarps * kWarpStageBytes;  // 64 KB
 constexpr int kThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
+// Dynamic shared memory a CTA may use on sm_100 (227 KB), less the 1 KB
+// alignment slack and the barrier block.
+constexpr int kSmemBudget = 232448 - 1024 - 256;
 
-template <int BN>
+// Per-warp epilogue staging for TMA stores: two ping-pong 32 x 32 tiles of the
+// output type, plus two bf16 tiles for the pre-activation when GELU is fused.
+// The rest of shared memory goes to the operand ring.
+template <typename OutT, int ACT>
+struct EpiStage {
+  static constexpr int kCTile = 32 * 32 * (int)sizeof(OutT);
+  static constexpr int kWarpBytes = 2 * kCTile + (ACT == ACT_GELU ? 2 * 2048 : 0);
+  static constexpr int kBytes = kEpiWarps * kWarpBytes;
+};
+
+template <int BN, typename OutT, int ACT>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 3 : 5;
+  static constexpr int kEpiBytes = EpiStage<OutT, ACT>::kBytes;
+  static constexpr int kStagesFit = (kSmemBudget - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kTmemCols = 2 * BN;  // 256 or 512: power of two
-  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
 };
 
 template <typename OutT>
@@ -267,7 +277,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
     }
     // TMA path: make sure the store that used this buffer two chunks ago has
     // finished reading shared memory, stage, then issue one bulk store.
-    constexpr int kCTile = 32 * 32 * (int)sizeof(OutT);
+    constexpr int kCTile = EpiStage<OutT, ACT>::kCTile;
     uint8_t* ctile = wstage + stage_pp * kCTile;
     uint8_t* atile = wstage + 2 * kCTile + stage_pp * 2048;
     if (lane == 0) bulk_wait_read<1>();
@@ -308,14 +318,14 @@ template <int BN, typename OutT, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmParams p, const __grid_constant__ EpiMaps maps) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, OutT, ACT>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
   uint8_t* sEpi = sB + S * Cfg::kBBytes;  // 1024-aligned: stage sizes are multiples of 8 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -476,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;   // two warps per quarter split the columns
     const bool vec = p.vec_ok != 0;
     const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
-    uint8_t* wstage = sEpi + (warp - 2) * kWarpStageBytes;
+    uint8_t* wstage = sEpi + (warp - 2) * EpiStage<OutT, ACT>::kWarpBytes;
     int stage_pp = 0;
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
@@ -518,21 +528,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 // signals the "empty"/"tmem full" barriers of both CTAs; both CTAs' epilogues
 // signal the even CTA's "tmem empty" barrier. No load uses cluster multicast.
 
-template <int BN>
+template <int BN, typename OutT, int ACT>
 struct Gemm2Cfg {
   static constexpr int kABytes = 128 * kBK * 2;
   static constexpr int kBBytes = (BN / 2) * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (192 * 1024 - kEpiStageBytes) / kStageBytes;
+  static constexpr int kEpiBytes = EpiStage<OutT, ACT>::kBytes;
+  static constexpr int kStagesFit = (kSmemBudget - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
 };
 
 template <int BN, typename OutT, int ACT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmParams p, const __grid_constant__ EpiMaps maps) {
-  using Cfg = Gemm2Cfg<BN>;
+  using Cfg = Gemm2Cfg<BN, OutT, ACT>;
   constexpr int S = Cfg::kStages;
   constexpr int BHALF = BN / 2;
   extern __shared__ uint8_t smem_raw[];
@@ -540,7 +552,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kABytes;
   uint8_t* sEpi = sB + S * Cfg::kBBytes;  // 1024-aligned: stage sizes are multiples of 8 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -707,7 +719,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const bool vec = p.vec_ok != 0;
     const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
-    uint8_t* wstage = sEpi + (warp - 2) * kWarpStageBytes;
+    uint8_t* wstage = sEpi + (warp - 2) * EpiStage<OutT, ACT>::kWarpBytes;
     int stage_pp = 0;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     int local = 0;
@@ -751,7 +763,7 @@ static bool is_mn_major_2d(const at::Tensor& t) {
 template <int BN, typename OutT, int ACT>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps,
                         int grid, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, OutT, ACT>;
   auto kern = gemm_tcgen05_kernel<BN, OutT, ACT>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -776,7 +788,7 @@ static void dispatch_act(int act, const CUtensorMap& ta, const CUtensorMap& tb, 
 template <int BN, typename OutT, int ACT>
 static void launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, const EpiMaps& maps,
                          int grid, cudaStream_t stream) {
-  using Cfg = Gemm2Cfg<BN>;
+  using Cfg = Gemm2Cfg<BN, OutT, ACT>;
   auto kern = gemm_2sm_kernel<BN, OutT, ACT>;
   static bool attr_set = false;
   if (!attr_set) {

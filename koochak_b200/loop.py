@@ -567,6 +567,9 @@ class _TrainLoop:
                 s.ddp_bucket_cap_mb_list[-1] if s.ddp_bucket_cap_mb_list else 25)
             self.model = DataParallel(self.model, bucket_cap_mb=float(cap), broadcast_buffers=s.ddp_broadcast_buffers,
                                       transport=s.comm_transport, find_unused_parameters=s.find_unused_parameters)
+            if isinstance(self.scaler, FusedGradScaler) and self.model.transport == "fused":
+                scaler = self.scaler
+                self.model.grad_scale_fn = lambda: scaler._scale
         else:
             from torch.nn.parallel import DistributedDataParallel
 
@@ -877,7 +880,14 @@ class _TrainLoop:
 
         t0 = self._profile_start()
         gate_stats = None
-        if isinstance(self.scaler, FusedGradScaler) and grads is not None:
+        dp = self.model if getattr(self.model, "fused_gate_available", None) is not None else None
+        if dp is not None and grads is not None and dp.fused_gate_available():
+            # The fused all-reduce already averaged, unscaled and measured the
+            # gradients: the gate is one small kernel and one host read.
+            gate_stats = dp.fused_gate(s.grad_clip_norm)
+            if isinstance(self.scaler, FusedGradScaler):
+                self.scaler.mark_unscaled(self.optimizer, gate_stats)
+        elif isinstance(self.scaler, FusedGradScaler) and grads is not None:
             self.scaler.unscale_(self.optimizer, max_norm=s.grad_clip_norm)
             gate_stats = self.scaler.last_stats
         elif isinstance(self.scaler, GradScaler):
@@ -906,6 +916,14 @@ class _TrainLoop:
                                  grad_clip_scaled_norm=int(clipping.used_scaled_norm))
         self._profile_add(stats.profile_timing_totals, "profile_loop_grad_clip_time_s", t0)
 
+    @staticmethod
+    def _raise_if_comm_failed(gate_stats: torch.Tensor) -> None:
+        if float(gate_stats[3]) != 0.0:
+            from .ops._ext import check_status
+
+            check_status(int(gate_stats.device.index or 0))
+            raise RuntimeError(f"gradient all-reduce reported device status {int(float(gate_stats[3]))}")
+
     def _apply_coef(self, coef: torch.Tensor, grads: list, fused_opt: bool) -> None:
         if fused_opt:
             self.optimizer.kb_grad_scale = coef
@@ -913,7 +931,10 @@ class _TrainLoop:
             torch._foreach_mul_(grads, coef)
 
     def _clip_from_stats(self, out: torch.Tensor, grads: list, fused_opt: bool) -> GradientClipStats:
-        norm, coef, bad = (float(v) for v in out.tolist())
+        vals = out.tolist()
+        norm, coef, bad = (float(v) for v in vals[:3])
+        if len(vals) > 3 and vals[3] != 0.0:
+            self._raise_if_comm_failed(out)
         if bad or not math.isfinite(norm) or 0.0 < coef < torch.finfo(torch.float32).tiny:
             # fp16 overflow or huge values: the reference path decides (and raises on inf/nan).
             return clip_grad_norm_(self.model.parameters(), float(self.settings.grad_clip_norm))

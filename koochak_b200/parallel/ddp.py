@@ -19,11 +19,17 @@ own bucketing:
 Reduction transports (``transport``):
 
 * ``"nccl"`` / ``"gloo"``: one averaging all-reduce per bucket (baseline);
-* ``"p2p"``: the native single-node path: every rank exposes its bucket in
-  CUDA IPC-shared memory, one kernel per bucket reduces this rank's shard by
-  reading all peers over NVLink (no NCCL in the data path) and another
-  gathers the reduced shards back, with bounded cross-GPU flag waits
-  (see ``parallel/symm.py``).
+* ``"fused"`` (alias ``"p2p"``): the native single-node path. Buckets live in
+  symmetric device memory; one kernel per bucket reduces this rank's shard
+  over NVLink (P2P loads or NVSwitch ``multimem``; no NCCL in the data
+  path), fused with the GradScaler unscale, the finite flag and per-tensor
+  sums of squares, and writes the result back to every rank, with bounded
+  cross-GPU flag waits (``koochak_b200/parallel/symm.py``). The gradient gate
+  then reads those statistics instead of passing over the gradients again
+  (``DataParallel.fused_gate``).
+
+Buckets are launched in index order on every rank, whatever order backward
+finishes them in, so every rank issues the same reductions in the same order.
 """
 
 from __future__ import annotations
@@ -39,19 +45,22 @@ __all__ = ["DataParallel", "Bucket"]
 
 
 class Bucket:
-    def __init__(self, index: int, params: List[nn.Parameter], device: torch.device) -> None:
+    def __init__(self, index: int, params: List[nn.Parameter], device: torch.device, align: int = 1,
+                 allocate: bool = True) -> None:
         self.index = index
         self.params = params
         self.offsets: List[int] = []
         total = 0
         for p in params:
             self.offsets.append(total)
-            total += p.numel()
+            total += (p.numel() + align - 1) // align * align
         self.numel = total
-        self.buffer = torch.zeros(total, device=device, dtype=torch.float32)
+        # The fused transport replaces this with a view of symmetric memory.
+        self.buffer = torch.zeros(total if allocate else 0, device=device, dtype=torch.float32)
         self.pending = 0
         self.work = None
         self.ready_event: Optional[torch.cuda.Event] = None
+        self.complete = False
 
     def view_of(self, i: int) -> torch.Tensor:
         p = self.params[i]
@@ -60,7 +69,8 @@ class Bucket:
 
 class DataParallel(nn.Module):
     def __init__(self, module: nn.Module, *, bucket_cap_mb: float = 25.0, broadcast_buffers: bool = True,
-                 transport: str = "auto", process_group=None, find_unused_parameters: bool = False) -> None:
+                 transport: str = "auto", process_group=None, find_unused_parameters: bool = False,
+                 comm_blocks: int = 32) -> None:
         super().__init__()
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("DataParallel needs an initialised process group")
@@ -77,6 +87,8 @@ class DataParallel(nn.Module):
         self.transport = self._pick_transport(transport, backend)
         self._sync_module_states()
         cap = max(1, int(bucket_cap_mb * 1024 * 1024 / 4))
+        align, own = (4, False) if self.transport == "fused" else (1, True)
+        self.params = params
         self.buckets: List[Bucket] = []
         current: List[nn.Parameter] = []
         size = 0
@@ -84,20 +96,31 @@ class DataParallel(nn.Module):
             current.append(p)
             size += p.numel()
             if size >= cap:
-                self.buckets.append(Bucket(len(self.buckets), current, self.device))
+                self.buckets.append(Bucket(len(self.buckets), current, self.device, align, own))
                 current, size = [], 0
         if current:
-            self.buckets.append(Bucket(len(self.buckets), current, self.device))
+            self.buckets.append(Bucket(len(self.buckets), current, self.device, align, own))
         self._where: Dict[int, tuple] = {}
         for b in self.buckets:
             for i, p in enumerate(b.params):
                 self._where[id(p)] = (b, i)
         self._comm_stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
-        self._p2p = None
-        if self.transport == "p2p":
-            from .symm import P2PReducer
+        self._fused = None
+        # GradScaler scale (a device scalar, or a callable returning it), applied
+        # as 1/scale by the fused path so the reduced gradients come out unscaled.
+        self.grad_scale: Optional[torch.Tensor] = None
+        self.grad_scale_fn: Optional[Callable[[], Optional[torch.Tensor]]] = None
+        self._fused_ready = False
+        if self.transport == "fused":
+            from .symm import FusedGradReducer
 
-            self._p2p = P2PReducer([b.numel for b in self.buckets], self.device, process_group)
+            tid = {id(p): i for i, p in enumerate(params)}
+            segments = [[(p.numel(), tid[id(p)]) for p in b.params] for b in self.buckets]
+            self._fused = FusedGradReducer(segments, len(params), self.device, process_group, blocks=comm_blocks)
+            for b, buf in zip(self.buckets, self._fused.buffers):
+                assert buf.numel() == b.numel
+                b.buffer = buf
+        self._next_launch = 0
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in params]
         self._armed = False
         self._callback_queued = False
@@ -109,7 +132,9 @@ class DataParallel(nn.Module):
             return "gloo"
         if t == "auto":
             return "nccl"
-        if t not in ("nccl", "p2p"):
+        if t == "p2p":
+            t = "fused"
+        if t not in ("nccl", "fused"):
             raise ValueError(f"unknown gradient-sync transport {transport!r}")
         return t
 
@@ -140,10 +165,15 @@ class DataParallel(nn.Module):
     def _arm(self) -> None:
         self._armed = True
         self._callback_queued = False
+        self._fused_ready = False
+        self._next_launch = 0
         for b in self.buckets:
             b.pending = len(b.params)
             b.work = None
             b.ready_event = None
+            b.complete = False
+        if self._fused is not None:
+            self._fused.begin_step()
 
     # ------------------------------------------------------------------ backward
     def _on_grad(self, p: nn.Parameter) -> None:
@@ -157,7 +187,14 @@ class DataParallel(nn.Module):
             b.view_of(i).copy_(p.grad)
         b.pending -= 1
         if b.pending == 0:
-            self._launch(b)
+            b.complete = True
+            self._launch_ready()
+
+    def _launch_ready(self) -> None:
+        # Strict index order: the reductions pair up across ranks by sequence.
+        while self._next_launch < len(self.buckets) and self.buckets[self._next_launch].complete:
+            self._launch(self.buckets[self._next_launch])
+            self._next_launch += 1
 
     def _launch(self, b: Bucket) -> None:
         if self._comm_stream is None:
@@ -174,9 +211,10 @@ class DataParallel(nn.Module):
             b.ready_event = done
 
     def _reduce_now(self, b: Bucket) -> None:
-        if self.transport == "p2p":
-            assert self._p2p is not None
-            self._p2p.all_reduce_mean(b.index, b.buffer)
+        if self.transport == "fused":
+            assert self._fused is not None
+            scale = self.grad_scale_fn() if self.grad_scale_fn is not None else self.grad_scale
+            self._fused.reduce(b.index, scale)
         elif self.transport == "nccl":
             dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
         else:
@@ -191,17 +229,33 @@ class DataParallel(nn.Module):
                 for i, p in enumerate(b.params):
                     if p.grad is None:
                         b.view_of(i).zero_()
-                    b.pending = 0
-                self._launch(b)
+                b.pending = 0
+                b.complete = True
+        self._launch_ready()
         cur = torch.cuda.current_stream(self.device) if self._comm_stream is not None else None
         for b in self.buckets:
             if cur is not None and b.ready_event is not None:
                 cur.wait_event(b.ready_event)
             for i, p in enumerate(b.params):
                 p.grad = b.view_of(i)
-        if self._p2p is not None:
-            self._p2p.check()
+        self._fused_ready = self._fused is not None
         self._armed = False
+
+    # ------------------------------------------------------------------ gate
+    def fused_gate_available(self) -> bool:
+        """True when the last backward was reduced by the fused path (statistics are ready)."""
+
+        return self._fused_ready
+
+    def fused_gate(self, max_norm: Optional[float]) -> torch.Tensor:
+        """Device fp32 [4] from the fused statistics: norm, clip coefficient, found_inf, status word.
+
+        The gradients are already averaged and (when ``grad_scale`` was set)
+        unscaled; the norm is that of the averaged gradients.
+        """
+
+        assert self._fused is not None and self._fused_ready
+        return self._fused.gate(max_norm)
 
     def state_dict(self, *args, **kwargs):
         return {f"module.{k}": v for k, v in self.module.state_dict(*args, **kwargs).items()}

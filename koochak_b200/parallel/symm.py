@@ -1,0 +1,186 @@
+"""Symmetric device memory and the fused gradient all-reduce built on it.
+
+(replaces the NCCL bucket all-reduce of torch DDP used at reference
+koochak/loop.py:705-723, and the unscale / finite check / norm pass of
+koochak/loop.py:1612-1637 and koochak/optim/grad_clip.py:47-73)
+
+``SymmetricWorkspace`` allocates one buffer per rank through PyTorch's
+symmetric-memory allocator (same size and layout on every GPU of the node,
+each rank's buffer mapped into every peer) and, where the NVSwitch supports
+it, a multicast mapping of the same buffer. Only the addresses come from
+PyTorch: the kernels that read and write peers are this package's own
+(``koochak_b200/csrc/comm.cu``).
+
+``FusedGradReducer`` lays the data-parallel buckets out inside such a
+workspace. For bucket ``b`` it launches one kernel that
+
+* waits (bounded) until every rank has written bucket ``b``,
+* reduces this rank's 1/W shard of it over NVLink (P2P loads from every peer,
+  or ``multimem.ld_reduce`` through the switch), multiplies by
+  ``inv_scale / W``, checks finiteness and accumulates per-tensor sums of
+  squares, and writes the result back to every rank (P2P or ``multimem.st``),
+* waits until every rank's writes have landed.
+
+After the last bucket every GPU holds the averaged, unscaled gradients and the
+complete per-tensor statistics, so the gradient gate is a one-thread kernel.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["SymmetricWorkspace", "FusedGradReducer", "plan_chunks", "shard_bounds"]
+
+_FLAG_BYTES = 128 * 8 * 4  # [max blocks][max ranks] u32 barrier slots
+_ALIGN = 256
+
+
+def _align(n: int, a: int = _ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+def shard_bounds(numel: int, world: int, rank: int, align: int = 4) -> Tuple[int, int]:
+    """[lo, hi) of ``rank``'s shard of ``numel`` elements; boundaries are multiples of ``align``."""
+
+    per = (numel + world - 1) // world
+    per = (per + align - 1) // align * align
+    lo = min(numel, rank * per)
+    hi = min(numel, lo + per)
+    return lo, hi
+
+
+def plan_chunks(segments: Sequence[Tuple[int, int, int]], lo: int, hi: int, max_chunk: int = 32768) -> List[Tuple[int, int, int]]:
+    """Split ``[lo, hi)`` of a bucket into (start, length, tensor id) pieces.
+
+    ``segments`` are (offset, numel, tensor id) of the tensors in the bucket
+    (offsets multiples of 4). Pieces never cross a tensor, start on a multiple
+    of 4 elements and hold at most ``max_chunk`` elements.
+    """
+
+    out: List[Tuple[int, int, int]] = []
+    for off, n, tid in segments:
+        a, b = max(lo, off), min(hi, off + n)
+        while a < b:
+            step = min(max_chunk, b - a)
+            if a + step < b:
+                step = max(4, step // 4 * 4)
+            out.append((a, step, tid))
+            a += step
+    return out
+
+
+class SymmetricWorkspace:
+    """One symmetric buffer per rank (and its multicast mapping when available)."""
+
+    def __init__(self, nbytes: int, device: torch.device, group=None, *, use_multicast: Optional[bool] = None) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.device = device
+        self.nbytes = _align(nbytes)
+        self.tensor = symm_mem.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.handle = symm_mem.rendezvous(self.tensor, self.group)
+        own = int(self.handle.buffer_ptrs[self.rank])
+        offset = self.tensor.data_ptr() - own
+        self.bases = [int(p) + offset for p in self.handle.buffer_ptrs]
+        mc = 0
+        if use_multicast is None:
+            use_multicast = os.environ.get("KOOCHAK_B200_MULTIMEM", "1") != "0"
+        if use_multicast and self.world > 1:
+            try:
+                if symm_mem._SymmetricMemory.has_multicast_support(symm_mem.DeviceType.CUDA, device.index or 0):
+                    mc = int(self.handle.multicast_ptr)
+            except Exception:  # no NVSwitch multicast here: plain peer loads and stores
+                mc = 0
+        self.mc_base = mc + offset if mc else 0
+
+    def view(self, offset: int, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        size = numel * torch.empty((), dtype=dtype).element_size()
+        return self.tensor.narrow(0, offset, size).view(dtype)
+
+
+class FusedGradReducer:
+    """Bucketed, fused gradient all-reduce over a symmetric workspace."""
+
+    def __init__(self, bucket_segments: Sequence[Sequence[Tuple[int, int]]], n_tensors: int, device: torch.device,
+                 group=None, *, blocks: int = 32, timeout_s: Optional[float] = None,
+                 use_multicast: Optional[bool] = None) -> None:
+        """``bucket_segments[b]`` lists (numel, tensor id) of bucket ``b``'s tensors, in layout order."""
+
+        from ..ops._ext import native
+
+        self._C = native()
+        self.n_tensors = int(n_tensors)
+        self.blocks = int(blocks)
+        self.timeout_s = float(timeout_s if timeout_s is not None else os.environ.get("KOOCHAK_B200_COMM_TIMEOUT_S", 300))
+        stats_bytes = _align(4 * (self.n_tensors + 1))
+        self.flags_off = 0
+        self.stats_off = [_FLAG_BYTES, _FLAG_BYTES + stats_bytes]
+        off = _align(_FLAG_BYTES + 2 * stats_bytes)
+        self.bucket_off: List[int] = []
+        self.bucket_numel: List[int] = []
+        self.layouts: List[List[Tuple[int, int, int]]] = []  # (offset, numel, tensor id)
+        for segs in bucket_segments:
+            layout, cur = [], 0
+            for numel, tid in segs:
+                layout.append((cur, int(numel), int(tid)))
+                cur += (int(numel) + 3) // 4 * 4
+            self.layouts.append(layout)
+            self.bucket_off.append(off)
+            self.bucket_numel.append(cur)
+            off = _align(off + 4 * cur)
+        self.ws = SymmetricWorkspace(off, device, group, use_multicast=use_multicast)
+        self.world, self.rank = self.ws.world, self.ws.rank
+        self.buffers = [self.ws.view(o, n, torch.float32) for o, n in zip(self.bucket_off, self.bucket_numel)]
+        self.chunks: List[torch.Tensor] = []
+        for layout, n in zip(self.layouts, self.bucket_numel):
+            lo, hi = shard_bounds(n, self.world, self.rank)
+            rows = plan_chunks(layout, lo, hi) or [(0, 0, 0)]
+            self.chunks.append(torch.tensor(rows, dtype=torch.int64, device=device))
+        self.stats = [self.ws.view(o, self.n_tensors + 1, torch.float32) for o in self.stats_off]
+        self.parity = 0
+        self.epoch = 1
+        with torch.no_grad():
+            self.ws.tensor.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.ws.group)
+        self.barrier()  # every rank's flags are zero and mapped
+
+    # ---------------------------------------------------------------- per step
+    def begin_step(self) -> None:
+        """Select and clear this step's statistics copy (call on the compute stream before backward)."""
+
+        self.parity ^= 1
+        self.stats[self.parity].zero_()
+
+    def current_stats(self) -> torch.Tensor:
+        return self.stats[self.parity]
+
+    def _next_epoch(self) -> int:
+        e = self.epoch
+        self.epoch = (self.epoch + 2) & 0xFFFFFFFF
+        return e
+
+    def reduce(self, b: int, scale: Optional[torch.Tensor] = None) -> None:
+        """All-reduce bucket ``b`` (average, unscale, statistics) on the current stream."""
+
+        self._C.comm_allreduce_bucket(self.ws.bases, self.ws.mc_base, self.flags_off, self.stats_off[self.parity],
+                                      self.bucket_off[b], self.chunks[b], self.n_tensors, self.rank,
+                                      self._next_epoch(), scale, self.blocks, self.timeout_s)
+
+    def barrier(self) -> None:
+        self._C.comm_barrier(self.ws.bases, self.flags_off, self.rank, self._next_epoch(), self.blocks,
+                             self.timeout_s, self.ws.device.index or 0)
+
+    def gate(self, max_norm: Optional[float]) -> torch.Tensor:
+        """Device fp32 [4]: global norm, clip coefficient, found_inf, status word."""
+
+        out = torch.empty(4, device=self.ws.device, dtype=torch.float32)
+        self._C.gate_from_stats(self.current_stats(), self.n_tensors, float(max_norm or 0.0), max_norm is not None, out)
+        return out
