@@ -146,13 +146,18 @@ def load_file_list(path) -> List[str]:
 
 
 def scan_source(root: str, *, exclude: Sequence[str] = (), include: Optional[Sequence[str]] = None,
-                groups: Optional[Mapping[str, Tuple[str, int]]] = None) -> List[SourceFile]:
+                groups: Optional[Mapping[str, Tuple[str, int]]] = None, files: Optional[Sequence[str]] = None,
+                skip_symlinks: bool = False, min_age_seconds: float = 0.0) -> List[SourceFile]:
+    """Regular files under ``root``: ``exclude`` globs prune, ``include`` globs keep, ``files`` lists exactly."""
+
     root = os.path.abspath(root)
-    wanted = set(include) if include is not None else None
+    wanted = set(files) if files is not None else None
+    globs = list(include or [])
+    newest = time.time() - float(min_age_seconds)
     out: List[SourceFile] = []
-    for d, dirs, files in os.walk(root, followlinks=False):
+    for d, dirs, names in os.walk(root, followlinks=False):
         dirs.sort()
-        for name in sorted(dirs + files):
+        for name in sorted(dirs + names):
             full = os.path.join(d, name)
             rel = os.path.relpath(full, root).replace(os.sep, "/")
             if any(fnmatchcase(rel, g) for g in exclude):
@@ -163,8 +168,14 @@ def scan_source(root: str, *, exclude: Sequence[str] = (), include: Optional[Seq
             if stat.S_ISDIR(st.st_mode):
                 continue
             if not stat.S_ISREG(st.st_mode):
+                if skip_symlinks and stat.S_ISLNK(st.st_mode):
+                    continue
                 raise ValueError(f"refusing non-regular file (symlink or special): {rel}; exclude it with a glob")
             if wanted is not None and rel not in wanted:
+                continue
+            if globs and not any(fnmatchcase(rel, g) for g in globs):
+                continue
+            if min_age_seconds and st.st_mtime > newest:
                 continue
             grp, order = (groups or {}).get(rel, (os.path.dirname(rel) or ".", _LAST))
             out.append(SourceFile(validate_key(rel, "path"), st.st_size, stat.S_IMODE(st.st_mode), st.st_mtime_ns,
@@ -262,15 +273,26 @@ def _write_pack(root: str, store: Store, pack: PlannedPack) -> Tuple[PackEntry, 
 
 def archive(root: str, store: Store, *, exclude: Sequence[str] = (), groups=None,
             include: Optional[Sequence[str]] = None, pack_bytes: int = DEFAULT_PACK_BYTES,
-            object_bytes: int = DEFAULT_OBJECT_BYTES, metadata: Optional[Mapping] = None, streams: Optional[int] = None,
-            delete_sources: bool = False) -> ArchiveReport:
+            object_bytes: Optional[int] = DEFAULT_OBJECT_BYTES, metadata: Optional[Mapping] = None,
+            streams: Optional[int] = None, delete_sources: bool = False, layout: str = "packed",
+            files: Optional[Sequence[str]] = None, skip_symlinks: bool = False, min_age_seconds: float = 0.0,
+            dry_run: bool = False):
+    """Archive ``root`` into ``store``; with ``dry_run`` return the ``ArchivePlan`` and write nothing."""
+
     t0 = time.perf_counter()
     root = os.path.abspath(root)
+    if layout not in ("packed", "objects"):
+        raise ValueError("layout must be 'packed' or 'objects'")
     table = load_groups(groups) if isinstance(groups, (str, os.PathLike)) else groups
-    files = scan_source(root, exclude=exclude, include=include, groups=table)
-    if not files:
+    found = scan_source(root, exclude=exclude, include=include, groups=table, files=files,
+                        skip_symlinks=skip_symlinks, min_age_seconds=min_age_seconds)
+    if not found:
         raise ValueError(f"nothing to archive under {root}")
-    plan = plan_archive(files, pack_bytes=pack_bytes, object_bytes=object_bytes)
+    if object_bytes is None:
+        object_bytes = max(1, min(DEFAULT_OBJECT_BYTES, pack_bytes))
+    plan = plan_archive(found, pack_bytes=pack_bytes, object_bytes=0 if layout == "objects" else object_bytes)
+    if dry_run:
+        return plan
     workers = streams or profile_of(store).streams
     packs: List[Optional[PackEntry]] = [None] * len(plan.packs)
     entries: List[FileEntry] = []

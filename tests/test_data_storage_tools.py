@@ -85,3 +85,43 @@ def test_copy_objects_resumes_and_checks(tmp_path):
     with pytest.raises(ValueError):
         copy_objects(a, b, bad)
     assert b.stat("d/k0") is None
+
+
+def test_packed_groups_stream_and_data_cli(tmp_path, capsys):
+    from koochak_b200.data.__main__ import main as data_main
+    from koochak_b200.data.packed import GroupStream, PackCache, PackedGroups
+
+    src = tmp_path / "src"
+    rows = ["path,group,order"]
+    for g in range(6):
+        for k in range(3):
+            p = src / f"rec{g}" / f"f{k}.bin"
+            p.parent.mkdir(parents=True, exist_ok=True)
+            p.write_bytes(bytes([g, k]) * 100)
+            rows.append(f"rec{g}/f{k}.bin,g{g},{g}")
+    (tmp_path / "groups.csv").write_text("\n".join(rows) + "\n")
+    coll = tmp_path / "coll"
+    assert data_main(["archive", str(src), str(coll), "--groups", str(tmp_path / "groups.csv"),
+                      "--pack-bytes", "4096"]) == 0
+    assert data_main(["verify", str(coll), "--deep"]) == 0
+    capsys.readouterr()
+    assert data_main(["ls", str(coll), "--include", "rec1/*"]) == 0
+    assert capsys.readouterr().out.split() == ["rec1/f0.bin", "rec1/f1.bin", "rec1/f2.bin"]
+    store = LocalStore(str(coll))
+    pg = PackedGroups.load(store)
+    assert set(pg.groups) == {f"g{g}" for g in range(6)}
+    plan = pg.plan(num_owners=2, seed=1)
+    seen = set()
+    for owner in range(2):
+        stream = GroupStream(store, pg, plan[owner], seed=1, window=2, prefetch=1, cache=PackCache(1 << 20))
+        it = iter(stream)
+        first_pass = [next(it) for _ in range(stream.groups_per_pass)]
+        names = {g.name for g in first_pass}
+        assert len(names) == stream.groups_per_pass and not (names & seen)
+        seen |= names
+        g0 = first_pass[0]
+        assert sorted(g0.files) == sorted(e.path for e in pg.groups[g0.name].files)
+        resumed = next(iter(GroupStream(store, pg, plan[owner], seed=1, window=2, prefetch=1, start=1)))
+        assert resumed.name == first_pass[1].name
+    assert seen == set(pg.groups)
+    assert pg.load_group(store, "g2").files["rec2/f1.bin"] == bytes([2, 1]) * 100
