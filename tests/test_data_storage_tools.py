@@ -125,3 +125,16 @@ def test_packed_groups_stream_and_data_cli(tmp_path, capsys):
         assert resumed.name == first_pass[1].name
     assert seen == set(pg.groups)
     assert pg.load_group(store, "g2").files["rec2/f1.bin"] == bytes([2, 1]) * 100
+
+
+def test_storage_probe_local(tmp_path):
+    from koochak_b200.storage.probe import probe
+
+    rep = probe(str(tmp_path / "p"), small_count=4, large_bytes=1 << 16, streams=(1, 2), dataset_shards=2,
+                shard_bytes=1 << 16, record_bytes=4096, readers=(1, 2), checkpoint_bytes=1 << 16,
+                checkpoint_parts=(1, 2))
+    assert rep["posix"]["exclusive_create"]["ok"] and rep["recommended_local_store"]["publish"] in ("link",
+                                                                                                   "exclusive")
+    assert rep["recommended_profile"]["streams"] in (1, 2)
+    assert all(v["verified"] for v in rep["checkpoint"].values())
+    assert os.listdir(tmp_path / "p") == []  # probe objects removed
