@@ -76,3 +76,76 @@ class PlainGPT2(nn.Module):
         if targets is None:
             return logits
         return F.cross_entropy(logits.float().view(-1, logits.size(-1)), targets.reshape(-1))
+
+
+class _LlamaLayer(nn.Module):
+    def __init__(self, d: int, h: int, ffn: int, eps: float) -> None:
+        super().__init__()
+        self.h = h
+        self.input_layernorm = nn.RMSNorm(d, eps=eps)
+        self.q_proj = nn.Linear(d, d, bias=False)
+        self.k_proj = nn.Linear(d, d, bias=False)
+        self.v_proj = nn.Linear(d, d, bias=False)
+        self.o_proj = nn.Linear(d, d, bias=False)
+        self.post_attention_layernorm = nn.RMSNorm(d, eps=eps)
+        self.gate_proj = nn.Linear(d, ffn, bias=False)
+        self.up_proj = nn.Linear(d, ffn, bias=False)
+        self.down_proj = nn.Linear(ffn, d, bias=False)
+
+    @staticmethod
+    def _rope(x, cos, sin):
+        half = x.shape[-1] // 2
+        x1, x2 = x[..., :half], x[..., half:]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+    def forward(self, x, cos, sin):
+        B, S, C = x.shape
+        D = C // self.h
+        h = self.input_layernorm(x)
+        q = self._rope(self.q_proj(h).view(B, S, self.h, D).transpose(1, 2), cos, sin)
+        k = self._rope(self.k_proj(h).view(B, S, self.h, D).transpose(1, 2), cos, sin)
+        v = self.v_proj(h).view(B, S, self.h, D).transpose(1, 2)
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        x = x + self.o_proj(y.transpose(1, 2).reshape(B, S, C))
+        h = self.post_attention_layernorm(x)
+        return x + self.down_proj(F.silu(self.gate_proj(h)) * self.up_proj(h))
+
+    def matrices(self):
+        return [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.o_proj.weight,
+                self.gate_proj.weight, self.up_proj.weight, self.down_proj.weight]
+
+
+class PlainLlama(nn.Module):
+    """Llama-style 1.3B by default: 24 layers, d=2048, 16 heads, RMSNorm, RoPE, SwiGLU 5504, vocab 32000."""
+
+    def __init__(self, n_layer: int = 24, n_head: int = 16, dim: int = 2048, ffn: int = 5504, vocab_size: int = 32000,
+                 eps: float = 1e-5, theta: float = 10000.0) -> None:
+        super().__init__()
+        self.n_head, self.dim, self.theta = n_head, dim, theta
+        self.embed_tokens = nn.Embedding(vocab_size, dim)
+        self.layers = nn.ModuleList([_LlamaLayer(dim, n_head, ffn, eps) for _ in range(n_layer)])
+        self.norm = nn.RMSNorm(dim, eps=eps)
+        self.lm_head = nn.Linear(dim, vocab_size, bias=False)
+        for name, m in self.named_modules():
+            if isinstance(m, nn.Linear):
+                std = 0.02 / math.sqrt(2 * n_layer) if name.endswith(("o_proj", "down_proj")) else 0.02
+                nn.init.normal_(m.weight, std=std)
+            elif isinstance(m, nn.Embedding):
+                nn.init.normal_(m.weight, std=0.02)
+
+    def blocks_matrices(self):
+        return [w for layer in self.layers for w in layer.matrices()]
+
+    def forward(self, idx, targets=None):
+        B, S = idx.shape
+        D = self.dim // self.n_head
+        inv = 1.0 / (self.theta ** (torch.arange(0, D, 2, device=idx.device, dtype=torch.float32) / D))
+        ang = torch.arange(S, device=idx.device, dtype=torch.float32)[:, None] * inv[None]
+        cos, sin = ang.cos(), ang.sin()
+        x = self.embed_tokens(idx)
+        for layer in self.layers:
+            x = layer(x, cos, sin)
+        logits = self.lm_head(self.norm(x))
+        if targets is None:
+            return logits
+        return F.cross_entropy(logits.float().view(-1, logits.size(-1)), targets.reshape(-1))

@@ -49,12 +49,22 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["koochak_b200", "reference"], default="koochak_b200")
-    ap.add_argument("--micro-batch", type=int, default=16)
-    ap.add_argument("--seq", type=int, default=1024)
-    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--model", choices=["gpt2", "llama"], default="gpt2",
+                    help="gpt2: GPT-2 124M (the headline workload); llama: Llama-style 1.3B, micro-batch 4 x 2048, "
+                         "grad_accum 4")
+    ap.add_argument("--micro-batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--grad-accum", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--comm", default="fused", help="gradient-sync transport: fused (in-kernel NVLink) | nccl")
-    return ap.parse_args()
+    args = ap.parse_args()
+    defaults = {"gpt2": dict(micro_batch=16, seq=1024, layers=12, grad_accum=1, vocab=50257),
+                "llama": dict(micro_batch=4, seq=2048, layers=24, grad_accum=4, vocab=32000)}[args.model]
+    for k, v in defaults.items():
+        if getattr(args, k, None) is None:
+            setattr(args, k, v)
+    return args
 
 
 # --------------------------------------------------------------------------- clocks
@@ -127,7 +137,12 @@ def build_koochak_workload(args, device):
     from koochak_b200.optim import build_optimizer
 
     torch.manual_seed(1234)
-    model = GPT2(n_layer=args.layers).to(device)
+    if args.model == "llama":
+        from koochak_b200.models import Llama
+
+        model = Llama(n_layer=args.layers, max_seq_len=args.seq).to(device)
+    else:
+        model = GPT2(n_layer=args.layers).to(device)
     opt = build_optimizer(model, {"name": "muon", "lr": 6e-4, "muon_lr": 0.02, "adam_lr": 6e-4,
                                   "weight_decay": 0.0})
     return model, opt
@@ -168,10 +183,10 @@ class CyclingDataset:
 
 def train_cfg_for(args, world: int, steps: int, out_dir: str, scalarize: bool) -> Dict[str, Any]:
     return {
-        "max_steps": steps, "log_every": 10 ** 9, "eval_every": 0, "ckpt_every": 10 ** 9, "grad_accum": 1,
+        "max_steps": steps, "log_every": 10 ** 9, "eval_every": 0, "ckpt_every": 10 ** 9,
         "grad_clip_norm": 1.0, "amp": "bf16", "ddp": world > 1, "out_dir": out_dir, "keep_last_k": 1,
         "scalarize_loss_every_step": scalarize, "ema": {"enabled": True, "decay": 0.999, "offload_to_cpu": False},
-        "comm_transport": args.comm, "warn_unsharded": False,
+        "comm_transport": args.comm, "warn_unsharded": False, "grad_accum": args.grad_accum,
     }
 
 
@@ -266,8 +281,7 @@ def run_phase(impl: str, args, world: int, rank: int, device, *, e2e: bool, samp
     else:
         training_loop, model, opt = build_reference_workload(args, device)
         counter = None
-    vocab = 50257
-    pool = synthetic_batches(4, args.micro_batch, args.seq, vocab, device, pinned=e2e, seed=100 + rank)
+    pool = synthetic_batches(4, args.micro_batch, args.seq, args.vocab, device, pinned=e2e, seed=100 + rank)
     timer = StepTimer(args.warmup, args.steps, world, sampler, wall=e2e, native_counter=counter)
     with tempfile.TemporaryDirectory(prefix="kb_bench_") as out_dir:
         cfg = train_cfg_for(args, world, total, out_dir, scalarize=e2e)
@@ -300,13 +314,17 @@ def build_reference_workload(args, device):
     from koochak.utils.nn_utils import tag_param  # type: ignore
 
     sys.path.insert(0, os.path.join(HERE, "baseline"))
-    from reference_workloads import PlainGPT2  # type: ignore
+    from reference_workloads import PlainGPT2, PlainLlama  # type: ignore
 
     torch.manual_seed(1234)
-    model = PlainGPT2(n_layer=args.layers).to(device)
-    for blk in model.blocks:
-        for w in blk.matrices():
-            tag_param(w, "wd")
+    if args.model == "llama":
+        model = PlainLlama(n_layer=args.layers).to(device)
+        mats = model.blocks_matrices()
+    else:
+        model = PlainGPT2(n_layer=args.layers).to(device)
+        mats = [w for blk in model.blocks for w in blk.matrices()]
+    for w in mats:
+        tag_param(w, "wd")
     opt = ref_build.build_optimizer(model, {"name": "muon", "lr": 6e-4, "muon_lr": 0.02, "adam_lr": 6e-4,
                                             "weight_decay": 0.0})
     return training_loop, model, opt
@@ -337,7 +355,7 @@ def main() -> int:
                                              device_id=device)
     sampler = ClockSampler(local) if rank == 0 else None
     res = run_phase(args.impl, args, world, rank, device, e2e=False, sampler=sampler)
-    tokens_per_step = args.micro_batch * args.seq * world
+    tokens_per_step = args.micro_batch * args.seq * args.grad_accum * world
     value = tokens_per_step / (res["ms_per_step"] / 1000.0)
     e2e = None
     if not args.no_e2e:
@@ -353,8 +371,12 @@ def main() -> int:
         "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
         "data": "synthetic uniform-random token ids, random-init weights",
-        "config": {"model": f"GPT-2 124M ({args.layers}L, d768, 12 heads, vocab 50257, tied head)",
-                   "global_batch": args.micro_batch * world, "micro_batch_per_gpu": args.micro_batch,
+        "config": {"model": (f"GPT-2 124M ({args.layers}L, d768, 12 heads, vocab 50257, tied head)"
+                             if args.model == "gpt2" else
+                             f"Llama-style 1.3B ({args.layers}L, d2048, 16 heads, RMSNorm, RoPE, SwiGLU 5504, "
+                             "vocab 32000)"),
+                   "global_batch": args.micro_batch * args.grad_accum * world,
+                   "micro_batch_per_gpu": args.micro_batch, "grad_accum": args.grad_accum,
                    "seq_len": args.seq, "parallelism": f"dp{world}", "optimizer": "Muon(NS5)+AdamW",
                    "ema_decay": 0.999, "grad_clip": 1.0,
                    "l2": "no flush: per-step working set (~6 GB activations) >> 126 MB L2"},

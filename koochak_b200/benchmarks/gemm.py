@@ -69,6 +69,28 @@ def ns_cases(c: int, batch: int = 12, r: int = 768):
     }
 
 
+def wait_profile(fn: Callable[[], object]) -> str:
+    """Fractions of the producer role's time that each role spent waiting, for one launch."""
+
+    from koochak_b200.ops import native
+
+    buf = torch.zeros(4096, dtype=torch.int64, device="cuda")
+    native().gemm_set_profile(buf)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        native().gemm_set_profile(None)
+    c = buf.view(-1, 8).double()
+    active = c[:, 4] > 0
+    c = c[active]
+    total = c[:, 4].sum().clamp_min(1)
+    return ("wait: load-slot {:.0%} mma-operands {:.0%} mma-accum {:.0%} epi-accum/warp {:.0%} "
+            "tiles/cta {:.1f}").format(float(c[:, 0].sum() / total), float(c[:, 1].sum() / total),
+                                      float(c[:, 2].sum() / total), float(c[:, 3].sum() / 8 / total),
+                                      float(c[:, 5].sum() / max(1, int((c[:, 5] > 0).sum()))))
+
+
 def main(argv: List[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--case", default="all", help="linear layer name, 'ns<c>' (e.g. ns768) or 'all'")
@@ -77,8 +99,21 @@ def main(argv: List[str] | None = None) -> None:
     ap.add_argument("--block-n", type=int, default=0, help="0 auto; 128/256 one-SM tiles; -128/-256 two-SM tiles")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS comparison")
+    ap.add_argument("--shape", default=None, help="M,N,K: one extra forward case of that shape (name 'custom')")
+    ap.add_argument("--debug-mode", type=int, default=0,
+                    help="diagnostic GEMM mode for timing studies: 1 skips operand loads, 2 skips the epilogue")
+    ap.add_argument("--profile", action="store_true",
+                    help="also report where each role of the GEMM waited (clock64 counters per CTA)")
     args = ap.parse_args(argv)
     torch.manual_seed(0)
+    if args.shape:
+        m, n, k = (int(v) for v in args.shape.split(","))
+        LINEAR["custom"] = (n, k)
+        args.tokens = m
+    if args.debug_mode:
+        from koochak_b200.ops import native
+
+        native().gemm_set_debug(args.debug_mode)
     names = list(LINEAR) + ["ns768", "ns2304", "ns3072"] if args.case == "all" else [args.case]
     for name in names:
         if name.startswith("ns"):
@@ -92,6 +127,8 @@ def main(argv: List[str] | None = None) -> None:
                 continue
             t = time_ms(ours, args.iters)
             line = f"{name:10s} {op:6s} ours {t * 1e3:8.1f} us {fl / t / 1e9:6.0f} TF/s"
+            if args.profile:
+                line += " | " + wait_profile(ours)
             if not args.no_compare:
                 tr = time_ms(ref, args.iters)
                 line += f" | cublas {tr * 1e3:8.1f} us {fl / tr / 1e9:6.0f} TF/s | ratio {tr / t:.2f}"

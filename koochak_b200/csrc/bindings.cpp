@@ -7,6 +7,8 @@ namespace kb {
 void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
                  const c10::optional<at::Tensor>& d, double alpha, double beta, const c10::optional<at::Tensor>& bias,
                  const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n);
+void gemm_set_profile(const c10::optional<at::Tensor>& buf);
+void gemm_set_debug(int64_t mode);
 void register_norm_ops(pybind11::module& m);
 void register_elementwise_ops(pybind11::module& m);
 void register_attention_ops(pybind11::module& m);
@@ -21,6 +23,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("d") = pybind11::none(), pybind11::arg("alpha") = 1.0, pybind11::arg("beta") = 0.0,
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("aux") = pybind11::none(),
         pybind11::arg("act") = 0, pybind11::arg("block_n") = 0);
+  m.def("gemm_set_profile", &kb::gemm_set_profile,
+        "route GEMM pipeline wait counters (int64, >= 4096 entries) to a buffer; None turns it off");
+  m.def("gemm_set_debug", &kb::gemm_set_debug,
+        "diagnostic GEMM modes for timing studies: bit 0 skips operand loads, bit 1 skips the epilogue (0: off)");
   m.def("read_and_clear_status", &kb::read_and_clear_status, "read and clear the device status word");
   m.def("num_sms", &kb::num_sms, "streaming multiprocessor count of a device");
   m.def("launch_count", []() { return kb::launch_counter().load(); }, "kernels launched by this library so far");

@@ -501,6 +501,63 @@ void rope_apply(at::Tensor& x, const at::Tensor& cosb, const at::Tensor& sinb, i
   KB_LAUNCHED();
 }
 
+// ------------------------------------------------------------ patchify (ViT)
+
+// images fp32 [B, C, H, W] -> patches [B * (H/P) * (W/P), C * P * P] in the
+// 16-bit compute type; column order (c, py, px) matches a Conv2d weight
+// [out, C, P, P] flattened, so the patch embedding is one GEMM. Each thread
+// moves four horizontally adjacent pixels (one 16-byte load).
+template <typename T>
+__global__ void patchify_kernel(const float* __restrict__ img, T* __restrict__ out, int B, int C, int H, int W,
+                                int P) {
+  const int w4 = W >> 2, gh = H / P, gw = W / P;
+  const long long total = (long long)B * C * H * w4;
+  const long long cols = (long long)C * P * P;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long r = i;
+    const int x = (int)(r % w4) * 4;
+    r /= w4;
+    const int y = (int)(r % H);
+    r /= H;
+    const int c = (int)(r % C);
+    const int b = (int)(r / C);
+    const float4 v = *reinterpret_cast<const float4*>(img + (((long long)b * C + c) * H + y) * W + x);
+    const long long row = ((long long)b * gh + y / P) * gw + x / P;
+    T* dst = out + row * cols + ((long long)c * P + y % P) * P + x % P;
+    uint2 packed;
+    if constexpr (std::is_same<T, __half>::value) {
+      packed.x = pack_f16(v.x, v.y);
+      packed.y = pack_f16(v.z, v.w);
+    } else {
+      packed.x = pack_bf16(v.x, v.y);
+      packed.y = pack_bf16(v.z, v.w);
+    }
+    *reinterpret_cast<uint2*>(dst) = packed;
+  }
+}
+
+void patchify(const at::Tensor& img, at::Tensor& out, int64_t patch) {
+  check_cuda_tensor(img, "images");
+  KB_CHECK(img.scalar_type() == at::kFloat && img.is_contiguous() && img.dim() == 4, "images must be fp32 NCHW");
+  const int B = (int)img.size(0), C = (int)img.size(1), H = (int)img.size(2), W = (int)img.size(3);
+  const int P = (int)patch;
+  KB_CHECK(P % 4 == 0 && H % P == 0 && W % P == 0, "patch size must divide the image and be a multiple of 4");
+  KB_CHECK(out.is_contiguous() && out.numel() == img.numel() &&
+               (out.scalar_type() == at::kHalf || out.scalar_type() == at::kBFloat16),
+           "patches must be contiguous fp16/bf16 with the image's element count");
+  const c10::cuda::CUDAGuard guard(img.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
+  const long long total = img.numel() / 4;
+  const int grid = (int)std::min<long long>((total + 255) / 256, (long long)num_sms(img.get_device()) * 16);
+  if (out.scalar_type() == at::kHalf)
+    patchify_kernel<__half><<<grid, 256, 0, stream>>>(img.data_ptr<float>(), (__half*)out.data_ptr(), B, C, H, W, P);
+  else
+    patchify_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(img.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(),
+                                                             B, C, H, W, P);
+  KB_LAUNCHED();
+}
+
 void register_elementwise_ops(pybind11::module& m) {
   m.def("embedding_forward", &embedding_forward);
   m.def("embedding_backward", &embedding_backward);
@@ -511,6 +568,7 @@ void register_elementwise_ops(pybind11::module& m) {
   m.def("swiglu_forward", &swiglu_forward);
   m.def("swiglu_backward", &swiglu_backward);
   m.def("rope_apply", &rope_apply);
+  m.def("patchify", &patchify);
 }
 
 }  // namespace kb

@@ -51,7 +51,30 @@ struct GemmParams {
   int kb_per_split;  // 64-wide K blocks per split (every split non-empty)
   int tma_store;     // epilogue writes C (and aux) through staged TMA stores
   int* status;
+  // Optional pipeline profile (null: off). Per CTA, 8 counters of clock64
+  // cycles: [0] producer waiting for a free stage, [1] MMA waiting for
+  // operands, [2] MMA waiting for a free accumulator, [3] epilogue warps
+  // waiting for a full accumulator (summed over warps), [4] producer role
+  // total, [5] tiles issued by the MMA thread.
+  unsigned long long* prof;
+  // Diagnostic modes (0 in normal use): bit 0 skips the operand loads (MMAs
+  // read whatever the ring holds), bit 1 skips the epilogue's math and
+  // stores. Results are meaningless; only the timing is of interest.
+  int debug;
 };
+
+__device__ __forceinline__ bool prof_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int code, bool on, long long& acc) {
+  if (!on) return mbar_wait(bar, parity, abort_flag, status, code);
+  const long long t0 = clock64();
+  const bool ok = mbar_wait(bar, parity, abort_flag, status, code);
+  acc += clock64() - t0;
+  return ok;
+}
+
+__device__ __forceinline__ void prof_add(const GemmParams& p, int idx, long long v) {
+  if (p.prof) atomicAdd(p.prof + blockIdx.x * 8 + idx, (unsigned long long)v);
+}
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -373,6 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed_parity[S];
       bool armed[S];
       for (int s = 0; s < S; ++s) armed[s] = false;
+      long long w_prod = 0;
+      const long long t_role = clock64();
       bool ok = true;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const int split = t / tiles_per_split;
@@ -386,9 +411,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = split * kb_per_split;
         const int kb1 = min(num_kb_total, kb0 + kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer)) {
+          if (!prof_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer, p.prof != nullptr, w_prod)) {
             ok = false;
             break;
+          }
+          if (p.debug & 1) {
+            mbar_arrive(&full[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           armed[stage] = true;
@@ -421,6 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(&full[s], armed_parity[s], &never, p.status, kStatusTimeoutDrain)) break;
         }
       }
+      prof_add(p, 0, w_prod);
+      prof_add(p, 4, clock64() - t_role);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -438,10 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int local = 0;
       bool ok = true;
       bool issued_any = false;
+      long long w_ops = 0, w_acc = 0;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma)) {
+        if (!prof_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_acc)) {
           ok = false;
           break;
         }
@@ -450,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int split = t / tiles_per_split;
         const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma)) {
+          if (!prof_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_ops)) {
             ok = false;
             break;
           }
@@ -479,6 +515,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         volatile int never = 0;
         mbar_wait(drain, 0, &never, p.status, kStatusTimeoutDrain);
       }
+      prof_add(p, 1, w_ops);
+      prof_add(p, 2, w_acc);
+      prof_add(p, 5, local);
     }
   } else {
     // -------------------------------------------------------------- epilogue
@@ -488,11 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
     uint8_t* wstage = sEpi + (warp - 2) * EpiStage<OutT, ACT>::kWarpBytes;
     int stage_pp = 0;
+    long long w_epi = 0;
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue)) break;
+      if (!prof_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue, p.prof != nullptr, w_epi)) break;
       tc_fence_after();
       const int split = t / tiles_per_split;
       const int ts = t - split * tiles_per_split;
@@ -500,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
+      if (!(p.debug & 2))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
                                m_blk * kBM + q * 32, b, n_blk * BN, split, half * (BN / 2), (half + 1) * (BN / 2), vec,
                                use_tma);
@@ -508,6 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
     if (use_tma && lane == 0) bulk_wait_all();
+    if (lane == 0) prof_add(p, 3, w_epi);
   }
 
   tc_fence_before();
@@ -605,6 +647,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t armed_parity[S];
       bool armed[S];
       for (int s = 0; s < S; ++s) armed[s] = false;
+      long long w_prod = 0;
+      const long long t_role = clock64();
       bool ok = true;
       for (int t = pair; t < total_tiles && ok; t += npairs) {
         const int split = t / tiles_per_split;
@@ -618,9 +662,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int kb0 = split * kb_per_split;
         const int kb1 = min(num_kb_total, kb0 + kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer)) {
+          if (!prof_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer, p.prof != nullptr, w_prod)) {
             ok = false;
             break;
+          }
+          if (p.debug & 1) {
+            if (leader) mbar_arrive(&full[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
           }
           if (leader) {
             mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
@@ -658,6 +710,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       }
+      prof_add(p, 0, w_prod);
+      prof_add(p, 4, clock64() - t_role);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -672,10 +726,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int local = 0;
       bool ok = true;
       bool issued_any = false;
+      long long w_ops = 0, w_acc = 0;
       for (int t = pair; t < total_tiles && ok; t += npairs, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma)) {
+        if (!prof_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_acc)) {
           ok = false;
           break;
         }
@@ -684,7 +739,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int split = t / tiles_per_split;
         const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma)) {
+          if (!prof_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_ops)) {
             ok = false;
             break;
           }
@@ -712,6 +767,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         volatile int never = 0;
         mbar_wait(drain, 0, &never, p.status, kStatusTimeoutDrain);
       }
+      prof_add(p, 1, w_ops);
+      prof_add(p, 2, w_acc);
+      prof_add(p, 5, local);
     }
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
@@ -721,12 +779,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool use_tma = p.tma_store != 0 && !(std::is_same<OutT, float>::value && ACT == ACT_GELU);
     uint8_t* wstage = sEpi + (warp - 2) * EpiStage<OutT, ACT>::kWarpBytes;
     int stage_pp = 0;
+    long long w_epi = 0;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     int local = 0;
     for (int t = pair; t < total_tiles; t += npairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue)) break;
+      if (!prof_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue, p.prof != nullptr, w_epi)) break;
       tc_fence_after();
       const int split = t / tiles_per_split;
       const int ts = t - split * tiles_per_split;
@@ -734,6 +793,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
+      if (!(p.debug & 2))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
                                m_blk * 256 + (int)rank * 128 + q * 32, b, n_blk * BN, split, half * (BN / 2),
                                (half + 1) * (BN / 2), vec, use_tma);
@@ -742,6 +802,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
     }
     if (use_tma && lane == 0) bulk_wait_all();
+    if (lane == 0) prof_add(p, 3, w_epi);
   }
 
   tc_fence_before();
@@ -808,6 +869,24 @@ static void dispatch_act2(int act, const CUtensorMap& ta, const CUtensorMap& tb,
     case ACT_GELU_BWD: launch_gemm2<BN, OutT, ACT_GELU_BWD>(ta, tb, p, maps, grid, s); break;
     default: KB_CHECK(false, "bad activation");
   }
+}
+
+// Pipeline profile buffer for the GEMM kernels (see GemmParams::prof); null
+// when profiling is off. Set from Python for diagnostics only.
+static unsigned long long* g_gemm_prof = nullptr;
+static int g_gemm_debug = 0;
+
+void gemm_set_debug(int64_t mode) { g_gemm_debug = (int)mode; }
+
+void gemm_set_profile(const c10::optional<at::Tensor>& buf) {
+  if (!buf.has_value() || !buf->defined()) {
+    g_gemm_prof = nullptr;
+    return;
+  }
+  check_cuda_tensor(*buf, "profile buffer");
+  KB_CHECK(buf->scalar_type() == at::kLong && buf->is_contiguous() && buf->numel() >= 8 * 2 * 256,
+           "gemm profile buffer must be int64 with at least 4096 entries");
+  g_gemm_prof = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
 }
 
 // Operand description: `t` is a 2-D [rows, cols] or 3-D [batch, rows, cols] view.
@@ -938,6 +1017,8 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   KB_CHECK(act != ACT_GELU_BWD || p.D != nullptr, "GELU backward needs the pre-activation as D");
   p.vec_ok = vec;
   p.status = device_status_ptr(dev);
+  p.prof = g_gemm_prof;
+  p.debug = g_gemm_debug;
 
   const int rows_per_tile = pair_mode ? 256 : 128;
   const int64_t tiles = batch * ((M + rows_per_tile - 1) / rows_per_tile) * ((N + bn - 1) / bn);

@@ -40,12 +40,46 @@ def shadow_of(param: torch.Tensor, dtype: torch.dtype) -> Optional[torch.Tensor]
 
 
 class LowPrecisionShadows:
-    """bf16/fp16 copies of a fixed list of fp32 matrix parameters."""
+    """bf16/fp16 copies of a fixed list of fp32 matrix parameters.
 
-    def __init__(self, params: Iterable[nn.Parameter]) -> None:
+    ``fused_groups`` lists groups of matrices with equal column counts whose
+    copies should be row blocks of one buffer (for example q, k and v): the
+    forward pass then runs one GEMM on the stacked weight while every matrix
+    stays its own parameter (Muon orthogonalises each separately).
+    """
+
+    def __init__(self, params: Iterable[nn.Parameter], fused_groups: Iterable[Iterable[nn.Parameter]] = ()) -> None:
         self.params: List[nn.Parameter] = list(params)
+        self.fused_groups: List[List[nn.Parameter]] = [list(g) for g in fused_groups]
+        known = {id(p) for p in self.params}
+        for g in self.fused_groups:
+            if any(id(p) not in known for p in g) or len({p.shape[1] for p in g}) != 1:
+                raise ValueError("fused shadow groups must be listed parameters with equal column counts")
+        self._fused: Dict[tuple, torch.Tensor] = {}
+
+    def _ensure_fused(self, dtype: torch.dtype) -> None:
+        for gi, g in enumerate(self.fused_groups):
+            buf = self._fused.get((gi, dtype))
+            if buf is not None and buf.device == g[0].device and all(
+                    getattr(getattr(p, "_kb_shadow", None), "_base", None) is buf for p in g):
+                continue
+            rows = sum(p.shape[0] for p in g)
+            buf = torch.empty((rows, g[0].shape[1]), device=g[0].device, dtype=dtype)
+            r = 0
+            for p in g:
+                p._kb_shadow = buf[r:r + p.shape[0]]  # type: ignore[attr-defined]
+                p._kb_shadow_version = -1  # type: ignore[attr-defined]
+                r += p.shape[0]
+            self._fused[(gi, dtype)] = buf
+
+    def fused(self, index: int, dtype: torch.dtype) -> torch.Tensor:
+        """The stacked copy of fused group ``index`` (valid after ``get(dtype)``)."""
+
+        return self._fused[(index, dtype)]
 
     def get(self, dtype: torch.dtype) -> Dict[int, torch.Tensor]:
+        if self.fused_groups:
+            self._ensure_fused(dtype)
         stale_src: List[torch.Tensor] = []
         stale_dst: List[torch.Tensor] = []
         out: Dict[int, torch.Tensor] = {}

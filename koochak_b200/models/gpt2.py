@@ -107,7 +107,7 @@ def _lp_copy_of(grad: torch.Tensor, dtype: torch.dtype):
 class _BlockFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, ln1_w, ln1_b, attn_w, attn_b, proj_w, proj_b, ln2_w, ln2_b, fc_w, fc_b, fcp_w, fcp_b,
-                lp, n_head, eps):
+                lp, n_head, eps, causal=True):
         attn_w16, proj_w16, fc_w16, fcp_w16 = lp
         cdt = attn_w16.dtype
         B, S, C = x.shape
@@ -116,7 +116,7 @@ class _BlockFn(torch.autograd.Function):
         h1, m1, r1 = kf.norm_forward(x2, ln1_w, ln1_b, eps, rms=False, out_dtype=cdt)
         qkv = kf.gemm(h1, attn_w16, bias=attn_b)
         q5 = qkv.view(B, S, 3, H, D)
-        a, lse = kf.flash_attention_forward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], causal=True)
+        a, lse = kf.flash_attention_forward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], causal=causal)
         a2 = a.view(M, C)
         x_mid = kf.gemm(a2, proj_w16, bias=proj_b, d=x2, beta=1.0, out_dtype=torch.float32)
         h2, m2, r2 = kf.norm_forward(x_mid, ln2_w, ln2_b, eps, rms=False, out_dtype=cdt)
@@ -126,6 +126,7 @@ class _BlockFn(torch.autograd.Function):
         ctx.save_for_backward(x2, h1, m1, r1, qkv, a2, lse, x_mid, h2, m2, r2, pre, g, ln1_w, ln2_w,
                               attn_w16, proj_w16, fc_w16, fcp_w16)
         ctx.dims = (B, S, C, H, D)
+        ctx.causal = causal
         return out.view(B, S, C)
 
     @staticmethod
@@ -155,7 +156,7 @@ class _BlockFn(torch.autograd.Function):
         q5 = qkv.view(B, S, 3, H, D)
         dqkv = torch.empty((B, S, 3, H, D), device=qkv.device, dtype=cdt)
         kf.flash_attention_backward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], a2.view(B, S, H, D), da.view(B, S, H, D),
-                                    lse, causal=True, dq=dqkv[:, :, 0], dk=dqkv[:, :, 1], dv=dqkv[:, :, 2])
+                                    lse, causal=ctx.causal, dq=dqkv[:, :, 0], dk=dqkv[:, :, 1], dv=dqkv[:, :, 2])
         dqkv2 = dqkv.view(M, 3 * C)
         dh1 = kf.gemm(dqkv2, attn_w16, b_mn_major=True)
         d_attn_w = kf.gemm(dqkv2, h1, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
@@ -163,7 +164,7 @@ class _BlockFn(torch.autograd.Function):
         dx, d_ln1_w, d_ln1_b, dx_lp = kf.norm_backward(dh1, x2, ln1_w, m1, r1, rms=False, dres=dx_mid,
                                                        dx_dtype=torch.float32, want_lp=True)
         return (_with_lp_copy(dx.view(B, S, C), dx_lp), d_ln1_w, d_ln1_b, d_attn_w, d_attn_b, d_proj_w, d_proj_b, d_ln2_w, d_ln2_b,
-                d_fc_w, d_fc_b, d_fcp_w, d_fcp_b, None, None, None)
+                d_fc_w, d_fc_b, d_fcp_w, d_fcp_b, None, None, None, None)
 
 
 class _EmbeddingFn(torch.autograd.Function):

@@ -207,6 +207,21 @@ def swiglu_ref(gu):
     return F.silu(g) * u
 
 
+def patchify(images, patch: int, dtype: torch.dtype):
+    """fp32 NCHW images -> [B * patches, C * patch * patch] rows in ``dtype`` (Conv2d weight column order)."""
+
+    B, C, H, W = images.shape
+    out = torch.empty((B * (H // patch) * (W // patch), C * patch * patch), device=images.device, dtype=dtype)
+    native().patchify(images.contiguous(), out, int(patch))
+    return out
+
+
+def patchify_ref(images, patch: int):
+    B, C, H, W = images.shape
+    x = images.reshape(B, C, H // patch, patch, W // patch, patch)
+    return x.permute(0, 2, 4, 1, 3, 5).reshape(B * (H // patch) * (W // patch), C * patch * patch)
+
+
 def rope_apply_(x, cos, sin, inverse=False):
     B, S, H, D = x.shape
     native().rope_apply(x, cos, sin, S, H, D, bool(inverse))

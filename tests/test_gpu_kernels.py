@@ -251,6 +251,55 @@ def test_gpt2_native_matches_reference_path():
         assert _rel(g_native[n], p.grad) < 0.08, n
 
 
+def test_patchify_matches_reference():
+    kf = _kf()
+    img = torch.randn(3, 3, 64, 48, device=DEV)
+    for dt in (torch.float16, torch.bfloat16):
+        got = kf.patchify(img, 16, dt)
+        assert torch.equal(got, kf.patchify_ref(img, 16).to(dt))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_vit_native_matches_reference_path(dtype):
+    from koochak_b200.models import ViT
+
+    torch.manual_seed(6)
+    model = ViT(depth=2, image_size=64, num_classes=100, dim=256, n_head=4).to(DEV)
+    x = torch.randn(4, 3, 64, 64, device=DEV)
+    y = torch.randint(0, 100, (4,), device=DEV)
+    with torch.autocast("cuda", dtype=dtype):
+        loss = model(x, y)
+    loss.backward()
+    g_native = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+    model.zero_grad(set_to_none=True)
+    ref = model._forward_reference(x, y)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 3e-2
+    for n, p in model.named_parameters():
+        assert _rel(g_native[n], p.grad) < 0.08, n
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_llama_native_matches_reference_path(head_dim):
+    from koochak_b200.models import Llama
+
+    torch.manual_seed(5)
+    model = Llama(n_layer=2, n_head=256 // head_dim, dim=256, ffn_dim=688, vocab_size=1024, max_seq_len=128).to(DEV)
+    idx = torch.randint(0, 1024, (2, 128), device=DEV)
+    tgt = torch.randint(0, 1024, (2, 128), device=DEV)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = model(idx, tgt)
+    loss.backward()
+    g_native = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+    model.zero_grad(set_to_none=True)
+    cos, sin = model.rope(128, DEV)
+    ref = model._forward_reference(idx, tgt, -100, cos, sin)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 2e-2
+    for n, p in model.named_parameters():
+        assert _rel(g_native[n], p.grad) < 0.08, n
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (520, 384, 200), (2048, 2304, 768), (1000, 776, 1024)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
 @pytest.mark.parametrize("block_n", [-128, -256])
