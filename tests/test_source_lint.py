@@ -1,0 +1,56 @@
+"""Source lint for rules the native code must keep on multi-GPU systems.
+
+* No TMA / bulk copy *load* with cluster multicast anywhere: every entry point
+  may run with peers' memory mapped, and a multicast load whose tensor map
+  reaches another GPU's memory must never be built. (``tcgen05.commit`` with a
+  multicast CTA mask is a barrier arrive, not a load, and stays allowed.)
+* None of the batched-memcpy runtime/driver entry points appear in any
+  source file (they are not used by this project).
+* Every ``mbarrier`` wait in the kernels goes through the bounded helper.
+"""
+
+from __future__ import annotations
+
+import pathlib
+import re
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+SOURCES = [p for p in (ROOT / "koochak_b200" / "csrc").rglob("*") if p.suffix in (".cu", ".cuh", ".h", ".cpp")]
+
+
+def _code(path: pathlib.Path) -> str:
+    text = path.read_text()
+    text = re.sub(r"//[^\n]*", "", text)
+    return re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+
+
+def test_sources_found():
+    names = {p.name for p in SOURCES}
+    assert {"gemm.cu", "comm.cu", "sm100.cuh"} <= names
+
+
+def test_no_multicast_bulk_loads():
+    bad = []
+    for p in SOURCES:
+        for ln, line in enumerate(_code(p).splitlines(), 1):
+            if "cp.async.bulk" in line and "multicast" in line:
+                bad.append(f"{p.name}:{ln}: {line.strip()}")
+    assert not bad, "cluster-multicast bulk loads are not allowed:\n" + "\n".join(bad)
+
+
+def test_no_batched_memcpy_entry_points():
+    pattern = re.compile("Memcpy" + r"(3D)?" + "Batch" + "Async")
+    files = [p for p in ROOT.rglob("*") if p.suffix in (".cu", ".cuh", ".h", ".cpp", ".py") and ".git" not in p.parts
+             and "_ref" not in p.parts and "_work" not in p.parts]
+    bad = [str(p.relative_to(ROOT)) for p in files if pattern.search(p.read_text(errors="ignore"))]
+    assert not bad, bad
+
+
+def test_mbarrier_waits_are_bounded():
+    raw_try_wait = []
+    for p in SOURCES:
+        code = _code(p)
+        for ln, line in enumerate(code.splitlines(), 1):
+            if "mbarrier.try_wait" in line and p.name != "sm100.cuh":
+                raw_try_wait.append(f"{p.name}:{ln}")
+    assert not raw_try_wait, "mbarrier waits must use the bounded helper in sm100.cuh: " + ", ".join(raw_try_wait)
