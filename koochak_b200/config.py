@@ -132,6 +132,7 @@ class TrainConfig:
     rank_timing_keys: Optional[list] = None
     profile_step_fn_timing: bool = False
     profile_step_fn_cuda_sync: bool = True
+    profile_nvtx: bool = False
     device_timing: bool = False
     comm_transport: str = "auto"
 

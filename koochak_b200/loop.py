@@ -190,6 +190,7 @@ class _TrainSettings:
     ddp_broadcast_buffers: bool
     device_timing: bool = False
     comm_transport: str = "auto"
+    profile_nvtx: bool = False
 
     @classmethod
     def from_cfg(cls, cfg: Any) -> "_TrainSettings":
@@ -245,6 +246,7 @@ class _TrainSettings:
             ddp_broadcast_buffers=bool(g(cfg, "ddp_broadcast_buffers", True)),
             device_timing=bool(g(cfg, "device_timing", False)),
             comm_transport=str(g(cfg, "comm_transport", "auto")),
+            profile_nvtx=bool(g(cfg, "profile_nvtx", False)),
         )
 
 
@@ -393,6 +395,7 @@ class _TrainLoop:
         train_config, config_json = _resolve_train_config(train_cfg, config_json)
         self.train_cfg = train_config
         self.settings = _TrainSettings.from_cfg(train_config)
+        self._nvtx_open = 0
         self.ema_settings = _EmaSettings.from_cfg(train_config)
         self.step_fn = step_fn
         self.optimizer = optimizer
@@ -780,12 +783,18 @@ class _TrainLoop:
         if self.settings.profile_step_timing and self.settings.profile_step_cuda_sync and self._on_cuda():
             torch.cuda.synchronize(self.device)
 
-    def _profile_start(self) -> float:
+    def _profile_start(self, phase: Optional[str] = None) -> float:
         self._profile_sync()
+        if self.settings.profile_nvtx and phase is not None and self._on_cuda():
+            torch.cuda.nvtx.range_push(f"koochak/{phase}")
+            self._nvtx_open += 1
         return time.perf_counter()
 
     def _profile_add(self, totals: Dict[str, float], key: str, start: float) -> float:
         self._profile_sync()
+        if self._nvtx_open:
+            torch.cuda.nvtx.range_pop()
+            self._nvtx_open -= 1
         elapsed = time.perf_counter() - start
         if self.settings.profile_step_timing:
             totals[key] = totals.get(key, 0.0) + elapsed
@@ -802,14 +811,14 @@ class _TrainLoop:
                 else nullcontext()
             with sync_cm, ac:
                 self._micro_position = (micro, "fetch")
-                t0 = self._profile_start()
+                t0 = self._profile_start("batch_wait")
                 batch = next(it) if use_prefetch else to_device(next(it), self.device)
                 stats.batch_wait_s += self._profile_add(stats.profile_timing_totals, "profile_loop_batch_wait_time_s",
                                                         t0)
                 for k, v in _skip_counts(batch).items():
                     stats.skip_count_totals[k] = stats.skip_count_totals.get(k, 0.0) + float(v)
                 self._micro_position = (micro, "step_fn")
-                t0 = self._profile_start()
+                t0 = self._profile_start("step_fn")
                 out = self.step_fn(self.model, batch, self._step_ctx(step))
                 self._profile_add(stats.profile_timing_totals, "profile_loop_step_fn_time_s", t0)
                 if collect_rank_timing and isinstance(out, Mapping):
@@ -826,7 +835,7 @@ class _TrainLoop:
                     raise RuntimeError("step_fn returned a 'loss' that is not a torch.Tensor")
                 loss = out["loss"] / n
             self._micro_position = (micro, "backward")
-            t0 = self._profile_start()
+            t0 = self._profile_start("backward")
             self.scaler.scale(loss).backward()
             self._profile_add(stats.profile_timing_totals, "profile_loop_backward_time_s", t0)
             d = loss.detach()
@@ -878,7 +887,7 @@ class _TrainLoop:
         fused_opt = bool(getattr(self.optimizer, "kb_fused", False)) or bool(
             getattr(getattr(self.optimizer, "inner", None), "kb_fused", False))
 
-        t0 = self._profile_start()
+        t0 = self._profile_start("unscale")
         gate_stats = None
         dp = self.model if getattr(self.model, "fused_gate_available", None) is not None else None
         if dp is not None and grads is not None and dp.fused_gate_available():
@@ -894,11 +903,11 @@ class _TrainLoop:
             self.scaler.unscale_(self.optimizer)
         self._profile_add(stats.profile_timing_totals, "profile_loop_unscale_time_s", t0)
 
-        t0 = self._profile_start()
+        t0 = self._profile_start("nonfinite_grad_check")
         self._check_nonfinite_grads(step)
         self._profile_add(stats.profile_timing_totals, "profile_loop_nonfinite_grad_check_time_s", t0)
 
-        t0 = self._profile_start()
+        t0 = self._profile_start("grad_clip")
         if clip:
             if grads is None:
                 clipping = clip_grad_norm_(self.model.parameters(), float(s.grad_clip_norm))
@@ -1260,7 +1269,7 @@ class _TrainLoop:
         step_start = self._profile_start()
         self._device_timer_start()
         totals: Dict[str, float] = {}
-        t0 = self._profile_start()
+        t0 = self._profile_start("setup_zero_grad")
         self.model.train()
         self.optimizer.zero_grad(set_to_none=True)
         self._profile_add(totals, "profile_loop_setup_zero_grad_time_s", t0)
@@ -1282,7 +1291,7 @@ class _TrainLoop:
 
         self._gradient_gate(step, stats)
 
-        t0 = self._profile_start()
+        t0 = self._profile_start("ema_wait")
         if self.ema is not None:
             self.ema.wait_before_param_mutation()
         for e in self.ema_dual:
@@ -1290,16 +1299,16 @@ class _TrainLoop:
         self._profile_add(stats.profile_timing_totals, "profile_loop_ema_wait_time_s", t0)
 
         self._maybe_fuse_ema(step)
-        t0 = self._profile_start()
+        t0 = self._profile_start("optimizer_step")
         self.scaler.step(self.optimizer)
         self._profile_add(stats.profile_timing_totals, "profile_loop_optimizer_step_time_s", t0)
-        t0 = self._profile_start()
+        t0 = self._profile_start("scaler_update")
         self.scaler.update()
         self._profile_add(stats.profile_timing_totals, "profile_loop_scaler_update_time_s", t0)
-        t0 = self._profile_start()
+        t0 = self._profile_start("ema_update")
         self._update_ema(step)
         self._profile_add(stats.profile_timing_totals, "profile_loop_ema_update_time_s", t0)
-        t0 = self._profile_start()
+        t0 = self._profile_start("scheduler")
         self._step_scheduler()
         self._profile_add(stats.profile_timing_totals, "profile_loop_scheduler_time_s", t0)
 
@@ -1308,7 +1317,7 @@ class _TrainLoop:
         device_ms = self._device_timer_stop()
         if collect:
             self._emit_rank_timing(step, stats, step_time_s)
-        t0 = self._profile_start()
+        t0 = self._profile_start("log_build")
         full, minimal = self._build_logs(step, stats, step_time_s)
         if device_ms is not None:
             minimal["step_device_ms"] = device_ms
@@ -1319,7 +1328,7 @@ class _TrainLoop:
             if full is not None:
                 full["profile_loop_log_build_time_s"] = built
             minimal["profile_loop_log_build_time_s"] = built
-        t0 = self._profile_start()
+        t0 = self._profile_start("log_emit")
         _emit(self.hooks, "on_update_end", minimal, self._step_ctx(step))
         if full is not None:
             _emit(self.hooks, "on_log", full, self._step_ctx(step))
@@ -1329,15 +1338,15 @@ class _TrainLoop:
         return self._finish_step(step, stats.profile_timing_totals)
 
     def _finish_step(self, step: int, totals: Dict[str, float]) -> bool:
-        t0 = self._profile_start()
+        t0 = self._profile_start("health_check")
         self._reconcile_stop_requests(step)
         self._profile_add(totals, "profile_loop_health_check_time_s", t0)
-        t0 = self._profile_start()
+        t0 = self._profile_start("eval")
         self._maybe_run_eval(step)
         self._profile_add(totals, "profile_loop_eval_time_s", t0)
         if self.evacuation_requested:
             return True
-        t0 = self._profile_start()
+        t0 = self._profile_start("checkpoint")
         at = step + int(self.settings.intervals_use_completed_steps)
         terminal_due = self.settings.intervals_use_completed_steps and at == self.settings.max_steps
         if at > 0 and at % self.settings.ckpt_every == 0 and not terminal_due:
