@@ -59,7 +59,9 @@ struct GemmParams {
   unsigned long long* prof;
   // Diagnostic modes (0 in normal use): bit 0 skips the operand loads (MMAs
   // read whatever the ring holds), bit 1 skips the epilogue's math and
-  // stores. Results are meaningless; only the timing is of interest.
+  // stores, bit 2 keeps only the epilogue's TMEM loads (32 columns each; with
+  // bit 3: 16, with bit 4: 64). Results are meaningless; only the timing is
+  // of interest.
   int debug;
 };
 
@@ -115,7 +117,9 @@ __device__ __forceinline__ void store_row32<float>(float* dst, const float (&v)[
 #pragma unroll
     for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
   } else {
-    for (int j = 0; j < valid; ++j) dst[j] = v[j];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) dst[j] = v[j];
   }
 }
 
@@ -133,7 +137,9 @@ __device__ __forceinline__ void store_row32<__nv_bfloat16>(__nv_bfloat16* dst, c
       *reinterpret_cast<uint4*>(dst + j) = p;
     }
   } else {
-    for (int j = 0; j < valid; ++j) dst[j] = __float2bfloat16_rn(v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) dst[j] = __float2bfloat16_rn(v[j]);
   }
 }
 
@@ -150,7 +156,9 @@ __device__ __forceinline__ void store_row32<__half>(__half* dst, const float (&v
       *reinterpret_cast<uint4*>(dst + j) = p;
     }
   } else {
-    for (int j = 0; j < valid; ++j) dst[j] = __float2half_rn(v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) dst[j] = __float2half_rn(v[j]);
   }
 }
 
@@ -173,6 +181,7 @@ __device__ __forceinline__ void load_row32(const T* src, float (&v)[32], int val
       }
     }
   } else {
+#pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = (j < valid) ? to_f32<T>(src[j]) : 0.f;
   }
 }
@@ -262,8 +271,9 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
   OutT* crow = reinterpret_cast<OutT*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc;
   const OutT* drow =
       p.D ? reinterpret_cast<const OutT*>(p.D) + (long long)b * p.strideD + (long long)row * p.ldd : nullptr;
-  __nv_bfloat16* arow =
-      p.aux ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux : nullptr;
+  // The GELU pre-activation is stored in the output's 16-bit type (bf16 for fp32 outputs).
+  using AuxT = typename std::conditional<sizeof(OutT) == 2, OutT, __nv_bfloat16>::type;
+  AuxT* arow = p.aux ? reinterpret_cast<AuxT*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux : nullptr;
   const bool atomic_out = std::is_same<OutT, float>::value && ACT == ACT_NONE && p.splits > 1;
   uint32_t r0[32], r1[32];
 
@@ -286,14 +296,16 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
         for (int j = 0; j < 32; j += 4)
           atomicAdd(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
       } else {
-        for (int j = 0; j < valid; ++j) atomicAdd(dst + j, v[j]);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < valid) atomicAdd(dst + j, v[j]);
       }
       return;
     }
     if (!use_tma) {
       if (!row_ok) return;
       if constexpr (ACT == ACT_GELU) {
-        if (arow) store_row32<__nv_bfloat16>(arow + col0, pre, valid, vec);
+        if (arow) store_row32<AuxT>(arow + col0, pre, valid, vec);
       }
       store_row32<OutT>(crow + col0, v, valid, vec);
       return;
@@ -307,7 +319,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
     __syncwarp();
     stage_row32<OutT>(ctile, lane, v);
     if constexpr (ACT == ACT_GELU) {
-      if (p.aux) stage_row32<__nv_bfloat16>(atile, lane, pre);
+      if (p.aux) stage_row32<AuxT>(atile, lane, pre);
     }
     fence_proxy_async_smem();
     __syncwarp();
@@ -321,6 +333,38 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
     stage_pp ^= 1;
   };
 
+  if (p.debug & 4) {
+    // Diagnostic: TMEM reads only (no math, no stores), with 16-, 32- or
+    // 64-column loads, to measure what the loads alone cost the MMA pipe.
+    uint32_t acc = 0;
+    if (p.debug & 8) {
+      for (int c = c_begin; c < c_end; c += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_row + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc ^= r[j];
+      }
+    } else if (p.debug & 16) {
+      for (int c = c_begin; c < c_end; c += 64) {
+        uint32_t r[64];
+        tmem_ld_32x32b_x64(tmem_row + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc ^= r[j];
+      }
+    } else {
+      for (int c = c_begin; c < c_end; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_row + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc ^= r[j];
+      }
+    }
+    if (acc == 0x12345678u) atomicCAS(p.status, 0, kStatusBadArgs);
+    return;
+  }
   tmem_ld_32x32b_x32(tmem_row + c_begin, r0);
   tmem_wait_ld_dep(r0);
 #pragma unroll 1
@@ -393,9 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------------------ producer
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed_parity[S];
-      bool armed[S];
-      for (int s = 0; s < S; ++s) armed[s] = false;
+      uint32_t armed = 0, armed_parity = 0;  // per-stage bits (registers, not a local array)
       long long w_prod = 0;
       const long long t_role = clock64();
       bool ok = true;
@@ -424,8 +466,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             continue;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          armed[stage] = true;
-          armed_parity[stage] = phase;
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
           uint8_t* b_dst = sB + stage * Cfg::kBBytes;
           const int k0 = kb * kBK;
@@ -449,9 +491,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Drain: every armed stage must have landed before this CTA may exit.
       for (int s = 0; s < S; ++s) {
-        if (armed[s]) {
+        if (armed & (1u << s)) {
           volatile int never = 0;
-          if (!mbar_wait(&full[s], armed_parity[s], &never, p.status, kStatusTimeoutDrain)) break;
+          if (!mbar_wait(&full[s], (armed_parity >> s) & 1u, &never, p.status, kStatusTimeoutDrain)) break;
         }
       }
       prof_add(p, 0, w_prod);
@@ -644,9 +686,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed_parity[S];
-      bool armed[S];
-      for (int s = 0; s < S; ++s) armed[s] = false;
+      uint32_t armed = 0, armed_parity = 0;  // per-stage bits (registers, not a local array)
       long long w_prod = 0;
       const long long t_role = clock64();
       bool ok = true;
@@ -676,8 +716,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           if (leader) {
             mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
-            armed[stage] = true;
-            armed_parity[stage] = phase;
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t fb = full0 + stage * 8;
           uint8_t* a_dst = sA + stage * Cfg::kABytes;
@@ -704,9 +744,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (leader) {
         // The leader's full barriers account for both CTAs' copies.
         for (int s = 0; s < S; ++s) {
-          if (armed[s]) {
+          if (armed & (1u << s)) {
             volatile int never = 0;
-            if (!mbar_wait(&full[s], armed_parity[s], &never, p.status, kStatusTimeoutDrain)) break;
+            if (!mbar_wait(&full[s], (armed_parity >> s) & 1u, &never, p.status, kStatusTimeoutDrain)) break;
           }
         }
       }
@@ -1008,7 +1048,9 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     p.bias = bias->data_ptr<float>();
   }
   if (aux.has_value() && aux->defined()) {
-    KB_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(-2) == M && aux->size(-1) == N, "aux mismatch");
+    const at::ScalarType aux_t = (ct == at::kFloat) ? at::kBFloat16 : ct;
+    KB_CHECK(aux->scalar_type() == aux_t && aux->size(-2) == M && aux->size(-1) == N,
+             "aux must be [.., M, N] in the output's 16-bit type (bf16 for fp32 outputs)");
     p.aux = aux->data_ptr();
     p.ldaux = aux->stride(-2);
     p.strideAux = batched ? aux->stride(0) : 0;
@@ -1068,7 +1110,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
         return make_tma(base, t, 3, dims, strides, box, es == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
       };
       maps.c = make(p.C, ct, p.ldc, p.strideC, esz);
-      if (p.aux != nullptr) maps.aux = make(p.aux, at::kBFloat16, p.ldaux, p.strideAux, 2);
+      if (p.aux != nullptr) maps.aux = make(p.aux, ct == at::kFloat ? at::kBFloat16 : ct, p.ldaux, p.strideAux, 2);
       p.tma_store = 1;
     }
   }
