@@ -50,6 +50,7 @@ struct GemmParams {
   int splits;  // split-K factor; > 1 means fp32 C is accumulated with atomics
   int kb_per_split;  // 64-wide K blocks per split (every split non-empty)
   int tma_store;     // epilogue writes C (and aux) through staged TMA stores
+  int stream_k;      // K-iterations of all tiles split evenly over the workers (fp32 atomics)
   int* status;
   // Optional pipeline profile (null: off). Per CTA, 8 counters of clock64
   // cycles: [0] producer waiting for a free stage, [1] MMA waiting for
@@ -77,6 +78,33 @@ __device__ __forceinline__ bool prof_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ void prof_add(const GemmParams& p, int idx, long long v) {
   if (p.prof) atomicAdd(p.prof + blockIdx.x * 8 + idx, (unsigned long long)v);
 }
+
+// Work unit k of worker w (a CTA, or a CTA pair) out of nw: output tile t and
+// the K-block range [kb0, kb1) it covers. Without stream-K a unit is one tile
+// (or one split of it); with stream-K the K-iterations of all tiles are cut
+// into nw equal contiguous ranges, so a worker may finish one tile and start
+// the next, and every partial tile is added into C with fp32 atomics.
+__device__ __forceinline__ bool work_unit(const GemmParams& p, int w, int nw, int k, int total_tiles,
+                                          int tiles_per_split, int num_kb, int& t, int& kb0, int& kb1) {
+  if (!p.stream_k) {
+    t = w + k * nw;
+    if (t >= total_tiles) return false;
+    const int split = t / tiles_per_split;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(num_kb, kb0 + p.kb_per_split);
+    return true;
+  }
+  const long long iters = (long long)total_tiles * num_kb;
+  const long long begin = iters * w / nw, end = iters * (w + 1) / nw;
+  const long long first = begin / num_kb;
+  const long long start = (k == 0) ? begin : (first + k) * num_kb;
+  if (start >= end) return false;
+  t = (int)(first + k);
+  kb0 = (int)(start - (long long)t * num_kb);
+  kb1 = (int)min((long long)num_kb, end - (long long)t * num_kb);
+  return true;
+}
+
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -274,7 +302,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
   // The GELU pre-activation is stored in the output's 16-bit type (bf16 for fp32 outputs).
   using AuxT = typename std::conditional<sizeof(OutT) == 2, OutT, __nv_bfloat16>::type;
   AuxT* arow = p.aux ? reinterpret_cast<AuxT*>(p.aux) + (long long)b * p.strideAux + (long long)row * p.ldaux : nullptr;
-  const bool atomic_out = std::is_same<OutT, float>::value && ACT == ACT_NONE && p.splits > 1;
+  const bool atomic_out = std::is_same<OutT, float>::value && ACT == ACT_NONE && (p.splits > 1 || p.stream_k);
   uint32_t r0[32], r1[32];
 
   auto handle = [&](const uint32_t (&raw)[32], int c) {
@@ -430,7 +458,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_per_split = tiles_per_batch * p.batch;
   const int total_tiles = tiles_per_split * p.splits;
   const int num_kb_total = (p.K + kBK - 1) / kBK;
-  const int kb_per_split = p.kb_per_split;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -441,7 +468,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long w_prod = 0;
       const long long t_role = clock64();
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      int t, kb0, kb1;
+      for (int unit = 0; ok && work_unit(p, blockIdx.x, gridDim.x, unit, total_tiles, tiles_per_split, num_kb_total,
+                                         t, kb0, kb1); ++unit) {
         const int split = t / tiles_per_split;
         const int ts = t - split * tiles_per_split;
         const int b = ts / tiles_per_batch;
@@ -450,8 +479,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m_blk = r - n_blk * num_m;
         const int m0 = m_blk * kBM;
         const int n0 = n_blk * BN;
-        const int kb0 = split * kb_per_split;
-        const int kb1 = min(num_kb_total, kb0 + kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!prof_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer, p.prof != nullptr, w_prod)) {
             ok = false;
@@ -516,7 +543,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool issued_any = false;
       long long w_ops = 0, w_acc = 0;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
+      int t, kb0, kb1;
+      for (; ok && work_unit(p, blockIdx.x, gridDim.x, local, total_tiles, tiles_per_split, num_kb_total, t, kb0,
+                             kb1); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!prof_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_acc)) {
@@ -525,8 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int split = t / tiles_per_split;
-        const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
+        const int nkb = kb1 - kb0;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!prof_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_ops)) {
             ok = false;
@@ -571,7 +599,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage_pp = 0;
     long long w_epi = 0;
     int local = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    int t, kb0, kb1;
+    for (; work_unit(p, blockIdx.x, gridDim.x, local, total_tiles, tiles_per_split, num_kb_total, t, kb0, kb1);
+         ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!prof_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue, p.prof != nullptr, w_epi)) break;
@@ -584,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m_blk = r - n_blk * num_m;
       if (!(p.debug & 2))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
-                               m_blk * kBM + q * 32, b, n_blk * BN, split, half * (BN / 2), (half + 1) * (BN / 2), vec,
+                               m_blk * kBM + q * 32, b, n_blk * BN, kb0 == 0 ? 0 : 1, half * (BN / 2), (half + 1) * (BN / 2), vec,
                                use_tma);
       tc_fence_before();
       __syncwarp();
@@ -676,7 +706,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int tiles_per_split = tiles_per_batch * p.batch;
   const int total_tiles = tiles_per_split * p.splits;
   const int num_kb_total = (p.K + kBK - 1) / kBK;
-  const int kb_per_split = p.kb_per_split;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
 
@@ -690,7 +719,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       long long w_prod = 0;
       const long long t_role = clock64();
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += npairs) {
+      int t, kb0, kb1;
+      for (int unit = 0; ok && work_unit(p, pair, npairs, unit, total_tiles, tiles_per_split, num_kb_total, t, kb0,
+                                         kb1); ++unit) {
         const int split = t / tiles_per_split;
         const int ts = t - split * tiles_per_split;
         const int b = ts / tiles_per_batch;
@@ -699,8 +730,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int m_blk = r - n_blk * num_m;
         const int m0 = m_blk * 256 + (int)rank * 128;
         const int n0 = n_blk * BN + (int)rank * BHALF;
-        const int kb0 = split * kb_per_split;
-        const int kb1 = min(num_kb_total, kb0 + kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!prof_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kStatusTimeoutProducer, p.prof != nullptr, w_prod)) {
             ok = false;
@@ -767,7 +796,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       bool issued_any = false;
       long long w_ops = 0, w_acc = 0;
-      for (int t = pair; t < total_tiles && ok; t += npairs, ++local) {
+      int t, kb0, kb1;
+      for (; ok && work_unit(p, pair, npairs, local, total_tiles, tiles_per_split, num_kb_total, t, kb0, kb1);
+           ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!prof_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_acc)) {
@@ -776,8 +807,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int split = t / tiles_per_split;
-        const int nkb = min(num_kb_total, (split + 1) * kb_per_split) - split * kb_per_split;
+        const int nkb = kb1 - kb0;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!prof_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma, p.prof != nullptr, w_ops)) {
             ok = false;
@@ -822,7 +852,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     long long w_epi = 0;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     int local = 0;
-    for (int t = pair; t < total_tiles; t += npairs, ++local) {
+    int t, kb0, kb1;
+    for (; work_unit(p, pair, npairs, local, total_tiles, tiles_per_split, num_kb_total, t, kb0, kb1); ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!prof_wait(&tfull[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue, p.prof != nullptr, w_epi)) break;
@@ -835,7 +866,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m_blk = r - n_blk * num_m;
       if (!(p.debug & 2))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
-                               m_blk * 256 + (int)rank * 128 + q * 32, b, n_blk * BN, split, half * (BN / 2),
+                               m_blk * 256 + (int)rank * 128 + q * 32, b, n_blk * BN, kb0 == 0 ? 0 : 1, half * (BN / 2),
                                (half + 1) * (BN / 2), vec, use_tma);
       tc_fence_before();
       __syncwarp();
@@ -1066,19 +1097,22 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   const int64_t tiles = batch * ((M + rows_per_tile - 1) / rows_per_tile) * ((N + bn - 1) / bn);
   const int sms = pair_mode ? (sms_all / 2) : sms_all;  // concurrent tile slots
   const int64_t num_kb = (K + 63) / 64;
-  // Split K when the output has too few tiles to fill the GPU and K is long
-  // (weight gradients): partial tiles are summed into C with fp32 atomics.
+  // Stream-K for fp32 outputs without an activation (weight gradients, long
+  // K) when whole tiles would leave part of the last wave idle: the K-blocks of
+  // all tiles are spread evenly over every worker and partial tiles are summed
+  // into C with fp32 atomics (C first set to beta * D, or zero).
   int splits = 1;
-  if (ct == at::kFloat && act == ACT_NONE && tiles < sms && num_kb >= 16) {
-    splits = (int)std::min<int64_t>({(2 * sms + tiles - 1) / tiles, num_kb / 8, (int64_t)16});
-    splits = std::max(1, splits);
+  int stream_k = 0;
+  if (ct == at::kFloat && act == ACT_NONE && num_kb >= 8) {
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double filled = double(tiles) / double(waves * sms);
+    if (filled < 0.9) stream_k = 1;
   }
-  const int64_t kb_per = (num_kb + splits - 1) / splits;
-  splits = (int)((num_kb + kb_per - 1) / kb_per);
-  p.splits = splits;
-  p.kb_per_split = (int)kb_per;
+  p.splits = 1;
+  p.kb_per_split = (int)num_kb;
+  p.stream_k = stream_k;
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
-  if (splits > 1) {
+  if (stream_k) {
     // C = beta * D (or 0); every split then adds its partial product.
     if (p.D != nullptr && p.beta != 0.f) {
       if (p.D != p.C || p.beta != 1.f) {
@@ -1097,7 +1131,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   std::memset(&maps, 0, sizeof(maps));
   {
     const int64_t esz = c.element_size();
-    bool ok = splits == 1 && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+    bool ok = !stream_k && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
               (!batched || (p.strideC * esz) % 16 == 0);
     if (ok && p.aux != nullptr)
       ok = (p.ldaux * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15) == 0 && (!batched || (p.strideAux * 2) % 16 == 0);
@@ -1115,7 +1149,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     }
   }
   if (pair_mode) {
-    const int grid2 = 2 * (int)std::min<int64_t>(tiles * splits, sms);
+    const int grid2 = 2 * (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles, sms));
     if (bn == 256) {
       if (ct == at::kFloat) dispatch_act2<256, float>((int)act, ta, tb, p, maps, grid2, stream);
       else if (ct == at::kBFloat16) dispatch_act2<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid2, stream);
@@ -1127,7 +1161,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     }
     return;
   }
-  const int grid = (int)std::min<int64_t>(tiles * splits, sms);
+  const int grid = (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles, sms));
   if (bn == 256) {
     if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, maps, grid, stream);
     else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid, stream);

@@ -251,6 +251,27 @@ def test_gpt2_native_matches_reference_path():
         assert _rel(g_native[n], p.grad) < 0.08, n
 
 
+@pytest.mark.parametrize("M,N,K", [(2304, 768, 16384), (768, 3072, 4096), (520, 776, 2000)])
+@pytest.mark.parametrize("block_n", [0, 128, -256])
+def test_gemm_stream_k_fp32(M, N, K, block_n):
+    """fp32 outputs spread over all SMs by K-iterations (stream-K), with bias and beta * D."""
+    kf = _kf()
+    torch.manual_seed(12)
+    a = torch.randn(K, M, device=DEV).bfloat16()
+    b = torch.randn(K, N, device=DEV).bfloat16()
+    ref = kf.gemm_ref(a, b, a_mn_major=True, b_mn_major=True)
+    out = kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32, block_n=block_n)
+    assert _rel(out, ref) < 1e-4
+    d = torch.randn(M, N, device=DEV)
+    bias = torch.randn(N, device=DEV)
+    out2 = kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32, d=d, beta=0.5, bias=bias,
+                   block_n=block_n)
+    assert _rel(out2, ref + bias + 0.5 * d) < 1e-4
+    acc = d.clone()
+    kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out=acc, d=acc, beta=1.0, block_n=block_n)
+    assert _rel(acc, ref + d) < 1e-4
+
+
 def test_patchify_matches_reference():
     kf = _kf()
     img = torch.randn(3, 3, 64, 48, device=DEV)
