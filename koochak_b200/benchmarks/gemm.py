@@ -56,15 +56,17 @@ def linear_cases(name: str, M: int, block_n: int):
     }
 
 
-def ns_cases(c: int, batch: int = 12, r: int = 768):
+def ns_cases(c: int, batch: int = 12, r: int = 768, block_n: int = 0):
     from koochak_b200.ops import functional as kf
 
     X = torch.randn(batch, r, c, device="cuda").bfloat16()
     A = torch.randn(batch, r, r, device="cuda").bfloat16()
     return {
-        "XXt": (2.0 * batch * r * r * c, lambda: kf.gemm(X, X), lambda: torch.bmm(X, X.transpose(1, 2))),
-        "AA": (2.0 * batch * r ** 3, lambda: kf.gemm(A, A, d=A, alpha=2.0, beta=-4.0), lambda: torch.bmm(A, A)),
-        "BX": (2.0 * batch * r * r * c, lambda: kf.gemm(A, X, b_mn_major=True, d=X, beta=3.0),
+        "XXt": (2.0 * batch * r * r * c, lambda: kf.gemm(X, X, block_n=block_n),
+                lambda: torch.bmm(X, X.transpose(1, 2))),
+        "AA": (2.0 * batch * r ** 3, lambda: kf.gemm(A, A, d=A, alpha=2.0, beta=-4.0, block_n=block_n),
+               lambda: torch.bmm(A, A)),
+        "BX": (2.0 * batch * r * r * c, lambda: kf.gemm(A, X, b_mn_major=True, d=X, beta=3.0, block_n=block_n),
                lambda: torch.bmm(A, X)),
     }
 
@@ -117,7 +119,7 @@ def main(argv: List[str] | None = None) -> None:
     names = list(LINEAR) + ["ns768", "ns2304", "ns3072"] if args.case == "all" else [args.case]
     for name in names:
         if name.startswith("ns"):
-            cases = ns_cases(int(name[2:]))
+            cases = ns_cases(int(name[2:]), block_n=args.block_n)
             items = [(op, fl, a, b) for op, (fl, a, b) in cases.items()]
         else:
             fl, cases = linear_cases(name, args.tokens, args.block_n)

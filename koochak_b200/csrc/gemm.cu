@@ -1030,10 +1030,14 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     bn = (int)-block_n;
     pair_mode = true;
   } else {
+    // Relative time per unit of tile work, measured on the model shapes: an
+    // N=128 MMA keeps the tensor pipe far less busy than an N=256 one, and the
+    // 2-SM pair halves each SM's operand traffic.
     double best = 1e30;
     const int cand_bn[4] = {128, 256, 128, 256};
     const bool cand_pair[4] = {false, false, true, true};
-    const double factor[4] = {1.15, 1.0, 0.9, 0.8};
+    const double factor[4] = {1.6, 1.05, 1.6, 1.0};
+    const bool sk_ok = c.scalar_type() == at::kFloat && act == ACT_NONE && (K + 63) / 64 >= 8;
     for (int i = 0; i < 4; ++i) {
       const int w = cand_bn[i];
       const bool pm = cand_pair[i];
@@ -1041,8 +1045,10 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
       const int rows = pm ? 256 : 128;
       const int64_t t = batch * ((M + rows - 1) / rows) * ((N + w - 1) / w);
       const int64_t slots = pm ? sms_all / 2 : sms_all;
-      const int64_t waves = (t + slots - 1) / slots;
-      const double cost = double(waves) * (double(w) / 256.0) * factor[i];
+      // With stream-K available the work spreads evenly (plus a partial-tile
+      // overhead); otherwise whole waves count.
+      const double waves = sk_ok ? double(t) / double(slots) + 0.15 : double((t + slots - 1) / slots);
+      const double cost = waves * (double(w) / 256.0) * factor[i];
       if (cost < best - 1e-9) {
         best = cost;
         bn = w;
