@@ -1,0 +1,95 @@
+"""Memory-bound and attention kernels on the GPT-2 124M step shapes.
+
+Each case is timed with CUDA events after warm-up and reported with the
+bytes it must move (and the resulting bandwidth) or, for attention, its
+FLOPs. The attention cases are also timed on PyTorch's SDPA (the library
+attention on this GPU) for reference.
+
+    python -m koochak_b200.benchmarks.kernels                  # all cases
+    python -m koochak_b200.benchmarks.kernels --case norm_bwd
+"""
+
+from __future__ import annotations
+
+import argparse
+from typing import Callable, Dict, List, Tuple
+
+import torch
+
+from .gemm import time_ms
+
+M, C, H, S, B, V = 16384, 768, 12, 1024, 16, 50304
+
+
+def cases() -> Dict[str, Tuple[Callable[[], object], float, str]]:
+    from koochak_b200.ops import functional as kf
+
+    dev = "cuda"
+    x = torch.randn(M, C, device=dev)
+    w = torch.rand(C, device=dev) + 0.5
+    bias = torch.randn(C, device=dev)
+    dy16 = torch.randn(M, C, device=dev).bfloat16()
+    dres = torch.randn(M, C, device=dev)
+    _, mean, rstd = kf.norm_forward(x, w, bias, 1e-5, rms=False, out_dtype=torch.bfloat16)
+    out: Dict[str, Tuple[Callable[[], object], float, str]] = {}
+    out["norm_fwd"] = (lambda: kf.norm_forward(x, w, bias, 1e-5, rms=False, out_dtype=torch.bfloat16),
+                       M * C * (4 + 2) + M * 8, "bytes")
+    out["norm_bwd"] = (lambda: kf.norm_backward(dy16, x, w, mean, rstd, rms=False, dres=dres, dx_dtype=torch.float32,
+                                                want_lp=True),
+                       M * C * (2 + 4 + 4 + 4 + 2) + M * 8, "bytes")
+    x2 = torch.randn(8192, 2048, device=dev)
+    w2 = torch.rand(2048, device=dev) + 0.5
+    dy2 = torch.randn(8192, 2048, device=dev).bfloat16()
+    dr2 = torch.randn(8192, 2048, device=dev)
+    _, _, r2 = kf.norm_forward(x2, w2, None, 1e-5, rms=True, out_dtype=torch.bfloat16)
+    out["rmsnorm_bwd_2048"] = (lambda: kf.norm_backward(dy2, x2, w2, None, r2, rms=True, dres=dr2,
+                                                        dx_dtype=torch.float32, want_lp=True),
+                               8192 * 2048 * (2 + 4 + 4 + 4 + 2) + 8192 * 4, "bytes")
+    g3072 = torch.randn(M, 3072, device=dev).bfloat16()
+    out["bias_grad_3072"] = (lambda: kf.bias_grad(g3072), M * 3072 * 2, "bytes")
+    logits = torch.randn(M, V, device=dev).bfloat16()
+    tgt = torch.randint(0, 50257, (M,), device=dev)
+    out["ce_fwd"] = (lambda: kf.cross_entropy_forward(logits, tgt, 50257), M * V * 2, "bytes")
+    _, lse = kf.cross_entropy_forward(logits, tgt, 50257)
+    gscale = torch.ones(1, device=dev)
+    lg2 = logits.clone()
+    out["ce_bwd"] = (lambda: kf.cross_entropy_backward_(lg2, tgt, lse, gscale, 50257), M * V * 4, "bytes")
+    qkv = torch.randn(B, S, 3, H, 64, device=dev).bfloat16()
+    q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
+    o, lse_a = kf.flash_attention_forward(q, k, v, causal=True)
+    do = torch.randn_like(o)
+    fl_fwd = 4.0 * B * H * S * S * 64 / 2  # causal
+    out["attn_fwd"] = (lambda: kf.flash_attention_forward(q, k, v, causal=True), fl_fwd, "flop")
+    out["attn_bwd"] = (lambda: kf.flash_attention_backward(q, k, v, o, do, lse_a, causal=True), 2.5 * fl_fwd, "flop")
+    qt, kt, vt = (t.transpose(1, 2).contiguous().requires_grad_(True) for t in (q, k, v))
+    sd = torch.nn.functional.scaled_dot_product_attention
+
+    def sdpa_fwd():
+        with torch.no_grad():
+            return sd(qt, kt, vt, is_causal=True)
+
+    ot = sd(qt, kt, vt, is_causal=True)
+    gt = torch.randn_like(ot)
+    out["attn_fwd_sdpa"] = (sdpa_fwd, fl_fwd, "flop")
+    out["attn_bwd_sdpa"] = (lambda: torch.autograd.grad(ot, (qt, kt, vt), gt, retain_graph=True), 2.5 * fl_fwd,
+                            "flop")
+    return out
+
+
+def main(argv: List[str] | None = None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--case", default="all")
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args(argv)
+    torch.manual_seed(0)
+    for name, (fn, amount, kind) in cases().items():
+        if args.case != "all" and name != args.case:
+            continue
+        t = time_ms(fn, args.iters)
+        rate = amount / (t * 1e-3)
+        unit = f"{rate / 1e9:8.0f} GB/s" if kind == "bytes" else f"{rate / 1e12:8.0f} TF/s"
+        print(f"{name:18s} {t * 1e3:9.1f} us  {unit}", flush=True)
+
+
+if __name__ == "__main__":
+    main()

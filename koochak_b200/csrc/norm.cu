@@ -7,8 +7,9 @@
 // fp32 and saved for the backward pass.
 //
 // Backward writes dx (optionally adding an incoming residual gradient in the
-// same pass) and accumulates dgamma/dbeta per CTA in registers; a persistent
-// grid keeps the partial buffer at (#CTAs x C) and a second kernel reduces it.
+// same pass) and accumulates dgamma/dbeta per CTA (in shared memory for rows up
+// to 2560 wide, in registers beyond); a persistent grid keeps the partial
+// buffer at (#CTAs x C) and a second kernel reduces it.
 #include "host_utils.h"
 #include "sm100.cuh"
 #include "noalloc.h"
@@ -121,113 +122,178 @@ __global__ void __launch_bounds__(32 * kNormWarps)
 
 // dx = rstd * (w*dy - mean(w*dy) - xhat*mean(w*dy*xhat))     (LayerNorm)
 // dx = rstd * (w*dy - xhat*mean(w*dy*xhat))                   (RMSNorm)
-template <int VPT, typename TIn, typename TG, typename TDx, bool RMS>
+//
+// One warp per row. For rows of up to 1024 values every load of a row (x, dy
+// and the residual gradient) is issued before the row's reductions, so each
+// warp keeps a whole row in flight; wider rows read the residual gradient at
+// the store (registers would spill otherwise). With SMEM_ACC the per-column
+// sums for dw / db live in shared memory (one private row per warp) and the
+// weights are read from shared memory, which keeps the kernel near 100
+// registers (two CTAs, sixteen rows in flight, per SM); without it (very wide
+// rows) the sums stay in registers.
+template <int VPT, typename TIn, typename TG, typename TDx, bool RMS, bool SMEM_ACC>
 __global__ void __launch_bounds__(32 * kNormWarps)
     norm_bwd_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
                     const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
                     const TDx* __restrict__ dres, TDx* __restrict__ dx, TG* __restrict__ dx_lp,
                     float* __restrict__ dw_part, float* __restrict__ db_part, int M, int C) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float dw_acc[VPT];
-  float db_acc[VPT];
+  // Shared memory: [kNormWarps][C] dw sums, then (SMEM_ACC only) [kNormWarps][C]
+  // db sums and [C] weights.
+  extern __shared__ float red[];
+  float* sdw = red + warp * C;
+  float* sdb = red + (kNormWarps + warp) * C;
+  float* sw = red + 2 * kNormWarps * C;
+  constexpr bool kEarlyRes = VPT <= 32;
+  float dw_acc[SMEM_ACC ? 1 : VPT];
+  float db_acc[SMEM_ACC ? 1 : VPT];
+  float wv[SMEM_ACC ? 1 : VPT];
+  if constexpr (SMEM_ACC) {
+    for (int c = lane; c < C; c += 32) {
+      sdw[c] = 0.f;
+      sdb[c] = 0.f;
+    }
+    for (int c = threadIdx.x; c < C; c += blockDim.x) sw[c] = w[c];
+    __syncthreads();
+  } else {
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    dw_acc[i] = 0.f;
-    db_acc[i] = 0.f;
-  }
-  float wv[VPT];
+    for (int i = 0; i < VPT; ++i) dw_acc[i] = db_acc[i] = 0.f;
 #pragma unroll
-  for (int j = 0; j < VPT / 4; ++j) {
-    const int col = 4 * lane + 128 * j;
-    float q[4] = {0.f, 0.f, 0.f, 0.f};
-    if (col < C) load4<float>(w + col, q);
+    for (int j = 0; j < VPT / 4; ++j) {
+      const int col = 4 * lane + 128 * j;
+      float q[4] = {0.f, 0.f, 0.f, 0.f};
+      if (col < C) load4<float>(w + col, q);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) wv[4 * j + t] = q[t];
+      for (int t = 0; t < 4; ++t) wv[4 * j + t] = q[t];
+    }
   }
   for (int row = blockIdx.x * kNormWarps + warp; row < M; row += gridDim.x * kNormWarps) {
-    const float mean = RMS ? 0.f : mean_in[row];
-    const float rstd = rstd_in[row];
     const TIn* xr = x + (long long)row * C;
     const TG* gr = dy + (long long)row * C;
-    float xh[VPT], g[VPT];
+    const TDx* drr = dres ? dres + (long long)row * C : nullptr;
+    float xq[VPT], g[VPT], rq[kEarlyRes ? VPT : 4];
+#pragma unroll
+    for (int j = 0; j < VPT / 4; ++j) {
+      const int col = 4 * lane + 128 * j;
+      float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f}, r[4] = {0.f, 0.f, 0.f, 0.f};
+      if (col < C) {
+        load4<TIn>(xr + col, a);
+        load4<TG>(gr + col, b);
+        if (kEarlyRes && drr) load4<TDx>(drr + col, r);
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        xq[4 * j + t] = a[t];
+        g[4 * j + t] = b[t];
+        if constexpr (kEarlyRes) rq[4 * j + t] = r[t];
+      }
+    }
+    const float mean = RMS ? 0.f : mean_in[row];
+    const float rstd = rstd_in[row];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT / 4; ++j) {
       const int col = 4 * lane + 128 * j;
-      float xq[4] = {0.f, 0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f};
-      if (col < C) {
-        load4<TIn>(xr + col, xq);
-        load4<TG>(gr + col, gq);
-      }
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const int i = 4 * j + t;
-        xh[i] = (col < C) ? (xq[t] - mean) * rstd : 0.f;
-        g[i] = gq[t];
-        const float wg = wv[i] * g[i];
+        xq[i] = (col < C) ? (xq[i] - mean) * rstd : 0.f;  // x-hat from here on
+        float wi;
+        if constexpr (SMEM_ACC) wi = (col < C) ? sw[col + t] : 0.f;
+        else wi = wv[i];
+        const float wg = wi * g[i];
         s1 += wg;
-        s2 += wg * xh[i];
-        dw_acc[i] += g[i] * xh[i];
-        db_acc[i] += g[i];
+        s2 += wg * xq[i];
+        if constexpr (!SMEM_ACC) {
+          dw_acc[i] += g[i] * xq[i];
+          db_acc[i] += g[i];
+        }
+      }
+      if constexpr (SMEM_ACC) {
+        if (col < C) {
+          float4 a = *reinterpret_cast<float4*>(sdw + col);
+          float4 b = *reinterpret_cast<float4*>(sdb + col);
+          a.x += g[4 * j] * xq[4 * j];
+          a.y += g[4 * j + 1] * xq[4 * j + 1];
+          a.z += g[4 * j + 2] * xq[4 * j + 2];
+          a.w += g[4 * j + 3] * xq[4 * j + 3];
+          b.x += g[4 * j];
+          b.y += g[4 * j + 1];
+          b.z += g[4 * j + 2];
+          b.w += g[4 * j + 3];
+          *reinterpret_cast<float4*>(sdw + col) = a;
+          *reinterpret_cast<float4*>(sdb + col) = b;
+        }
       }
     }
     s1 = warp_sum(s1) / C;
     s2 = warp_sum(s2) / C;
     TDx* dxr = dx + (long long)row * C;
-    const TDx* drr = dres ? dres + (long long)row * C : nullptr;
 #pragma unroll
     for (int j = 0; j < VPT / 4; ++j) {
       const int col = 4 * lane + 128 * j;
       if (col < C) {
         float o[4];
-        float rq[4] = {0.f, 0.f, 0.f, 0.f};
-        if (drr) load4<TDx>(drr + col, rq);
+        float late[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!kEarlyRes && drr) load4<TDx>(drr + col, late);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int i = 4 * j + t;
-          const float wg = wv[i] * g[i];
-          o[t] = rstd * (wg - (RMS ? 0.f : s1) - xh[i] * s2) + rq[t];
+          float wi, r;
+          if constexpr (SMEM_ACC) wi = sw[col + t];
+          else wi = wv[i];
+          if constexpr (kEarlyRes) r = rq[i];
+          else r = late[t];
+          o[t] = rstd * (wi * g[i] - (RMS ? 0.f : s1) - xq[i] * s2) + r;
         }
         store4<TDx>(dxr + col, o);
         if (dx_lp) store4<TG>(dx_lp + (long long)row * C + col, o);
       }
     }
   }
-  // Per-warp partials -> shared memory -> one row of partials per CTA.
-  extern __shared__ float red[];  // [kNormWarps][C]
-#pragma unroll
-  for (int j = 0; j < VPT / 4; ++j) {
-    const int col = 4 * lane + 128 * j;
-    if (col < C) {
-#pragma unroll
-      for (int t = 0; t < 4; ++t) red[warp * C + col + t] = dw_acc[4 * j + t];
-    }
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < kNormWarps; ++k) s += red[k * C + c];
-    dw_part[(long long)blockIdx.x * C + c] = s;
-  }
-  if (!RMS && db_part != nullptr) {
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < VPT / 4; ++j) {
-      const int col = 4 * lane + 128 * j;
-      if (col < C) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t) red[warp * C + col + t] = db_acc[4 * j + t];
-      }
-    }
+  if constexpr (SMEM_ACC) {
     __syncthreads();
     for (int c = threadIdx.x; c < C; c += blockDim.x) {
-      float s = 0.f;
+      float a = 0.f, b = 0.f;
 #pragma unroll
-      for (int k = 0; k < kNormWarps; ++k) s += red[k * C + c];
-      db_part[(long long)blockIdx.x * C + c] = s;
+      for (int k = 0; k < kNormWarps; ++k) {
+        a += red[k * C + c];
+        b += red[(kNormWarps + k) * C + c];
+      }
+      dw_part[(long long)blockIdx.x * C + c] = a;
+      if (!RMS && db_part != nullptr) db_part[(long long)blockIdx.x * C + c] = b;
+    }
+  } else {
+    // Register sums -> one [kNormWarps][C] shared buffer: dw first, then db.
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      if (pass == 1 && (RMS || db_part == nullptr)) break;
+      if (pass == 1) __syncthreads();
+#pragma unroll
+      for (int j = 0; j < VPT / 4; ++j) {
+        const int col = 4 * lane + 128 * j;
+        if (col < C) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) sdw[col + t] = pass == 0 ? dw_acc[4 * j + t] : db_acc[4 * j + t];
+        }
+      }
+      __syncthreads();
+      float* dst = pass == 0 ? dw_part : db_part;
+      for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float a = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormWarps; ++k) a += red[k * C + c];
+        dst[(long long)blockIdx.x * C + c] = a;
+      }
     }
   }
+}
+
+// Whether norm_bwd_kernel keeps its column sums in shared memory for this row
+// width, and the dynamic shared memory it then needs.
+static inline bool norm_bwd_smem_acc(int C) { return C <= 2560; }
+static inline int norm_bwd_smem_bytes(int C) {
+  return (norm_bwd_smem_acc(C) ? (2 * kNormWarps + 1) : kNormWarps) * C * (int)sizeof(float);
 }
 
 // out[c] (+)= sum_r part[r, c]; a CTA owns 32 columns, 8 row groups per column.
@@ -326,7 +392,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
   const int dev = x.get_device();
-  const int grid = std::max(1, std::min(num_sms(dev) * 4, (M + kNormWarps - 1) / kNormWarps));
+  const int grid = std::max(1, std::min(num_sms(dev) * 2, (M + kNormWarps - 1) / kNormWarps));
   KB_CHECK(workspace.scalar_type() == at::kFloat && workspace.numel() >= 2LL * grid * C, "norm bwd: workspace too small");
   float* dw_part = workspace.data_ptr<float>();
   float* db_part = rms ? nullptr : dw_part + (long long)grid * C;
@@ -335,36 +401,39 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const bool has_res = dres.has_value() && dres->defined();
   KB_CHECK(dx.scalar_type() == x.scalar_type(), "norm bwd: dx must have the dtype of x");
   if (has_res) KB_CHECK(dres->scalar_type() == dx.scalar_type() && dres->is_contiguous(), "dres must match dx");
-  const int smem = kNormWarps * C * (int)sizeof(float);
+  const int smem = norm_bwd_smem_bytes(C);
+  const bool sacc = norm_bwd_smem_acc(C);
   with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
     with_type(x.scalar_type(), [&](auto tin) {
       using TIn = decltype(tin);
       with_lp_type(dy.scalar_type(), [&](auto tg) {
         using TG = decltype(tg);
-        {
-          using TDx = TIn;
-          const TDx* rp = has_res ? (const TDx*)dres->data_ptr() : nullptr;
-          TG* lp = nullptr;
-          if (dx_lp.has_value() && dx_lp->defined()) {
-            KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
-                     "dx_lp must be contiguous, of dy's dtype and dx's size");
-            lp = (TG*)dx_lp->data_ptr();
-          }
-          if (smem > 48 * 1024) {
-            KB_CUDA_CHECK(cudaFuncSetAttribute(norm_bwd_kernel<V, TIn, TG, TDx, true>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-            KB_CUDA_CHECK(cudaFuncSetAttribute(norm_bwd_kernel<V, TIn, TG, TDx, false>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-          }
-          if (rms)
-            norm_bwd_kernel<V, TIn, TG, TDx, true><<<grid, 32 * kNormWarps, smem, stream>>>(
-                (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), nullptr,
-                rstd.data_ptr<float>(), rp, (TDx*)dx.data_ptr(), lp, dw_part, nullptr, M, C);
-          else
-            norm_bwd_kernel<V, TIn, TG, TDx, false><<<grid, 32 * kNormWarps, smem, stream>>>(
-                (const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(), mp, rstd.data_ptr<float>(),
-                rp, (TDx*)dx.data_ptr(), lp, dw_part, db_part, M, C);
+        using TDx = TIn;
+        const TDx* rp = has_res ? (const TDx*)dres->data_ptr() : nullptr;
+        TG* lp = nullptr;
+        if (dx_lp.has_value() && dx_lp->defined()) {
+          KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
+                   "dx_lp must be contiguous, of dy's dtype and dx's size");
+          lp = (TG*)dx_lp->data_ptr();
+        }
+        auto go = [&](auto rms_c, auto sacc_c) {
+          constexpr bool R = decltype(rms_c)::value;
+          constexpr bool SA = decltype(sacc_c)::value;
+          auto kern = norm_bwd_kernel<V, TIn, TG, TDx, R, SA>;
+          if (smem > 48 * 1024)
+            KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+          kern<<<grid, 32 * kNormWarps, smem, stream>>>((const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(),
+                                                        w.data_ptr<float>(), R ? nullptr : mp, rstd.data_ptr<float>(),
+                                                        rp, (TDx*)dx.data_ptr(), lp, dw_part, R ? nullptr : db_part,
+                                                        M, C);
+        };
+        if (rms) {
+          if (sacc) go(std::true_type{}, std::true_type{});
+          else go(std::true_type{}, std::false_type{});
+        } else {
+          if (sacc) go(std::false_type{}, std::true_type{});
+          else go(std::false_type{}, std::false_type{});
         }
       });
     });
@@ -381,7 +450,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
 }
 
 int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
-  const int grid = std::max<int64_t>(1, std::min<int64_t>(num_sms((int)device) * 4, (M + kNormWarps - 1) / kNormWarps));
+  const int grid = std::max<int64_t>(1, std::min<int64_t>(num_sms((int)device) * 2, (M + kNormWarps - 1) / kNormWarps));
   return 2LL * grid * C;
 }
 
@@ -456,16 +525,18 @@ extern "C" __attribute__((visibility("default"))) int kb_layernorm_backward_noal
   int sms = 0;
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (err != cudaSuccess) return (int)err;
-  long long grid = std::min<long long>((long long)sms * 4, (M + kNormWarps - 1) / kNormWarps);
+  long long grid = std::min<long long>((long long)sms * 2, (M + kNormWarps - 1) / kNormWarps);
   grid = std::min<long long>(grid, kNoAllocScratchFloats / (2LL * C));
   grid = std::max<long long>(grid, 1);
   float* dw_part = scratch;
   float* db_part = scratch + grid * C;
-  const int smem = kNormWarps * C * (int)sizeof(float);
+  const int smem = norm_bwd_smem_bytes(C);
+  const bool sacc = norm_bwd_smem_acc(C);
   bool launched = false;
   with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
-    auto kern = norm_bwd_kernel<V, float, __nv_bfloat16, float, false>;
+    auto kern = sacc ? norm_bwd_kernel<V, float, __nv_bfloat16, float, false, true>
+                     : norm_bwd_kernel<V, float, __nv_bfloat16, float, false, false>;
     if (smem > 48 * 1024) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
     }
