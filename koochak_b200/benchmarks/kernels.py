@@ -59,10 +59,31 @@ def cases() -> Dict[str, Tuple[Callable[[], object], float, str]]:
     o, lse_a = kf.flash_attention_forward(q, k, v, causal=True)
     do = torch.randn_like(o)
     fl_fwd = 4.0 * B * H * S * S * 64 / 2  # causal
+    sd = torch.nn.functional.scaled_dot_product_attention
     out["attn_fwd"] = (lambda: kf.flash_attention_forward(q, k, v, causal=True), fl_fwd, "flop")
+    from koochak_b200.ops import native
+
+    def fwd_mma_sync():
+        native().attention_set_impl(1)
+        try:
+            return kf.flash_attention_forward(q, k, v, causal=True)
+        finally:
+            native().attention_set_impl(0)
+
+    out["attn_fwd_mma_sync"] = (fwd_mma_sync, fl_fwd, "flop")
+    qkv2 = torch.randn(4, 4096, 3, 16, 128, device=dev).bfloat16()
+    q2, k2, v2 = qkv2[:, :, 0], qkv2[:, :, 1], qkv2[:, :, 2]
+    fl2 = 4.0 * 4 * 16 * 4096 * 4096 * 128
+    out["attn_fwd_d128_s4096"] = (lambda: kf.flash_attention_forward(q2, k2, v2, causal=False), fl2, "flop")
+    q2t, k2t, v2t = (t.transpose(1, 2).contiguous() for t in (q2, k2, v2))
+
+    def sdpa_fwd2():
+        with torch.no_grad():
+            return sd(q2t, k2t, v2t)
+
+    out["attn_fwd_d128_s4096_sdpa"] = (sdpa_fwd2, fl2, "flop")
     out["attn_bwd"] = (lambda: kf.flash_attention_backward(q, k, v, o, do, lse_a, causal=True), 2.5 * fl_fwd, "flop")
     qt, kt, vt = (t.transpose(1, 2).contiguous().requires_grad_(True) for t in (q, k, v))
-    sd = torch.nn.functional.scaled_dot_product_attention
 
     def sdpa_fwd():
         with torch.no_grad():

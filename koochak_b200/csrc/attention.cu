@@ -554,6 +554,13 @@ static void launch_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   KB_LAUNCHED();
 }
 
+bool flash_attention_forward_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                                at::Tensor& lse, double scale, bool causal, cudaStream_t s);
+
+// 0: tcgen05 forward where the shape allows it (default); 1: the mma.sync kernels.
+static int g_attn_impl = 0;
+void attention_set_impl(int64_t impl) { g_attn_impl = (int)impl; }
+
 void flash_attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                              at::Tensor& lse, double scale, bool causal) {
   const int64_t D = q.size(3);
@@ -567,6 +574,7 @@ void flash_attention_forward(const at::Tensor& q, const at::Tensor& k, const at:
            "lse must be fp32 [B, H, S]");
   const c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  if (g_attn_impl == 0 && flash_attention_forward_tc(q, k, v, o, lse, scale, causal, s)) return;
   const bool f16 = q.scalar_type() == at::kHalf;
   const float sc = (float)scale;
 #define KB_FWD(DD, CC, FF) launch_fwd<DD, CC, FF>(q, k, v, o, lse, sc, s)
@@ -660,6 +668,8 @@ void flash_attention_backward(const at::Tensor& q, const at::Tensor& k, const at
 }
 
 void register_attention_ops(pybind11::module& m) {
+  m.def("attention_set_impl", &attention_set_impl,
+        "attention forward implementation: 0 = tcgen05 (default), 1 = mma.sync kernels");
   m.def("flash_attention_forward", &flash_attention_forward);
   m.def("flash_attention_backward", &flash_attention_backward);
 }

@@ -98,17 +98,32 @@ def test_norm_forward_backward(C, rms):
         assert _rel(db, br.grad) < 1e-3
 
 
+@pytest.fixture(params=["tcgen05", "mma_sync"])
+def attn_impl(request):
+    from koochak_b200.ops import native
+
+    native().attention_set_impl(0 if request.param == "tcgen05" else 1)
+    yield request.param
+    native().attention_set_impl(0)
+
+
 @pytest.mark.parametrize("B,S,H,D,causal", [(2, 256, 4, 64, True), (2, 200, 3, 64, False), (1, 384, 2, 128, True),
-                                            (3, 197, 2, 64, False), (1, 130, 2, 128, False)])
-def test_flash_attention(B, S, H, D, causal):
+                                            (3, 197, 2, 64, False), (1, 130, 2, 128, False),
+                                            (1, 1100, 2, 64, True), (1, 700, 1, 128, False)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_flash_attention(B, S, H, D, causal, dtype, attn_impl):
     kf = _kf()
     torch.manual_seed(3)
-    qkv = torch.randn(B, S, 3, H, D, device=DEV).bfloat16()
+    qkv = torch.randn(B, S, 3, H, D, device=DEV).to(dtype)
     q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
     o, lse = kf.flash_attention_forward(q, k, v, causal=causal)
     qr, kr, vr = (t.float().detach().requires_grad_(True) for t in (q, k, v))
     ref = kf.attention_ref(qr, kr, vr, causal=causal)
     assert _rel(o, ref) < 2e-2
+    sc = torch.einsum("bqhd,bkhd->bhqk", qr, kr) / math.sqrt(D)
+    if causal:
+        sc = sc.masked_fill(torch.ones(S, S, device=DEV, dtype=torch.bool).triu(1), float("-inf"))
+    assert (lse - torch.logsumexp(sc, -1)).abs().max().item() < 2e-2
     do = torch.randn_like(o)
     ref.backward(do.float())
     dqkv = torch.empty_like(qkv)
