@@ -39,10 +39,10 @@ namespace kb {
 constexpr int kTcBM = 128;        // query rows per tile (two tiles per CTA)
 constexpr int kTcBN = 128;        // keys per step
 constexpr int kTcThreads = 384;   // warpgroup 0: producer, MMA (+2 idle); warpgroups 1, 2: softmax
-// Register split (launch: 168 per thread): warpgroup 0 gives back down to 56,
-// the softmax warpgroups take 224 (56*128 + 2*224*128 = 384*168).
-constexpr int kTcRegsCtl = 56;
-constexpr int kTcRegsSoftmax = 224;
+// Register split (launch: 168 per thread): warpgroup 0 gives back down to 72,
+// the softmax warpgroups take 216 (72*128 + 2*216*128 = 384*168).
+constexpr int kTcRegsCtl = 72;
+constexpr int kTcRegsSoftmax = 216;
 constexpr float kRescaleLog2 = 8.f;
 
 template <int D>
@@ -50,7 +50,8 @@ struct TcFwdCfg {
   static constexpr int kChunks = D / 64;                 // 64-wide (128-byte) column chunks of a row
   static constexpr int kTileBytes = kTcBN * D * 2;       // one Q, K or V tile
   static constexpr int kStages = D == 64 ? 4 : 2;        // K/V ring depth
-  static constexpr int kSmemBytes = (2 + 2 * kStages) * kTileBytes + 1024 + 256;
+  static constexpr int kQBufs = D == 64 ? 2 : 1;         // Q buffers (of two tiles): the next item's Q prefetches
+  static constexpr int kSmemBytes = (2 * kQBufs + 2 * kStages) * kTileBytes + 1024 + 256;
   static constexpr int kOCol = 2 * kTcBN;                // TMEM column of O_0
 };
 
@@ -100,7 +101,7 @@ __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
 struct TcFwdArgs {
   uint16_t* o;
   float* lse;
-  int H, Sq, Sk;
+  int B, H, Sq, Sk;
   long long o_ld, o_bs;
   float scale_log2;
   int* status;
@@ -108,7 +109,11 @@ struct TcFwdArgs {
 
 // One softmax step of one row: reads S (128 columns at s_tm) into registers,
 // updates the row's reference maximum m (scaled, log2 units) and sum l,
-// rescales O when m moves, and writes P over S's first 64 columns.
+// writes P over S's first 64 columns, and rescales O when m moved (after P,
+// when the scores no longer occupy registers; O is not read by the tensor
+// cores until this step's P is published, and it holds every earlier P V
+// product: the completion of this block's S MMA implies that of the previous
+// P V MMA).
 template <int D, bool MASK, bool F16>
 __device__ __forceinline__ void softmax_step(uint32_t s_tm, uint32_t o_tm, int key0, int key_lim, float scale_log2,
                                              bool first, float& m, float& l) {
@@ -137,18 +142,6 @@ __device__ __forceinline__ void softmax_step(uint32_t s_tm, uint32_t o_tm, int k
     factor = ex2_approx(m - mxs);  // 0 while m is -inf
     m = mxs;
   }
-  if (!first && __any_sync(0xffffffffu, upd)) {
-    // O_t (which holds every earlier P V product) takes the new reference.
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      uint32_t ov[32];
-      tmem_ld_32x32b_x32(o_tm + 32 * c, ov);
-      tmem_wait_ld_dep(ov);
-#pragma unroll
-      for (int t = 0; t < 32; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * factor);
-      tmem_st_32x32b_x32(o_tm + 32 * c, ov);
-    }
-  }
   l *= factor;
   // Masked scores are -inf here, so their exponentials are exactly 0.
   const float mneg = m == -INFINITY ? 0.f : -m;
@@ -171,8 +164,42 @@ __device__ __forceinline__ void softmax_step(uint32_t s_tm, uint32_t o_tm, int k
     }
     tmem_st_32x32b_x16(s_tm + 16 * c, pk);
   }
+  if (!first && __any_sync(0xffffffffu, upd)) {
+    // O_t (which holds every earlier P V product) takes the new reference.
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t ov[32];
+      tmem_ld_32x32b_x32(o_tm + 32 * c, ov);
+      tmem_wait_ld_dep(ov);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) ov[t] = __float_as_uint(__uint_as_float(ov[t]) * factor);
+      tmem_st_32x32b_x32(o_tm + 32 * c, ov);
+    }
+  }
   tmem_wait_st();
   l += (rs0.x + rs0.y) + (rs1.x + rs1.y);
+}
+
+// Work item `idx` of a persistent CTA: a 256-row query block of one (batch,
+// head). Causal items are ordered by decreasing cost (most key blocks first),
+// so the static round-robin assignment over CTAs stays balanced.
+struct TcItem {
+  int b, h, bh, q0, n0, n1;  // n0 / n1: key blocks that query tile 0 / 1 needs (n0 <= n1)
+};
+
+template <bool CAUSAL>
+__device__ __forceinline__ TcItem tc_item(int idx, int H, int BH, int Sq, int Sk) {
+  const int num_qb = (Sq + 2 * kTcBM - 1) / (2 * kTcBM);
+  TcItem it;
+  const int qb = CAUSAL ? num_qb - 1 - idx / BH : idx / BH;
+  it.bh = idx % BH;
+  it.b = it.bh / H;
+  it.h = it.bh % H;
+  it.q0 = qb * 2 * kTcBM;
+  const int nk = (Sk + kTcBN - 1) / kTcBN;
+  it.n0 = CAUSAL ? min(nk, (it.q0 + kTcBM - 1) / kTcBN + 1) : nk;
+  it.n1 = CAUSAL ? min(nk, (it.q0 + 2 * kTcBM - 1) / kTcBN + 1) : nk;
+  return it;
 }
 
 template <int D, bool CAUSAL, bool F16>
@@ -181,36 +208,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const __grid_constant__ CUtensorMap tv, const TcFwdArgs a) {
   using Cfg = TcFwdCfg<D>;
   constexpr int ST = Cfg::kStages;
+  constexpr int QB = Cfg::kQBufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                              // two tiles
-  uint8_t* sK = sQ + 2 * Cfg::kTileBytes;
+  uint8_t* sQ = smem;                              // QB buffers of two tiles
+  uint8_t* sK = sQ + QB * 2 * Cfg::kTileBytes;
   uint8_t* sV = sK + ST * Cfg::kTileBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * Cfg::kTileBytes);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;
-  uint64_t* v_full = k_full + ST;
-  uint64_t* kv_empty = v_full + ST;
-  uint64_t* s_full = kv_empty + ST;   // [2], per tile
-  uint64_t* p_full = s_full + 2;      // [2], per tile (4 softmax warps arrive)
-  uint64_t* o_done = p_full + 2;      // [2], per tile: last P V product complete
-  uint64_t* drain = o_done + 2;
+  uint64_t* q_full = bars;             // [QB]
+  uint64_t* q_empty = q_full + QB;     // [QB]: every S MMA of the item that used the buffer is done
+  uint64_t* k_full = q_empty + QB;     // [ST]
+  uint64_t* v_full = k_full + ST;      // [ST]
+  uint64_t* kv_empty = v_full + ST;    // [ST]
+  uint64_t* s_full = kv_empty + ST;    // [2], per tile
+  uint64_t* p_full = s_full + 2;       // [2], per tile (4 softmax warps arrive)
+  uint64_t* o_done = p_full + 2;       // [2], per tile: the item's last P V product is complete
+  uint64_t* o_empty = o_done + 2;      // [2], per tile: the epilogue has read O (4 warps arrive)
+  uint64_t* drain = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_qb = (a.Sq + 2 * kTcBM - 1) / (2 * kTcBM);
-  const int qb = CAUSAL ? (num_qb - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-  const int bh = blockIdx.y;
-  const int b = bh / a.H, h = bh % a.H;
-  const int q0 = qb * 2 * kTcBM;
-  const int nk = (a.Sk + kTcBN - 1) / kTcBN;
-  // Key blocks each query tile needs (tile 0 never needs more than tile 1).
-  const int n_t0 = CAUSAL ? min(nk, (q0 + kTcBM - 1) / kTcBN + 1) : nk;
-  const int n_max = CAUSAL ? min(nk, (q0 + 2 * kTcBM - 1) / kTcBN + 1) : nk;
+  const int BH = a.B * a.H;
+  const int n_items = ((a.Sq + 2 * kTcBM - 1) / (2 * kTcBM)) * BH;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < QB; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -220,6 +246,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_empty[i], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -236,33 +263,55 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kTcRegsCtl));
-   if (warp == 0) {
-    if (lane == 0) {
+    if (warp == 0 && lane == 0) {
       // ---------------------------------------------------------------- producer
-      uint32_t armed = 0, armed_par = 0;
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kTileBytes);
+      uint32_t armed = 0, armed_par = 0, q_armed = 0, q_par = 0;
+      bool ok = true;
+      int kv_it = 0, n_it = 0;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ++n_it) {
+        const TcItem it = tc_item<CAUSAL>(idx, a.H, BH, a.Sq, a.Sk);
+        const int qbuf = n_it % QB;
+        const uint32_t qph = (n_it / QB) & 1;
+        if (!mbar_wait(&q_empty[qbuf], qph ^ 1, abort_flag, a.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&q_full[qbuf], 2 * Cfg::kTileBytes);
+        q_armed |= 1u << qbuf;
+        q_par = (q_par & ~(1u << qbuf)) | (qph << qbuf);
+        uint8_t* q_dst = sQ + qbuf * 2 * Cfg::kTileBytes;
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int c = 0; c < Cfg::kChunks; ++c)
-          tma_load_4d(&tq, q_full, sQ + t * Cfg::kTileBytes + c * (kTcBM * 128), 64 * c, q0 + t * kTcBM, h, b);
-      for (int j = 0; j < n_max; ++j) {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, a.status, kStatusTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
-        mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
-        armed |= 1u << st;
-        armed_par = (armed_par & ~(1u << st)) | (ph << st);
+          for (int c = 0; c < Cfg::kChunks; ++c)
+            tma_load_4d(&tq, &q_full[qbuf], q_dst + t * Cfg::kTileBytes + c * (kTcBM * 128), 64 * c,
+                        it.q0 + t * kTcBM, it.h, it.b);
+        for (int j = 0; j < it.n1; ++j, ++kv_it) {
+          const int st = kv_it % ST;
+          const uint32_t ph = (kv_it / ST) & 1;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, a.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
+          mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
+          armed |= 1u << st;
+          armed_par = (armed_par & ~(1u << st)) | (ph << st);
 #pragma unroll
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          tma_load_4d(&tk, &k_full[st], sK + st * Cfg::kTileBytes + c * (kTcBN * 128), 64 * c, j * kTcBN, h, b);
-          tma_load_4d(&tv, &v_full[st], sV + st * Cfg::kTileBytes + c * (kTcBN * 128), 64 * c, j * kTcBN, h, b);
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            tma_load_4d(&tk, &k_full[st], sK + st * Cfg::kTileBytes + c * (kTcBN * 128), 64 * c, j * kTcBN, it.h,
+                        it.b);
+            tma_load_4d(&tv, &v_full[st], sV + st * Cfg::kTileBytes + c * (kTcBN * 128), 64 * c, j * kTcBN, it.h,
+                        it.b);
+          }
         }
       }
-      // Every issued copy must land before the CTA may exit.
+      // Every issued copy must land before the CTA may exit (the last arming
+      // of each barrier is the newest phase, so waiting on it covers the rest).
       volatile int never = 0;
-      mbar_wait(q_full, 0, &never, a.status, kStatusTimeoutDrain);
+      for (int i = 0; i < QB; ++i)
+        if (q_armed & (1u << i))
+          if (!mbar_wait(&q_full[i], (q_par >> i) & 1u, &never, a.status, kStatusTimeoutDrain)) break;
       for (int s = 0; s < ST; ++s) {
         if (armed & (1u << s)) {
           const uint32_t ph = (armed_par >> s) & 1u;
@@ -270,58 +319,77 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (!mbar_wait(&v_full[s], ph, &never, a.status, kStatusTimeoutDrain)) break;
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_s = idesc_f16(kTcBM, kTcBN, F16, false, false);
       constexpr uint32_t idesc_o = idesc_f16(kTcBM, D, F16, false, true);
-      bool ok = mbar_wait(q_full, 0, abort_flag, a.status, kStatusTimeoutMma);
-      bool issued = false;
-      auto issue_s = [&](int j, int t) -> bool {
-        const int st = j % ST;
-        if (!mbar_wait(&k_full[st], (j / ST) & 1, abort_flag, a.status, kStatusTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + t * Cfg::kTileBytes);
-        const uint32_t k_addr = smem_u32(sK + st * Cfg::kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (kTcBN * 128) + (kk & 3) * 32;  // chunk, then 32 B per K=16 step
-          umma_f16_ss(tmem + t * kTcBN, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
-                      idesc_s, kk != 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-        issued = true;
-        return true;
-      };
-      if (ok) ok = issue_s(0, 0);
-      if (ok) ok = issue_s(0, 1);
-      for (int j = 0; j < n_max && ok; ++j) {
-        const int st = j % ST;
-        if (!mbar_wait(&v_full[st], (j / ST) & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+      bool ok = true, issued = false;
+      int kv_it = 0, n_it = 0;
+      uint32_t p_cnt0 = 0, p_cnt1 = 0;
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ++n_it) {
+        const TcItem it = tc_item<CAUSAL>(idx, a.H, BH, a.Sq, a.Sk);
+        const int qbuf = n_it % QB;
+        if (!mbar_wait(&q_full[qbuf], (n_it / QB) & 1, abort_flag, a.status, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
-        const uint32_t v_addr = smem_u32(sV + st * Cfg::kTileBytes);
+        const uint32_t q_base = smem_u32(sQ + qbuf * 2 * Cfg::kTileBytes);
+        auto issue_s = [&](int kvi, int t) -> bool {
+          const int st = kvi % ST;
+          if (!mbar_wait(&k_full[st], (kvi / ST) & 1, abort_flag, a.status, kStatusTimeoutMma)) return false;
+          tc_fence_after();
+          const uint32_t q_addr = q_base + t * Cfg::kTileBytes;
+          const uint32_t k_addr = smem_u32(sK + st * Cfg::kTileBytes);
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if ((t == 0 ? n_t0 : n_max) <= j || !ok) continue;
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag, a.status, kStatusTimeoutMma)) {
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kTcBN * 128) + (kk & 3) * 32;  // chunk, then 32 B per K=16 step
+            umma_f16_ss(tmem + t * kTcBN, sw128_desc(q_addr + off, 16, 1024), sw128_desc(k_addr + off, 16, 1024),
+                        idesc_s, kk != 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[t]);
+          issued = true;
+          return true;
+        };
+        if (!issue_s(kv_it, 0) || !issue_s(kv_it, 1)) {
+          ok = false;
+          break;
+        }
+        if (it.n1 == 1) umma_commit(&q_empty[qbuf]);
+        for (int j = 0; j < it.n1 && ok; ++j, ++kv_it) {
+          const int st = kv_it % ST;
+          if (!mbar_wait(&v_full[st], (kv_it / ST) & 1, abort_flag, a.status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
-          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sV + st * Cfg::kTileBytes);
 #pragma unroll
-          for (int kk = 0; kk < kTcBN / 16; ++kk)
-            umma_f16_ts(tmem + Cfg::kOCol + t * D, tmem + t * kTcBN + kk * 8,
-                        sw128_desc(v_addr + kk * 2048, kTcBN * 128, 1024), idesc_o, (j | kk) != 0 ? 1u : 0u);
-          if (j + 1 < (t == 0 ? n_t0 : n_max)) {
-            if (!issue_s(j + 1, t)) ok = false;
-          } else {
-            umma_commit(&o_done[t]);
+          for (int t = 0; t < 2; ++t) {
+            const int n = t == 0 ? it.n0 : it.n1;
+            if (j >= n || !ok) continue;
+            uint32_t& p_cnt = t == 0 ? p_cnt0 : p_cnt1;
+            if (!mbar_wait(&p_full[t], p_cnt & 1, abort_flag, a.status, kStatusTimeoutMma) ||
+                (j == 0 && !mbar_wait(&o_empty[t], (n_it & 1) ^ 1, abort_flag, a.status, kStatusTimeoutMma))) {
+              ok = false;
+              break;
+            }
+            ++p_cnt;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kTcBN / 16; ++kk)
+              umma_f16_ts(tmem + Cfg::kOCol + t * D, tmem + t * kTcBN + kk * 8,
+                          sw128_desc(v_addr + kk * 2048, kTcBN * 128, 1024), idesc_o, (j | kk) != 0 ? 1u : 0u);
+            if (j + 1 < n) {
+              if (!issue_s(kv_it + 1, t)) {
+                ok = false;
+                break;
+              }
+              if (t == 1 && j + 2 == it.n1) umma_commit(&q_empty[qbuf]);
+            } else {
+              umma_commit(&o_done[t]);
+            }
           }
+          umma_commit(&kv_empty[st]);
         }
-        umma_commit(&kv_empty[st]);
       }
       if (issued) {
         umma_commit(drain);
@@ -329,44 +397,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_wait(drain, 0, &never, a.status, kStatusTimeoutDrain);
       }
     }
-   }
     tc_fence_before();
     named_bar_sync(1, kTcThreads);
     if (warp == 1) tmem_dealloc(tmem, 512);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTcRegsSoftmax));
-    // ---------------------------------------------------------------- softmax
+    // ---------------------------------------------------------------- softmax + epilogue
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile == TMEM lane
-    const int qrow = q0 + t * kTcBM + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_tm = tmem + lane_off + t * kTcBN;
     const uint32_t o_tm = tmem + lane_off + Cfg::kOCol + t * D;
-    const int n = t == 0 ? n_t0 : n_max;
-    const int row_first = q0 + t * kTcBM;  // first query row of the tile
-    float m = -INFINITY, l = 0.f;
+    uint32_t s_cnt = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1, abort_flag, a.status, kStatusTimeoutEpilogue)) {
+    int n_it = 0;
+    for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x, ++n_it) {
+      const TcItem it = tc_item<CAUSAL>(idx, a.H, BH, a.Sq, a.Sk);
+      const int n = t == 0 ? it.n0 : it.n1;
+      const int row_first = it.q0 + t * kTcBM;  // first query row of the tile
+      const int qrow = row_first + r;
+      const int key_lim = CAUSAL ? min(a.Sk, qrow + 1) : a.Sk;
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j, ++s_cnt) {
+        if (!mbar_wait(&s_full[t], s_cnt & 1, abort_flag, a.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int key0 = j * kTcBN;
+        const bool need_mask = (key0 + kTcBN > a.Sk) || (CAUSAL && key0 + kTcBN - 1 > row_first);
+        if (need_mask) softmax_step<D, true, F16>(s_tm, o_tm, key0, key_lim, a.scale_log2, j == 0, m, l);
+        else softmax_step<D, false, F16>(s_tm, o_tm, key0, key_lim, a.scale_log2, j == 0, m, l);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      }
+      if (!ok || !mbar_wait(&o_done[t], n_it & 1, abort_flag, a.status, kStatusTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int key0 = j * kTcBN;
-      const bool need_mask = (key0 + kTcBN > a.Sk) || (CAUSAL && key0 + kTcBN - 1 > row_first);
-      const int key_lim = CAUSAL ? min(a.Sk, qrow + 1) : a.Sk;
-      if (need_mask) softmax_step<D, true, F16>(s_tm, o_tm, key0, key_lim, a.scale_log2, j == 0, m, l);
-      else softmax_step<D, false, F16>(s_tm, o_tm, key0, key_lim, a.scale_log2, j == 0, m, l);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    }
-    if (ok && !mbar_wait(&o_done[t], 0, abort_flag, a.status, kStatusTimeoutEpilogue)) ok = false;
-    if (ok) {
-      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* orow = a.o + (long long)b * a.o_bs + (long long)qrow * a.o_ld + (long long)h * D;
+      uint16_t* orow = a.o + (long long)it.b * a.o_bs + (long long)qrow * a.o_ld + (long long)it.h * D;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
@@ -384,9 +457,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[t]);
       if (qrow < a.Sq) {
         const float l2 = (m == -INFINITY || l <= 0.f) ? -INFINITY : (m + log2f(l));
-        a.lse[(long long)bh * a.Sq + qrow] = l2 * 0.6931471805599453f;
+        a.lse[(long long)it.bh * a.Sq + qrow] = l2 * 0.6931471805599453f;
       }
     }
     if (!ok) *abort_flag = 1;
@@ -415,6 +491,7 @@ static void launch_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Te
   TcFwdArgs args;
   args.o = (uint16_t*)o.data_ptr();
   args.lse = lse.data_ptr<float>();
+  args.B = B;
   args.H = H;
   args.Sq = Sq;
   args.Sk = Sk;
@@ -428,7 +505,8 @@ static void launch_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Te
     KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     set = true;
   }
-  dim3 grid((Sq + 2 * kTcBM - 1) / (2 * kTcBM), B * H);
+  const long long items = (long long)((Sq + 2 * kTcBM - 1) / (2 * kTcBM)) * B * H;
+  const int grid = (int)std::min<long long>(items, num_sms(q.get_device()));
   kern<<<grid, kTcThreads, Cfg::kSmemBytes, s>>>(tq, tk, tv, args);
   KB_LAUNCHED();
 }
