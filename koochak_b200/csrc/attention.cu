@@ -554,12 +554,19 @@ static void launch_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   KB_LAUNCHED();
 }
 
+bool flash_attention_backward_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                 const at::Tensor& dout, const at::Tensor& lse, const float* delta, float* dq_acc,
+                                 at::Tensor& dk, at::Tensor& dv, double scale, bool causal, cudaStream_t s);
 bool flash_attention_forward_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                                 at::Tensor& lse, double scale, bool causal, cudaStream_t s);
 
 // 0: tcgen05 forward where the shape allows it (default); 1: the mma.sync kernels.
 static int g_attn_impl = 0;
 void attention_set_impl(int64_t impl) { g_attn_impl = (int)impl; }
+extern int g_attn_bwd_debug;
+void attention_set_debug(int64_t bits) { g_attn_bwd_debug = (int)bits; }
+extern long long* g_attn_bwd_trace;
+void attention_set_trace(int64_t ptr) { g_attn_bwd_trace = reinterpret_cast<long long*>(ptr); }
 
 void flash_attention_forward(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                              at::Tensor& lse, double scale, bool causal) {
@@ -648,7 +655,8 @@ void flash_attention_backward(const at::Tensor& q, const at::Tensor& k, const at
   }
   const float sc = (float)scale;
 #define KB_BWD(DD, CC, FF) launch_bwd<DD, CC, FF>(q, k, v, dout, lse, delta_t, acc_t, dk, dv, sc, s)
-  if (D == 64) {
+  if (g_attn_impl == 0 && flash_attention_backward_tc(q, k, v, dout, lse, delta, acc, dk, dv, scale, causal, s)) {
+  } else if (D == 64) {
     if (causal) { if (f16) KB_BWD(64, true, true); else KB_BWD(64, true, false); }
     else { if (f16) KB_BWD(64, false, true); else KB_BWD(64, false, false); }
   } else {
@@ -668,6 +676,10 @@ void flash_attention_backward(const at::Tensor& q, const at::Tensor& k, const at
 }
 
 void register_attention_ops(pybind11::module& m) {
+  m.def("attention_set_debug", &attention_set_debug,
+        "Diagnostics for the tcgen05 attention backward (bit 0: skip dQ reductions, bit 1: skip elementwise math)");
+  m.def("attention_set_trace", &attention_set_trace,
+        "Diagnostics: device address of an int64[168] buffer for clock64 stamps of one backward CTA (0 = off)");
   m.def("attention_set_impl", &attention_set_impl,
         "attention forward implementation: 0 = tcgen05 (default), 1 = mma.sync kernels");
   m.def("flash_attention_forward", &flash_attention_forward);
