@@ -255,38 +255,49 @@ __global__ void __launch_bounds__(kFwdThreads)
 
 // ---------------------------------------------------------------- backward
 
-// delta[b,h,s] = sum_d dO[b,s,h,d] * O[b,s,h,d]
-template <bool F16>
+// delta[b,h,s] = sum_d dO[b,s,h,d] * O[b,s,h,d], and the fp32 dQ accumulator
+// row (b,s,h) set to zero. D/8 threads per row, 16-byte loads; rows in
+// (b, s, h) order so that neighbouring threads read neighbouring memory.
+template <bool F16, int D>
 __global__ void flash_bwd_pre_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ dout,
-                                     float* __restrict__ delta, int H, int S, int D, long long o_ld, long long do_ld,
-                                     long long o_bs, long long do_bs) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  const int total = gridDim.y * H * S;  // gridDim.y = B
-  (void)total;
-  const int b = blockIdx.y;
-  if (warp >= H * S) return;
-  const int s = warp / H, h = warp % H;
-  const uint16_t* orow = o + b * o_bs + (long long)s * o_ld + (long long)h * D;
-  const uint16_t* drow = dout + b * do_bs + (long long)s * do_ld + (long long)h * D;
-  float acc = 0.f;
-  for (int d = 2 * lane; d < D; d += 64) {
-    const uint32_t a = *reinterpret_cast<const uint32_t*>(orow + d);
-    const uint32_t c = *reinterpret_cast<const uint32_t*>(drow + d);
-    float a0, a1, c0, c1;
-    if constexpr (F16) {
-      const __half2 x = *reinterpret_cast<const __half2*>(&a);
-      const __half2 y = *reinterpret_cast<const __half2*>(&c);
-      a0 = __low2float(x); a1 = __high2float(x); c0 = __low2float(y); c1 = __high2float(y);
-    } else {
-      const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162*>(&c);
-      a0 = __low2float(x); a1 = __high2float(x); c0 = __low2float(y); c1 = __high2float(y);
+                                     float* __restrict__ delta, float* __restrict__ acc, long long rows, int H, int S,
+                                     long long o_ld, long long do_ld, long long o_bs, long long do_bs) {
+  constexpr int TPR = D / 8;
+  const long long gt = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long row = gt / TPR;
+  const int part = (int)(gt % TPR);
+  float sum = 0.f;
+  const bool in = row < rows;
+  long long b = 0, s = 0, h = 0;
+  if (in) {
+    b = row / ((long long)S * H);
+    const long long rem = row - b * S * H;
+    s = rem / H;
+    h = rem - s * H;
+    const uint4 x = *reinterpret_cast<const uint4*>(o + b * o_bs + s * o_ld + h * D + part * 8);
+    const uint4 y = *reinterpret_cast<const uint4*>(dout + b * do_bs + s * do_ld + h * D + part * 8);
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a0, a1, c0, c1;
+      if constexpr (F16) {
+        const __half2 u = *reinterpret_cast<const __half2*>(&xs[i]);
+        const __half2 w = *reinterpret_cast<const __half2*>(&ys[i]);
+        a0 = __low2float(u); a1 = __high2float(u); c0 = __low2float(w); c1 = __high2float(w);
+      } else {
+        const __nv_bfloat162 u = *reinterpret_cast<const __nv_bfloat162*>(&xs[i]);
+        const __nv_bfloat162 w = *reinterpret_cast<const __nv_bfloat162*>(&ys[i]);
+        a0 = __low2float(u); a1 = __high2float(u); c0 = __low2float(w); c1 = __high2float(w);
+      }
+      sum += a0 * c0 + a1 * c1;
     }
-    acc += a0 * c0 + a1 * c1;
+    float4* ar = reinterpret_cast<float4*>(acc + row * D + part * 8);
+    ar[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    ar[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  acc = warp_sum(acc);
-  if (lane == 0) delta[((long long)b * H + h) * S + s] = acc;
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (in && part == 0) delta[(b * H + h) * S + s] = sum;
 }
 
 constexpr int kBwdBN = 64;  // keys per CTA
@@ -502,25 +513,22 @@ __global__ void __launch_bounds__(kBwdThreads)
   }
 }
 
-// dq[b,s,h,:] = bf16(dq_acc[b,s,h,:])
+// dq[b,s,h,:] = 16-bit(dq_acc[b,s,h,:]), eight elements per thread.
 template <bool F16>
-__global__ void dq_convert_kernel(const float* __restrict__ acc, uint16_t* __restrict__ dq, long long rows, int HD,
+__global__ void dq_convert_kernel(const float* __restrict__ acc, uint16_t* __restrict__ dq, long long nvec, int HD8,
                                   long long dq_ld, long long dq_bs, int S) {
-  const long long total = rows * HD;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / HD;
-    const int c = (int)(i - r * HD);
-    const long long bb = r / S, s = r % S;
-    const float x = acc[i];
-    uint16_t out;
-    if constexpr (F16) {
-      __half hv = __float2half_rn(x);
-      out = *reinterpret_cast<uint16_t*>(&hv);
-    } else {
-      __nv_bfloat16 bv = __float2bfloat16_rn(x);
-      out = *reinterpret_cast<uint16_t*>(&bv);
-    }
-    dq[bb * dq_bs + s * dq_ld + c] = out;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / HD8;
+    const int c = (int)(i - r * HD8) * 8;
+    const long long bb = r / S, s = r - bb * S;
+    const float4 a0 = *reinterpret_cast<const float4*>(acc + i * 8);
+    const float4 a1 = *reinterpret_cast<const float4*>(acc + i * 8 + 4);
+    uint4 w;
+    w.x = pack2<F16>(a0.x, a0.y);
+    w.y = pack2<F16>(a0.z, a0.w);
+    w.z = pack2<F16>(a1.x, a1.y);
+    w.w = pack2<F16>(a1.z, a1.w);
+    *reinterpret_cast<uint4*>(dq + bb * dq_bs + s * dq_ld + c) = w;
   }
 }
 
@@ -640,17 +648,19 @@ void flash_attention_backward(const at::Tensor& q, const at::Tensor& k, const at
   float* delta = acc + acc_elems;
   at::Tensor acc_t = workspace.narrow(0, 0, acc_elems);
   at::Tensor delta_t = workspace.narrow(0, acc_elems, delta_elems);
-  KB_CUDA_CHECK(cudaMemsetAsync(acc, 0, acc_elems * sizeof(float), s));
   {
-    dim3 grid((H * Sq * 32 + 255) / 256, B);
-    if (f16)
-      flash_bwd_pre_kernel<true><<<grid, 256, 0, s>>>((const uint16_t*)o.data_ptr(), (const uint16_t*)dout.data_ptr(),
-                                                      delta, H, Sq, (int)D, o.stride(1), dout.stride(1), o.stride(0),
-                                                      dout.stride(0));
-    else
-      flash_bwd_pre_kernel<false><<<grid, 256, 0, s>>>((const uint16_t*)o.data_ptr(), (const uint16_t*)dout.data_ptr(),
-                                                       delta, H, Sq, (int)D, o.stride(1), dout.stride(1), o.stride(0),
-                                                       dout.stride(0));
+    // delta pre-pass; also zeroes the dQ accumulator.
+    const long long rows = (long long)B * Sq * H;
+    const long long threads = rows * (D / 8);
+    const int blocks = (int)((threads + 255) / 256);
+    const uint16_t* op = (const uint16_t*)o.data_ptr();
+    const uint16_t* dp = (const uint16_t*)dout.data_ptr();
+#define KB_PRE(FF, DD)                                                                                          \
+  flash_bwd_pre_kernel<FF, DD><<<blocks, 256, 0, s>>>(op, dp, delta, acc, rows, H, Sq, o.stride(1), dout.stride(1), \
+                                                      o.stride(0), dout.stride(0))
+    if (D == 64) { if (f16) KB_PRE(true, 64); else KB_PRE(false, 64); }
+    else { if (f16) KB_PRE(true, 128); else KB_PRE(false, 128); }
+#undef KB_PRE
     KB_LAUNCHED();
   }
   const float sc = (float)scale;
@@ -664,14 +674,14 @@ void flash_attention_backward(const at::Tensor& q, const at::Tensor& k, const at
     else { if (f16) KB_BWD(128, false, true); else KB_BWD(128, false, false); }
   }
 #undef KB_BWD
-  const long long rows = (long long)B * Sq;
-  const int blocks = (int)std::min<long long>((rows * H * D + 255) / 256, num_sms(q.get_device()) * 16LL);
+  const long long nvec = (long long)B * Sq * H * D / 8;
+  const int blocks = (int)std::min<long long>((nvec + 255) / 256, num_sms(q.get_device()) * 16LL);
   if (f16)
-    dq_convert_kernel<true><<<blocks, 256, 0, s>>>(acc, (uint16_t*)dq.data_ptr(), rows, (int)(H * D), dq.stride(1),
-                                                   dq.stride(0), Sq);
+    dq_convert_kernel<true><<<blocks, 256, 0, s>>>(acc, (uint16_t*)dq.data_ptr(), nvec, (int)(H * D / 8),
+                                                   dq.stride(1), dq.stride(0), Sq);
   else
-    dq_convert_kernel<false><<<blocks, 256, 0, s>>>(acc, (uint16_t*)dq.data_ptr(), rows, (int)(H * D), dq.stride(1),
-                                                    dq.stride(0), Sq);
+    dq_convert_kernel<false><<<blocks, 256, 0, s>>>(acc, (uint16_t*)dq.data_ptr(), nvec, (int)(H * D / 8),
+                                                    dq.stride(1), dq.stride(0), Sq);
   KB_LAUNCHED();
 }
 

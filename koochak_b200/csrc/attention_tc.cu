@@ -61,37 +61,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// (a0, a1) * (b0, b1) + (c0, c1) on the paired fp32 pipe.
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\tmov.b64 rc, {%5, %6};\n\t"
-      "fma.rn.f32x2 %0, ra, rb, rc;\n\t}"
-      : "=l"(d)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
-  return r;
-}
-
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  uint64_t d;
-  asm("{\n\t.reg .b64 ra, rb;\n\t"
-      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
-      "add.rn.f32x2 %0, ra, rb;\n\t}"
-      : "=l"(d)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
-  return r;
-}
-
 template <bool F16>
 __device__ __forceinline__ uint32_t pack_pair(float a, float b) {
   if constexpr (F16) return pack_f16(a, b);

@@ -137,6 +137,19 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// 4-byte asynchronous global -> shared copy; copies zeros when !valid (the
+// source is then not read).
+__device__ __forceinline__ void cp_async_4_zfill(void* smem_dst, const void* gsrc, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem_dst)), "l"(gsrc),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+// One arrival on `bar` (counted in its expected arrivals) once every earlier
+// cp.async of this thread has landed.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // TMA reduction (element-wise add) of a shared-memory tile into a 4-D tensor
 // (bulk-group completion). Coordinates must be non-negative.
 __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* src, int x, int y, int z,
@@ -411,6 +424,53 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool fp16_inputs,
 }
 
 // ----------------------------------------------------------------- misc math
+
+// Three-input maximum.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// (a0, a1) * (b0, b1) + (c0, c1) on the paired fp32 pipe.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\tmov.b64 rc, {%5, %6};\n\t"
+      "fma.rn.f32x2 %0, ra, rb, rc;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+// (a0 + b0, a1 + b1) on the paired fp32 pipe.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, ra, rb;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+// (a0 * b0, a1 * b1) on the paired fp32 pipe.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+      "mul.rn.f32x2 %0, ra, rb;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
 
 __device__ __forceinline__ float tanh_fast(float x) {
   float y;
