@@ -137,11 +137,12 @@ struct TcBwdArgs {
   long long* trace;  // diagnostics: clock64 stamps of CTA (0, 0) when non-null
 };
 
-// Trace slots: [0] entry, [1] after setup, then per step s (< 16, counted over
-// the CTA's work items) 10 slots at 8 + 10 s:
+// Trace slots: [0] entry, [1] after setup, then per step s (< 10, counted over
+// the CTA's work items) 16 slots at 8 + 16 s:
 // +0 MMA q_full ok, +1 S/dP issued, +2 p_ready seen, +3 dV/dK issued, +4 dQ issued,
 // +5 elementwise sdp_full seen, +6 elementwise arrived, +7 dQ warp dq_full seen, +8 dQ warp done,
-// +9 producer staged LSE / delta (TMA already issued).
+// +9 producer staged LSE / delta (TMA already issued), +10..+14 elementwise
+// chunk 0 loaded, chunk 0 stored, chunk 1 loaded, chunk 1 stored, fences done.
 constexpr int kBwTraceSlots = 168;
 __device__ __forceinline__ void bw_stamp(const TcBwdArgs& a, int slot) {
   if (a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && slot < kBwTraceSlots) a.trace[slot] = clock64();
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
             cp_async_4_zfill(&sDelta[st * kBwBQ + t], a.delta + gi, in);
           }
           cp_async_mbar_arrive_noinc(&q_full[st]);
-          if (lane == 0) bw_stamp(a, 8 + 10 * step + 9);
+          if (lane == 0) bw_stamp(a, 8 + 16 * step + 9);
         }
       }
       if (lane == 0) {
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         if (Cfg::kDqInScores && !mbar_wait(dq_empty, (stp & 1) ^ 1, abort_flag, a.status, kStatusTimeoutMma))
           return false;
         tc_fence_after();
-        bw_stamp(a, 8 + 10 * stp);
+        bw_stamp(a, 8 + 16 * stp);
         const uint32_t q_addr = smem_u32(sQ + st * Cfg::kTile), do_addr = smem_u32(sDO + st * Cfg::kTile);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
                       idesc_t, kk != 0 ? 1u : 0u);
         }
         umma_commit(sdp_full);
-        bw_stamp(a, 8 + 10 * stp + 1);
+        bw_stamp(a, 8 + 16 * stp + 1);
         issued = true;
         return true;
       };
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
             ok = false;
             break;
           }
-          bw_stamp(a, 8 + 10 * step + 2);
+          bw_stamp(a, 8 + 16 * step + 2);
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQ + st * Cfg::kTile), do_addr = smem_u32(sDO + st * Cfg::kTile);
 #pragma unroll
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
             umma_f16_ts(tmem + Cfg::kColDK, tmem + Cfg::kColDP + Cfg::a_col(kk),
                         sw128_desc(q_addr + kk * 2048, 128 * 128, 1024), idesc_kv, acc);
           }
-          bw_stamp(a, 8 + 10 * step + 3);
+          bw_stamp(a, 8 + 16 * step + 3);
           // D = 64: the next step's scores go ahead of this step's dQ (which
           // reads only shared memory), so its elementwise work overlaps dQ.
           if (!Cfg::kDqInScores && more && !issue_sdp(step + 1)) {
@@ -388,7 +389,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
                           sw128_desc(k_addr + h2 * (128 * 128) + kk * 2048, 128 * 128, 1024), idesc_q,
                           kk != 0 ? 1u : 0u);
           umma_commit(dq_full);
-          bw_stamp(a, 8 + 10 * step + 4);
+          bw_stamp(a, 8 + 16 * step + 4);
           umma_commit(&q_empty[st]);
           if (Cfg::kDqInScores && more && !issue_sdp(step + 1)) {
             ok = false;
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           break;
         }
         tc_fence_after();
-        if (threadIdx.x == 128) bw_stamp(a, 8 + 10 * step + 5);
+        if (threadIdx.x == 128) bw_stamp(a, 8 + 16 * step + 5);
         const int q0 = (it.i_start + st_i) * kBwBQ + 64 * half;  // first query of this warp's columns
         // Masked: queries before the key (causal) and queries past Sq.
         const bool need_mask = (CAUSAL && q0 < it.k0 + kBwBK - 1) || q0 + 64 > a.Sq;
@@ -473,6 +474,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
               tmem_ld_32x32b_x32(t_dp + 64 * half + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&dv[32 * c]));
               tmem_wait_ld_dep(*reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
               tmem_wait_ld_dep(*reinterpret_cast<uint32_t(*)[32]>(&dv[32 * c]));
+              if (threadIdx.x == 128) bw_stamp(a, 8 + 16 * step + 10 + 2 * c);
             }
             uint32_t pk[16], dk[16];
 #pragma unroll
@@ -516,14 +518,16 @@ __global__ void __launch_bounds__(kBwThreads, 1)
               *reinterpret_cast<uint4*>(row + unit * 16) =
                   make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
             }
+            if (threadIdx.x == 128) bw_stamp(a, 8 + 16 * step + 11 + 2 * c);
           }
         }
         fence_proxy_async_smem();
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
+        if (threadIdx.x == 128) bw_stamp(a, 8 + 16 * step + 14);
         if (lane == 0) mbar_arrive(p_ready);
-        if (threadIdx.x == 128) bw_stamp(a, 8 + 10 * step + 6);
+        if (threadIdx.x == 128) bw_stamp(a, 8 + 16 * step + 6);
       }
       // dK, dV rows of this key: this warp writes columns [D/2 * half, D/2 * (half + 1)).
       if (!ok || !mbar_wait(kv_done, n_it & 1, abort_flag, a.status, kStatusTimeoutEpilogue)) {
@@ -581,7 +585,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           break;
         }
         tc_fence_after();
-        if (threadIdx.x == 384) bw_stamp(a, 8 + 10 * step + 7);
+        if (threadIdx.x == 384) bw_stamp(a, 8 + 16 * step + 7);
         const int qb0 = (it.i_start + st_i) * kBwBQ;
         const int qg = qb0 + qr;
         if constexpr (Cfg::kDqTma) {
@@ -636,7 +640,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(dq_empty);
         }
-        if (threadIdx.x == 384) bw_stamp(a, 8 + 10 * step + 8);
+        if (threadIdx.x == 384) bw_stamp(a, 8 + 16 * step + 8);
       }
     }
     if (Cfg::kDqTma && leader) bulk_wait_all();

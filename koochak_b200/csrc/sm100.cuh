@@ -82,6 +82,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return done != 0;
 }
 
+// As mbar_try_wait, but the thread may sleep up to `hint_ns` while the phase
+// is incomplete (it wakes as soon as the phase completes), so waiting warps do
+// not take issue slots from the warps that share their scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Waits for the phase with the given parity. Returns false (and raises the
 // CTA abort flag, and records `code`) when the budget runs out or when some
 // other role of the CTA has already aborted.
@@ -92,8 +107,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const unsigned long long start = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i) {
-      if (mbar_try_wait(addr, parity)) return true;
+    for (int i = 0; i < 8; ++i) {
+      if (mbar_try_wait_sleep(addr, parity, 20000u)) return true;
     }
     if (*abort_flag) return false;
     if (global_timer_ns() - start > kWaitBudgetNs) {
