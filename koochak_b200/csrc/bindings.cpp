@@ -14,6 +14,7 @@ void register_elementwise_ops(pybind11::module& m);
 void register_attention_ops(pybind11::module& m);
 void register_optim_ops(pybind11::module& m);
 void register_comm_ops(pybind11::module& m);
+void register_muon_gather_ops(pybind11::module& m);
 }  // namespace kb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -35,4 +36,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   kb::register_attention_ops(m);
   kb::register_optim_ops(m);
   kb::register_comm_ops(m);
+  kb::register_muon_gather_ops(m);
 }

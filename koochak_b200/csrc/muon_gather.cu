@@ -1,0 +1,188 @@
+// Sharded Muon: the parameter update of the owning rank, fused with the
+// all-gather of the updated parameter to every rank of the node.
+//
+// (replaces, for the native distributed Muon path, the per-rank update plus
+//  the padded parameter all-gather of the reference:
+//  koochak/optim/muon.py:256-277, MuonWithAuxAdam.step)
+//
+// Every Muon matrix of a parameter group lives in one symmetric fp32 slab: the
+// same offset on every GPU, each rank's slab mapped into every peer (and, with
+// NVSwitch multicast, one multicast alias of the whole slab). The rank that
+// owns a matrix runs momentum and Newton-Schulz on it; this kernel then forms
+//
+//   p_new = p * (1 - lr * wd) - lr * scale * U        (U = X or X^T)
+//
+// and stores p_new into every rank's copy in the same pass: one
+// `multimem.st.v4.f32` through the switch when a multicast alias exists,
+// otherwise one 16-byte P2P store per rank. The owner's bf16 compute copy is
+// written too. Peers learn that the stores have landed from a bounded flag
+// barrier launched after the last bucket (comm.cu: comm_barrier); the fence at
+// the end of every thread orders its remote stores before that release.
+//
+// The math is the same expression, in the same order, as muon_epilogue_kernel
+// (optim.cu), so a sharded step is bit-identical to a single-GPU step.
+// No TMA and no cluster multicast: plain and multimem stores only.
+#include "host_utils.h"
+#include "sm100.cuh"
+
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace kb {
+
+namespace {
+
+constexpr int kGatherMats = 64;
+constexpr int kGatherRanks = 8;
+
+struct GatherMats {
+  int R, C;                            // parameter shape (rows, cols); C % 4 == 0
+  int world;
+  float* p[kGatherMats];               // this rank's copy (inside the slab)
+  __nv_bfloat16* shadow[kGatherMats];  // bf16 compute copy on this rank, or null
+  long long delta[kGatherRanks];       // bytes from this rank's slab to rank r's
+  long long mc_delta;                  // bytes from this rank's slab to the multicast alias (0: none)
+};
+
+__device__ __forceinline__ void mm_st_v4(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ T* shifted(T* p, long long bytes) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + bytes);
+}
+
+// One CTA per 32 x 32 block of one matrix; a thread owns 4 consecutive columns
+// of one row, so every store is 16 bytes and a warp covers 4 full 128-byte rows.
+template <bool MULTIMEM>
+__global__ void __launch_bounds__(256)
+    muon_update_gather_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X, float lr,
+                              float wd, float scale, int transpose) {
+  const int i = blockIdx.z;
+  const int R = mm.R, C = mm.C;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const __nv_bfloat16* x = X + (long long)i * R * C;
+  __shared__ float tile[32][33];
+  if (transpose) {
+    // X is [C, R]: read coalesced along R, tile[c - c0][r - r0].
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + ty + 8 * k, r = r0 + tx;
+      tile[ty + 8 * k][tx] = (r < R && c < C) ? __bfloat162float(x[(long long)c * R + r]) : 0.f;
+    }
+    __syncthreads();
+  }
+  const int row = threadIdx.x >> 3, col = (threadIdx.x & 7) * 4;
+  const int r = r0 + row, c = c0 + col;
+  if (r < R && c < C) {  // C % 4 == 0: the whole 4-vector is in range
+    const long long idx = (long long)r * C + c;
+    float u[4];
+    if (transpose) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) u[j] = tile[col + j][row];
+    } else {
+      const uint2 raw = *reinterpret_cast<const uint2*>(x + idx);
+      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+      u[0] = __low2float(lo);
+      u[1] = __high2float(lo);
+      u[2] = __low2float(hi);
+      u[3] = __high2float(hi);
+    }
+    float* p = mm.p[i] + idx;
+    const float4 old = *reinterpret_cast<const float4*>(p);
+    const float decay = 1.f - lr * wd;
+    float4 pn;
+    pn.x = old.x * decay - lr * (scale * u[0]);
+    pn.y = old.y * decay - lr * (scale * u[1]);
+    pn.z = old.z * decay - lr * (scale * u[2]);
+    pn.w = old.w * decay - lr * (scale * u[3]);
+    if constexpr (MULTIMEM) {
+      mm_st_v4(shifted(p, mm.mc_delta), pn);
+    } else {
+      for (int q = 0; q < mm.world; ++q) __stcg(shifted(reinterpret_cast<float4*>(p), mm.delta[q]), pn);
+    }
+    if (__nv_bfloat16* sh = mm.shadow[i]) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(pn.x, pn.y);
+      __nv_bfloat162 b = __floats2bfloat162_rn(pn.z, pn.w);
+      uint2 packed;
+      packed.x = *reinterpret_cast<uint32_t*>(&a);
+      packed.y = *reinterpret_cast<uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(sh + idx) = packed;
+    }
+  }
+  if constexpr (MULTIMEM) asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
+}  // namespace
+
+// params: this rank's owned matrices (views into the symmetric slab), all [R, C]
+// fp32; X: bf16 [n, r, c] orthogonalised updates (r, c = C, R when transpose).
+// bases: every rank's slab base address; mc_base: multicast alias or 0.
+void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor& X,
+                        const std::vector<at::Tensor>& shadow, double lr, double wd, double scale, bool transpose,
+                        const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank) {
+  const size_t n = params.size();
+  if (n == 0) return;
+  const int world = (int)bases.size();
+  KB_CHECK(world >= 1 && world <= kGatherRanks, "muon_update_gather: world size must be 1..8");
+  KB_CHECK(rank >= 0 && rank < world, "muon_update_gather: bad rank");
+  KB_CHECK(shadow.empty() || shadow.size() == n, "muon_update_gather: shadow list length");
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int R = (int)params[0].size(0);
+  const int C = (int)(params[0].numel() / R);
+  KB_CHECK(C % 4 == 0, "muon_update_gather: column count must be a multiple of 4");
+  KB_CHECK(X.scalar_type() == at::kBFloat16 && X.is_contiguous() && X.numel() >= (int64_t)n * R * C,
+           "muon_update_gather: X must be contiguous bf16 [n, R*C]");
+  KB_CHECK(reinterpret_cast<uintptr_t>(X.data_ptr()) % 16 == 0, "muon_update_gather: X must be 16-byte aligned");
+  for (int q = 0; q < world; ++q) KB_CHECK(bases[q] != 0 && bases[q] % 16 == 0, "muon_update_gather: bad slab base");
+  KB_CHECK(mc_base % 16 == 0, "muon_update_gather: multicast base must be 16-byte aligned");
+  for (size_t base = 0; base < n; base += kGatherMats) {
+    const int count = (int)std::min<size_t>(kGatherMats, n - base);
+    GatherMats mm{};
+    mm.R = R;
+    mm.C = C;
+    mm.world = world;
+    for (int q = 0; q < world; ++q) mm.delta[q] = bases[q] - bases[rank];
+    mm.mc_delta = mc_base ? mc_base - bases[rank] : 0;
+    for (int j = 0; j < count; ++j) {
+      const at::Tensor& p = params[base + j];
+      KB_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous() && p.numel() == (int64_t)R * C,
+               "muon_update_gather: same-shape fp32 contiguous matrices required");
+      const int64_t addr = reinterpret_cast<int64_t>(p.data_ptr());
+      KB_CHECK(addr % 16 == 0 && addr >= bases[rank], "muon_update_gather: parameter must lie in the local slab");
+      mm.p[j] = p.data_ptr<float>();
+      const at::Tensor* sh = shadow.empty() ? nullptr : &shadow[base + j];
+      mm.shadow[j] = (sh && sh->numel() == (int64_t)R * C && sh->scalar_type() == at::kBFloat16 &&
+                      sh->is_contiguous() && reinterpret_cast<uintptr_t>(sh->data_ptr()) % 8 == 0)
+                         ? reinterpret_cast<__nv_bfloat16*>(sh->data_ptr())
+                         : nullptr;
+      KB_CHECK(sh == nullptr || sh->numel() == 0 || mm.shadow[j] != nullptr,
+               "muon_update_gather: shadow must be a contiguous 8-byte aligned bf16 copy of the parameter");
+    }
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()) + (int64_t)base * R * C;
+    dim3 grid((C + 31) / 32, (R + 31) / 32, count);
+    if (mc_base != 0) {
+      muon_update_gather_kernel<true><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose);
+    } else {
+      muon_update_gather_kernel<false><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose);
+    }
+    KB_LAUNCHED();
+  }
+}
+
+void register_muon_gather_ops(pybind11::module& m) {
+  m.def("muon_update_gather", &muon_update_gather,
+        "owner's Muon update written into every rank's parameter copy (P2P or multimem stores)", pybind11::arg("params"),
+        pybind11::arg("X"), pybind11::arg("shadow"), pybind11::arg("lr"), pybind11::arg("wd"), pybind11::arg("scale"),
+        pybind11::arg("transpose"), pybind11::arg("bases"), pybind11::arg("mc_base"), pybind11::arg("rank"));
+}
+
+}  // namespace kb

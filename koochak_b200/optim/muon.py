@@ -22,9 +22,14 @@ Execution:
   correction, decoupled weight decay, EMA and bf16 copy).
 * Distributed classes (chosen when a process group exists) shard the Muon
   work: within each shape bucket, matrix k is owned by rank k % world (its
-  momentum lives only there); owners update their matrices and one
-  all-gather per bucket publishes the new values. Adam groups run on every
-  rank, as in the reference.
+  momentum lives only there). On CUDA the group's matrices are stored in one
+  symmetric-memory slab (``parallel.symm.SymmetricParamSlab``) and the
+  owner's update kernel stores each new matrix into every rank's copy over
+  NVLink (P2P stores, or ``multimem.st`` through NVSwitch), followed by one
+  bounded cross-GPU barrier per step: the all-gather is fused into the
+  update. ``KOOCHAK_B200_MUON_GATHER=nccl`` (or matrices whose column count
+  is not a multiple of 4) selects one NCCL all-gather per bucket instead.
+  Adam groups run on every rank, as in the reference.
 
 The training loop passes the gradient-clip coefficient as a device scalar
 (``optimizer.kb_grad_scale``) so gradients are scaled on read instead of being
@@ -427,7 +432,7 @@ def _muon_buckets(params: Sequence[torch.nn.Parameter]) -> Dict[Tuple[int, int],
     return buckets
 
 
-def _native_muon_bucket(optimizer, group, params: List[torch.nn.Parameter], R: int, C: int) -> None:
+def _native_muon_bucket(optimizer, group, params: List[torch.nn.Parameter], R: int, C: int, slab=None) -> None:
     from ..ops._ext import native
 
     n = len(params)
@@ -450,6 +455,12 @@ def _native_muon_bucket(optimizer, group, params: List[torch.nn.Parameter], R: i
     native().muon_prologue(grads, moms, X, ss, _clip_scale(optimizer), float(group["momentum"]), True, transpose)
     native().muon_scale(X, ss, n)
     X = newton_schulz_batched(X, 5)
+    if slab is not None:
+        ws = slab.ws
+        native().muon_update_gather(params, X, _shadow_list(params), float(group["lr"]), float(group["weight_decay"]),
+                                    0.2 * math.sqrt(max(R, C)), transpose, ws.bases, ws.mc_base, ws.rank)
+        _mark_shadows(params)
+        return
     ema, d = _ema_list(optimizer, params)
     native().muon_epilogue(params, X, ema, _shadow_list(params), float(group["lr"]), float(group["weight_decay"]),
                            0.2 * math.sqrt(max(R, C)), transpose, d)
@@ -466,6 +477,17 @@ def _native_muon_group(optimizer, group, distributed: bool) -> None:
             _native_muon_bucket(optimizer, group, [params[i] for i in idx], R, C)
         return
     world, rank = dist.get_world_size(), dist.get_rank()
+    slab = _param_slab(optimizer, group, params)
+    if slab is not None:
+        for (R, C), idx in buckets.items():
+            owned = [params[i] for k, i in enumerate(idx) if k % world == rank]
+            if owned:
+                _native_muon_bucket(optimizer, group, owned, R, C, slab=slab)
+            for k, i in enumerate(idx):
+                if k % world != rank and getattr(params[i], "_kb_shadow", None) is not None:
+                    params[i]._kb_shadow_version = -1  # rewritten by its owner: recast before the next forward
+        slab.barrier()
+        return
     for (R, C), idx in buckets.items():
         owned = [params[i] for k, i in enumerate(idx) if k % world == rank]
         if owned:
@@ -480,6 +502,26 @@ def _native_muon_group(optimizer, group, distributed: bool) -> None:
             if k % world == rank:
                 continue
             params[i].detach().view(-1).copy_(recv[(k % world) * per_rank + k // world])
+
+
+def _param_slab(optimizer, group, params: List[torch.nn.Parameter]):
+    """The group's symmetric parameter slab (built on first use), or None for the NCCL all-gather."""
+
+    if os.environ.get("KOOCHAK_B200_MUON_GATHER", "peer") != "peer":
+        return None
+    if dist.get_backend() != "nccl" or dist.get_world_size() > 8:
+        return None
+    if any(p.dim() < 2 or (p.numel() // p.shape[0]) % 4 != 0 for p in params):
+        return None
+    slabs = optimizer.__dict__.setdefault("_kb_param_slabs", {})
+    key = id(group)
+    slab = slabs.get(key)
+    if slab is None or not slab.holds(params):
+        from ..parallel.symm import SymmetricParamSlab
+
+        slab = SymmetricParamSlab(params, params[0].device)
+        slabs[key] = slab
+    return slab
 
 
 def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) -> None:

@@ -33,7 +33,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
-__all__ = ["SymmetricWorkspace", "FusedGradReducer", "plan_chunks", "shard_bounds"]
+__all__ = ["SymmetricWorkspace", "FusedGradReducer", "SymmetricParamSlab", "plan_chunks", "shard_bounds"]
 
 _FLAG_BYTES = 128 * 8 * 4  # [max blocks][max ranks] u32 barrier slots
 _ALIGN = 256
@@ -184,3 +184,56 @@ class FusedGradReducer:
         out = torch.empty(4, device=self.ws.device, dtype=torch.float32)
         self._C.gate_from_stats(self.current_stats(), self.n_tensors, float(max_norm or 0.0), max_norm is not None, out)
         return out
+
+
+class SymmetricParamSlab:
+    """fp32 parameters stored in symmetric memory, so an owner can write its update into every rank's copy.
+
+    Each listed parameter's storage is moved (``p.data = view``) into one
+    symmetric buffer laid out identically on every rank, values preserved.
+    The sharded Muon step (``optim/muon.py``) then has the owning rank of
+    each matrix store its updated value into all ranks' slabs from inside the
+    update kernel (``csrc/muon_gather.cu``), replacing the per-bucket
+    all-gather; ``barrier()`` (bounded, cross-GPU) is the point after which
+    every rank may read the new values.
+    """
+
+    def __init__(self, params: Sequence[torch.Tensor], device: torch.device, group=None, *,
+                 timeout_s: Optional[float] = None, use_multicast: Optional[bool] = None) -> None:
+        from ..ops._ext import native
+
+        self._C = native()
+        self.params = list(params)
+        self.timeout_s = float(timeout_s if timeout_s is not None else os.environ.get("KOOCHAK_B200_COMM_TIMEOUT_S", 300))
+        offsets, off = [], _FLAG_BYTES
+        for p in self.params:
+            offsets.append(off)
+            off = _align(off + 4 * p.numel())
+        self.ws = SymmetricWorkspace(off, device, group, use_multicast=use_multicast)
+        self.world, self.rank = self.ws.world, self.ws.rank
+        self.epoch = 1
+        with torch.no_grad():
+            self.ws.tensor.narrow(0, 0, _FLAG_BYTES).zero_()
+            for p, o in zip(self.params, offsets):
+                view = self.ws.view(o, p.numel(), torch.float32).view(p.shape)
+                view.copy_(p.detach())
+                p.data = view
+                if getattr(p, "_kb_shadow", None) is not None:
+                    p._kb_shadow_version = -1  # type: ignore[attr-defined]
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.ws.group)
+        self.barrier()
+
+    def holds(self, params: Sequence[torch.Tensor]) -> bool:
+        """True while ``params`` are exactly this slab's parameters and still stored in it."""
+
+        if len(params) != len(self.params) or any(a is not b for a, b in zip(params, self.params)):
+            return False
+        lo = self.ws.tensor.data_ptr()
+        hi = lo + self.ws.nbytes
+        return all(lo <= p.data_ptr() < hi for p in self.params)
+
+    def barrier(self) -> None:
+        e = self.epoch
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        self._C.comm_barrier(self.ws.bases, 0, self.rank, e, 1, self.timeout_s, self.ws.device.index or 0)
