@@ -150,7 +150,46 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_bucket_kernel(const Co
     bool bad = false;
     const long long off = a.data_off + start * 4;  // bytes; start is a multiple of 4 elements
     const int n4 = len >> 2;
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    // Main part: kUnroll float4 per thread per pass, all loads (from every
+    // rank) issued before the first use, so each thread keeps
+    // kUnroll * world loads in flight over NVLink.
+    constexpr int kUnroll = 4;
+    const int stride = blockDim.x;
+    int i0 = threadIdx.x;
+    for (; i0 + (kUnroll - 1) * stride < n4; i0 += kUnroll * stride) {
+      float4 v[kUnroll];
+      if constexpr (MULTIMEM) {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          v[u] = mm_ld_reduce_f32x4(reinterpret_cast<const float*>(a.mc_base + off) + 4 * (i0 + u * stride));
+      } else {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) v[u] = __ldcg(at_rank<const float4>(a, 0, off) + i0 + u * stride);
+        for (int r = 1; r < a.world; ++r) {
+          float4 w[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) w[u] = __ldcg(at_rank<const float4>(a, r, off) + i0 + u * stride);
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            v[u].x += w[u].x; v[u].y += w[u].y; v[u].z += w[u].z; v[u].w += w[u].w;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        float4 x = v[u];
+        x.x *= mul; x.y *= mul; x.z *= mul; x.w *= mul;
+        bad |= !finite4(x);
+        ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+        const int i = i0 + u * stride;
+        if constexpr (MULTIMEM) {
+          mm_st_f32x4(reinterpret_cast<float*>(a.mc_base + off) + 4 * i, x);
+        } else {
+          for (int r = 0; r < a.world; ++r) __stcg(at_rank<float4>(a, r, off) + i, x);
+        }
+      }
+    }
+    for (int i = i0; i < n4; i += blockDim.x) {
       float4 v;
       if constexpr (MULTIMEM) {
         v = mm_ld_reduce_f32x4(reinterpret_cast<const float*>(a.mc_base + off) + 4 * i);

@@ -141,7 +141,7 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
   KB_CHECK(C % 4 == 0, "muon_update_gather: column count must be a multiple of 4");
   KB_CHECK(X.scalar_type() == at::kBFloat16 && X.is_contiguous() && X.numel() >= (int64_t)n * R * C,
            "muon_update_gather: X must be contiguous bf16 [n, R*C]");
-  KB_CHECK(reinterpret_cast<uintptr_t>(X.data_ptr()) % 16 == 0, "muon_update_gather: X must be 16-byte aligned");
+  KB_CHECK(reinterpret_cast<uintptr_t>(X.data_ptr()) % 8 == 0, "muon_update_gather: X must be 8-byte aligned");
   for (int q = 0; q < world; ++q) KB_CHECK(bases[q] != 0 && bases[q] % 16 == 0, "muon_update_gather: bad slab base");
   KB_CHECK(mc_base % 16 == 0, "muon_update_gather: multicast base must be 16-byte aligned");
   for (size_t base = 0; base < n; base += kGatherMats) {

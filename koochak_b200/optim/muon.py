@@ -12,7 +12,8 @@ Execution:
 * CPU or non-fp32 parameters run the plain-PyTorch functions below (they are
   also the oracle of the tests).
 * CUDA fp32 parameters run the native path. Muon matrices are bucketed by
-  shape; per bucket one kernel applies the clip coefficient, momentum and
+  shape, and buckets whose shapes differ only by a transpose share one
+  Newton-Schulz batch; per bucket one kernel applies the clip coefficient, momentum and
   Nesterov and writes bf16 (transposed when rows > cols) while accumulating
   the Frobenius norms, one kernel normalises, the 5 Newton-Schulz iterations
   are 15 batched tcgen05 GEMMs with the ``b*A + c*A@A`` and ``a*X + B@X``
@@ -432,39 +433,69 @@ def _muon_buckets(params: Sequence[torch.nn.Parameter]) -> Dict[Tuple[int, int],
     return buckets
 
 
-def _native_muon_bucket(optimizer, group, params: List[torch.nn.Parameter], R: int, C: int, slab=None) -> None:
+def _native_muon_bucket(optimizer, group, parts: List[Tuple[int, int, List[torch.nn.Parameter]]],
+                        slab=None) -> None:
+    """Muon on matrices that orthogonalise as one batch.
+
+    ``parts`` lists (R, C, params) groups whose shapes agree up to a
+    transpose (all [R, C] or [C, R]): the prologue writes each matrix in its
+    wide orientation [min, max] into one bf16 batch, Newton-Schulz runs once
+    over the whole batch (fewer, fuller GEMM launches), and each part's
+    epilogue transposes back as needed.
+    """
+
     from ..ops._ext import native
 
-    n = len(params)
-    dev = params[0].device
-    transpose = R > C
-    r, c = (C, R) if transpose else (R, C)
-    grads, moms = [], []
-    for p in params:
-        _ensure_grad(p)
-        st = optimizer.state[p]
-        if "momentum_buffer" not in st:
-            st["momentum_buffer"] = torch.zeros_like(p)
-        g = p.grad
-        if g.dtype != torch.float32 or not g.is_contiguous():
-            g = g.float().contiguous()
-        grads.append(g)
-        moms.append(st["momentum_buffer"])
+    n = sum(len(ps) for _, _, ps in parts)
+    dev = parts[0][2][0].device
+    r, c = min(parts[0][0], parts[0][1]), max(parts[0][0], parts[0][1])
     X = torch.empty((n, r, c), device=dev, dtype=torch.bfloat16)
     ss = torch.empty(n, device=dev, dtype=torch.float32)
-    native().muon_prologue(grads, moms, X, ss, _clip_scale(optimizer), float(group["momentum"]), True, transpose)
+    base = 0
+    for R, C, params in parts:
+        grads, moms = [], []
+        for p in params:
+            _ensure_grad(p)
+            st = optimizer.state[p]
+            if "momentum_buffer" not in st:
+                st["momentum_buffer"] = torch.zeros_like(p)
+            g = p.grad
+            if g.dtype != torch.float32 or not g.is_contiguous():
+                g = g.float().contiguous()
+            grads.append(g)
+            moms.append(st["momentum_buffer"])
+        k = len(params)
+        native().muon_prologue(grads, moms, X[base:base + k], ss[base:base + k], _clip_scale(optimizer),
+                               float(group["momentum"]), True, R > C)
+        base += k
     native().muon_scale(X, ss, n)
     X = newton_schulz_batched(X, 5)
-    if slab is not None:
-        ws = slab.ws
-        native().muon_update_gather(params, X, _shadow_list(params), float(group["lr"]), float(group["weight_decay"]),
-                                    0.2 * math.sqrt(max(R, C)), transpose, ws.bases, ws.mc_base, ws.rank)
+    base = 0
+    for R, C, params in parts:
+        k = len(params)
+        Xi = X[base:base + k]
+        base += k
+        if slab is not None:
+            ws = slab.ws
+            native().muon_update_gather(params, Xi, _shadow_list(params), float(group["lr"]),
+                                        float(group["weight_decay"]), 0.2 * math.sqrt(max(R, C)), R > C, ws.bases,
+                                        ws.mc_base, ws.rank)
+        else:
+            ema, d = _ema_list(optimizer, params)
+            native().muon_epilogue(params, Xi, ema, _shadow_list(params), float(group["lr"]),
+                                   float(group["weight_decay"]), 0.2 * math.sqrt(max(R, C)), R > C, d)
         _mark_shadows(params)
-        return
-    ema, d = _ema_list(optimizer, params)
-    native().muon_epilogue(params, X, ema, _shadow_list(params), float(group["lr"]), float(group["weight_decay"]),
-                           0.2 * math.sqrt(max(R, C)), transpose, d)
-    _mark_shadows(params)
+
+
+def _batches(owned: Dict[Tuple[int, int], List[torch.nn.Parameter]]
+             ) -> List[List[Tuple[int, int, List[torch.nn.Parameter]]]]:
+    """Join shape buckets that differ only by a transpose into one Newton-Schulz batch."""
+
+    joined: Dict[Tuple[int, int], List[Tuple[int, int, List[torch.nn.Parameter]]]] = {}
+    for (R, C), ps in owned.items():
+        if ps:
+            joined.setdefault((min(R, C), max(R, C)), []).append((R, C, ps))
+    return list(joined.values())
 
 
 def _native_muon_group(optimizer, group, distributed: bool) -> None:
@@ -473,28 +504,26 @@ def _native_muon_group(optimizer, group, distributed: bool) -> None:
         return
     buckets = _muon_buckets(params)
     if not distributed:
-        for (R, C), idx in buckets.items():
-            _native_muon_bucket(optimizer, group, [params[i] for i in idx], R, C)
+        for parts in _batches({key: [params[i] for i in idx] for key, idx in buckets.items()}):
+            _native_muon_bucket(optimizer, group, parts)
         return
     world, rank = dist.get_world_size(), dist.get_rank()
+    owned = {key: [params[i] for k, i in enumerate(idx) if k % world == rank] for key, idx in buckets.items()}
     slab = _param_slab(optimizer, group, params)
+    for parts in _batches(owned):
+        _native_muon_bucket(optimizer, group, parts, slab=slab)
     if slab is not None:
-        for (R, C), idx in buckets.items():
-            owned = [params[i] for k, i in enumerate(idx) if k % world == rank]
-            if owned:
-                _native_muon_bucket(optimizer, group, owned, R, C, slab=slab)
+        for idx in buckets.values():
             for k, i in enumerate(idx):
                 if k % world != rank and getattr(params[i], "_kb_shadow", None) is not None:
                     params[i]._kb_shadow_version = -1  # rewritten by its owner: recast before the next forward
         slab.barrier()
         return
     for (R, C), idx in buckets.items():
-        owned = [params[i] for k, i in enumerate(idx) if k % world == rank]
-        if owned:
-            _native_muon_bucket(optimizer, group, owned, R, C)
+        mine = owned[(R, C)]
         per_rank = (len(idx) + world - 1) // world
         send = torch.zeros((per_rank, R * C), device=params[0].device, dtype=torch.float32)
-        for j, p in enumerate(owned):
+        for j, p in enumerate(mine):
             send[j].copy_(p.detach().reshape(-1))
         recv = torch.empty((world * per_rank, R * C), device=send.device, dtype=torch.float32)
         dist.all_gather_into_tensor(recv, send)

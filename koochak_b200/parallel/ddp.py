@@ -35,6 +35,7 @@ finishes them in, so every rank issues the same reductions in the same order.
 from __future__ import annotations
 
 import contextlib
+import os
 from typing import Callable, Dict, List, Optional, Sequence
 
 import torch
@@ -70,7 +71,7 @@ class Bucket:
 class DataParallel(nn.Module):
     def __init__(self, module: nn.Module, *, bucket_cap_mb: float = 25.0, broadcast_buffers: bool = True,
                  transport: str = "auto", process_group=None, find_unused_parameters: bool = False,
-                 comm_blocks: int = 32) -> None:
+                 comm_blocks: Optional[int] = None) -> None:
         super().__init__()
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("DataParallel needs an initialised process group")
@@ -116,6 +117,8 @@ class DataParallel(nn.Module):
 
             tid = {id(p): i for i, p in enumerate(params)}
             segments = [[(p.numel(), tid[id(p)]) for p in b.params] for b in self.buckets]
+            if comm_blocks is None:  # CTAs per bucket kernel (they share the GPU with the overlapped backward)
+                comm_blocks = int(os.environ.get("KOOCHAK_B200_COMM_BLOCKS", 32))
             self._fused = FusedGradReducer(segments, len(params), self.device, process_group, blocks=comm_blocks)
             for b, buf in zip(self.buckets, self._fused.buffers):
                 assert buf.numel() == b.numel

@@ -191,7 +191,7 @@ def test_optimizer_kernels_match_reference():
     from koochak_b200.optim.muon import SingleDeviceMuonWithAuxAdam
 
     torch.manual_seed(6)
-    shapes = [(96, 64), (64, 160), (64, 160), (32,), (128, 48, 2)]
+    shapes = [(96, 64), (64, 160), (64, 160), (32,), (128, 48, 2), (64, 96)]
 
     def make():
         torch.manual_seed(7)

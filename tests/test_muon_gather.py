@@ -25,7 +25,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-SHAPES = [(256, 512)] * 3 + [(512, 256)] * 3 + [(384, 384)] * 2 + [(128, 640)]
+SHAPES = [(256, 512)] * 3 + [(512, 256)] * 3 + [(384, 384)] * 2 + [(128, 640), (640, 128)]
 
 
 def _worker(rank: int, world: int, port: int, use_mc: bool, result_dir: str) -> None:
