@@ -119,6 +119,8 @@ class DataParallel(nn.Module):
             segments = [[(p.numel(), tid[id(p)]) for p in b.params] for b in self.buckets]
             if comm_blocks is None:  # CTAs per bucket kernel (they share the GPU with the overlapped backward)
                 comm_blocks = int(os.environ.get("KOOCHAK_B200_COMM_BLOCKS", 32))
+            # CTAs for the reductions that nothing overlaps (after backward).
+            self._tail_blocks = max(comm_blocks, int(os.environ.get("KOOCHAK_B200_COMM_TAIL_BLOCKS", 128)))
             self._fused = FusedGradReducer(segments, len(params), self.device, process_group, blocks=comm_blocks)
             for b, buf in zip(self.buckets, self._fused.buffers):
                 assert buf.numel() == b.numel
@@ -193,31 +195,35 @@ class DataParallel(nn.Module):
             b.complete = True
             self._launch_ready()
 
-    def _launch_ready(self) -> None:
+    def _launch_ready(self, tail: bool = False) -> None:
         # Strict index order: the reductions pair up across ranks by sequence.
+        # Buckets launched once backward has finished (``tail``), and the last
+        # bucket, have no compute left to overlap with: they get the wider
+        # grid. Every rank makes the same choice for the same bucket.
         while self._next_launch < len(self.buckets) and self.buckets[self._next_launch].complete:
-            self._launch(self.buckets[self._next_launch])
+            b = self.buckets[self._next_launch]
+            self._launch(b, wide=tail or b.index == len(self.buckets) - 1)
             self._next_launch += 1
 
-    def _launch(self, b: Bucket) -> None:
+    def _launch(self, b: Bucket, wide: bool = False) -> None:
         if self._comm_stream is None:
-            self._reduce_now(b)
+            self._reduce_now(b, wide)
             return
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self._comm_stream):
             self._comm_stream.wait_event(ev)
-            self._reduce_now(b)
+            self._reduce_now(b, wide)
             b.buffer.record_stream(self._comm_stream)
             done = torch.cuda.Event()
             done.record(self._comm_stream)
             b.ready_event = done
 
-    def _reduce_now(self, b: Bucket) -> None:
+    def _reduce_now(self, b: Bucket, wide: bool = False) -> None:
         if self.transport == "fused":
             assert self._fused is not None
             scale = self.grad_scale_fn() if self.grad_scale_fn is not None else self.grad_scale
-            self._fused.reduce(b.index, scale)
+            self._fused.reduce(b.index, scale, blocks=self._tail_blocks if wide else None)
         elif self.transport == "nccl":
             dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
         else:
@@ -234,7 +240,7 @@ class DataParallel(nn.Module):
                         b.view_of(i).zero_()
                 b.pending = 0
                 b.complete = True
-        self._launch_ready()
+        self._launch_ready(tail=True)
         cur = torch.cuda.current_stream(self.device) if self._comm_stream is not None else None
         for b in self.buckets:
             if cur is not None and b.ready_event is not None:

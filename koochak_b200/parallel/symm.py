@@ -167,12 +167,17 @@ class FusedGradReducer:
         self.epoch = (self.epoch + 2) & 0xFFFFFFFF
         return e
 
-    def reduce(self, b: int, scale: Optional[torch.Tensor] = None) -> None:
-        """All-reduce bucket ``b`` (average, unscale, statistics) on the current stream."""
+    def reduce(self, b: int, scale: Optional[torch.Tensor] = None, blocks: Optional[int] = None) -> None:
+        """All-reduce bucket ``b`` (average, unscale, statistics) on the current stream.
 
+        ``blocks`` overrides the grid size for this launch (every rank must
+        pass the same value for the same bucket); at most 128.
+        """
+
+        nb = min(int(blocks), 128) if blocks else self.blocks
         self._C.comm_allreduce_bucket(self.ws.bases, self.ws.mc_base, self.flags_off, self.stats_off[self.parity],
                                       self.bucket_off[b], self.chunks[b], self.n_tensors, self.rank,
-                                      self._next_epoch(), scale, self.blocks, self.timeout_s)
+                                      self._next_epoch(), scale, nb, self.timeout_s)
 
     def barrier(self) -> None:
         self._C.comm_barrier(self.ws.bases, self.flags_off, self.rank, self._next_epoch(), self.blocks,

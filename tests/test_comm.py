@@ -96,7 +96,8 @@ def _worker(rank: int, world: int, port: int, use_mc: bool, result_dir: str) -> 
                     allv = torch.randn(world, n, generator=g)
                     red.buffers[b][off:off + n].copy_(allv[rank].cuda())
                     expect[t] = (b, off, allv.mean(0) / scale.item())
-                red.reduce(b, scale)
+                # Second step: the last bucket runs on a wider grid than the rest (as after backward).
+                red.reduce(b, scale, blocks=32 if step == 1 and b == len(red.layouts) - 1 else None)
             torch.cuda.synchronize()
             stats = red.current_stats().cpu()
             for t, (b, off, ref) in expect.items():
