@@ -36,7 +36,7 @@ import sys
 import tempfile
 import threading
 import time
-from typing import Any, Dict, List, Optional
+from typing import Any, Dict, List, Optional, Tuple
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "tokens/sec at 1/2/4/8 B200 (GPT-2 124M DDP+Muon); exposed comm ms/step"
@@ -80,7 +80,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int) -> None:
         self.gpu_index = gpu_index
         self.proc: Optional[subprocess.Popen] = None
-        self.lines: List[str] = []
+        self.lines: List[Tuple[float, str]] = []  # (arrival time, csv line)
         self._thread: Optional[threading.Thread] = None
 
     def start(self) -> None:
@@ -95,12 +95,20 @@ class ClockSampler:
         def read():
             assert self.proc is not None and self.proc.stdout is not None
             for line in self.proc.stdout:
-                self.lines.append(line.strip())
+                self.lines.append((time.perf_counter(), line.strip()))
 
         self._thread = threading.Thread(target=read, daemon=True)
         self._thread.start()
 
-    def stop(self) -> Dict[str, Any]:
+    def stop(self, t_lo: Optional[float] = None, t_hi: Optional[float] = None) -> Dict[str, Any]:
+        """Stop sampling; summarise the samples that arrived in [t_lo, t_hi].
+
+        The sampler is started during warm-up, so a timed region shorter than
+        the sampling period still has samples under load: when none arrived
+        inside the window, the ones from the second before it are used and
+        ``window`` says so.
+        """
+
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -111,7 +119,12 @@ class ClockSampler:
             self._thread.join(timeout=2)
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        window = "timed"
+        picked = [ln for t, ln in self.lines if (t_lo is None or t >= t_lo) and (t_hi is None or t <= t_hi)]
+        if not picked and t_lo is not None:
+            picked = [ln for t, ln in self.lines if t_lo - 1.0 <= t <= (t_hi if t_hi is not None else t_lo)]
+            window = "last second of warm-up"
+        for line in picked:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -124,7 +137,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 # --------------------------------------------------------------------------- workloads
@@ -217,9 +230,11 @@ class StepTimer:
 
     def __call__(self, log, ctx):
         step = int(ctx["step"])
+        if step == 0 and self.warmup > 1 and self.sampler is not None:
+            self.sampler.start()  # during warm-up: nvidia-smi needs a few hundred ms for its first sample
         if step == self.warmup - 1:
             self._barrier()
-            if self.sampler is not None:
+            if self.sampler is not None and self.sampler.proc is None:
                 self.sampler.start()
             if self.native_counter is not None:
                 self.launch0 = self.native_counter()
@@ -232,7 +247,7 @@ class StepTimer:
             if self.native_counter is not None:
                 self.launch1 = self.native_counter()
             if self.sampler is not None:
-                self.clocks = self.sampler.stop()
+                self.clocks = self.sampler.stop(self.t0, self.t1)
 
     def ms_per_step(self) -> float:
         if self.wall:

@@ -120,6 +120,63 @@ __global__ void __launch_bounds__(256)
   __threadfence_system();
 }
 
+// Matrices already in their wide orientation (no transpose): one contiguous
+// index for every operand, so a CTA takes 4096 consecutive elements, four
+// float4 per thread with all loads issued first. Same expression as above.
+constexpr int kGatherFlatVecs = 4;
+constexpr int kGatherFlatPerCta = 256 * kGatherFlatVecs;  // float4 per CTA
+
+template <bool MULTIMEM>
+__global__ void __launch_bounds__(256)
+    muon_update_gather_flat_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X,
+                                   float lr, float wd, float scale) {
+  const int i = blockIdx.y;
+  const long long n4 = (long long)mm.R * mm.C / 4;
+  float4* p = reinterpret_cast<float4*>(mm.p[i]);
+  uint2* sh = reinterpret_cast<uint2*>(mm.shadow[i]);
+  const uint2* x = reinterpret_cast<const uint2*>(X + (long long)i * mm.R * mm.C);
+  const long long j0 = (long long)blockIdx.x * kGatherFlatPerCta + threadIdx.x;
+  const float decay = 1.f - lr * wd;
+  float4 pv[kGatherFlatVecs];
+  uint2 xv[kGatherFlatVecs];
+#pragma unroll
+  for (int k = 0; k < kGatherFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      pv[k] = p[j];
+      xv[k] = x[j];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kGatherFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&xv[k].x);
+      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&xv[k].y);
+      float4 pn;
+      pn.x = pv[k].x * decay - lr * (scale * __low2float(lo));
+      pn.y = pv[k].y * decay - lr * (scale * __high2float(lo));
+      pn.z = pv[k].z * decay - lr * (scale * __low2float(hi));
+      pn.w = pv[k].w * decay - lr * (scale * __high2float(hi));
+      if constexpr (MULTIMEM) {
+        mm_st_v4(shifted(reinterpret_cast<float*>(p + j), mm.mc_delta), pn);
+      } else {
+        for (int q = 0; q < mm.world; ++q) __stcg(shifted(p + j, mm.delta[q]), pn);
+      }
+      if (sh) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(pn.x, pn.y);
+        __nv_bfloat162 b = __floats2bfloat162_rn(pn.z, pn.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&a);
+        packed.y = *reinterpret_cast<uint32_t*>(&b);
+        sh[j] = packed;
+      }
+    }
+  }
+  if constexpr (MULTIMEM) asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
 }  // namespace
 
 // params: this rank's owned matrices (views into the symmetric slab), all [R, C]
@@ -168,6 +225,17 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
                "muon_update_gather: shadow must be a contiguous 8-byte aligned bf16 copy of the parameter");
     }
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()) + (int64_t)base * R * C;
+    if (!transpose) {  // C % 4 == 0, params 16-byte and X / shadows 8-byte aligned (checked above)
+      const long long n4 = (long long)R * C / 4;
+      dim3 fgrid((unsigned)((n4 + kGatherFlatPerCta - 1) / kGatherFlatPerCta), count);
+      if (mc_base != 0) {
+        muon_update_gather_flat_kernel<true><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale);
+      } else {
+        muon_update_gather_flat_kernel<false><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale);
+      }
+      KB_LAUNCHED();
+      continue;
+    }
     dim3 grid((C + 31) / 32, (R + 31) / 32, count);
     if (mc_base != 0) {
       muon_update_gather_kernel<true><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose);

@@ -418,6 +418,122 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Flat variants for matrices already in their wide orientation (no
+// transpose): every operand shares one contiguous index, so a CTA takes 4096
+// consecutive elements, four float4 per thread with all loads issued before
+// the first use (the tiled kernels above keep one 4-byte load per thread in
+// flight). Same expressions as the tiled kernels.
+constexpr int kFlatVecs = 4;                  // float4 per thread
+constexpr int kFlatVecsPerCta = 256 * kFlatVecs;
+
+__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+  uint2 r;
+  r.x = *reinterpret_cast<uint32_t*>(&lo);
+  r.y = *reinterpret_cast<uint32_t*>(&hi);
+  return r;
+}
+
+__device__ __forceinline__ float4 unpack_bf16x4(uint2 r) {
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&r.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&r.y);
+  return make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+}
+
+__global__ void __launch_bounds__(256)
+    muon_prologue_flat_kernel(const __grid_constant__ MuonMats mm, __nv_bfloat16* __restrict__ X,
+                              float* __restrict__ sumsq, const float* __restrict__ coef_ptr, float beta, int nesterov) {
+  const int i = blockIdx.y;
+  const long long n4 = (long long)mm.R * mm.C / 4;
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  const float4* g = reinterpret_cast<const float4*>(mm.g[i]);
+  float4* m = reinterpret_cast<float4*>(mm.mom[i]);
+  uint2* x = reinterpret_cast<uint2*>(X + (long long)i * mm.R * mm.C);
+  const long long j0 = (long long)blockIdx.x * kFlatVecsPerCta + threadIdx.x;
+  float4 gv[kFlatVecs], mv[kFlatVecs];
+#pragma unroll
+  for (int k = 0; k < kFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      gv[k] = g[j];
+      mv[k] = m[j];
+    }
+  }
+  float local = 0.f;
+#pragma unroll
+  for (int k = 0; k < kFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      float gi[4] = {gv[k].x * coef, gv[k].y * coef, gv[k].z * coef, gv[k].w * coef};
+      float mi[4] = {mv[k].x, mv[k].y, mv[k].z, mv[k].w};
+      float u[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mi[e] = mi[e] + (1.f - beta) * (gi[e] - mi[e]);
+        const float t = nesterov ? gi[e] + beta * (mi[e] - gi[e]) : mi[e];
+        u[e] = __bfloat162float(__float2bfloat16_rn(t));
+        local += u[e] * u[e];
+      }
+      m[j] = make_float4(mi[0], mi[1], mi[2], mi[3]);
+      x[j] = pack_bf16x4(u[0], u[1], u[2], u[3]);
+    }
+  }
+  local = warp_sum(local);
+  __shared__ float part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k];
+    atomicAdd(&sumsq[i], t);
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    muon_epilogue_flat_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr,
+                              float wd, float scale, float ema_decay) {
+  const int i = blockIdx.y;
+  const long long n4 = (long long)mm.R * mm.C / 4;
+  float4* p = reinterpret_cast<float4*>(mm.p[i]);
+  float4* e = reinterpret_cast<float4*>(mm.ema[i]);
+  uint2* sh = reinterpret_cast<uint2*>(mm.shadow[i]);
+  const uint2* x = reinterpret_cast<const uint2*>(X + (long long)i * mm.R * mm.C);
+  const long long j0 = (long long)blockIdx.x * kFlatVecsPerCta + threadIdx.x;
+  const float decay = 1.f - lr * wd;
+  float4 pv[kFlatVecs];
+  uint2 xv[kFlatVecs];
+#pragma unroll
+  for (int k = 0; k < kFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      pv[k] = p[j];
+      xv[k] = x[j];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kFlatVecs; ++k) {
+    const long long j = j0 + k * 256;
+    if (j < n4) {
+      const float4 u = unpack_bf16x4(xv[k]);
+      float4 pn;
+      pn.x = pv[k].x * decay - lr * (scale * u.x);
+      pn.y = pv[k].y * decay - lr * (scale * u.y);
+      pn.z = pv[k].z * decay - lr * (scale * u.z);
+      pn.w = pv[k].w * decay - lr * (scale * u.w);
+      p[j] = pn;
+      if (e) {
+        const float4 ev = e[j];
+        e[j] = make_float4(ev.x * ema_decay + (1.f - ema_decay) * pn.x, ev.y * ema_decay + (1.f - ema_decay) * pn.y,
+                           ev.z * ema_decay + (1.f - ema_decay) * pn.z, ev.w * ema_decay + (1.f - ema_decay) * pn.w);
+      }
+      if (sh) sh[j] = pack_bf16x4(pn.x, pn.y, pn.z, pn.w);
+    }
+  }
+}
+
+static bool aligned(const void* ptr, uintptr_t a) { return ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % a == 0; }
+
 static MuonMats make_mats(const std::vector<at::Tensor>& grads, const std::vector<at::Tensor>& moms,
                           const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& ema,
                           const std::vector<at::Tensor>& shadow, size_t base, int count) {
@@ -456,10 +572,19 @@ void muon_prologue(const std::vector<at::Tensor>& grads, const std::vector<at::T
   for (size_t base = 0; base < n; base += kMuonMax) {
     const int count = (int)std::min<size_t>(kMuonMax, n - base);
     MuonMats mm = make_mats(grads, moms, {}, {}, {}, base, count);
-    dim3 grid((C + 31) / 32, (R + 31) / 32, count);
-    muon_prologue_kernel<<<grid, 256, 0, s>>>(mm, (__nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C,
-                                              sumsq.data_ptr<float>() + base, cp, (float)beta, nesterov ? 1 : 0,
-                                              transpose ? 1 : 0);
+    __nv_bfloat16* xb = (__nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C;
+    bool flat = !transpose && ((int64_t)R * C) % 4 == 0 && aligned(xb, 8);
+    for (int j = 0; j < count && flat; ++j) flat = aligned(mm.g[j], 16) && aligned(mm.mom[j], 16);
+    if (flat) {
+      const long long n4 = (long long)R * C / 4;
+      dim3 grid((unsigned)((n4 + kFlatVecsPerCta - 1) / kFlatVecsPerCta), count);
+      muon_prologue_flat_kernel<<<grid, 256, 0, s>>>(mm, xb, sumsq.data_ptr<float>() + base, cp, (float)beta,
+                                                     nesterov ? 1 : 0);
+    } else {
+      dim3 grid((C + 31) / 32, (R + 31) / 32, count);
+      muon_prologue_kernel<<<grid, 256, 0, s>>>(mm, xb, sumsq.data_ptr<float>() + base, cp, (float)beta,
+                                                nesterov ? 1 : 0, transpose ? 1 : 0);
+    }
     KB_LAUNCHED();
   }
 }
@@ -485,9 +610,19 @@ void muon_epilogue(const std::vector<at::Tensor>& params, const at::Tensor& X, c
   for (size_t base = 0; base < n; base += kMuonMax) {
     const int count = (int)std::min<size_t>(kMuonMax, n - base);
     MuonMats mm = make_mats({}, {}, params, ema, shadow, base, count);
-    dim3 grid((C + 31) / 32, (R + 31) / 32, count);
-    muon_epilogue_kernel<<<grid, 256, 0, s>>>(mm, (const __nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C,
-                                              (float)lr, (float)wd, (float)scale, transpose ? 1 : 0, (float)ema_decay);
+    const __nv_bfloat16* xb = (const __nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C;
+    bool flat = !transpose && ((int64_t)R * C) % 4 == 0 && aligned(xb, 8);
+    for (int j = 0; j < count && flat; ++j)
+      flat = aligned(mm.p[j], 16) && aligned(mm.ema[j], 16) && aligned(mm.shadow[j], 8);
+    if (flat) {
+      const long long n4 = (long long)R * C / 4;
+      dim3 grid((unsigned)((n4 + kFlatVecsPerCta - 1) / kFlatVecsPerCta), count);
+      muon_epilogue_flat_kernel<<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, (float)ema_decay);
+    } else {
+      dim3 grid((C + 31) / 32, (R + 31) / 32, count);
+      muon_epilogue_kernel<<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose ? 1 : 0,
+                                                (float)ema_decay);
+    }
     KB_LAUNCHED();
   }
 }
