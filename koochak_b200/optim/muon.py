@@ -22,14 +22,15 @@ Execution:
   groups are one multi-tensor kernel (clip coefficient, moments, bias
   correction, decoupled weight decay, EMA and bf16 copy).
 * Distributed classes (chosen when a process group exists) shard the Muon
-  work: within each shape bucket, matrix k is owned by rank k % world (its
-  momentum lives only there). On CUDA the group's matrices are stored in one
+  work: matrix i of the size-sorted group is owned by rank i % world, as in
+  the reference (its momentum lives only there). On CUDA the group's matrices are stored in one
   symmetric-memory slab (``parallel.symm.SymmetricParamSlab``) and the
   owner's update kernel stores each new matrix into every rank's copy over
   NVLink (P2P stores, or ``multimem.st`` through NVSwitch), followed by one
   bounded cross-GPU barrier per step: the all-gather is fused into the
   update. ``KOOCHAK_B200_MUON_GATHER=nccl`` (or matrices whose column count
-  is not a multiple of 4) selects one NCCL all-gather per bucket instead.
+  is not a multiple of 4) selects one NCCL all-gather per shape bucket
+  instead, with matrix k of each bucket owned by rank k % world.
   Adam groups run on every rank, as in the reference.
 
 The training loop passes the gradient-clip coefficient as a device scalar
@@ -508,17 +509,22 @@ def _native_muon_group(optimizer, group, distributed: bool) -> None:
             _native_muon_bucket(optimizer, group, parts)
         return
     world, rank = dist.get_world_size(), dist.get_rank()
-    owned = {key: [params[i] for k, i in enumerate(idx) if k % world == rank] for key, idx in buckets.items()}
     slab = _param_slab(optimizer, group, params)
-    for parts in _batches(owned):
-        _native_muon_bucket(optimizer, group, parts, slab=slab)
     if slab is not None:
-        for idx in buckets.values():
-            for k, i in enumerate(idx):
-                if k % world != rank and getattr(params[i], "_kb_shadow", None) is not None:
-                    params[i]._kb_shadow_version = -1  # rewritten by its owner: recast before the next forward
+        # Owner of matrix i is rank i % W over the (size-sorted) group, as in
+        # the reference's distributed step, so rank 0 holds the momentum of the
+        # same matrices in both frameworks.
+        owned = {key: [params[i] for i in idx if i % world == rank] for key, idx in buckets.items()}
+        for parts in _batches(owned):
+            _native_muon_bucket(optimizer, group, parts, slab=slab)
+        for i, p in enumerate(params):
+            if i % world != rank and getattr(p, "_kb_shadow", None) is not None:
+                p._kb_shadow_version = -1  # rewritten by its owner: recast before the next forward
         slab.barrier()
         return
+    owned = {key: [params[i] for k, i in enumerate(idx) if k % world == rank] for key, idx in buckets.items()}
+    for parts in _batches(owned):
+        _native_muon_bucket(optimizer, group, parts)
     for (R, C), idx in buckets.items():
         mine = owned[(R, C)]
         per_rank = (len(idx) + world - 1) // world

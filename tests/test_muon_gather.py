@@ -1,8 +1,8 @@
 """Sharded Muon with the parameter all-gather fused into the owner's update kernel.
 
 Each rank runs the distributed ``MuonWithAuxAdam`` on the same parameters and
-the same (already averaged) gradients; matrix k of a shape bucket is owned by
-rank k % world, whose update kernel stores the new matrix into every rank's
+the same (already averaged) gradients; matrix i of the size-sorted group is
+owned by rank i % world (the reference's rule), whose update kernel stores the new matrix into every rank's
 copy (P2P stores, or ``multimem.st`` where the switch offers multicast). The
 oracle is the single-GPU ``SingleDeviceMuonWithAuxAdam`` on a copy of the
 parameters on the same GPU: every rank must end up with the single-GPU result
@@ -77,6 +77,11 @@ def _worker(rank: int, world: int, port: int, use_mc: bool, result_dir: str) -> 
             lo = slab.ws.tensor.data_ptr()
             if not all(lo <= p.data_ptr() < lo + slab.ws.nbytes for p in dist_p):
                 msgs.append("parameters are not stored in the slab")
+        # Ownership follows the reference: index in the size-sorted group mod world.
+        order = opt.param_groups[0]["params"]
+        for i, p in enumerate(order):
+            if ("momentum_buffer" in opt.state[p]) != (i % world == rank):
+                msgs.append(f"matrix {i} of the sorted group: momentum on the wrong rank")
         # Owners wrote their bf16 copies; the others are marked for recast.
         for p in dist_p:
             owned = "momentum_buffer" in opt.state[p]
