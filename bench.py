@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--grad-accum", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--bucket-mb", type=int, default=None,
+                    help="data-parallel gradient bucket size in MB (train.ddp_bucket_cap_mb; both arms)")
     ap.add_argument("--comm", default="fused", help="gradient-sync transport: fused (in-kernel NVLink) | nccl")
     args = ap.parse_args()
     defaults = {"gpt2": dict(micro_batch=16, seq=1024, layers=12, grad_accum=1, vocab=50257),
@@ -200,6 +202,7 @@ def train_cfg_for(args, world: int, steps: int, out_dir: str, scalarize: bool) -
         "grad_clip_norm": 1.0, "amp": "bf16", "ddp": world > 1, "out_dir": out_dir, "keep_last_k": 1,
         "scalarize_loss_every_step": scalarize, "ema": {"enabled": True, "decay": 0.999, "offload_to_cpu": False},
         "comm_transport": args.comm, "warn_unsharded": False, "grad_accum": args.grad_accum,
+        **({"ddp_bucket_cap_mb": args.bucket_mb} if args.bucket_mb else {}),
     }
 
 
