@@ -25,6 +25,16 @@ LINEAR: Dict[str, Tuple[int, int]] = {  # name -> (N out, K in)
     "lm_head": (50304, 768),
 }
 
+# Llama-style 1.3B at 4 x 2048 tokens per GPU (M = 8192): fused q/k/v, output
+# projection, fused gate/up, down projection, LM head.
+LINEAR_LLAMA: Dict[str, Tuple[int, int]] = {
+    "l_qkv": (6144, 2048),
+    "l_o": (2048, 2048),
+    "l_gate_up": (11008, 2048),
+    "l_down": (2048, 5504),
+    "l_lm_head": (32000, 2048),
+}
+
 
 def time_ms(fn: Callable[[], object], iters: int, warmup: int = 3) -> float:
     for _ in range(warmup):
@@ -97,7 +107,9 @@ def main(argv: List[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--case", default="all", help="linear layer name, 'ns<c>' (e.g. ns768) or 'all'")
     ap.add_argument("--op", default="all", help="fwd | dgrad | wgrad | XXt | AA | BX | all")
-    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--tokens", type=int, default=None, help="M (default 16384 for gpt2, 8192 for llama)")
+    ap.add_argument("--model", choices=["gpt2", "llama"], default="gpt2",
+                    help="which model's linear and Newton-Schulz shapes 'all' covers")
     ap.add_argument("--block-n", type=int, default=0, help="0 auto; 128/256 one-SM tiles; -128/-256 two-SM tiles")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS comparison")
@@ -108,6 +120,9 @@ def main(argv: List[str] | None = None) -> None:
                     help="also report where each role of the GEMM waited (clock64 counters per CTA)")
     args = ap.parse_args(argv)
     torch.manual_seed(0)
+    if args.tokens is None:
+        args.tokens = 16384 if args.model == "gpt2" else 8192
+    LINEAR.update(LINEAR_LLAMA)
     if args.shape:
         m, n, k = (int(v) for v in args.shape.split(","))
         LINEAR["custom"] = (n, k)
@@ -116,9 +131,18 @@ def main(argv: List[str] | None = None) -> None:
         from koochak_b200.ops import native
 
         native().gemm_set_debug(args.debug_mode)
-    names = list(LINEAR) + ["ns768", "ns2304", "ns3072"] if args.case == "all" else [args.case]
+    if args.case != "all":
+        names = [args.case]
+    elif args.model == "gpt2":
+        names = [n for n in LINEAR if n not in LINEAR_LLAMA] + ["ns768", "ns2304", "ns3072"]
+    else:
+        names = list(LINEAR_LLAMA) + ["nsL2048", "nsL5504"]
     for name in names:
-        if name.startswith("ns"):
+        if name.startswith("nsL"):
+            # Llama Muon batches: 2048 x c matrices, 8 per batch (one rank's share at 8 GPUs x 3)
+            cases = ns_cases(int(name[3:]), batch=8, r=2048, block_n=args.block_n)
+            items = [(op, fl, a, b) for op, (fl, a, b) in cases.items()]
+        elif name.startswith("ns"):
             cases = ns_cases(int(name[2:]), block_n=args.block_n)
             items = [(op, fl, a, b) for op, (fl, a, b) in cases.items()]
         else:

@@ -6,10 +6,14 @@ GPT-2 124M shapes (``--preset gpt2``: 12 x [2304x768, 768x768, 3072x768,
 1.3B ones (``--preset llama``), gradients drawn N(0, 1e-3). Phases, each timed
 with CUDA events on the launching stream after warm-up, max over ranks:
 
-* ``sync``: gradient all-reduce + GradScaler unscale + finite flag +
+* ``sync``: gradient reduction + GradScaler unscale + finite flag +
   per-tensor sums of squares + clip coefficient.
-  - fused: one kernel per 25 MB bucket over NVLink (``FusedGradReducer``,
-    P2P or NVSwitch multimem), then the one-thread gate;
+  - fused: one kernel per bucket (``--bucket-mb``, default 25) over NVLink
+    (``FusedGradReducer``, P2P or NVSwitch multimem), then the seal + gate
+    kernel. Two plans: ``allreduce`` (every reduced value to every rank) and
+    ``sharded`` (what the sharded optimizer asks for: matrix i of the
+    size-sorted Muon group reduced into rank i % W only, every vector
+    reduce-scattered);
   - nccl: ``dist.all_reduce`` per bucket, then the unscale/finite/norm pass
     (``torch._amp_foreach_non_finite_check_and_unscale_`` + per-tensor
     ``torch._foreach_norm``), i.e. what torch DDP + GradScaler + clipping do.
@@ -19,8 +23,9 @@ with CUDA events on the launching stream after warm-up, max over ranks:
     (symmetric slab, P2P or multimem) + one bounded barrier;
   - nccl: the same update, then one NCCL all-gather per shape bucket.
 
-Roofline for ``sync``: the bytes that must cross NVLink per GPU for an
-all-reduce of B bytes, 2 (W-1)/W B, at the measured 770 GB/s per direction.
+Roofline for ``sync``: the bytes that must cross NVLink per GPU per
+direction, at the measured 770 GB/s: 2 (W-1)/W B for an all-reduce of B
+bytes, (W-1)/W B for the sharded plan (each element reduced once, by one rank).
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
         -m koochak_b200.benchmarks.gradsync --preset gpt2
@@ -74,41 +79,46 @@ def _time(fn, iters: int, warmup: int) -> float:
     return float(ms)
 
 
-def _buckets(sizes: List[int], cap: int) -> List[List[int]]:
-    out, cur, n = [], [], 0
-    for i, s in enumerate(sizes):
-        if cur and n + s > cap:
-            out.append(cur)
-            cur, n = [], 0
-        cur.append(i)
-        n += s
-    if cur:
-        out.append(cur)
-    return out
-
-
-def bench_sync(grads: List[torch.Tensor], iters: int, warmup: int, blocks: List[int]) -> Dict[str, float]:
+def bench_sync(grads: List[torch.Tensor], n_mats: int, iters: int, warmup: int, blocks: List[int],
+               bucket_mb: float) -> Dict[str, float]:
+    from koochak_b200.parallel.ddp import split_buckets
     from koochak_b200.parallel.symm import FusedGradReducer
 
     world = dist.get_world_size()
     sizes = [g.numel() for g in grads]
-    buckets = _buckets(sizes, 25 * 2 ** 20 // 4)
+    # Gradient order: reverse of registration, as backward produces them.
+    order = list(reversed(range(len(grads))))
+    buckets = [[order[j] for j in b] for b in split_buckets([sizes[i] for i in order], [int(bucket_mb * 2 ** 20 / 4)])]
     segs = [[(sizes[i], i) for i in b] for b in buckets]
     scale = torch.tensor([1024.0], device="cuda")
-    out: Dict[str, float] = {}
-    for nb in blocks:
-        red = FusedGradReducer(segs, len(grads), grads[0].device, blocks=nb)
-        for b in range(len(buckets)):
-            for (off, n, t) in red.layouts[b]:
-                red.buffers[b][off:off + n].copy_(grads[t].view(-1))
-
-        def fused():
-            red.begin_step()
+    # Muon ownership: matrix i of the size-sorted group on rank i % W.
+    by_size = sorted(range(n_mats), key=lambda i: sizes[i], reverse=True)
+    owners = {t: k % world for k, t in enumerate(by_size)}
+    out: Dict[str, float] = {"buckets": float(len(buckets))}
+    nbytes = 4 * sum(sizes)
+    for plan, owner_of, shard_rest in (("allreduce", {}, False), ("sharded", owners, True)):
+        for nb in blocks:
+            red = FusedGradReducer(segs, len(grads), grads[0].device, blocks=nb, owner_of=owner_of,
+                                   shard_rest=shard_rest)
             for b in range(len(buckets)):
-                red.reduce(b, scale)
-            red.gate(1.0)
+                for (off, n, t) in red.layouts[b]:
+                    red.buffers[b][off:off + n].copy_(grads[t].view(-1))
 
-        out[f"fused_ms_blocks{nb}"] = _time(fused, iters, warmup)
+            def fused():
+                red.begin_step()
+                for b in range(len(buckets)):
+                    red.reduce(b, scale)
+                red.seal_gate(1.0)
+
+            out[f"{plan}_ms_blocks{nb}"] = _time(fused, iters, warmup)
+            out["multimem"] = float(bool(red.ws.mc_base))
+            del red
+            torch.cuda.empty_cache()
+        best = min(v for k, v in out.items() if k.startswith(f"{plan}_ms_blocks"))
+        out[f"{plan}_ms"] = best
+        mult = 2.0 if plan == "allreduce" else 1.0
+        out[f"{plan}_roofline_ms"] = mult * (world - 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3
+        out[f"{plan}_frac_of_roofline"] = out[f"{plan}_roofline_ms"] / best
 
     flat = [torch.cat([grads[i].view(-1) for i in b]) for b in buckets]
     views = []
@@ -126,12 +136,7 @@ def bench_sync(grads: List[torch.Tensor], iters: int, warmup: int, blocks: List[
         total = torch.linalg.vector_norm(norms.double())
         torch.clamp(1.0 / (total + 1e-6), max=1.0)
 
-    nbytes = 4 * sum(red.bucket_numel)
-    out["fused_ms"] = min(v for k, v in out.items() if k.startswith("fused_ms_"))
-    out.update({"nccl_ms": _time(nccl, iters, warmup), "grad_bytes": float(nbytes),
-                "multimem": float(bool(red.ws.mc_base))})
-    out["roofline_ms"] = 2 * (world - 1) / world * nbytes / (LINK_GBS * 1e9) * 1e3
-    out["fused_frac_of_roofline"] = out["roofline_ms"] / out["fused_ms"]
+    out.update({"nccl_ms": _time(nccl, iters, warmup), "grad_bytes": float(nbytes)})
     return out
 
 
@@ -163,7 +168,8 @@ def main() -> int:
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--phase", choices=["sync", "muon", "all"], default="all")
-    ap.add_argument("--blocks", default="32", help="comma-separated CTA counts of the fused all-reduce to time")
+    ap.add_argument("--blocks", default="32", help="comma-separated CTA counts of the fused reduction to time")
+    ap.add_argument("--bucket-mb", type=float, default=25.0, help="gradient bucket size")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -178,7 +184,8 @@ def main() -> int:
             g = torch.Generator(device="cpu").manual_seed(1 + rank)
             grads = [(torch.randn(r * c, generator=g) * 1e-3).to(dev) for r, c in mats]
             grads += [(torch.randn(n, generator=g) * 1e-3).to(dev) for n in vecs]
-            out["sync"] = bench_sync(grads, args.iters, args.warmup, [int(b) for b in args.blocks.split(",")])
+            out["sync"] = bench_sync(grads, len(mats), args.iters, args.warmup,
+                                     [int(b) for b in args.blocks.split(",")], args.bucket_mb)
             del grads
             torch.cuda.empty_cache()
         if args.phase in ("muon", "all"):

@@ -94,6 +94,26 @@ def cases() -> Dict[str, Tuple[Callable[[], object], float, str]]:
     out["attn_fwd_sdpa"] = (sdpa_fwd, fl_fwd, "flop")
     out["attn_bwd_sdpa"] = (lambda: torch.autograd.grad(ot, (qt, kt, vt), gt, retain_graph=True), 2.5 * fl_fwd,
                             "flop")
+    # Llama-style 1.3B: B4, H16, S2048, D128, causal.
+    qkvl = torch.randn(4, 2048, 3, 16, 128, device=dev).bfloat16()
+    ql, kl, vl = qkvl[:, :, 0], qkvl[:, :, 1], qkvl[:, :, 2]
+    ol, lsel = kf.flash_attention_forward(ql, kl, vl, causal=True)
+    dol = torch.randn_like(ol)
+    fl_l = 4.0 * 4 * 16 * 2048 * 2048 * 128 / 2
+    out["attn_fwd_llama"] = (lambda: kf.flash_attention_forward(ql, kl, vl, causal=True), fl_l, "flop")
+    out["attn_bwd_llama"] = (lambda: kf.flash_attention_backward(ql, kl, vl, ol, dol, lsel, causal=True),
+                             2.5 * fl_l, "flop")
+    qlt, klt, vlt = (t.transpose(1, 2).contiguous().requires_grad_(True) for t in (ql, kl, vl))
+
+    def sdpa_fwd_l():
+        with torch.no_grad():
+            return sd(qlt, klt, vlt, is_causal=True)
+
+    olt = sd(qlt, klt, vlt, is_causal=True)
+    glt = torch.randn_like(olt)
+    out["attn_fwd_llama_sdpa"] = (sdpa_fwd_l, fl_l, "flop")
+    out["attn_bwd_llama_sdpa"] = (lambda: torch.autograd.grad(olt, (qlt, klt, vlt), glt, retain_graph=True),
+                                  2.5 * fl_l, "flop")
     return out
 
 
@@ -104,7 +124,7 @@ def main(argv: List[str] | None = None) -> None:
     args = ap.parse_args(argv)
     torch.manual_seed(0)
     for name, (fn, amount, kind) in cases().items():
-        if args.case != "all" and name != args.case:
+        if args.case != "all" and not name.startswith(args.case):
             continue
         t = time_ms(fn, args.iters)
         rate = amount / (t * 1e-3)

@@ -21,12 +21,27 @@
 //
 // The math is the same expression, in the same order, as muon_epilogue_kernel
 // (optim.cu), so a sharded step is bit-identical to a single-GPU step.
+//
+// adam_shard_gather_kernel is the same idea for the aux-Adam parameters
+// (reference koochak/optim/muon.py:289-333, replicated there): after the
+// gradient sync reduced each Adam tensor's per-rank shard into that rank only
+// (a reduce-scatter), each rank runs AdamW on its own shard -- clip
+// coefficient applied on read, moments, bias correction, decoupled weight
+// decay, the same expression as adamw_kernel (optim.cu) -- and stores the new
+// parameter values into every rank's copy. Moment tensors are kept full-size
+// on every rank but only the shard's elements are updated there; a
+// checkpoint gathers them (optim/muon.py).
+//
+// Every parameter handed to these kernels must lie inside the local slab: the
+// host checks [ptr, ptr + bytes) against the slab's extent, because every
+// store to a peer lands at the same offset of that peer's slab.
 // No TMA and no cluster multicast: plain and multimem stores only.
 #include "host_utils.h"
 #include "sm100.cuh"
 
 #include <torch/extension.h>
 
+#include <cmath>
 #include <vector>
 
 namespace kb {
@@ -184,7 +199,7 @@ __global__ void __launch_bounds__(256)
 // bases: every rank's slab base address; mc_base: multicast alias or 0.
 void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor& X,
                         const std::vector<at::Tensor>& shadow, double lr, double wd, double scale, bool transpose,
-                        const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank) {
+                        const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank, int64_t slab_bytes) {
   const size_t n = params.size();
   if (n == 0) return;
   const int world = (int)bases.size();
@@ -214,7 +229,8 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
       KB_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous() && p.numel() == (int64_t)R * C,
                "muon_update_gather: same-shape fp32 contiguous matrices required");
       const int64_t addr = reinterpret_cast<int64_t>(p.data_ptr());
-      KB_CHECK(addr % 16 == 0 && addr >= bases[rank], "muon_update_gather: parameter must lie in the local slab");
+      KB_CHECK(addr % 16 == 0 && addr >= bases[rank] && addr + 4 * (int64_t)R * C <= bases[rank] + slab_bytes,
+               "muon_update_gather: parameter must lie in the local slab");
       mm.p[j] = p.data_ptr<float>();
       const at::Tensor* sh = shadow.empty() ? nullptr : &shadow[base + j];
       mm.shadow[j] = (sh && sh->numel() == (int64_t)R * C && sh->scalar_type() == at::kBFloat16 &&
@@ -246,11 +262,183 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
   }
 }
 
+
+// ------------------------------------------------------------ sharded AdamW
+
+namespace {
+
+constexpr int kShardT = 64;             // tensors per launch
+constexpr int kShardChunk = 4096;       // elements per work item (a multiple of 4)
+
+struct AdamShard {
+  int n, world;
+  float* p[kShardT];          // this rank's copy (inside the slab)
+  const float* g[kShardT];    // reduced gradient, indexed like p (valid on [lo, hi))
+  float* m[kShardT];
+  float* v[kShardT];
+  long long lo[kShardT];      // shard [lo, hi) of tensor i, lo % 4 == 0
+  long long hi[kShardT];
+  long long first[kShardT + 1];  // prefix sum of work items per tensor
+  float bc1[kShardT], bc2[kShardT];
+  long long delta[kGatherRanks];
+  long long mc_delta;
+};
+
+template <bool MULTIMEM>
+__device__ __forceinline__ void publish4(const AdamShard& a, float* p, float4 v) {
+  if constexpr (MULTIMEM) {
+    mm_st_v4(shifted(p, a.mc_delta), v);
+  } else {
+    for (int q = 0; q < a.world; ++q) __stcg(shifted(reinterpret_cast<float4*>(p), a.delta[q]), v);
+  }
+}
+
+template <bool MULTIMEM>
+__device__ __forceinline__ void publish1(const AdamShard& a, float* p, float v) {
+  if constexpr (MULTIMEM) {
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(shifted(p, a.mc_delta)), "f"(v) : "memory");
+  } else {
+    for (int q = 0; q < a.world; ++q) __stcg(shifted(p, a.delta[q]), v);
+  }
+}
+
+__device__ __forceinline__ float adam_elem(float p, float g, float& m, float& v, float b1, float b2, float inv_bc1,
+                                           float inv_bc2, float eps, float lr, float decay) {
+  m = m + (1.f - b1) * (g - m);
+  v = v + (1.f - b2) * (g * g - v);
+  const float upd = (m * inv_bc1) / (sqrtf(v * inv_bc2) + eps);
+  return p * decay - lr * upd;
+}
+
+template <bool MULTIMEM>
+__global__ void __launch_bounds__(256)
+    adam_shard_gather_kernel(const __grid_constant__ AdamShard a, const float* __restrict__ coef_ptr, float lr,
+                             float b1, float b2, float eps, float wd, int skip_ptr_valid,
+                             const float* __restrict__ skip_ptr) {
+  // A step that the gradient gate marked non-finite (GradScaler overflow) is skipped on the device.
+  if (skip_ptr_valid && *skip_ptr != 0.f) return;
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  const float decay = 1.f - lr * wd;
+  const long long total = a.first[a.n];
+  for (long long w = blockIdx.x; w < total; w += gridDim.x) {
+    int i = 0;
+    while (a.first[i + 1] <= w) ++i;
+    const long long s0 = a.lo[i] + (w - a.first[i]) * kShardChunk;
+    const long long s1 = min(a.hi[i], s0 + kShardChunk);
+    const float inv_bc1 = 1.f / a.bc1[i], inv_bc2 = 1.f / a.bc2[i];
+    float* p = a.p[i];
+    const float* g = a.g[i];
+    float* m = a.m[i];
+    float* v = a.v[i];
+    const long long n4 = (s1 - s0) >> 2;
+    for (long long k = threadIdx.x; k < n4; k += blockDim.x) {
+      const long long j = s0 + 4 * k;
+      const float4 pv = *reinterpret_cast<const float4*>(p + j);
+      const float4 gv = *reinterpret_cast<const float4*>(g + j);
+      float4 mv = *reinterpret_cast<const float4*>(m + j);
+      float4 vv = *reinterpret_cast<const float4*>(v + j);
+      float4 pn;
+      pn.x = adam_elem(pv.x, gv.x * coef, mv.x, vv.x, b1, b2, inv_bc1, inv_bc2, eps, lr, decay);
+      pn.y = adam_elem(pv.y, gv.y * coef, mv.y, vv.y, b1, b2, inv_bc1, inv_bc2, eps, lr, decay);
+      pn.z = adam_elem(pv.z, gv.z * coef, mv.z, vv.z, b1, b2, inv_bc1, inv_bc2, eps, lr, decay);
+      pn.w = adam_elem(pv.w, gv.w * coef, mv.w, vv.w, b1, b2, inv_bc1, inv_bc2, eps, lr, decay);
+      *reinterpret_cast<float4*>(m + j) = mv;
+      *reinterpret_cast<float4*>(v + j) = vv;
+      publish4<MULTIMEM>(a, p + j, pn);
+    }
+    for (long long j = s0 + 4 * n4 + threadIdx.x; j < s1; j += blockDim.x) {  // ragged end of a tensor
+      float mj = m[j], vj = v[j];
+      const float pn = adam_elem(p[j], g[j] * coef, mj, vj, b1, b2, inv_bc1, inv_bc2, eps, lr, decay);
+      m[j] = mj;
+      v[j] = vj;
+      publish1<MULTIMEM>(a, p + j, pn);
+    }
+  }
+  if constexpr (MULTIMEM) asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
+}  // namespace
+
+// params / grads / exp_avg / exp_avg_sq: full-size fp32 tensors (params inside
+// the local slab); lo / hi: this rank's shard of each; steps: Adam step count
+// per tensor (after increment); coef: clip coefficient (device scalar) or
+// None; skip: a device fp32 flag (non-zero: skip the update) or None.
+void adam_shard_gather(const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& grads,
+                       const std::vector<at::Tensor>& exp_avg, const std::vector<at::Tensor>& exp_avg_sq,
+                       const std::vector<int64_t>& lo, const std::vector<int64_t>& hi,
+                       const std::vector<int64_t>& steps, const c10::optional<at::Tensor>& coef,
+                       const c10::optional<at::Tensor>& skip, double lr, double beta1, double beta2, double eps,
+                       double weight_decay, const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank,
+                       int64_t slab_bytes) {
+  const size_t n = params.size();
+  KB_CHECK(grads.size() == n && exp_avg.size() == n && exp_avg_sq.size() == n && lo.size() == n && hi.size() == n &&
+               steps.size() == n,
+           "adam_shard_gather: list lengths differ");
+  if (n == 0) return;
+  const int world = (int)bases.size();
+  KB_CHECK(world >= 1 && world <= kGatherRanks, "adam_shard_gather: world size must be 1..8");
+  KB_CHECK(rank >= 0 && rank < world, "adam_shard_gather: bad rank");
+  for (int q = 0; q < world; ++q) KB_CHECK(bases[q] != 0 && bases[q] % 16 == 0, "adam_shard_gather: bad slab base");
+  KB_CHECK(mc_base % 16 == 0, "adam_shard_gather: multicast base must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const float* cp = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
+  const float* sp = (skip.has_value() && skip->defined()) ? skip->data_ptr<float>() : nullptr;
+  for (size_t base = 0; base < n; base += kShardT) {
+    const int count = (int)std::min<size_t>(kShardT, n - base);
+    AdamShard a{};
+    a.n = count;
+    a.world = world;
+    for (int q = 0; q < world; ++q) a.delta[q] = bases[q] - bases[rank];
+    a.mc_delta = mc_base ? mc_base - bases[rank] : 0;
+    a.first[0] = 0;
+    for (int j = 0; j < count; ++j) {
+      const size_t k = base + j;
+      const at::Tensor& p = params[k];
+      KB_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous() && grads[k].scalar_type() == at::kFloat &&
+                   grads[k].is_contiguous() && exp_avg[k].is_contiguous() && exp_avg_sq[k].is_contiguous() &&
+                   grads[k].numel() == p.numel() && exp_avg[k].numel() == p.numel() &&
+                   exp_avg_sq[k].numel() == p.numel(),
+               "adam_shard_gather: full-size fp32 contiguous tensors required");
+      KB_CHECK(lo[k] >= 0 && lo[k] <= hi[k] && hi[k] <= p.numel() && lo[k] % 4 == 0,
+               "adam_shard_gather: shard bounds out of range (lo must be a multiple of 4)");
+      const int64_t addr = reinterpret_cast<int64_t>(p.data_ptr());
+      KB_CHECK(addr % 16 == 0 && addr >= bases[rank] && addr + 4 * p.numel() <= bases[rank] + slab_bytes,
+               "adam_shard_gather: parameter must lie in the local slab");
+      for (const at::Tensor* t : {&grads[k], &exp_avg[k], &exp_avg_sq[k]})
+        KB_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "adam_shard_gather: 16-byte alignment required");
+      a.p[j] = p.data_ptr<float>();
+      a.g[j] = grads[k].data_ptr<float>();
+      a.m[j] = exp_avg[k].data_ptr<float>();
+      a.v[j] = exp_avg_sq[k].data_ptr<float>();
+      a.lo[j] = lo[k];
+      a.hi[j] = hi[k];
+      a.first[j + 1] = a.first[j] + (hi[k] - lo[k] + kShardChunk - 1) / kShardChunk;
+      a.bc1[j] = (float)(1.0 - std::pow(beta1, (double)steps[k]));
+      a.bc2[j] = (float)(1.0 - std::pow(beta2, (double)steps[k]));
+    }
+    if (a.first[count] == 0) continue;
+    const int grid = (int)std::min<long long>(a.first[count], 4LL * num_sms(params[0].get_device()));
+    if (mc_base != 0) {
+      adam_shard_gather_kernel<true><<<grid, 256, 0, s>>>(a, cp, (float)lr, (float)beta1, (float)beta2, (float)eps,
+                                                         (float)weight_decay, sp != nullptr, sp);
+    } else {
+      adam_shard_gather_kernel<false><<<grid, 256, 0, s>>>(a, cp, (float)lr, (float)beta1, (float)beta2, (float)eps,
+                                                          (float)weight_decay, sp != nullptr, sp);
+    }
+    KB_LAUNCHED();
+  }
+}
+
 void register_muon_gather_ops(pybind11::module& m) {
   m.def("muon_update_gather", &muon_update_gather,
         "owner's Muon update written into every rank's parameter copy (P2P or multimem stores)", pybind11::arg("params"),
         pybind11::arg("X"), pybind11::arg("shadow"), pybind11::arg("lr"), pybind11::arg("wd"), pybind11::arg("scale"),
-        pybind11::arg("transpose"), pybind11::arg("bases"), pybind11::arg("mc_base"), pybind11::arg("rank"));
+        pybind11::arg("transpose"), pybind11::arg("bases"), pybind11::arg("mc_base"), pybind11::arg("rank"),
+        pybind11::arg("slab_bytes"));
+  m.def("adam_shard_gather", &adam_shard_gather,
+        "AdamW on this rank's shard of each tensor, new values written into every rank's copy (P2P or multimem)");
 }
 
 }  // namespace kb

@@ -1,15 +1,30 @@
-"""GPU health rules, nvidia-smi sampling, and Slurm recovery (reference: koochak/health/gpu.py:19-630).
+"""GPU health: nvidia-smi readings, the rules that call a GPU unhealthy, and what a failure triggers.
 
-A GPU that is busy (utilization >= 80%) fails a sample when it shows a
-hardware slowdown, power-brake slowdown, low SM clock (< 70% of max) or
-thermal trouble. Non-thermal problems must repeat on 2 consecutive samples;
-thermal problems get a 2-hour grace period (continuous, samples at most 5
-minutes apart). A confirmed failure makes every rank checkpoint and exit 42,
-optionally after asking Slurm to requeue or cancel the job with the bad
-nodes excluded (never from inside Scruffy or a nested step).
+(behaviour of reference koochak/health/gpu.py:19-630)
 
-This module only reads GPU state (nvidia-smi queries); it changes no GPU
-setting.
+Rules (``evaluate_sample``). Only a busy GPU (utilization >= 80%) is judged.
+It fails a sample for any of: software or hardware thermal slowdown, the
+aggregate hardware slowdown flag, the power-brake slowdown, GPU temperature
+>= 86 C, memory temperature >= 94 C, or an SM clock below 70% of its maximum.
+``sw_power_cap`` alone is normal on a power-capped part and never fails.
+
+Verdicts (``_Verdicts``). Non-thermal reasons must repeat on two consecutive
+samples. Thermal reasons are a slow problem: they fail only after two hours
+of continuous thermal evidence (samples at most five minutes apart, measured
+on the monotonic clock). While a GPU is thermally limited its slow clock and
+the aggregate slowdown flag are consequences, not separate faults; the power
+brake stays fast.
+
+Consequences (``SlurmRecovery``). A confirmed failure makes every rank
+checkpoint and exit 42. Optionally (``KOOCHAK_GPU_HEALTH_SLURM_ACTION``
+``requeue`` / ``cancel``; default ``exit``) rank 0 asks Slurm to requeue or
+cancel the job with the bad nodes excluded -- never from inside a Scruffy
+workload or a nested job step, and never when
+``KOOCHAK_GPU_HEALTH_SLURM_DISABLE`` is set.
+
+This module only reads GPU state; it changes no GPU setting. Time and
+command execution are injectable (``clock``, ``runner``) so every rule and
+Slurm action is testable without a GPU or a scheduler.
 """
 
 from __future__ import annotations
@@ -21,99 +36,97 @@ import shutil
 import socket
 import subprocess
 import time
-from dataclasses import asdict, dataclass
+from dataclasses import asdict, dataclass, field
 from pathlib import Path
-from typing import Any, Dict, Iterable, List, Optional, Sequence
+from typing import Any, Callable, Dict, Iterable, List, Optional, Sequence, Tuple
 
 import torch
 
 from ..utils.paths import canonical_dir
 
-__all__ = ["GpuHealthSample", "GpuHealthFailure", "GpuHealthWatchdog", "evaluate_sample",
-           "summarize_failures_for_stdout", "parse_nvidia_smi_csv", "sample_from_nvidia_smi_row",
+__all__ = ["GpuHealthSample", "GpuHealthFailure", "GpuHealthWatchdog", "SlurmRecovery", "Thresholds",
+           "evaluate_sample", "summarize_failures_for_stdout", "parse_nvidia_smi_csv", "sample_from_nvidia_smi_row",
            "current_local_rank", "current_slurm_node", "query_id_for_cuda_device", "EXIT_CODE",
-           "PRIMARY_QUERY_FIELDS", "FALLBACK_QUERY_FIELDS"]
+           "PRIMARY_QUERY_FIELDS", "FALLBACK_QUERY_FIELDS", "THERMAL_GRACE_SECONDS",
+           "THERMAL_MAX_SAMPLE_GAP_SECONDS", "THERMAL_REASONS"]
 
+
+@dataclass(frozen=True)
+class Thresholds:
+    busy_util_pct: float = 80.0
+    max_gpu_temp_c: float = 86.0
+    max_memory_temp_c: float = 94.0
+    min_sm_clock_frac: float = 0.70
+    consecutive: int = 2
+    thermal_grace_s: float = 2 * 60 * 60
+    thermal_max_gap_s: float = 5 * 60
+
+
+DEFAULT = Thresholds()
 WARMUP_STEPS = 20
 CHECK_EVERY_STEPS = 10
-REQUIRE_UTILIZATION_PCT = 80.0
-CONSECUTIVE_FAILURES = 2
-THERMAL_GRACE_SECONDS = 2 * 60 * 60
-THERMAL_MAX_SAMPLE_GAP_SECONDS = 5 * 60
-THERMAL_REASONS = frozenset({"sw_thermal_slowdown", "hw_thermal_slowdown", "gpu_temp_high", "memory_temp_high"})
-MAX_GPU_TEMP_C = 86.0
-MAX_MEMORY_TEMP_C = 94.0
-MIN_SM_CLOCK_FRAC = 0.70
 EXIT_CODE = 42
+THERMAL_GRACE_SECONDS = int(DEFAULT.thermal_grace_s)
+THERMAL_MAX_SAMPLE_GAP_SECONDS = int(DEFAULT.thermal_max_gap_s)
+THERMAL_REASONS = frozenset({"sw_thermal_slowdown", "hw_thermal_slowdown", "gpu_temp_high", "memory_temp_high"})
+_THERMAL_CONSEQUENCES = frozenset({"hw_slowdown", "sm_clock_low"})
 
-_REASON_FIELDS = ["clocks_throttle_reasons.active", "clocks_throttle_reasons.sw_thermal_slowdown",
-                  "clocks_throttle_reasons.hw_slowdown", "clocks_throttle_reasons.hw_thermal_slowdown",
-                  "clocks_throttle_reasons.hw_power_brake_slowdown", "clocks_throttle_reasons.sw_power_cap"]
+# nvidia-smi --query-gpu fields, in the order the CSV columns come back.
+_THROTTLE = ["clocks_throttle_reasons.active", "clocks_throttle_reasons.sw_thermal_slowdown",
+             "clocks_throttle_reasons.hw_slowdown", "clocks_throttle_reasons.hw_thermal_slowdown",
+             "clocks_throttle_reasons.hw_power_brake_slowdown", "clocks_throttle_reasons.sw_power_cap"]
 PRIMARY_QUERY_FIELDS = ["index", "uuid", "name", "temperature.gpu", "temperature.memory", "pstate", "power.draw",
                         "power.limit", "clocks.sm", "clocks.mem", "clocks.max.sm", "utilization.gpu",
-                        "utilization.memory", *_REASON_FIELDS]
-# Older drivers reject temperature.memory / clocks.max.sm.
-FALLBACK_QUERY_FIELDS = ["index", "uuid", "name", "temperature.gpu", "pstate", "power.draw", "power.limit",
-                         "clocks.sm", "clocks.mem", "utilization.gpu", "utilization.memory", *_REASON_FIELDS]
+                        "utilization.memory", *_THROTTLE]
+# For drivers that reject temperature.memory and clocks.max.sm.
+FALLBACK_QUERY_FIELDS = [f for f in PRIMARY_QUERY_FIELDS if f not in ("temperature.memory", "clocks.max.sm")]
 
 
-def _env_on(name: str) -> bool:
-    v = os.environ.get(name)
-    return v is not None and v.strip().lower() not in {"", "0", "false", "no", "off"}
+# ----------------------------------------------------------------------------- environment
 
 
-def _num(value: Any) -> Optional[float]:
-    if value is None:
-        return None
-    text = str(value).strip()
-    if not text or text.upper() == "N/A":
-        return None
-    try:
-        return float(text.split()[0])
-    except ValueError:
-        return None
-
-
-def _active(value: Any) -> bool:
-    return str(value).strip().lower() == "active"
+def _env_flag(name: str) -> bool:
+    raw = os.environ.get(name)
+    return raw is not None and raw.strip().lower() not in {"", "0", "false", "no", "off"}
 
 
 def _short_host(value: Optional[str]) -> Optional[str]:
-    if value is None:
-        return None
-    text = value.strip()
-    return text.split(".")[0] if text else None
+    text = (value or "").strip()
+    return text.split(".", 1)[0] if text else None
 
 
 def current_slurm_node() -> str:
-    return (_short_host(os.environ.get("SLURMD_NODENAME")) or _short_host(os.environ.get("HOSTNAME"))
-            or _short_host(socket.gethostname()) or "unknown")
+    for candidate in (os.environ.get("SLURMD_NODENAME"), os.environ.get("HOSTNAME"), socket.gethostname()):
+        short = _short_host(candidate)
+        if short:
+            return short
+    return "unknown"
 
 
 def current_local_rank() -> Optional[int]:
+    """The first launcher variable naming a local rank (``None`` if absent or not an integer)."""
+
     for key in ("LOCAL_RANK", "SLURM_LOCALID", "MPI_LOCALRANKID", "OMPI_COMM_WORLD_LOCAL_RANK",
                 "MV2_COMM_WORLD_LOCAL_RANK"):
-        v = os.environ.get(key)
-        if v is None:
-            continue
-        try:
-            return int(v)
-        except ValueError:
-            return None
+        if key in os.environ:
+            try:
+                return int(os.environ[key])
+            except ValueError:
+                return None
     return None
 
 
 def query_id_for_cuda_device(cuda_device: Optional[int]) -> str:
-    """nvidia-smi ``-i`` id for a CUDA ordinal, honouring ``CUDA_VISIBLE_DEVICES``."""
+    """nvidia-smi ``-i`` id of a CUDA ordinal, through ``CUDA_VISIBLE_DEVICES`` when it is set."""
 
     if cuda_device is None:
         return "0"
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if visible:
-        parts = [p.strip() for p in visible.split(",") if p.strip()]
-        if 0 <= int(cuda_device) < len(parts):
-            return parts[int(cuda_device)]
-    return str(int(cuda_device))
+    visible = [p.strip() for p in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if p.strip()]
+    index = int(cuda_device)
+    return visible[index] if 0 <= index < len(visible) else str(index)
+
+
+# ----------------------------------------------------------------------------- samples
 
 
 @dataclass
@@ -162,37 +175,70 @@ class GpuHealthFailure:
     thermal_duration_seconds: float = 0.0
 
     def to_dict(self) -> Dict[str, Any]:
-        out = self.sample.to_dict()
-        out.update(event="gpu_health_failure", reasons=list(self.reasons),
-                   consecutive_failures=int(self.consecutive_failures), slurm_action=self.slurm_action,
-                   thermal_duration_seconds=self.thermal_duration_seconds)
-        return out
+        record = self.sample.to_dict()
+        record["event"] = "gpu_health_failure"
+        record["reasons"] = list(self.reasons)
+        record["consecutive_failures"] = int(self.consecutive_failures)
+        record["slurm_action"] = self.slurm_action
+        record["thermal_duration_seconds"] = self.thermal_duration_seconds
+        return record
+
+
+def _number(text: Optional[str]) -> Optional[float]:
+    """First token of an nvidia-smi value as a float (``N/A``, blanks and junk: ``None``)."""
+
+    words = (text or "").split()
+    if not words or words[0].upper() == "N/A":
+        return None
+    try:
+        return float(words[0])
+    except ValueError:
+        return None
+
+
+def _flag(text: Optional[str]) -> bool:
+    return (text or "").strip().lower() == "active"
+
+
+def _text(text: Optional[str]) -> Optional[str]:
+    return text
+
+
+# Sample attribute <- (nvidia-smi field, parser).
+_COLUMNS: Dict[str, Tuple[str, Callable[[Optional[str]], Any]]] = {
+    "gpu_index": ("index", _text), "gpu_uuid": ("uuid", _text), "gpu_name": ("name", _text),
+    "gpu_temp_c": ("temperature.gpu", _number), "memory_temp_c": ("temperature.memory", _number),
+    "pstate": ("pstate", _text), "power_draw_w": ("power.draw", _number), "power_limit_w": ("power.limit", _number),
+    "sm_clock_mhz": ("clocks.sm", _number), "mem_clock_mhz": ("clocks.mem", _number),
+    "max_sm_clock_mhz": ("clocks.max.sm", _number), "gpu_util_pct": ("utilization.gpu", _number),
+    "mem_util_pct": ("utilization.memory", _number), "throttle_active_mask": ("clocks_throttle_reasons.active", _text),
+    "sw_thermal_slowdown": ("clocks_throttle_reasons.sw_thermal_slowdown", _flag),
+    "hw_slowdown": ("clocks_throttle_reasons.hw_slowdown", _flag),
+    "hw_thermal_slowdown": ("clocks_throttle_reasons.hw_thermal_slowdown", _flag),
+    "hw_power_brake_slowdown": ("clocks_throttle_reasons.hw_power_brake_slowdown", _flag),
+    "sw_power_cap": ("clocks_throttle_reasons.sw_power_cap", _flag),
+}
 
 
 def sample_from_nvidia_smi_row(*, step: int, rank: int, world_size: int, hostname: str, slurm_node: str,
                                cuda_device: Optional[int], gpu_query_id: str, fields: Sequence[str],
                                row: Sequence[str]) -> GpuHealthSample:
-    v = {f: (row[i].strip() if i < len(row) else "N/A") for i, f in enumerate(fields)}
-    return GpuHealthSample(
-        step=int(step), rank=int(rank), local_rank=current_local_rank(), world_size=int(world_size),
-        hostname=hostname, slurm_node=slurm_node, cuda_device=cuda_device, gpu_query_id=gpu_query_id,
-        gpu_index=v.get("index"), gpu_uuid=v.get("uuid"), gpu_name=v.get("name"),
-        gpu_temp_c=_num(v.get("temperature.gpu")), memory_temp_c=_num(v.get("temperature.memory")),
-        pstate=v.get("pstate"), power_draw_w=_num(v.get("power.draw")), power_limit_w=_num(v.get("power.limit")),
-        sm_clock_mhz=_num(v.get("clocks.sm")), mem_clock_mhz=_num(v.get("clocks.mem")),
-        max_sm_clock_mhz=_num(v.get("clocks.max.sm")), gpu_util_pct=_num(v.get("utilization.gpu")),
-        mem_util_pct=_num(v.get("utilization.memory")), throttle_active_mask=v.get("clocks_throttle_reasons.active"),
-        sw_thermal_slowdown=_active(v.get("clocks_throttle_reasons.sw_thermal_slowdown")),
-        hw_slowdown=_active(v.get("clocks_throttle_reasons.hw_slowdown")),
-        hw_thermal_slowdown=_active(v.get("clocks_throttle_reasons.hw_thermal_slowdown")),
-        hw_power_brake_slowdown=_active(v.get("clocks_throttle_reasons.hw_power_brake_slowdown")),
-        sw_power_cap=_active(v.get("clocks_throttle_reasons.sw_power_cap")), timestamp_unix=time.time())
+    """A sample from one CSV row whose columns are ``fields`` (missing columns read as ``N/A``)."""
+
+    cells = dict(zip(fields, (c.strip() for c in row)))
+    readings = {attr: parse(cells.get(name, "N/A")) for attr, (name, parse) in _COLUMNS.items()}
+    return GpuHealthSample(step=int(step), rank=int(rank), local_rank=current_local_rank(),
+                           world_size=int(world_size), hostname=hostname, slurm_node=slurm_node,
+                           cuda_device=cuda_device, gpu_query_id=gpu_query_id, timestamp_unix=time.time(),
+                           **readings)
 
 
 def parse_nvidia_smi_csv(*, stdout: str, fields: Sequence[str], step: int, rank: int, world_size: int,
                          hostname: str, slurm_node: str, cuda_device: Optional[int],
                          gpu_query_id: str) -> Optional[GpuHealthSample]:
-    rows = list(csv.reader(stdout.strip().splitlines())) if stdout.strip() else []
+    """The sample of the first CSV row of ``stdout`` (``None`` when there is none)."""
+
+    rows = [r for r in csv.reader(stdout.strip().splitlines())] if stdout.strip() else []
     if not rows:
         return None
     return sample_from_nvidia_smi_row(step=step, rank=rank, world_size=world_size, hostname=hostname,
@@ -200,114 +246,285 @@ def parse_nvidia_smi_csv(*, stdout: str, fields: Sequence[str], step: int, rank:
                                       fields=fields, row=rows[0])
 
 
-def evaluate_sample(sample: GpuHealthSample) -> List[str]:
-    """Failure reasons of one sample; an idle GPU (< 80% utilization) never fails."""
+# ----------------------------------------------------------------------------- rules
 
-    if sample.gpu_util_pct is None or sample.gpu_util_pct < REQUIRE_UTILIZATION_PCT:
+
+def _clock_low(s: GpuHealthSample, th: Thresholds) -> bool:
+    if s.sm_clock_mhz is None or not s.max_sm_clock_mhz:
+        return False
+    return s.max_sm_clock_mhz > 0 and s.sm_clock_mhz < th.min_sm_clock_frac * s.max_sm_clock_mhz
+
+
+def _at_least(value: Optional[float], limit: float) -> bool:
+    return value is not None and value >= limit
+
+
+_RULES: List[Tuple[str, Callable[[GpuHealthSample, Thresholds], bool]]] = [
+    ("sw_thermal_slowdown", lambda s, th: s.sw_thermal_slowdown),
+    ("hw_slowdown", lambda s, th: s.hw_slowdown),
+    ("hw_thermal_slowdown", lambda s, th: s.hw_thermal_slowdown),
+    ("hw_power_brake_slowdown", lambda s, th: s.hw_power_brake_slowdown),
+    ("gpu_temp_high", lambda s, th: _at_least(s.gpu_temp_c, th.max_gpu_temp_c)),
+    ("memory_temp_high", lambda s, th: _at_least(s.memory_temp_c, th.max_memory_temp_c)),
+    ("sm_clock_low", _clock_low),
+]
+
+
+def evaluate_sample(sample: GpuHealthSample, thresholds: Thresholds = DEFAULT) -> List[str]:
+    """Failure reasons of one sample, in a fixed order; an idle GPU never fails."""
+
+    if not _at_least(sample.gpu_util_pct, thresholds.busy_util_pct):
         return []
-    checks = [
-        ("sw_thermal_slowdown", sample.sw_thermal_slowdown),
-        ("hw_slowdown", sample.hw_slowdown),
-        ("hw_thermal_slowdown", sample.hw_thermal_slowdown),
-        ("hw_power_brake_slowdown", sample.hw_power_brake_slowdown),
-        ("gpu_temp_high", sample.gpu_temp_c is not None and sample.gpu_temp_c >= MAX_GPU_TEMP_C),
-        ("memory_temp_high", sample.memory_temp_c is not None and sample.memory_temp_c >= MAX_MEMORY_TEMP_C),
-        ("sm_clock_low", sample.sm_clock_mhz is not None and sample.max_sm_clock_mhz is not None
-         and sample.max_sm_clock_mhz > 0 and sample.sm_clock_mhz / sample.max_sm_clock_mhz < MIN_SM_CLOCK_FRAC),
-    ]
-    return [name for name, hit in checks if hit]
+    return [reason for reason, broken in _RULES if broken(sample, thresholds)]
+
+
+@dataclass
+class _Verdicts:
+    """Turns per-sample reasons into failures: two in a row for faults, a long episode for heat."""
+
+    thresholds: Thresholds = DEFAULT
+    streak: int = 0
+    episode_start: Optional[float] = None
+    episode_last: Optional[float] = None
+    episode_samples: int = 0
+
+    def clear(self) -> None:
+        self.streak = 0
+        self.episode_start = self.episode_last = None
+        self.episode_samples = 0
+
+    def _heat(self, hot: bool, now: float) -> float:
+        if not hot:
+            self.episode_start = self.episode_last = None
+            self.episode_samples = 0
+            return 0.0
+        broken_run = self.episode_last is None or now - self.episode_last > self.thresholds.thermal_max_gap_s
+        if broken_run:
+            self.episode_start, self.episode_samples = now, 0
+        self.episode_last = now
+        self.episode_samples += 1
+        return now - float(self.episode_start)
+
+    def judge(self, reasons: List[str], now: float) -> Tuple[Optional[Tuple[List[str], int]], float]:
+        """((failure reasons, count) or None, thermal episode length so far)."""
+
+        hot = any(r in THERMAL_REASONS for r in reasons)
+        duration = self._heat(hot, now)
+        faults = [r for r in reasons
+                  if r not in THERMAL_REASONS and not (hot and r in _THERMAL_CONSEQUENCES)]
+        self.streak = self.streak + 1 if faults else 0
+        if self.streak >= self.thresholds.consecutive:
+            return (faults, self.streak), duration
+        if hot and duration >= self.thresholds.thermal_grace_s and self.episode_samples >= 2:
+            return (reasons, self.episode_samples), duration
+        return None, duration
+
+
+# ----------------------------------------------------------------------------- Slurm
+
+
+def _run(cmd: Sequence[str]) -> Dict[str, Any]:
+    shown = " ".join(cmd)
+    try:
+        done = subprocess.run(list(cmd), check=False, capture_output=True, text=True, timeout=20.0)
+    except (OSError, subprocess.SubprocessError) as exc:
+        return {"cmd": shown, "returncode": None, "stdout": "", "stderr": str(exc)}
+    return {"cmd": shown, "returncode": done.returncode, "stdout": done.stdout.strip(), "stderr": done.stderr.strip()}
+
+
+@dataclass
+class SlurmRecovery:
+    """What rank 0 asks Slurm to do about bad nodes, from the environment at start-up."""
+
+    requested_action: str = "exit"
+    disabled: bool = False
+    blocked_reason: Optional[str] = None
+    runner: Callable[[Sequence[str]], Dict[str, Any]] = field(default=_run, repr=False)
+
+    @classmethod
+    def from_env(cls, runner: Optional[Callable[[Sequence[str]], Dict[str, Any]]] = None) -> "SlurmRecovery":
+        wanted = os.environ.get("KOOCHAK_GPU_HEALTH_SLURM_ACTION", "exit").strip().lower()
+        return cls(requested_action=wanted if wanted in {"requeue", "cancel", "exit"} else "exit",
+                   disabled=_env_flag("KOOCHAK_GPU_HEALTH_SLURM_DISABLE"), blocked_reason=cls._blocked(),
+                   runner=runner or _run)
+
+    @staticmethod
+    def _blocked() -> Optional[str]:
+        if os.environ.get("SCRUFFY_JOB_ID") or os.environ.get("SCRUFFY_ROOT"):
+            return "parent Slurm mutation is forbidden for Scruffy workloads"
+        step = os.environ.get("SLURM_STEP_ID") or os.environ.get("SLURM_STEPID")
+        if step and step.strip().lower() not in {"batch", "extern"}:
+            return f"parent Slurm mutation is forbidden from nested step {step}"
+        return None
+
+    @property
+    def action(self) -> str:
+        return "exit" if self.blocked_reason else self.requested_action
+
+    def node_names(self, nodes: Sequence[str]) -> List[str]:
+        """Node names as Slurm spells them in this job's node list (short host names otherwise)."""
+
+        short = sorted({_short_host(n) or n for n in nodes})
+        nodelist = os.environ.get("SLURM_JOB_NODELIST")
+        if not nodelist:
+            return short
+        listing = self.runner(["scontrol", "show", "hostnames", nodelist])
+        if listing.get("returncode") != 0:
+            return short
+        known = {_short_host(h): h for h in (ln.strip() for ln in str(listing.get("stdout", "")).splitlines()) if h}
+        return sorted({known.get(_short_host(n), _short_host(n) or n) for n in nodes})
+
+    def _exclude_from_pending_twins(self, nodes_csv: str) -> List[Dict[str, Any]]:
+        user, name = os.environ.get("USER"), os.environ.get("SLURM_JOB_NAME")
+        if not (user and name):
+            return []
+        listing = self.runner(["squeue", "-h", "-u", user, "-t", "PENDING", "-n", name, "-o", "%i"])
+        out = [listing]
+        if listing.get("returncode") == 0:
+            out += [self.runner(["scontrol", "update", f"JobId={jid}", f"ExcNodeList={nodes_csv}"])
+                    for jid in str(listing.get("stdout", "")).split()]
+        return out
+
+    def recover(self, bad_nodes: Sequence[str]) -> List[Dict[str, Any]]:
+        if self.disabled or self.action == "exit":
+            return []
+        job = os.environ.get("SLURM_JOB_ID")
+        if not job:
+            return [{"cmd": "<slurm>", "returncode": None, "stderr": "SLURM_JOB_ID is not set"}]
+        if not bad_nodes:
+            return [{"cmd": "<slurm>", "returncode": None, "stderr": "no bad nodes reported"}]
+        nodes_csv = ",".join(bad_nodes)
+        if self.action == "requeue":
+            return ([self.runner(["scontrol", "update", f"JobId={job}", f"ExcNodeList={nodes_csv}"])]
+                    + self._exclude_from_pending_twins(nodes_csv) + [self.runner(["scontrol", "requeue", job])])
+        return self._exclude_from_pending_twins(nodes_csv) + [self.runner(["scancel", job])]
+
+
+# ----------------------------------------------------------------------------- watchdog
+
+
+class _HealthLog:
+    """JSONL files under ``<out_dir>/gpu_health``; with ``strict`` a write error propagates."""
+
+    def __init__(self, out_dir: str, rank: int) -> None:
+        self.root = Path(out_dir) / "gpu_health"
+        self.rank = rank
+        self.strict = False
+        self.warned = False
+
+    def directory(self) -> Path:
+        self.root.mkdir(parents=True, exist_ok=True)
+        return self.root
+
+    def append(self, stem: str, payload: Dict[str, Any]) -> None:
+        try:
+            with (self.directory() / f"{stem}_rank{self.rank}.jsonl").open("a", encoding="utf-8") as fh:
+                fh.write(json.dumps(payload, sort_keys=True) + "\n")
+        except OSError as exc:
+            if self.strict:
+                raise
+            if stem != "gpu_health_notices" and not self.warned:
+                self.warned = True
+                print(f"[gpu-health] failed to write {stem} log: {exc}", flush=True)
 
 
 class GpuHealthWatchdog:
-    """Per-rank rules state; also the base of the node-level background monitor."""
+    """One GPU's readings and verdicts; also the base of the node-level background monitor."""
 
-    def __init__(self, *, device: torch.device, out_dir: str, rank: int, world_size: int) -> None:
+    def __init__(self, *, device: torch.device, out_dir: str, rank: int, world_size: int,
+                 clock: Callable[[], float] = time.monotonic,
+                 runner: Optional[Callable[[Sequence[str]], Dict[str, Any]]] = None) -> None:
         self.device = device
         self.out_dir = canonical_dir(out_dir)
         self.rank = int(rank)
         self.world_size = int(world_size)
         self.hostname = socket.gethostname()
         self.slurm_node = current_slurm_node()
-        self.cuda_device = int(device.index) if device.type == "cuda" and device.index is not None else None
+        self.cuda_device = device.index if device.type == "cuda" and device.index is not None else None
         self.local_rank = current_local_rank()
         self.gpu_query_id = query_id_for_cuda_device(self.cuda_device)
         self.nvidia_smi = shutil.which("nvidia-smi")
-        self.enabled = device.type == "cuda" and not _env_on("KOOCHAK_GPU_HEALTH_DISABLE")
-        self.slurm_disabled = _env_on("KOOCHAK_GPU_HEALTH_SLURM_DISABLE")
-        action = os.environ.get("KOOCHAK_GPU_HEALTH_SLURM_ACTION", "exit").strip().lower()
-        self.requested_slurm_action = action if action in {"requeue", "cancel", "exit"} else "exit"
-        self.slurm_mutation_blocked_reason = self._slurm_mutation_blocked_reason()
-        self.slurm_action = "exit" if self.slurm_mutation_blocked_reason else self.requested_slurm_action
+        self.enabled = device.type == "cuda" and not _env_flag("KOOCHAK_GPU_HEALTH_DISABLE")
+        self.slurm = SlurmRecovery.from_env(runner)
         self.exit_code = EXIT_CODE
-        self._consecutive_failures = 0
-        self._thermal_started_at: Optional[float] = None
-        self._thermal_last_sample_at: Optional[float] = None
-        self._thermal_samples = 0
-        self._notice_written = False
+        self.clock = clock
+        self.verdicts = _Verdicts()
+        self.log = _HealthLog(self.out_dir, self.rank)
+        self._noticed = False
+
+    # Slurm policy, as attributes of the watchdog.
+    slurm_action = property(lambda self: self.slurm.action)
+    requested_slurm_action = property(lambda self: self.slurm.requested_action)
+    slurm_disabled = property(lambda self: self.slurm.disabled)
+    slurm_mutation_blocked_reason = property(lambda self: self.slurm.blocked_reason)
 
     def should_check_step(self, step: int) -> bool:
         return self.enabled and step >= WARMUP_STEPS and step % CHECK_EVERY_STEPS == 0
 
     def check_local(self, step: int) -> Optional[GpuHealthFailure]:
-        sample = self._query_sample(step)
+        """Query this GPU and judge the reading; a missing reading ends any streak or heat episode."""
+
+        sample = self.read_sample(step)
         if sample is None:
-            self._consecutive_failures = 0
-            self._thermal_duration(False, time.monotonic())
+            self.verdicts.clear()
             return None
         return self.observe_sample(sample)
 
     def observe_sample(self, sample: GpuHealthSample) -> Optional[GpuHealthFailure]:
-        reasons = evaluate_sample(sample)
-        thermal = bool(THERMAL_REASONS.intersection(reasons))
-        duration = self._thermal_duration(thermal, time.monotonic())
-        self._append_jsonl("gpu_health", {**sample.to_dict(), "thermal_duration_seconds": duration,
-                                          "thermal_grace_seconds": THERMAL_GRACE_SECONDS})
-        # Under thermal throttling, slow clocks and the aggregate HW slowdown
-        # flag are consequences; they wait out the thermal grace period too.
-        urgent = [r for r in reasons if r not in THERMAL_REASONS
-                  and not (thermal and r in {"hw_slowdown", "sm_clock_low"})]
-        self._consecutive_failures = self._consecutive_failures + 1 if urgent else 0
-        if self._consecutive_failures >= CONSECUTIVE_FAILURES:
-            reasons, count = urgent, self._consecutive_failures
-        elif thermal and duration >= THERMAL_GRACE_SECONDS and self._thermal_samples >= 2:
-            count = self._thermal_samples
-        else:
+        reasons = evaluate_sample(sample, self.verdicts.thresholds)
+        verdict, duration = self.verdicts.judge(reasons, self.clock())
+        self.log.append("gpu_health", {**sample.to_dict(), "thermal_duration_seconds": duration,
+                                       "thermal_grace_seconds": THERMAL_GRACE_SECONDS})
+        if verdict is None:
             return None
-        failure = GpuHealthFailure(sample=sample, reasons=reasons, consecutive_failures=count,
+        failed_reasons, count = verdict
+        failure = GpuHealthFailure(sample=sample, reasons=failed_reasons, consecutive_failures=count,
                                    slurm_action=self.slurm_action, thermal_duration_seconds=duration)
-        self._append_jsonl("gpu_health_failures", failure.to_dict())
+        self.log.append("gpu_health_failures", failure.to_dict())
         return failure
 
-    def _thermal_duration(self, thermal: bool, now: float) -> float:
-        if not thermal:
-            self._thermal_started_at = self._thermal_last_sample_at = None
-            self._thermal_samples = 0
-            return 0.0
-        if self._thermal_last_sample_at is None or now - self._thermal_last_sample_at > THERMAL_MAX_SAMPLE_GAP_SECONDS:
-            self._thermal_started_at = now
-            self._thermal_samples = 0
-        self._thermal_last_sample_at = now
-        self._thermal_samples += 1
-        assert self._thermal_started_at is not None
-        return now - self._thermal_started_at
+    def read_sample(self, step: int) -> Optional[GpuHealthSample]:
+        """One nvidia-smi query of this GPU (the fallback field list for older drivers)."""
+
+        if self.nvidia_smi is None:
+            self._notice("nvidia-smi is not available on PATH")
+            return None
+        for fields in (PRIMARY_QUERY_FIELDS, FALLBACK_QUERY_FIELDS):
+            argv = [self.nvidia_smi, "-i", self.gpu_query_id, f"--query-gpu={','.join(fields)}",
+                    "--format=csv,noheader,nounits"]
+            try:
+                done = subprocess.run(argv, check=False, capture_output=True, text=True, timeout=10.0)
+            except (OSError, subprocess.SubprocessError) as exc:
+                self._notice(f"nvidia-smi query failed: {exc}")
+                return None
+            if done.returncode == 0:
+                sample = parse_nvidia_smi_csv(stdout=done.stdout, fields=fields, step=step, rank=self.rank,
+                                              world_size=self.world_size, hostname=self.hostname,
+                                              slurm_node=self.slurm_node, cuda_device=self.cuda_device,
+                                              gpu_query_id=self.gpu_query_id)
+                if sample is not None:
+                    return sample
+        self._notice("nvidia-smi did not return a parseable GPU health row")
+        return None
 
     def gather_failures(self, local_failure: Optional[GpuHealthFailure]) -> List[Dict[str, Any]]:
-        payload = local_failure.to_dict() if local_failure is not None else None
-        if torch.distributed.is_available() and torch.distributed.is_initialized():
-            got: List[Optional[Dict[str, Any]]] = [None] * torch.distributed.get_world_size()
-            torch.distributed.all_gather_object(got, payload)
-            return [g for g in got if g is not None]
-        return [payload] if payload is not None else []
+        """Every rank's failure record (a collective when a process group exists)."""
+
+        mine = None if local_failure is None else local_failure.to_dict()
+        if not (torch.distributed.is_available() and torch.distributed.is_initialized()):
+            return [] if mine is None else [mine]
+        everyone: List[Optional[Dict[str, Any]]] = [None] * torch.distributed.get_world_size()
+        torch.distributed.all_gather_object(everyone, mine)
+        return [f for f in everyone if f is not None]
 
     def bad_nodes_from_failures(self, failures: Sequence[Dict[str, Any]]) -> List[str]:
-        nodes = set()
+        names = set()
         for f in failures:
             node = f.get("slurm_node")
-            if not node or str(node).lower() == "unknown":
-                node = f.get("hostname")
+            node = f.get("hostname") if not node or str(node).lower() == "unknown" else node
             if node:
-                nodes.add(str(node))
-        return self._normalize_against_slurm_nodelist(sorted(nodes))
+                names.add(str(node))
+        return self.slurm.node_names(sorted(names))
 
     def write_failure_summary(self, *, step: int, failures: Sequence[Dict[str, Any]], checkpoint_path: Optional[str],
                               slurm_results: Optional[Sequence[Dict[str, Any]]] = None) -> str:
@@ -320,131 +537,33 @@ class GpuHealthWatchdog:
             "slurm_mutation_blocked_reason": self.slurm_mutation_blocked_reason,
             "slurm_disabled": self.slurm_disabled, "slurm_results": list(slurm_results or []),
         }
-        path = self._health_dir() / f"gpu_health_failure_step{step:09d}.json"
-        tmp = path.with_suffix(path.suffix + ".tmp")
-        tmp.write_text(json.dumps(summary, indent=2, sort_keys=True) + "\n", encoding="utf-8")
-        os.replace(tmp, path)
-        return str(path)
+        target = self.log.directory() / f"gpu_health_failure_step{step:09d}.json"
+        partial = target.with_name(target.name + ".tmp")
+        partial.write_text(json.dumps(summary, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+        os.replace(partial, target)
+        return str(target)
 
     def perform_slurm_recovery(self, failures: Sequence[Dict[str, Any]]) -> List[Dict[str, Any]]:
-        if self.slurm_disabled or self.slurm_action == "exit":
+        if self.slurm.disabled or self.slurm.action == "exit":
             return []
-        job_id = os.environ.get("SLURM_JOB_ID")
-        if not job_id:
-            return [{"cmd": "<slurm>", "returncode": None, "stderr": "SLURM_JOB_ID is not set"}]
-        bad = self.bad_nodes_from_failures(failures)
-        if not bad:
-            return [{"cmd": "<slurm>", "returncode": None, "stderr": "no bad nodes reported"}]
-        csv_nodes = ",".join(bad)
-        results: List[Dict[str, Any]] = []
-        if self.slurm_action == "requeue":
-            results.append(self._run_command(["scontrol", "update", f"JobId={job_id}", f"ExcNodeList={csv_nodes}"]))
-            results.extend(self._exclude_pending_same_name(csv_nodes))
-            results.append(self._run_command(["scontrol", "requeue", job_id]))
-        elif self.slurm_action == "cancel":
-            results.extend(self._exclude_pending_same_name(csv_nodes))
-            results.append(self._run_command(["scancel", job_id]))
-        return results
+        return self.slurm.recover(self.bad_nodes_from_failures(failures))
 
-    @staticmethod
-    def _slurm_mutation_blocked_reason() -> Optional[str]:
-        if os.environ.get("SCRUFFY_JOB_ID") or os.environ.get("SCRUFFY_ROOT"):
-            return "parent Slurm mutation is forbidden for Scruffy workloads"
-        step_id = os.environ.get("SLURM_STEP_ID") or os.environ.get("SLURM_STEPID")
-        if step_id and step_id.strip().lower() not in {"batch", "extern"}:
-            return f"parent Slurm mutation is forbidden from nested step {step_id}"
-        return None
-
-    def _query_sample(self, step: int) -> Optional[GpuHealthSample]:
-        if self.nvidia_smi is None:
-            self._write_notice("nvidia-smi is not available on PATH")
-            return None
-        for fields in (PRIMARY_QUERY_FIELDS, FALLBACK_QUERY_FIELDS):
-            cmd = [self.nvidia_smi, "-i", self.gpu_query_id, f"--query-gpu={','.join(fields)}",
-                   "--format=csv,noheader,nounits"]
-            try:
-                proc = subprocess.run(cmd, check=False, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
-                                      timeout=10.0)
-            except (OSError, subprocess.SubprocessError) as exc:
-                self._write_notice(f"nvidia-smi query failed: {exc}")
-                return None
-            if proc.returncode != 0:
-                continue
-            sample = parse_nvidia_smi_csv(stdout=proc.stdout, fields=fields, step=step, rank=self.rank,
-                                          world_size=self.world_size, hostname=self.hostname,
-                                          slurm_node=self.slurm_node, cuda_device=self.cuda_device,
-                                          gpu_query_id=self.gpu_query_id)
-            if sample is not None:
-                return sample
-        self._write_notice("nvidia-smi did not return a parseable GPU health row")
-        return None
-
-    def _exclude_pending_same_name(self, csv_nodes: str) -> List[Dict[str, Any]]:
-        user, name = os.environ.get("USER"), os.environ.get("SLURM_JOB_NAME")
-        if not user or not name:
-            return []
-        listing = self._run_command(["squeue", "-h", "-u", user, "-t", "PENDING", "-n", name, "-o", "%i"])
-        out = [listing]
-        if listing.get("returncode") != 0:
-            return out
-        for jid in str(listing.get("stdout", "")).split():
-            out.append(self._run_command(["scontrol", "update", f"JobId={jid}", f"ExcNodeList={csv_nodes}"]))
-        return out
-
-    def _normalize_against_slurm_nodelist(self, nodes: Sequence[str]) -> List[str]:
-        nodelist = os.environ.get("SLURM_JOB_NODELIST")
-        fallback = sorted({_short_host(n) or n for n in nodes})
-        if not nodelist:
-            return fallback
-        res = self._run_command(["scontrol", "show", "hostnames", nodelist])
-        if res.get("returncode") != 0:
-            return fallback
-        names = [ln.strip() for ln in str(res.get("stdout", "")).splitlines() if ln.strip()]
-        by_short = {_short_host(n): n for n in names}
-        return sorted({by_short.get(_short_host(n), _short_host(n) or n) for n in nodes})
-
-    def _run_command(self, cmd: Sequence[str]) -> Dict[str, Any]:
-        try:
-            p = subprocess.run(list(cmd), check=False, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
-                               timeout=20.0)
-            return {"cmd": " ".join(cmd), "returncode": p.returncode, "stdout": p.stdout.strip(),
-                    "stderr": p.stderr.strip()}
-        except (OSError, subprocess.SubprocessError) as exc:
-            return {"cmd": " ".join(cmd), "returncode": None, "stdout": "", "stderr": str(exc)}
-
-    def _health_dir(self) -> Path:
-        path = Path(self.out_dir) / "gpu_health"
-        path.mkdir(parents=True, exist_ok=True)
-        return path
-
-    def _append_jsonl(self, stem: str, payload: Dict[str, Any]) -> None:
-        try:
-            with (self._health_dir() / f"{stem}_rank{self.rank}.jsonl").open("a", encoding="utf-8") as fh:
-                fh.write(json.dumps(payload, sort_keys=True) + "\n")
-        except OSError as exc:
-            if getattr(self, "_strict_logging", False):
-                raise
-            if stem != "gpu_health_notices" and not self._notice_written:
-                self._notice_written = True
-                print(f"[gpu-health] failed to write {stem} log: {exc}", flush=True)
-
-    def _write_notice(self, message: str) -> None:
-        if self._notice_written:
+    def _notice(self, message: str) -> None:
+        if self._noticed:
             return
-        self._notice_written = True
-        self._append_jsonl("gpu_health_notices", {
+        self._noticed = True
+        self.log.append("gpu_health_notices", {
             "event": "gpu_health_notice", "rank": self.rank, "hostname": self.hostname,
             "slurm_node": self.slurm_node, "cuda_device": self.cuda_device, "gpu_query_id": self.gpu_query_id,
             "message": message, "timestamp_unix": time.time()})
 
 
 def summarize_failures_for_stdout(failures: Iterable[Dict[str, Any]]) -> str:
-    parts = []
-    for f in failures:
-        parts.append(
-            f"rank={f.get('rank')} local_rank={f.get('local_rank')} host={f.get('hostname')} "
-            f"node={f.get('slurm_node')} gpu={f.get('gpu_index')} uuid={f.get('gpu_uuid')} "
-            f"reasons={','.join(str(r) for r in f.get('reasons', []))} temp={f.get('gpu_temp_c')}C "
-            f"mem={f.get('memory_temp_c')}C sm={f.get('sm_clock_mhz')}/{f.get('max_sm_clock_mhz')}MHz "
-            f"util={f.get('gpu_util_pct')}%")
-    return " | ".join(parts)
+    def one(f: Dict[str, Any]) -> str:
+        return (f"rank={f.get('rank')} local_rank={f.get('local_rank')} host={f.get('hostname')} "
+                f"node={f.get('slurm_node')} gpu={f.get('gpu_index')} uuid={f.get('gpu_uuid')} "
+                f"reasons={','.join(str(r) for r in f.get('reasons', []))} temp={f.get('gpu_temp_c')}C "
+                f"mem={f.get('memory_temp_c')}C sm={f.get('sm_clock_mhz')}/{f.get('max_sm_clock_mhz')}MHz "
+                f"util={f.get('gpu_util_pct')}%")
+
+    return " | ".join(one(f) for f in failures)

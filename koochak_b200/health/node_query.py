@@ -1,4 +1,15 @@
-"""One nvidia-smi query for all GPUs a node monitor owns (reference: koochak/health/node_query.py:22-107)."""
+"""One nvidia-smi call reads every GPU that a node's monitor is responsible for.
+
+(behaviour of reference koochak/health/node_query.py:22-107)
+
+``NodeQuery`` runs that call as the monitor's only child process, with a
+10 s limit, and can kill and reap it from another thread when the monitor
+shuts down. ``query_node_samples`` matches the returned rows to the
+monitored GPUs (by nvidia-smi index or UUID prefix) and refuses anything it
+cannot trust: a missing or ambiguous row, a row without temperature / clock
+/ utilization / UUID, negative or non-finite readings, two ranks mapped to
+one physical GPU.
+"""
 
 from __future__ import annotations
 
@@ -6,7 +17,7 @@ import csv
 import math
 import subprocess
 import threading
-from typing import Callable, Sequence
+from typing import Callable, Dict, List, Optional, Sequence
 
 from .gpu import FALLBACK_QUERY_FIELDS, PRIMARY_QUERY_FIELDS, GpuHealthSample, GpuHealthWatchdog, \
     sample_from_nvidia_smi_row
@@ -17,77 +28,94 @@ QUERY_TIMEOUT_SECONDS = 10.0
 
 
 class NodeQuery:
-    """Owns the monitor's single child process; ``cancel`` kills and reaps it."""
+    """Runs one query at a time; ``cancel`` stops the current one and refuses new ones."""
 
     def __init__(self) -> None:
-        self._lock = threading.Lock()
-        self._proc: subprocess.Popen | None = None
-        self._closing = False
+        self._guard = threading.Lock()
+        self._child: Optional[subprocess.Popen] = None
+        self._stopped = False
 
-    def run(self, argv: list[str]) -> subprocess.CompletedProcess:
-        with self._lock:
-            if self._closing:
+    def _spawn(self, argv: List[str]) -> subprocess.Popen:
+        with self._guard:
+            if self._stopped:
                 raise RuntimeError("GPU health query stopped")
-            proc = subprocess.Popen(argv, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
-            self._proc = proc
+            self._child = subprocess.Popen(argv, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            return self._child
+
+    def run(self, argv: List[str]) -> subprocess.CompletedProcess:
+        child = self._spawn(argv)
         try:
-            out, err = proc.communicate(timeout=QUERY_TIMEOUT_SECONDS)
-            return subprocess.CompletedProcess(argv, proc.returncode, out, err)
+            out, err = child.communicate(timeout=QUERY_TIMEOUT_SECONDS)
         except BaseException:
-            proc.kill()
-            proc.communicate()
+            child.kill()
+            child.communicate()
             raise
         finally:
-            with self._lock:
-                self._proc = None
+            with self._guard:
+                self._child = None
+        return subprocess.CompletedProcess(argv, child.returncode, out, err)
 
     def cancel(self) -> None:
-        with self._lock:
-            self._closing = True
-            proc = self._proc
-            if proc is not None:
-                proc.kill()
-        if proc is not None:
-            proc.wait(timeout=QUERY_TIMEOUT_SECONDS)
+        with self._guard:
+            self._stopped = True
+            child = self._child
+            if child is not None:
+                child.kill()
+        if child is not None:
+            child.wait(timeout=QUERY_TIMEOUT_SECONDS)
+
+
+def _row_for(query_id: str, rows: Sequence[Sequence[str]]) -> Sequence[str]:
+    def names(row: Sequence[str]) -> bool:
+        index, uuid = row[0].strip(), row[1].strip()
+        return index == query_id or (query_id.startswith("GPU-") and uuid.startswith(query_id))
+
+    hits = [r for r in rows if names(r)]
+    if len(hits) != 1:
+        raise RuntimeError(f"GPU health query cannot identify assigned GPU {query_id}")
+    return hits[0]
+
+
+def _finite_non_negative(value: Optional[float]) -> bool:
+    return value is not None and math.isfinite(value) and value >= 0
+
+
+def _checked(w: GpuHealthWatchdog, row: Sequence[str], fields: Sequence[str], step: int) -> GpuHealthSample:
+    s = sample_from_nvidia_smi_row(step=step, rank=w.rank, world_size=w.world_size, hostname=w.hostname,
+                                   slurm_node=w.slurm_node, cuda_device=w.cuda_device, gpu_query_id=w.gpu_query_id,
+                                   fields=fields, row=row)
+    s.local_rank = w.local_rank
+    if not s.gpu_uuid or not all(_finite_non_negative(v) for v in (s.gpu_temp_c, s.sm_clock_mhz, s.gpu_util_pct)):
+        raise RuntimeError(f"GPU health query lacks required values for GPU {w.gpu_query_id}")
+    optional = (s.memory_temp_c, s.power_draw_w, s.power_limit_w, s.mem_clock_mhz, s.max_sm_clock_mhz,
+                s.mem_util_pct)
+    if not all(v is None or _finite_non_negative(v) for v in optional):
+        raise RuntimeError(f"GPU health query has invalid readings for GPU {w.gpu_query_id}")
+    return s
 
 
 def query_node_samples(watchdogs: Sequence[GpuHealthWatchdog], step: int, *,
-                       run: Callable[[list[str]], subprocess.CompletedProcess]) -> list[GpuHealthSample]:
-    """One parseable, distinct row per assigned physical GPU, or RuntimeError."""
+                       run: Callable[[List[str]], subprocess.CompletedProcess]) -> List[GpuHealthSample]:
+    """One trusted sample per monitored GPU, in ``watchdogs`` order; ``RuntimeError`` otherwise."""
 
     exe = watchdogs[0].nvidia_smi
     if exe is None:
         raise RuntimeError("nvidia-smi is not available on PATH")
-    ids = [w.gpu_query_id for w in watchdogs]
-    error = "nvidia-smi did not return GPU health rows"
+    selection = ",".join(w.gpu_query_id for w in watchdogs)
+    last_error = "nvidia-smi did not return GPU health rows"
     for fields in (PRIMARY_QUERY_FIELDS, FALLBACK_QUERY_FIELDS):
-        proc = run([exe, "-i", ",".join(ids), f"--query-gpu={','.join(fields)}", "--format=csv,noheader,nounits"])
-        if proc.returncode != 0:
-            error = f"nvidia-smi exited {proc.returncode}: {proc.stderr.strip()}"
+        done = run([exe, "-i", selection, f"--query-gpu={','.join(fields)}", "--format=csv,noheader,nounits"])
+        if done.returncode != 0:
+            last_error = f"nvidia-smi exited {done.returncode}: {done.stderr.strip()}"
             continue
-        rows = list(csv.reader(proc.stdout.strip().splitlines()))
+        rows = list(csv.reader(done.stdout.strip().splitlines()))
         if len(rows) != len(watchdogs) or any(len(r) != len(fields) for r in rows):
             raise RuntimeError("nvidia-smi returned an incomplete GPU health query")
-        samples = [_sample_for(w, rows, fields, step) for w in watchdogs]
-        if len({s.gpu_uuid for s in samples}) != len(samples):
+        samples = [_checked(w, _row_for(w.gpu_query_id, rows), fields, step) for w in watchdogs]
+        by_uuid: Dict[str, int] = {}
+        for s in samples:
+            by_uuid[str(s.gpu_uuid)] = by_uuid.get(str(s.gpu_uuid), 0) + 1
+        if any(n > 1 for n in by_uuid.values()):
             raise RuntimeError("GPU health query mapped several ranks to the same GPU")
         return samples
-    raise RuntimeError(error)
-
-
-def _sample_for(w: GpuHealthWatchdog, rows, fields, step) -> GpuHealthSample:
-    qid = w.gpu_query_id
-    hits = [r for r in rows if r[0].strip() == qid or (qid.startswith("GPU-") and r[1].strip().startswith(qid))]
-    if len(hits) != 1:
-        raise RuntimeError(f"GPU health query cannot identify assigned GPU {qid}")
-    s = sample_from_nvidia_smi_row(step=step, rank=w.rank, world_size=w.world_size, hostname=w.hostname,
-                                   slurm_node=w.slurm_node, cuda_device=w.cuda_device, gpu_query_id=qid,
-                                   fields=fields, row=hits[0])
-    s.local_rank = w.local_rank
-    required = (s.gpu_temp_c, s.sm_clock_mhz, s.gpu_util_pct)
-    if any(v is None or not math.isfinite(v) or v < 0 for v in required) or not s.gpu_uuid:
-        raise RuntimeError(f"GPU health query lacks required values for GPU {qid}")
-    optional = (s.memory_temp_c, s.power_draw_w, s.power_limit_w, s.mem_clock_mhz, s.max_sm_clock_mhz, s.mem_util_pct)
-    if any(v is not None and (not math.isfinite(v) or v < 0) for v in optional):
-        raise RuntimeError(f"GPU health query has invalid readings for GPU {qid}")
-    return s
+    raise RuntimeError(last_error)

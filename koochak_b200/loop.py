@@ -566,10 +566,15 @@ class _TrainLoop:
         if self._on_cuda() and str(torch.distributed.get_backend()).lower() == "nccl":
             from .parallel.ddp import DataParallel
 
-            cap = s.ddp_bucket_cap_mb if s.ddp_bucket_cap_mb is not None else (
-                s.ddp_bucket_cap_mb_list[-1] if s.ddp_bucket_cap_mb_list else 25)
-            self.model = DataParallel(self.model, bucket_cap_mb=float(cap), broadcast_buffers=s.ddp_broadcast_buffers,
-                                      transport=s.comm_transport, find_unused_parameters=s.find_unused_parameters)
+            caps = ([float(s.ddp_bucket_cap_mb)] if s.ddp_bucket_cap_mb is not None else
+                    [float(c) for c in s.ddp_bucket_cap_mb_list] if s.ddp_bucket_cap_mb_list else [25.0])
+            owners, shard_rest = {}, False
+            commit = getattr(self.optimizer, "kb_commit_gradient_plan", None)
+            if str(s.comm_transport).lower() in ("fused", "p2p") and callable(commit):
+                owners, shard_rest = commit(self.world_size)
+            self.model = DataParallel(self.model, bucket_cap_mb=caps, broadcast_buffers=s.ddp_broadcast_buffers,
+                                      transport=s.comm_transport, find_unused_parameters=s.find_unused_parameters,
+                                      owners=owners, shard_rest=shard_rest)
             if isinstance(self.scaler, FusedGradScaler) and self.model.transport == "fused":
                 scaler = self.scaler
                 self.model.grad_scale_fn = lambda: scaler._scale

@@ -480,7 +480,7 @@ def _native_muon_bucket(optimizer, group, parts: List[Tuple[int, int, List[torch
             ws = slab.ws
             native().muon_update_gather(params, Xi, _shadow_list(params), float(group["lr"]),
                                         float(group["weight_decay"]), 0.2 * math.sqrt(max(R, C)), R > C, ws.bases,
-                                        ws.mc_base, ws.rank)
+                                        ws.mc_base, ws.rank, ws.nbytes)
         else:
             ema, d = _ema_list(optimizer, params)
             native().muon_epilogue(params, Xi, ema, _shadow_list(params), float(group["lr"]),
@@ -499,30 +499,68 @@ def _batches(owned: Dict[Tuple[int, int], List[torch.nn.Parameter]]
     return list(joined.values())
 
 
-def _native_muon_group(optimizer, group, distributed: bool) -> None:
+def _slab_ok(params: Sequence[torch.Tensor]) -> bool:
+    """Whether the symmetric-slab (in-kernel peer store) path can hold these parameters."""
+
+    if os.environ.get("KOOCHAK_B200_MUON_GATHER", "peer") != "peer":
+        return False
+    if not dist.is_initialized() or dist.get_backend() != "nccl" or dist.get_world_size() > 8:
+        return False
+    return _native_ready(params)
+
+
+def _muon_path(group: Dict[str, Any], normuon: bool, distributed: bool) -> str:
+    """How a Muon group is stepped: 'ref' (PyTorch ops), 'native', 'slab' (native + peer stores) or 'nccl'."""
+
+    params = list(group["params"])
+    if normuon or not _native_ready(params):
+        return "ref"
+    if not distributed:
+        return "native"
+    if _slab_ok(params) and all(p.dim() >= 2 and (p.numel() // p.shape[0]) % 4 == 0 for p in params):
+        return "slab"
+    return "nccl"
+
+
+def muon_owners(group: Dict[str, Any], path: str, world: int) -> List[int]:
+    """Owner rank of each parameter of a distributed Muon group (its momentum lives only there).
+
+    Matrix i of the size-sorted group belongs to rank i % W, the reference's
+    rule (its distributed step updates ``params[base + rank]``), for the
+    PyTorch and slab paths; the NCCL all-gather fallback, which gathers per
+    shape bucket, owns matrix k of each bucket on rank k % W.
+    """
+
+    params = list(group["params"])
+    if path != "nccl":
+        return [i % world for i in range(len(params))]
+    owners = [0] * len(params)
+    for idx in _muon_buckets(params).values():
+        for k, i in enumerate(idx):
+            owners[i] = k % world
+    return owners
+
+
+def _native_muon_group(optimizer, group, path: str, slab=None) -> None:
     params: List[torch.nn.Parameter] = list(group["params"])
     if not params:
         return
     buckets = _muon_buckets(params)
-    if not distributed:
+    if path == "native":
         for parts in _batches({key: [params[i] for i in idx] for key, idx in buckets.items()}):
             _native_muon_bucket(optimizer, group, parts)
         return
     world, rank = dist.get_world_size(), dist.get_rank()
-    slab = _param_slab(optimizer, group, params)
-    if slab is not None:
-        # Owner of matrix i is rank i % W over the (size-sorted) group, as in
-        # the reference's distributed step, so rank 0 holds the momentum of the
-        # same matrices in both frameworks.
-        owned = {key: [params[i] for i in idx if i % world == rank] for key, idx in buckets.items()}
+    owners = muon_owners(group, path, world)
+    owned = {key: [params[i] for i in idx if owners[i] == rank] for key, idx in buckets.items()}
+    if path == "slab":
+        assert slab is not None
         for parts in _batches(owned):
             _native_muon_bucket(optimizer, group, parts, slab=slab)
         for i, p in enumerate(params):
-            if i % world != rank and getattr(p, "_kb_shadow", None) is not None:
+            if owners[i] != rank and getattr(p, "_kb_shadow", None) is not None:
                 p._kb_shadow_version = -1  # rewritten by its owner: recast before the next forward
-        slab.barrier()
         return
-    owned = {key: [params[i] for k, i in enumerate(idx) if k % world == rank] for key, idx in buckets.items()}
     for parts in _batches(owned):
         _native_muon_bucket(optimizer, group, parts)
     for (R, C), idx in buckets.items():
@@ -539,41 +577,127 @@ def _native_muon_group(optimizer, group, distributed: bool) -> None:
             params[i].detach().view(-1).copy_(recv[(k % world) * per_rank + k // world])
 
 
-def _param_slab(optimizer, group, params: List[torch.nn.Parameter]):
-    """The group's symmetric parameter slab (built on first use), or None for the NCCL all-gather."""
+def _sharded_adam_group(optimizer, group, slab) -> None:
+    """AdamW on this rank's shard of every tensor of an Adam group, published into every rank's copy.
 
-    if os.environ.get("KOOCHAK_B200_MUON_GATHER", "peer") != "peer":
-        return None
-    if dist.get_backend() != "nccl" or dist.get_world_size() > 8:
-        return None
-    if any(p.dim() < 2 or (p.numel() // p.shape[0]) % 4 != 0 for p in params):
-        return None
-    slabs = optimizer.__dict__.setdefault("_kb_param_slabs", {})
-    key = id(group)
-    slab = slabs.get(key)
+    The gradient sync reduce-scattered these tensors (``shard_bounds`` per
+    tensor), so only the shard of ``p.grad`` holds averaged values here.
+    """
+
+    from ..ops._ext import native
+    from ..parallel.symm import shard_bounds
+
+    params = list(group["params"])
+    if not params:
+        return
+    world, rank = dist.get_world_size(), dist.get_rank()
+    grads, m, v, steps, lo, hi = [], [], [], [], [], []
+    for p in params:
+        _ensure_grad(p)
+        st = optimizer.state[p]
+        if "exp_avg" not in st:
+            st["exp_avg"] = torch.zeros_like(p)
+            st["exp_avg_sq"] = torch.zeros_like(p)
+            st["step"] = 0
+        st["step"] = int(st["step"]) + 1
+        a, b = shard_bounds(p.numel(), world, rank)
+        grads.append(p.grad)
+        m.append(st["exp_avg"])
+        v.append(st["exp_avg_sq"])
+        steps.append(int(st["step"]))
+        lo.append(a)
+        hi.append(b)
+    b1, b2 = group["betas"]
+    ws = slab.ws
+    native().adam_shard_gather(params, grads, m, v, lo, hi, steps, _clip_scale(optimizer),
+                               getattr(optimizer, "kb_skip_flag", None), float(group["lr"]), float(b1), float(b2),
+                               float(group["eps"]), float(group["weight_decay"]), ws.bases, ws.mc_base, ws.rank,
+                               ws.nbytes)
+    for p in params:
+        if getattr(p, "_kb_shadow", None) is not None:
+            p._kb_shadow_version = -1  # only this rank's shard was written locally: recast before the next forward
+
+
+def _optimizer_slab(optimizer, params: List[torch.nn.Parameter]):
+    """The optimizer's symmetric parameter slab holding ``params`` (built, or rebuilt, on demand)."""
+
+    slab = optimizer.__dict__.get("_kb_slab")
     if slab is None or not slab.holds(params):
         from ..parallel.symm import SymmetricParamSlab
 
         slab = SymmetricParamSlab(params, params[0].device)
-        slabs[key] = slab
+        optimizer.__dict__["_kb_slab"] = slab
     return slab
 
 
 def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) -> None:
+    plan = getattr(optimizer, "_kb_plan", None) if distributed else None
+    shard_adam = bool(plan and plan["shard_rest"])
+    paths = []
+    slab_params: List[torch.nn.Parameter] = []
     for group in optimizer.param_groups:
+        if group.get("use_muon", True):
+            path = _muon_path(group, normuon, distributed)
+            if path == "slab":
+                slab_params += list(group["params"])
+        else:
+            native_ok = _native_ready(group["params"]) and not _foreach_adam_enabled(group)
+            path = ("sharded" if shard_adam else "native") if native_ok else "ref"
+            if path == "sharded":
+                slab_params += list(group["params"])
+        paths.append(path)
+    if shard_adam and "ref" in [p for g, p in zip(optimizer.param_groups, paths) if not g.get("use_muon", True)]:
+        raise RuntimeError("the gradient sync reduce-scattered the Adam tensors, but an Adam group cannot take "
+                           "the sharded native path")
+    slab = _optimizer_slab(optimizer, slab_params) if slab_params else None
+    for group, path in zip(optimizer.param_groups, paths):
         params = group["params"]
         if group.get("use_muon", True):
             with _profile_range("optimizer.muon.update"):
-                if not normuon and _native_ready(params):
-                    _native_muon_group(optimizer, group, distributed)
-                else:
+                if path == "ref":
                     _ref_muon_group(optimizer, group, muon_fn, distributed)
+                else:
+                    _native_muon_group(optimizer, group, path, slab)
         else:
             with _profile_range("optimizer.adam.update"):
-                if _native_ready(params) and not _foreach_adam_enabled(group):
+                if path == "sharded":
+                    _sharded_adam_group(optimizer, group, slab)
+                elif path == "native":
                     _native_adam_group(optimizer, group)
                 else:
                     _ref_adam_group(optimizer, group)
+    if slab is not None:
+        slab.barrier()  # every rank's peer stores of this step have landed
+
+
+def gradient_plan(optimizer, world: int) -> Tuple[Dict[int, int], bool]:
+    """Where the data-parallel sync must deliver each reduced gradient for this optimizer.
+
+    Returns (owners, shard_rest): ``owners`` maps ``id(param)`` of every
+    distributed Muon matrix to the rank whose step reads its gradient, and
+    ``shard_rest`` says whether every Adam tensor can be reduce-scattered
+    (its update runs sharded, ``_sharded_adam_group``). Both are empty/False
+    when a group needs gradients everywhere (non-native or foreach Adam
+    groups, a non-distributed optimizer).
+    """
+
+    if not (getattr(optimizer, "_distributed", False) and world > 1):
+        return {}, False
+    normuon = bool(getattr(optimizer, "_normuon", False))
+    owners: Dict[int, int] = {}
+    shard_rest = True
+    for group in optimizer.param_groups:
+        params = list(group["params"])
+        if group.get("use_muon", True):
+            path = _muon_path(group, normuon, True)
+            for p, r in zip(params, muon_owners(group, path, world)):
+                owners[id(p)] = r
+        elif not (_native_ready(params) and not _foreach_adam_enabled(group) and _slab_ok(params)):
+            shard_rest = False
+    if not shard_rest:
+        # Replicated Adam steps read every gradient; Muon owners still only need their own matrices.
+        pass
+    return owners, shard_rest
 
 
 def _sorted_desc(params: Iterable[torch.nn.Parameter]) -> List[torch.nn.Parameter]:
@@ -603,7 +727,7 @@ def _closure(closure):
 
 
 class _KbOptimizer(torch.optim.Optimizer):
-    """Base: fused-path hooks (clip coefficient, fused EMA) consumed by one step."""
+    """Base: fused-path hooks (clip coefficient, fused EMA) consumed by one step, and sharded-state handling."""
 
     kb_fused = True
     _normuon = False
@@ -622,6 +746,94 @@ class _KbOptimizer(torch.optim.Optimizer):
             self.kb_grad_scale = None
             self.kb_ema = None
         return loss
+
+    def kb_commit_gradient_plan(self, world: int) -> Tuple[Dict[int, int], bool]:
+        """Fix where reduced gradients must arrive (see ``gradient_plan``); later steps rely on it."""
+
+        owners, shard_rest = gradient_plan(self, world)
+        self._kb_plan = {"world": world, "owners": dict(owners), "shard_rest": bool(shard_rest)}
+        return owners, shard_rest
+
+    def _muon_state_keys(self) -> List[str]:
+        return ["momentum_buffer", "second_momentum_buffer"] if self._normuon else ["momentum_buffer"]
+
+    @torch.no_grad()
+    def gathered_state_dict(self) -> Dict[str, Any]:
+        """The full optimizer state, on every rank (a collective: every rank must call it).
+
+        A distributed step keeps each Muon matrix's momentum only on its
+        owner, and with a sharded Adam step each rank's Adam moments are
+        current only on its shard. This gathers both (owners' buffers summed
+        with zeros elsewhere, which is exact) so the returned state dict has
+        the layout and values of a single-process run: every Muon matrix's
+        ``momentum_buffer`` in the reference's parameter order, full
+        ``exp_avg`` / ``exp_avg_sq``. Non-distributed: ``state_dict()``.
+        """
+
+        if not self._distributed_now():
+            return self.state_dict()
+        world, rank = dist.get_world_size(), dist.get_rank()
+        plan = getattr(self, "_kb_plan", None) or {}
+        temp: List[torch.nn.Parameter] = []
+        for group in self.param_groups:
+            params = list(group["params"])
+            if not params:
+                continue
+            dev = params[0].device
+            if group.get("use_muon", True):
+                owners = muon_owners(group, _muon_path(group, self._normuon, True), world)
+                for key in self._muon_state_keys():
+                    present = torch.tensor([float(owners[i] == rank and key in self.state.get(p, {}))
+                                            for i, p in enumerate(params)], device=dev)
+                    dist.all_reduce(present)
+                    for i, p in enumerate(params):
+                        if float(present[i]) == 0.0:
+                            continue
+                        st = self.state[p]
+                        mine = owners[i] == rank
+                        if key == "momentum_buffer":
+                            shape = p.shape
+                        else:
+                            shape = (p.shape[0], 1) if p.ndim > 2 else (*p.shape[:-1], 1)
+                        buf = st[key].detach().clone() if mine else torch.zeros(shape, device=dev, dtype=p.dtype)
+                        dist.all_reduce(buf)
+                        if not mine:
+                            st[key] = buf
+                            temp.append(p)
+            elif plan.get("shard_rest"):
+                from ..parallel.symm import shard_bounds
+
+                for p in params:
+                    st = self.state.get(p)
+                    if not st or "exp_avg" not in st:
+                        continue
+                    lo, hi = shard_bounds(p.numel(), world, rank)
+                    for key in ("exp_avg", "exp_avg_sq"):
+                        flat = st[key].view(-1)
+                        flat[:lo].zero_()
+                        flat[hi:].zero_()
+                        dist.all_reduce(st[key])  # every rank now holds the complete moments
+        sd = self.state_dict()
+        for p in temp:  # borrowed from the owners for this dict only
+            for key in self._muon_state_keys():
+                self.state[p].pop(key, None)
+            if not self.state[p]:
+                del self.state[p]
+        return sd
+
+    def load_state_dict(self, state_dict: Dict[str, Any]) -> None:
+        super().load_state_dict(state_dict)
+        if not self._distributed_now():
+            return
+        # A gathered checkpoint holds every matrix's momentum: keep only the owned ones.
+        world, rank = dist.get_world_size(), dist.get_rank()
+        for group in self.param_groups:
+            if not group.get("use_muon", True):
+                continue
+            owners = muon_owners(group, _muon_path(group, self._normuon, True), world)
+            for p, r in zip(group["params"], owners):
+                if r != rank and p in self.state:
+                    del self.state[p]
 
 
 class Muon(_KbOptimizer):

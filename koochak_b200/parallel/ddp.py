@@ -7,26 +7,37 @@
 buffers broadcast before every forward when ``broadcast_buffers``), with its
 own bucketing:
 
-* parameters are grouped into buckets of ``bucket_cap_mb`` in reverse
-  registration order (the order backward produces gradients), identically on
-  every rank;
+* parameters are grouped into buckets in reverse registration order (the
+  order backward produces gradients), identically on every rank; bucket ``i``
+  holds up to ``bucket_caps_mb[min(i, len - 1)]`` MB (torch DDP's
+  ``bucket_cap_mb_list`` rule; a single ``bucket_cap_mb`` is a one-entry list);
 * a post-accumulate-grad hook copies each finished gradient into its bucket's
   flat fp32 buffer; when a bucket is complete its reduction is launched on a
   dedicated communication stream while backward keeps running;
 * at the end of backward the compute stream waits for every bucket and each
-  ``param.grad`` becomes a view of the averaged bucket.
+  ``param.grad`` becomes a view of its bucket (gradients are always bucket
+  views, i.e. torch DDP's ``gradient_as_bucket_view=True``; ``static_graph``
+  changes nothing here because buckets are fixed at wrap time).
 
 Reduction transports (``transport``):
 
 * ``"nccl"`` / ``"gloo"``: one averaging all-reduce per bucket (baseline);
 * ``"fused"`` (alias ``"p2p"``): the native single-node path. Buckets live in
-  symmetric device memory; one kernel per bucket reduces this rank's shard
-  over NVLink (P2P loads or NVSwitch ``multimem``; no NCCL in the data
-  path), fused with the GradScaler unscale, the finite flag and per-tensor
-  sums of squares, and writes the result back to every rank, with bounded
-  cross-GPU flag waits (``koochak_b200/parallel/symm.py``). The gradient gate
-  then reads those statistics instead of passing over the gradients again
-  (``DataParallel.fused_gate``).
+  symmetric device memory; one kernel per bucket reduces this rank's part
+  over NVLink (P2P loads or NVSwitch ``multimem``; no NCCL in the data path),
+  fused with the GradScaler unscale, the finite flag and per-tensor sums of
+  squares (``koochak_b200/parallel/symm.py``, ``csrc/comm.cu``). The gradient
+  gate then reads those statistics instead of passing over the gradients
+  again (``DataParallel.fused_gate``).
+
+With the fused transport an optimizer that shards its update can say where
+each reduced gradient is needed (``owners``, ``shard_rest``): a parameter
+listed in ``owners`` is reduced only into its owner's memory, and with
+``shard_rest`` every other parameter is reduce-scattered (rank ``r`` keeps
+the reduced values of ``shard_bounds(numel, world, r)``). ``param.grad`` then
+holds the averaged gradient only where this rank needs it and this rank's own
+local gradient elsewhere; the optimizer (``optim/muon.py``) reads exactly the
+averaged parts.
 
 Buckets are launched in index order on every rank, whatever order backward
 finishes them in, so every rank issues the same reductions in the same order.
@@ -36,13 +47,34 @@ from __future__ import annotations
 
 import contextlib
 import os
-from typing import Callable, Dict, List, Optional, Sequence
+from typing import Callable, Dict, List, Optional, Sequence, Union
 
 import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-__all__ = ["DataParallel", "Bucket"]
+__all__ = ["DataParallel", "Bucket", "split_buckets"]
+
+
+def split_buckets(numels: Sequence[int], caps: Sequence[int]) -> List[List[int]]:
+    """Group parameter indices (already in gradient order) into buckets.
+
+    Bucket ``i`` is closed as soon as it holds at least ``caps[min(i, len(caps) - 1)]``
+    elements, so one large tensor always forms a bucket of its own.
+    """
+
+    out: List[List[int]] = []
+    cur: List[int] = []
+    size = 0
+    for i, n in enumerate(numels):
+        cur.append(i)
+        size += int(n)
+        if size >= caps[min(len(out), len(caps) - 1)]:
+            out.append(cur)
+            cur, size = [], 0
+    if cur:
+        out.append(cur)
+    return out
 
 
 class Bucket:
@@ -59,7 +91,6 @@ class Bucket:
         # The fused transport replaces this with a view of symmetric memory.
         self.buffer = torch.zeros(total if allocate else 0, device=device, dtype=torch.float32)
         self.pending = 0
-        self.work = None
         self.ready_event: Optional[torch.cuda.Event] = None
         self.complete = False
 
@@ -69,9 +100,12 @@ class Bucket:
 
 
 class DataParallel(nn.Module):
-    def __init__(self, module: nn.Module, *, bucket_cap_mb: float = 25.0, broadcast_buffers: bool = True,
-                 transport: str = "auto", process_group=None, find_unused_parameters: bool = False,
-                 comm_blocks: Optional[int] = None) -> None:
+    def __init__(self, module: nn.Module, *, bucket_cap_mb: Union[float, Sequence[float]] = 25.0,
+                 broadcast_buffers: bool = True, transport: str = "auto", process_group=None,
+                 find_unused_parameters: bool = False, comm_blocks: Optional[int] = None,
+                 owners: Optional[Dict[int, int]] = None, shard_rest: bool = False) -> None:
+        """``owners`` maps ``id(param)`` to the rank that alone needs its reduced gradient (fused transport only)."""
+
         super().__init__()
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("DataParallel needs an initialised process group")
@@ -87,20 +121,17 @@ class DataParallel(nn.Module):
         backend = str(dist.get_backend(process_group)).lower()
         self.transport = self._pick_transport(transport, backend)
         self._sync_module_states()
-        cap = max(1, int(bucket_cap_mb * 1024 * 1024 / 4))
+        caps_mb = [float(bucket_cap_mb)] if isinstance(bucket_cap_mb, (int, float)) else [float(c) for c in bucket_cap_mb]
+        if not caps_mb or any(c <= 0 for c in caps_mb):
+            raise ValueError("bucket caps must be positive")
+        caps = [max(1, int(c * 1024 * 1024 / 4)) for c in caps_mb]
         align, own = (4, False) if self.transport == "fused" else (1, True)
         self.params = params
-        self.buckets: List[Bucket] = []
-        current: List[nn.Parameter] = []
-        size = 0
-        for p in reversed(params):
-            current.append(p)
-            size += p.numel()
-            if size >= cap:
-                self.buckets.append(Bucket(len(self.buckets), current, self.device, align, own))
-                current, size = [], 0
-        if current:
-            self.buckets.append(Bucket(len(self.buckets), current, self.device, align, own))
+        order = list(reversed(params))
+        self.buckets: List[Bucket] = [
+            Bucket(i, [order[j] for j in idx], self.device, align, own)
+            for i, idx in enumerate(split_buckets([p.numel() for p in order], caps))
+        ]
         self._where: Dict[int, tuple] = {}
         for b in self.buckets:
             for i, p in enumerate(b.params):
@@ -112,19 +143,27 @@ class DataParallel(nn.Module):
         self.grad_scale: Optional[torch.Tensor] = None
         self.grad_scale_fn: Optional[Callable[[], Optional[torch.Tensor]]] = None
         self._fused_ready = False
+        self.owners: Dict[int, int] = {}
+        self.shard_rest = False
         if self.transport == "fused":
             from .symm import FusedGradReducer
 
             tid = {id(p): i for i, p in enumerate(params)}
+            self.owners = {k: int(v) for k, v in (owners or {}).items() if k in tid}
+            self.shard_rest = bool(shard_rest)
             segments = [[(p.numel(), tid[id(p)]) for p in b.params] for b in self.buckets]
             if comm_blocks is None:  # CTAs per bucket kernel (they share the GPU with the overlapped backward)
                 comm_blocks = int(os.environ.get("KOOCHAK_B200_COMM_BLOCKS", 32))
             # CTAs for the reductions that nothing overlaps (after backward).
             self._tail_blocks = max(comm_blocks, int(os.environ.get("KOOCHAK_B200_COMM_TAIL_BLOCKS", 128)))
-            self._fused = FusedGradReducer(segments, len(params), self.device, process_group, blocks=comm_blocks)
+            self._fused = FusedGradReducer(segments, len(params), self.device, process_group, blocks=comm_blocks,
+                                           owner_of={tid[k]: r for k, r in self.owners.items()},
+                                           shard_rest=self.shard_rest)
             for b, buf in zip(self.buckets, self._fused.buffers):
                 assert buf.numel() == b.numel
                 b.buffer = buf
+        elif owners or shard_rest:
+            raise ValueError("owners / shard_rest need the fused transport")
         self._next_launch = 0
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in params]
         self._armed = False
@@ -148,6 +187,12 @@ class DataParallel(nn.Module):
         for t in list(self.module.parameters()) + list(self.module.buffers()):
             dist.broadcast(t.data, src=0, group=self.group)
 
+    @property
+    def sharded(self) -> bool:
+        """True when some reduced gradients live only on the rank that owns them."""
+
+        return bool(self.owners) or self.shard_rest
+
     # ------------------------------------------------------------------ forward
     def forward(self, *args, **kwargs):
         if self.broadcast_buffers and self.world > 1:
@@ -168,13 +213,16 @@ class DataParallel(nn.Module):
             self.require_sync = prev
 
     def _arm(self) -> None:
+        if self._fused is not None and self._fused_ready:
+            # The previous synchronised backward was never gated: close its
+            # reductions on every rank before the buckets are written again.
+            self._fused.seal_gate(None)
         self._armed = True
         self._callback_queued = False
         self._fused_ready = False
         self._next_launch = 0
         for b in self.buckets:
             b.pending = len(b.params)
-            b.work = None
             b.ready_event = None
             b.complete = False
         if self._fused is not None:
@@ -196,10 +244,11 @@ class DataParallel(nn.Module):
             self._launch_ready()
 
     def _launch_ready(self, tail: bool = False) -> None:
-        # Strict index order: the reductions pair up across ranks by sequence.
-        # Buckets launched once backward has finished (``tail``), and the last
-        # bucket, have no compute left to overlap with: they get the wider
-        # grid. Every rank makes the same choice for the same bucket.
+        # Strict index order: every rank issues the same reductions in the same
+        # sequence. Buckets launched once backward has finished (``tail``), and
+        # the last bucket, have no compute left to overlap with and get the
+        # wider grid; the fused kernels' arrival protocol does not need the
+        # grids of different ranks to agree.
         while self._next_launch < len(self.buckets) and self.buckets[self._next_launch].complete:
             b = self.buckets[self._next_launch]
             self._launch(b, wide=tail or b.index == len(self.buckets) - 1)
@@ -259,12 +308,14 @@ class DataParallel(nn.Module):
     def fused_gate(self, max_norm: Optional[float]) -> torch.Tensor:
         """Device fp32 [4] from the fused statistics: norm, clip coefficient, found_inf, status word.
 
-        The gradients are already averaged and (when ``grad_scale`` was set)
+        Waits (on the device, bounded) for every rank's last bucket kernel
+        first. The gradients are averaged and (when ``grad_scale`` was set)
         unscaled; the norm is that of the averaged gradients.
         """
 
         assert self._fused is not None and self._fused_ready
-        return self._fused.gate(max_norm)
+        self._fused_ready = False
+        return self._fused.seal_gate(max_norm)
 
     def state_dict(self, *args, **kwargs):
         return {f"module.{k}": v for k, v in self.module.state_dict(*args, **kwargs).items()}

@@ -1,4 +1,4 @@
-"""Symmetric device memory and the fused gradient all-reduce built on it.
+"""Symmetric device memory and the fused gradient synchronisation built on it.
 
 (replaces the NCCL bucket all-reduce of torch DDP used at reference
 koochak/loop.py:705-723, and the unscale / finite check / norm pass of
@@ -12,17 +12,17 @@ PyTorch: the kernels that read and write peers are this package's own
 (``koochak_b200/csrc/comm.cu``).
 
 ``FusedGradReducer`` lays the data-parallel buckets out inside such a
-workspace. For bucket ``b`` it launches one kernel that
-
-* waits (bounded) until every rank has written bucket ``b``,
-* reduces this rank's 1/W shard of it over NVLink (P2P loads from every peer,
-  or ``multimem.ld_reduce`` through the switch), multiplies by
-  ``inv_scale / W``, checks finiteness and accumulates per-tensor sums of
-  squares, and writes the result back to every rank (P2P or ``multimem.st``),
-* waits until every rank's writes have landed.
-
-After the last bucket every GPU holds the averaged, unscaled gradients and the
-complete per-tensor statistics, so the gradient gate is a one-thread kernel.
+workspace. For bucket ``b`` it launches one kernel that waits (bounded) until
+every rank has produced bucket ``b`` and then, for each chunk of this rank's
+part of the bucket, sums the ranks' values over NVLink (P2P loads, or
+``multimem.ld_reduce`` through the switch), multiplies by ``inv_scale / W``,
+checks finiteness, accumulates per-tensor sums of squares into every rank's
+statistics, and stores the result either into every rank (a replicated
+tensor: all-reduce) or into this rank only (a tensor whose owner alone needs
+the reduced gradient: a Muon matrix, or this rank's shard of a tensor whose
+optimizer update is sharded). Which rank handles which part is fixed by
+``plan_bucket_chunks``. After the last bucket, ``seal_gate`` waits for every
+rank's bucket kernels and forms the clip statistics in one small kernel.
 """
 
 from __future__ import annotations
@@ -33,9 +33,10 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
-__all__ = ["SymmetricWorkspace", "FusedGradReducer", "SymmetricParamSlab", "plan_chunks", "shard_bounds"]
+__all__ = ["SymmetricWorkspace", "FusedGradReducer", "SymmetricParamSlab", "plan_chunks", "plan_bucket_chunks",
+           "shard_bounds"]
 
-_FLAG_BYTES = 128 * 8 * 4  # [max blocks][max ranks] u32 barrier slots
+_FLAG_BYTES = 256  # [max ranks] u32 arrival slots, padded to the allocation alignment
 _ALIGN = 256
 
 
@@ -73,6 +74,36 @@ def plan_chunks(segments: Sequence[Tuple[int, int, int]], lo: int, hi: int, max_
     return out
 
 
+MODE_ALL = 0    # reduced value written to every rank
+MODE_LOCAL = 1  # reduced value written to the reducing rank only
+
+
+def plan_bucket_chunks(layout: Sequence[Tuple[int, int, int]], world: int, rank: int,
+                       owner_of: Optional[Dict[int, int]] = None, shard_rest: bool = False,
+                       max_chunk: int = 32768) -> List[Tuple[int, int, int, int]]:
+    """This rank's (start, length, tensor id, mode) pieces of one bucket.
+
+    ``layout`` lists (offset, numel, tensor id) of the bucket's tensors.
+    A tensor in ``owner_of`` is reduced whole by its owner, into the owner's
+    memory only. Every other tensor is split evenly over the ranks
+    (``shard_bounds``); each rank reduces its piece and writes it to every
+    rank, or, with ``shard_rest``, to itself only (a reduce-scatter whose
+    shards are the per-tensor ``shard_bounds``).
+    """
+
+    owner_of = owner_of or {}
+    out: List[Tuple[int, int, int, int]] = []
+    for off, n, tid in layout:
+        if tid in owner_of:
+            if owner_of[tid] == rank:
+                out += [(a, ln, t, MODE_LOCAL) for a, ln, t in plan_chunks([(off, n, tid)], off, off + n, max_chunk)]
+            continue
+        lo, hi = shard_bounds(n, world, rank)
+        mode = MODE_LOCAL if shard_rest else MODE_ALL
+        out += [(a, ln, t, mode) for a, ln, t in plan_chunks([(off, n, tid)], off + lo, off + hi, max_chunk)]
+    return out
+
+
 class SymmetricWorkspace:
     """One symmetric buffer per rank (and its multicast mapping when available)."""
 
@@ -106,12 +137,18 @@ class SymmetricWorkspace:
 
 
 class FusedGradReducer:
-    """Bucketed, fused gradient all-reduce over a symmetric workspace."""
+    """Bucketed, fused gradient reduction over a symmetric workspace."""
 
     def __init__(self, bucket_segments: Sequence[Sequence[Tuple[int, int]]], n_tensors: int, device: torch.device,
                  group=None, *, blocks: int = 32, timeout_s: Optional[float] = None,
-                 use_multicast: Optional[bool] = None) -> None:
-        """``bucket_segments[b]`` lists (numel, tensor id) of bucket ``b``'s tensors, in layout order."""
+                 use_multicast: Optional[bool] = None, owner_of: Optional[Dict[int, int]] = None,
+                 shard_rest: bool = False) -> None:
+        """``bucket_segments[b]`` lists (numel, tensor id) of bucket ``b``'s tensors, in layout order.
+
+        ``owner_of`` (tensor id -> rank) and ``shard_rest`` select where each
+        reduced value goes (``plan_bucket_chunks``); by default every tensor
+        is all-reduced.
+        """
 
         from ..ops._ext import native
 
@@ -119,6 +156,8 @@ class FusedGradReducer:
         self.n_tensors = int(n_tensors)
         self.blocks = int(blocks)
         self.timeout_s = float(timeout_s if timeout_s is not None else os.environ.get("KOOCHAK_B200_COMM_TIMEOUT_S", 300))
+        self.owner_of = dict(owner_of or {})
+        self.shard_rest = bool(shard_rest)
         stats_bytes = _align(4 * (self.n_tensors + 1))
         self.flags_off = 0
         self.stats_off = [_FLAG_BYTES, _FLAG_BYTES + stats_bytes]
@@ -139,9 +178,11 @@ class FusedGradReducer:
         self.world, self.rank = self.ws.world, self.ws.rank
         self.buffers = [self.ws.view(o, n, torch.float32) for o, n in zip(self.bucket_off, self.bucket_numel)]
         self.chunks: List[torch.Tensor] = []
-        for layout, n in zip(self.layouts, self.bucket_numel):
-            lo, hi = shard_bounds(n, self.world, self.rank)
-            rows = plan_chunks(layout, lo, hi) or [(0, 0, 0)]
+        self.work: List[int] = []  # elements this rank reduces per bucket
+        for layout in self.layouts:
+            rows = plan_bucket_chunks(layout, self.world, self.rank, self.owner_of, self.shard_rest)
+            self.work.append(sum(r[1] for r in rows))
+            rows = rows or [(0, 0, 0, MODE_ALL)]
             self.chunks.append(torch.tensor(rows, dtype=torch.int64, device=device))
         self.stats = [self.ws.view(o, self.n_tensors + 1, torch.float32) for o in self.stats_off]
         self.parity = 0
@@ -164,27 +205,35 @@ class FusedGradReducer:
 
     def _next_epoch(self) -> int:
         e = self.epoch
-        self.epoch = (self.epoch + 2) & 0xFFFFFFFF
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
         return e
 
     def reduce(self, b: int, scale: Optional[torch.Tensor] = None, blocks: Optional[int] = None) -> None:
-        """All-reduce bucket ``b`` (average, unscale, statistics) on the current stream.
+        """Reduce bucket ``b`` (average, unscale, statistics) on the current stream.
 
-        ``blocks`` overrides the grid size for this launch (every rank must
-        pass the same value for the same bucket); at most 128.
+        ``blocks`` overrides the grid size of this launch (at most 148); the
+        arrival protocol does not need it to agree across ranks.
         """
 
-        nb = min(int(blocks), 128) if blocks else self.blocks
-        self._C.comm_allreduce_bucket(self.ws.bases, self.ws.mc_base, self.flags_off, self.stats_off[self.parity],
-                                      self.bucket_off[b], self.chunks[b], self.n_tensors, self.rank,
-                                      self._next_epoch(), scale, nb, self.timeout_s)
+        nb = min(int(blocks), 148) if blocks else self.blocks
+        self._C.comm_grad_sync(self.ws.bases, self.ws.mc_base, self.flags_off, self.stats_off[self.parity],
+                               self.bucket_off[b], self.chunks[b], self.n_tensors, self.rank, self._next_epoch(),
+                               scale, nb, self.timeout_s)
 
     def barrier(self) -> None:
-        self._C.comm_barrier(self.ws.bases, self.flags_off, self.rank, self._next_epoch(), self.blocks,
-                             self.timeout_s, self.ws.device.index or 0)
+        self._C.comm_barrier(self.ws.bases, self.flags_off, self.rank, self._next_epoch(), 1, self.timeout_s,
+                             self.ws.device.index or 0)
+
+    def seal_gate(self, max_norm: Optional[float]) -> torch.Tensor:
+        """After the last bucket: wait for every rank, then device fp32 [4] = norm, clip coefficient, found_inf, status."""
+
+        out = torch.empty(4, device=self.ws.device, dtype=torch.float32)
+        self._C.comm_gate_seal(self.ws.bases, self.flags_off, self.stats_off[self.parity], self.n_tensors, self.rank,
+                               self._next_epoch(), self.timeout_s, float(max_norm or 0.0), max_norm is not None, out)
+        return out
 
     def gate(self, max_norm: Optional[float]) -> torch.Tensor:
-        """Device fp32 [4]: global norm, clip coefficient, found_inf, status word."""
+        """Device fp32 [4] from this rank's statistics (no wait for peers)."""
 
         out = torch.empty(4, device=self.ws.device, dtype=torch.float32)
         self._C.gate_from_stats(self.current_stats(), self.n_tensors, float(max_norm or 0.0), max_norm is not None, out)

@@ -1,72 +1,81 @@
-"""Small running statistics (reference: koochak/utils/stats.py:10-89)."""
+"""Running statistics of scalar series for logs.
+
+(behaviour of reference koochak/utils/stats.py:10-89)
+
+* ``SmoothedMeter``: statistics of the last ``window_size`` values plus the
+  weighted mean of everything seen;
+* ``Throughput``: items per second across the last ``window_size`` updates;
+* ``EMA``: exponential moving average of one scalar (the first value seeds it).
+"""
 
 from __future__ import annotations
 
-import collections
 import statistics
 import time
-from typing import Deque, Optional
+from collections import deque
+from typing import Callable, Deque, Iterable, Optional, Tuple
 
 __all__ = ["SmoothedMeter", "Throughput", "EMA"]
 
 
+def _or_zero(fn: Callable[[Iterable[float]], float], values: Deque[float]) -> float:
+    return float(fn(values)) if values else 0.0
+
+
 class SmoothedMeter:
-    """Windowed median/mean plus a global mean of a scalar series."""
+    """Windowed median / mean / extrema and a global (count-weighted) mean."""
 
     def __init__(self, window_size: int = 100) -> None:
         self.window_size = int(window_size)
-        self.deque: Deque[float] = collections.deque(maxlen=self.window_size)
+        self.deque: Deque[float] = deque(maxlen=self.window_size)
         self.total = 0.0
         self.count = 0
 
     def update(self, value: float, n: int = 1) -> None:
-        v = float(value)
-        self.deque.append(v)
-        self.total += v * n
+        x = float(value)
+        self.deque.append(x)
         self.count += n
+        self.total += x * n
 
-    @property
-    def median(self) -> float:
-        return float(statistics.median(self.deque)) if self.deque else 0.0
-
-    @property
-    def avg(self) -> float:
-        return sum(self.deque) / len(self.deque) if self.deque else 0.0
+    median = property(lambda self: _or_zero(statistics.median, self.deque))
+    avg = property(lambda self: _or_zero(statistics.fmean, self.deque))
+    max = property(lambda self: _or_zero(max, self.deque))
+    min = property(lambda self: _or_zero(min, self.deque))
 
     @property
     def global_avg(self) -> float:
-        return self.total / max(1, self.count)
-
-    @property
-    def max(self) -> float:
-        return max(self.deque) if self.deque else 0.0
-
-    @property
-    def min(self) -> float:
-        return min(self.deque) if self.deque else 0.0
+        return self.total / self.count if self.count > 0 else 0.0
 
 
 class Throughput:
-    """Items per second over a sliding window of timestamps."""
+    """Items per second between the oldest and newest of the last ``window_size`` updates."""
 
     def __init__(self, window_size: int = 50) -> None:
-        self.times: Deque[float] = collections.deque(maxlen=window_size)
-        self.counts: Deque[int] = collections.deque(maxlen=window_size)
+        self._events: Deque[Tuple[float, int]] = deque(maxlen=window_size)
 
     def update(self, n_items: int) -> None:
-        self.times.append(time.time())
-        self.counts.append(int(n_items))
+        self._events.append((time.time(), int(n_items)))
+
+    @property
+    def times(self):
+        return [t for t, _ in self._events]
+
+    @property
+    def counts(self):
+        return [n for _, n in self._events]
 
     @property
     def it_per_s(self) -> float:
-        if len(self.times) < 2:
+        if len(self._events) < 2:
             return 0.0
-        span = self.times[-1] - self.times[0]
-        return sum(self.counts) / span if span > 0 else 0.0
+        elapsed = self._events[-1][0] - self._events[0][0]
+        if elapsed <= 0:
+            return 0.0
+        return sum(n for _, n in self._events) / elapsed
 
 
 class EMA:
-    """Exponential moving average of a scalar: v = a*v + (1-a)*x."""
+    """``value <- alpha * value + (1 - alpha) * x``; the first update sets ``value = x``."""
 
     def __init__(self, alpha: float = 0.98) -> None:
         self.alpha = float(alpha)
@@ -74,5 +83,5 @@ class EMA:
 
     def update(self, x: float) -> float:
         x = float(x)
-        self.value = x if self.value is None else self.alpha * self.value + (1.0 - self.alpha) * x
+        self.value = x if self.value is None else x + self.alpha * (self.value - x)
         return self.value

@@ -15,7 +15,8 @@ import socket
 import pytest
 import torch
 
-from koochak_b200.parallel.symm import plan_chunks, shard_bounds
+from koochak_b200.parallel.ddp import split_buckets
+from koochak_b200.parallel.symm import MODE_ALL, MODE_LOCAL, plan_bucket_chunks, plan_chunks, shard_bounds
 
 
 def _free_port() -> int:
@@ -42,6 +43,41 @@ def test_shards_cover_bucket_once(world):
             covered[start:start + length] += 1
     for s_off, s_n, _ in segs:
         assert bool((covered[s_off:s_off + s_n] == 1).all())
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+@pytest.mark.parametrize("shard_rest", [False, True])
+def test_bucket_plan_owners_and_shards(world, shard_rest):
+    """Owned tensors are reduced whole by their owner only; the rest split evenly, each element once."""
+
+    sizes = [768, 5, 2304 * 768, 3, 1024, 7, 4096]
+    layout, off = [], 0
+    for tid, n in enumerate(sizes):
+        layout.append((off, n, tid))
+        off += (n + 3) // 4 * 4
+    owner_of = {2: world - 1, 6: 0}
+    covered = torch.zeros(off, dtype=torch.int32)
+    for r in range(world):
+        for start, length, tid, mode in plan_bucket_chunks(layout, world, r, owner_of, shard_rest, max_chunk=1000):
+            o, n, _ = layout[tid]
+            assert start % 4 == 0 and 0 < length <= 1000 and o <= start and start + length <= o + n
+            if tid in owner_of:
+                assert r == owner_of[tid] and mode == MODE_LOCAL
+            else:
+                assert mode == (MODE_LOCAL if shard_rest else MODE_ALL)
+                lo, hi = shard_bounds(n, world, r)
+                assert o + lo <= start and start + length <= o + hi, "chunk outside this rank's shard"
+            covered[start:start + length] += 1
+    for o, n, _ in layout:
+        assert bool((covered[o:o + n] == 1).all())
+
+
+def test_split_buckets_cap_list():
+    """Bucket i closes at caps[min(i, len - 1)] elements; a large tensor forms a bucket of its own."""
+
+    assert split_buckets([4, 4, 4, 4, 4], [8]) == [[0, 1], [2, 3], [4]]
+    assert split_buckets([4, 4, 4, 4, 4], [4, 12]) == [[0], [1, 2, 3], [4]]
+    assert split_buckets([100, 1, 1], [8]) == [[0], [1, 2]]
 
 
 @pytest.mark.gpu
@@ -81,55 +117,67 @@ def _worker(rank: int, world: int, port: int, use_mc: bool, result_dir: str) -> 
         for bucket in sizes:
             segs.append([(n, tid + i) for i, n in enumerate(bucket)])
             tid += len(bucket)
-        red = FusedGradReducer(segs, tid, torch.device("cuda", rank), blocks=8, timeout_s=20.0,
-                               use_multicast=use_mc)
-        mode = "mc" if red.ws.mc_base else "p2p"
         ok = True
         msgs = []
-        for step in range(2):
+        modes = "mc" if use_mc else "p2p"
+        # (owner_of, shard_rest): plain all-reduce; tensor 1 owned by rank 1 and tensor 3 by rank 0 with the
+        # rest reduce-scattered.
+        for owner_of, shard_rest in (({}, False), ({1: 1, 3: 0}, True)):
+            red = FusedGradReducer(segs, tid, torch.device("cuda", rank), blocks=8, timeout_s=20.0,
+                                   use_multicast=use_mc, owner_of=owner_of, shard_rest=shard_rest)
+            modes = "mc" if red.ws.mc_base else "p2p"
+            for step in range(2):
+                red.begin_step()
+                scale = torch.tensor([4.0 if step else 1.0], device="cuda")
+                expect = {}
+                for b, layout in enumerate(red.layouts):
+                    for off, n, t in layout:
+                        g = torch.Generator(device="cpu").manual_seed(1000 * step + 10 * t)
+                        allv = torch.randn(world, n, generator=g)
+                        red.buffers[b][off:off + n].copy_(allv[rank].cuda())
+                        expect[t] = (b, off, allv.mean(0) / scale.item(), allv[rank])
+                    # The ranks launch the same bucket with different grids (rank 1: 4x wider on step 1).
+                    red.reduce(b, scale, blocks=8 * (1 + 3 * rank * step))
+                gate = red.seal_gate(1.0)
+                torch.cuda.synchronize()
+                stats = red.current_stats().cpu()
+                for t, (b, off, ref, local) in expect.items():
+                    n = ref.numel()
+                    got = red.buffers[b][off:off + n].cpu()
+                    if t in owner_of:
+                        want = ref if owner_of[t] == rank else local
+                    elif shard_rest:
+                        lo, hi = shard_bounds(n, world, rank)
+                        want = local.clone()
+                        want[lo:hi] = ref[lo:hi]
+                    else:
+                        want = ref
+                    if not torch.allclose(got, want, rtol=1e-5, atol=1e-6):
+                        ok = False
+                        msgs.append(f"{owner_of} step {step} tensor {t}: max err {(got - want).abs().max():.3g}")
+                    ss = float((ref.double() ** 2).sum())
+                    if abs(float(stats[t]) - ss) > 1e-3 * ss + 1e-4:
+                        ok = False
+                        msgs.append(f"{owner_of} step {step} tensor {t}: sumsq {float(stats[t])} vs {ss}")
+                norm = float(sum(float((e[2].double() ** 2).sum()) for e in expect.values())) ** 0.5
+                g = gate.cpu()
+                if abs(float(g[0]) - norm) > 1e-3 * norm or float(g[3]) != 0.0 or float(g[2]) != 0.0:
+                    ok = False
+                    msgs.append(f"{owner_of} step {step}: gate {g.tolist()} vs norm {norm}")
+            # A non-finite value on one rank sets found_inf everywhere.
             red.begin_step()
-            scale = torch.tensor([4.0 if step else 1.0], device="cuda")
-            expect = {}
-            for b, layout in enumerate(red.layouts):
-                for off, n, t in layout:
-                    g = torch.Generator(device="cpu").manual_seed(1000 * step + 10 * t)
-                    allv = torch.randn(world, n, generator=g)
-                    red.buffers[b][off:off + n].copy_(allv[rank].cuda())
-                    expect[t] = (b, off, allv.mean(0) / scale.item())
-                # Second step: the last bucket runs on a wider grid than the rest (as after backward).
-                red.reduce(b, scale, blocks=32 if step == 1 and b == len(red.layouts) - 1 else None)
-            torch.cuda.synchronize()
-            stats = red.current_stats().cpu()
-            for t, (b, off, ref) in expect.items():
-                got = red.buffers[b][off:off + ref.numel()].cpu()
-                if not torch.allclose(got, ref, rtol=1e-5, atol=1e-6):
-                    ok = False
-                    msgs.append(f"step {step} tensor {t}: max err {(got - ref).abs().max():.3g}")
-                ss = float((ref.double() ** 2).sum())
-                if abs(float(stats[t]) - ss) > 1e-3 * ss + 1e-4:
-                    ok = False
-                    msgs.append(f"step {step} tensor {t}: sumsq {float(stats[t])} vs {ss}")
-            if float(stats[tid]) != 0.0:
+            for b in range(len(red.buffers)):
+                red.buffers[b].zero_()
+            if rank == 0:
+                red.buffers[1][5] = float("inf")
+            for b in range(len(red.buffers)):
+                red.reduce(b, None)
+            g = red.seal_gate(None).cpu()
+            if float(g[2]) != 1.0:
                 ok = False
-                msgs.append("found_inf set on finite data")
-        gate = red.gate(1.0).cpu()
-        if float(gate[3]) != 0.0:
-            ok = False
-            msgs.append(f"status {float(gate[3])}")
-        # A non-finite value on one rank sets found_inf everywhere.
-        red.begin_step()
-        for b in range(len(red.buffers)):
-            red.buffers[b].zero_()
-        if rank == 0:
-            red.buffers[1][5] = float("inf")
-        for b in range(len(red.buffers)):
-            red.reduce(b, None)
-        torch.cuda.synchronize()
-        if float(red.current_stats()[tid]) != 1.0:
-            ok = False
-            msgs.append("found_inf not set")
+                msgs.append(f"{owner_of}: found_inf not set")
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write(("ok " if ok else "FAIL ") + mode + "\n" + "\n".join(msgs))
+            f.write(("ok " if ok else "FAIL ") + modes + "\n" + "\n".join(msgs))
     finally:
         dist.destroy_process_group()
 

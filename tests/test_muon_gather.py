@@ -68,11 +68,10 @@ def _worker(rank: int, world: int, port: int, use_mc: bool, result_dir: str) -> 
                 err = float((p.detach() - q.detach()).abs().max())
                 if not err <= 1e-6:
                     msgs.append(f"step {step} matrix {k} {tuple(p.shape)}: max err {err:.3g}")
-        slabs = getattr(opt, "_kb_param_slabs", {})
-        if len(slabs) != 1:
-            msgs.append(f"expected one symmetric slab, found {len(slabs)}")
+        slab = opt.__dict__.get("_kb_slab")
+        if slab is None:
+            msgs.append("expected a symmetric parameter slab")
         else:
-            slab = next(iter(slabs.values()))
             mode = "mc" if slab.ws.mc_base else "p2p"
             lo = slab.ws.tensor.data_ptr()
             if not all(lo <= p.data_ptr() < lo + slab.ws.nbytes for p in dist_p):
