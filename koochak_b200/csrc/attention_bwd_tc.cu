@@ -701,7 +701,7 @@ void launch_bwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
     set = true;
   }
   const long long items = (long long)((Sk + kBwBK - 1) / kBwBK) * B * H;
-  const int grid = (int)std::min<long long>(items, num_sms(q.get_device()));
+  const int grid = (int)std::min<long long>(items, compute_sms(q.get_device()));
   kern<<<grid, kBwThreads, Cfg::kSmemBytes, s>>>(tq, tk, tv, tdo, tdq, args);
   KB_LAUNCHED();
 }

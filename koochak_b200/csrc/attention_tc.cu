@@ -475,7 +475,7 @@ static void launch_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Te
     set = true;
   }
   const long long items = (long long)((Sq + 2 * kTcBM - 1) / (2 * kTcBM)) * B * H;
-  const int grid = (int)std::min<long long>(items, num_sms(q.get_device()));
+  const int grid = (int)std::min<long long>(items, compute_sms(q.get_device()));
   kern<<<grid, kTcThreads, Cfg::kSmemBytes, s>>>(tq, tk, tv, args);
   KB_LAUNCHED();
 }

@@ -30,6 +30,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "diagnostic GEMM modes for timing studies: bit 0 skips operand loads, bit 1 skips the epilogue (0: off)");
   m.def("read_and_clear_status", &kb::read_and_clear_status, "read and clear the device status word");
   m.def("num_sms", &kb::num_sms, "streaming multiprocessor count of a device");
+  m.def("set_sm_reserve", [](int64_t n) { kb::sm_reserve().store((int)std::max<int64_t>(0, n)); },
+        "SMs kept free of persistent GEMM / attention grids (for kernels overlapped beside them)");
+  m.def("sm_reserve", []() { return kb::sm_reserve().load(); }, "current SM reserve");
   m.def("launch_count", []() { return kb::launch_counter().load(); }, "kernels launched by this library so far");
   kb::register_norm_ops(m);
   kb::register_elementwise_ops(m);

@@ -1021,7 +1021,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   // block_n > 0 forces a 1-SM width, block_n < 0 forces a 2-SM width |block_n|;
   // 0 picks the configuration with the lowest estimated time (waves x tile work,
   // weighted by each configuration's measured relative efficiency).
-  const int sms_all = num_sms(dev);
+  const int sms_all = compute_sms(dev);
   int bn = 0;
   bool pair_mode = false;
   if (block_n == 128 || block_n == 256) {

@@ -10,6 +10,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <array>
 #include <atomic>
 #include <cstdint>
@@ -156,6 +157,23 @@ inline int num_sms(int device) {
   KB_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
   if (device >= 0 && device < 64) cached[device] = n;
   return n;
+}
+
+// SMs kept free of the kernels that occupy a whole SM for their lifetime
+// (persistent GEMM and attention), so that kernels running beside them --
+// the data-parallel gradient reductions overlapped with backward -- always
+// find SMs to run on instead of waiting for a persistent grid to drain.
+// Set from Python around the overlapped region; 0 (the default) uses every SM.
+inline std::atomic<int>& sm_reserve() {
+  static std::atomic<int> n{0};
+  return n;
+}
+
+// SMs available to a persistent kernel: all of them less the reserve, kept
+// even so that CTA pairs (cta_group::2) still tile it, and at least 2.
+inline int compute_sms(int device) {
+  const int n = num_sms(device) - sm_reserve().load();
+  return std::max(2, n & ~1);
 }
 
 inline void check_cuda_tensor(const at::Tensor& t, const char* name) {

@@ -103,8 +103,17 @@ class DataParallel(nn.Module):
     def __init__(self, module: nn.Module, *, bucket_cap_mb: Union[float, Sequence[float]] = 25.0,
                  broadcast_buffers: bool = True, transport: str = "auto", process_group=None,
                  find_unused_parameters: bool = False, comm_blocks: Optional[int] = None,
-                 owners: Optional[Dict[int, int]] = None, shard_rest: bool = False) -> None:
-        """``owners`` maps ``id(param)`` to the rank that alone needs its reduced gradient (fused transport only)."""
+                 owners: Optional[Dict[int, int]] = None, shard_rest: bool = False,
+                 reserve_sms: Optional[int] = None) -> None:
+        """``owners`` maps ``id(param)`` to the rank that alone needs its reduced gradient (fused transport only).
+
+        ``reserve_sms``: while reductions overlap backward, keep that many SMs
+        free of the persistent GEMM / attention grids and run the reductions on
+        them (fused transport only). ``None`` picks it from
+        ``KOOCHAK_B200_COMM_RESERVE_SMS``, else 24 when the gradients exceed
+        1 GiB (long reductions that would otherwise wait for whole persistent
+        grids to drain) and 0 below that.
+        """
 
         super().__init__()
         if not (dist.is_available() and dist.is_initialized()):
@@ -143,6 +152,8 @@ class DataParallel(nn.Module):
         self.grad_scale: Optional[torch.Tensor] = None
         self.grad_scale_fn: Optional[Callable[[], Optional[torch.Tensor]]] = None
         self._fused_ready = False
+        self._reserve = 0
+        self._reserving = False
         self.owners: Dict[int, int] = {}
         self.shard_rest = False
         if self.transport == "fused":
@@ -162,6 +173,11 @@ class DataParallel(nn.Module):
             for b, buf in zip(self.buckets, self._fused.buffers):
                 assert buf.numel() == b.numel
                 b.buffer = buf
+            if reserve_sms is None:
+                env = os.environ.get("KOOCHAK_B200_COMM_RESERVE_SMS")
+                total = 4 * sum(b.numel for b in self.buckets)
+                reserve_sms = int(env) if env is not None else (24 if total > (1 << 30) else 0)
+            self._reserve = max(0, int(reserve_sms))
         elif owners or shard_rest:
             raise ValueError("owners / shard_rest need the fused transport")
         self._next_launch = 0
@@ -212,7 +228,15 @@ class DataParallel(nn.Module):
         finally:
             self.require_sync = prev
 
+    def _set_reserve(self, on: bool) -> None:
+        if self._reserve and on != self._reserving:
+            from ..ops._ext import native
+
+            native().set_sm_reserve(self._reserve if on else 0)
+            self._reserving = on
+
     def _arm(self) -> None:
+        self._set_reserve(False)
         if self._fused is not None and self._fused_ready:
             # The previous synchronised backward was never gated: close its
             # reductions on every rank before the buckets are written again.
@@ -251,7 +275,10 @@ class DataParallel(nn.Module):
         # grids of different ranks to agree.
         while self._next_launch < len(self.buckets) and self.buckets[self._next_launch].complete:
             b = self.buckets[self._next_launch]
-            self._launch(b, wide=tail or b.index == len(self.buckets) - 1)
+            wide = tail or b.index == len(self.buckets) - 1
+            if not wide:
+                self._set_reserve(True)
+            self._launch(b, wide=wide)
             self._next_launch += 1
 
     def _launch(self, b: Bucket, wide: bool = False) -> None:
@@ -272,7 +299,8 @@ class DataParallel(nn.Module):
         if self.transport == "fused":
             assert self._fused is not None
             scale = self.grad_scale_fn() if self.grad_scale_fn is not None else self.grad_scale
-            self._fused.reduce(b.index, scale, blocks=self._tail_blocks if wide else None)
+            blocks = self._tail_blocks if wide else (self._reserve or None)
+            self._fused.reduce(b.index, scale, blocks=blocks)
         elif self.transport == "nccl":
             dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
         else:
@@ -289,6 +317,7 @@ class DataParallel(nn.Module):
                         b.view_of(i).zero_()
                 b.pending = 0
                 b.complete = True
+        self._set_reserve(False)
         self._launch_ready(tail=True)
         cur = torch.cuda.current_stream(self.device) if self._comm_stream is not None else None
         for b in self.buckets:

@@ -1,16 +1,24 @@
-"""Checkpoint publication and auto-resume (reference: koochak/storage/checkpoint.py:74-459).
+"""Checkpoint publication, validation and auto-resume.
 
-On-disk format (kept byte-compatible with the reference):
+(behaviour of reference koochak/storage/checkpoint.py:74-459)
 
-* ``step{N:09d}.pt``: ``torch.save`` bytes of the checkpoint dict, written
-  create-only through a :class:`Store`;
-* ``step{N:09d}.pt.ready.json``: written after the payload and therefore its
-  commit point: canonical JSON (sorted keys, ``,``/``:`` separators, trailing
-  newline) of exactly ``{v, artifact_id, path, size_bytes, sha256, manifest_path}``;
-* ``latest.pt``: a symlink, only for hard-link (``publish="link"``) stores.
+On-disk format, shared with the reference so either framework resumes the
+other's runs:
 
-Resume trusts a numbered checkpoint only when its manifest, size and SHA-256
-agree with the payload bytes it then loads.
+* ``step{N:09d}.pt`` -- ``torch.save`` bytes of the checkpoint dict, put
+  create-only through a ``Store``;
+* ``step{N:09d}.pt.ready.json`` -- the commit point, written after the
+  payload: canonical JSON (sorted keys, ``,``/``:`` separators, trailing
+  newline) of exactly ``{v, artifact_id, path, size_bytes, sha256,
+  manifest_path}`` (``_Manifest``);
+* ``latest.pt`` -- a symlink to the newest payload, only on hard-link
+  (``publish="link"``) local stores.
+
+A numbered checkpoint is trusted for resume only when its manifest names it,
+its size and SHA-256 match the bytes, those bytes load as a dict, and its
+``step`` / ``next_step`` cursor agrees with the file name
+(``_verify``). Pruning removes the manifest before the payload, so a
+half-pruned checkpoint is never mistaken for a valid one.
 """
 
 from __future__ import annotations
@@ -39,12 +47,11 @@ __all__ = ["BackgroundPublisher", "add_module_prefix", "best", "checkpoint_path"
            "strip_module_prefix", "PUBLICATION_SUFFIX", "AutoResumeSelection"]
 
 PUBLICATION_SUFFIX = ".ready.json"
-_NUMBERED = re.compile(r"step(\d+)\.pt")
-_STEP_RE = re.compile(r"step(\d+)\.pt$")
-_MANIFEST_KEYS = frozenset({"v", "artifact_id", "path", "size_bytes", "sha256", "manifest_path"})
-_ABSENT = (FileNotFoundError, IsADirectoryError, NotADirectoryError)
-_CORRUPT = (EOFError, RuntimeError, ValueError, TypeError, AttributeError, IndexError, KeyError, ImportError,
-            MemoryError, OverflowError, pickle.PickleError)
+_STEP_NAME = re.compile(r"step(\d+)\.pt")
+_STEP_PATTERN = r"step(\d+)\.pt$"
+# Errors that mean "this candidate is not usable", not "resume failed".
+_UNUSABLE = (FileNotFoundError, IsADirectoryError, NotADirectoryError, EOFError, RuntimeError, ValueError, TypeError,
+             AttributeError, IndexError, KeyError, ImportError, MemoryError, OverflowError, pickle.PickleError)
 
 Location = Union[str, "os.PathLike[str]", Store]
 
@@ -56,220 +63,228 @@ class AutoResumeSelection:
     next_step: int
 
 
+@dataclass(frozen=True)
+class _Manifest:
+    """The ``.ready.json`` record of one published checkpoint payload."""
+
+    path: str
+    size_bytes: int
+    sha256: str
+
+    FIELDS = frozenset({"v", "artifact_id", "path", "size_bytes", "sha256", "manifest_path"})
+
+    @classmethod
+    def for_payload(cls, path: str, size: int, sha256: str) -> "_Manifest":
+        return cls(os.path.abspath(path), int(size), sha256)
+
+    def record(self) -> Dict[str, Any]:
+        return {"v": 1, "artifact_id": f"checkpoint/{os.path.basename(self.path)}", "path": self.path,
+                "size_bytes": self.size_bytes, "sha256": self.sha256, "manifest_path": publication_path(self.path)}
+
+    def encode(self) -> bytes:
+        text = json.dumps(self.record(), sort_keys=True, separators=(",", ":"), ensure_ascii=False)
+        return (text + "\n").encode("utf-8")
+
+    @classmethod
+    def well_formed(cls, record: Any) -> bool:
+        return isinstance(record, dict) and set(record) == cls.FIELDS and record.get("v") == 1
+
+
 def serialize(ckpt: Dict[str, Any]) -> bytes:
-    buf = io.BytesIO()
-    torch.save(ckpt, buf)
-    return buf.getvalue()
+    out = io.BytesIO()
+    torch.save(ckpt, out)
+    return out.getvalue()
 
 
 def checkpoint_store(location: Location) -> Store:
-    """Directory -> owner-only LocalStore; ``scheme://`` -> configured store; a Store as-is."""
+    """A store for checkpoints: a directory becomes an owner-only ``LocalStore``, a URI its configured store."""
 
     if isinstance(location, Store):
         return location
     text = os.fspath(location)
-    if "://" in text:
-        return open_store(text)
-    return LocalStore(canonical_dir(text), file_mode=0o600)
+    return open_store(text) if "://" in text else LocalStore(canonical_dir(text), file_mode=0o600)
 
 
 def checkpoint_path(store: Store, name: str) -> str:
-    path = store.local_path(name)
-    if path is None:
+    found = store.local_path(name)
+    if found is None:
         raise TypeError(f"{store!r} exposes no filesystem paths; checkpoint stores must be filesystem-backed")
-    return path
+    return found
 
 
 def publication_path(path: str) -> str:
     return os.path.abspath(path) + PUBLICATION_SUFFIX
 
 
-def _manifest(path: str, size: int, sha256: str) -> dict[str, Any]:
-    absolute = os.path.abspath(path)
-    return {"v": 1, "artifact_id": f"checkpoint/{os.path.basename(absolute)}", "path": absolute,
-            "size_bytes": size, "sha256": sha256, "manifest_path": publication_path(absolute)}
+def publication(path: str) -> dict:
+    """The manifest of the checkpoint at ``path`` (ValueError when malformed)."""
 
-
-def _encode_manifest(record: dict[str, Any]) -> bytes:
-    return (json.dumps(record, sort_keys=True, separators=(",", ":"), ensure_ascii=False) + "\n").encode("utf-8")
-
-
-def publication(path: str) -> dict[str, Any]:
-    mpath = publication_path(path)
-    with open(mpath, encoding="utf-8") as fh:
+    where = publication_path(path)
+    with open(where, encoding="utf-8") as fh:
         record = json.load(fh)
-    if not isinstance(record, dict) or set(record) != _MANIFEST_KEYS or record.get("v") != 1:
-        raise ValueError(f"invalid checkpoint publication manifest: {mpath}")
+    if not _Manifest.well_formed(record):
+        raise ValueError(f"invalid checkpoint publication manifest: {where}")
     return record
 
 
-def _copy_as_latest(step_path: str, latest_path: str) -> Optional[str]:
-    try:
-        shutil.copy2(step_path, latest_path)
-        return latest_path
-    except OSError:
-        return None
+def _point_latest_at(step_path: str) -> Optional[str]:
+    """``latest.pt`` -> the new payload (a symlink; a copy where links cannot be made)."""
 
+    link = os.path.join(os.path.dirname(os.path.abspath(step_path)), "latest.pt")
 
-def _refresh_latest_link(step_path: str) -> Optional[str]:
-    directory = os.path.dirname(os.path.abspath(step_path))
-    latest_path = os.path.join(directory, "latest.pt")
-    if os.path.islink(latest_path) or os.path.exists(latest_path):
+    def copy() -> Optional[str]:
         try:
-            os.remove(latest_path)
+            shutil.copy2(step_path, link)
+            return link
+        except OSError:
+            return None
+
+    if os.path.lexists(link):
+        try:
+            os.remove(link)
         except FileNotFoundError:
             pass
         except OSError:
-            return _copy_as_latest(step_path, latest_path)
+            return copy()
     try:
-        os.symlink(os.path.basename(step_path), latest_path)
-        return latest_path
+        os.symlink(os.path.basename(step_path), link)
+        return link
     except (OSError, NotImplementedError):
-        return _copy_as_latest(step_path, latest_path)
+        return copy()
 
 
-def _numbered(store: Store) -> List[Tuple[int, str]]:
-    out = []
-    for key in store.list("step"):
-        m = _NUMBERED.fullmatch(key)
-        if m:
-            out.append((int(m.group(1)), key))
-    return sorted(out)
+def _steps(store: Store) -> List[Tuple[int, str]]:
+    """(step, key) of every numbered payload in the store, oldest first."""
+
+    found = ((_STEP_NAME.fullmatch(k), k) for k in store.list("step"))
+    return sorted((int(m.group(1)), k) for m, k in found if m is not None)
 
 
-def _validated(store: Store, name: str) -> Optional[AutoResumeSelection]:
-    """The checkpoint behind ``name`` if its manifest, size, digest and cursor all agree."""
+def _verify(store: Store, name: str) -> Optional[AutoResumeSelection]:
+    """The checkpoint behind ``name`` when manifest, bytes and cursor all agree; otherwise None."""
 
-    m = _NUMBERED.fullmatch(name)
-    if m is None:
+    numbered = _STEP_NAME.fullmatch(name)
+    if numbered is None:
         return None
-    absolute = os.path.abspath(checkpoint_path(store, name))
-    mpath = publication_path(absolute)
+    payload_path = os.path.abspath(checkpoint_path(store, name))
+    manifest_path = publication_path(payload_path)
     try:
-        if any(not os.path.isfile(p) or os.path.islink(p) for p in (absolute, mpath)):
+        if not all(os.path.isfile(p) and not os.path.islink(p) for p in (payload_path, manifest_path)):
             return None
         record = json.loads(store.get(name + PUBLICATION_SUFFIX).decode("utf-8"))
-        if not isinstance(record, dict) or set(record) != _MANIFEST_KEYS or record["v"] != 1:
-            return None
-        if record["artifact_id"] != f"checkpoint/{name}" or record["path"] != absolute \
-                or record["manifest_path"] != mpath:
+        expected = {"artifact_id": f"checkpoint/{name}", "path": payload_path, "manifest_path": manifest_path}
+        if not _Manifest.well_formed(record) or any(record[k] != v for k, v in expected.items()):
             return None
         info = store.stat(name)
         if info is None or type(record["size_bytes"]) is not int or record["size_bytes"] != info.size:
             return None
         payload = store.get(name)
-        if len(payload) != info.size or record["sha256"] != hashlib.sha256(payload).hexdigest():
+        if len(payload) != info.size or hashlib.sha256(payload).hexdigest() != record["sha256"]:
             return None
         ckpt = torch.load(io.BytesIO(payload), weights_only=False, map_location="cpu")
         if not isinstance(ckpt, dict):
             return None
         step, nxt = ckpt.get("step"), ckpt.get("next_step")
-        if type(step) is not int or type(nxt) is not int or nxt < 0 or step != int(m.group(1)):
-            return None
-        if nxt not in (step, step + 1):  # periodic (step+1) or terminal (step)
-            return None
-    except _ABSENT:
+        cursor_ok = (type(step) is int and type(nxt) is int and step == int(numbered.group(1))
+                     and nxt >= 0 and nxt in (step, step + 1))  # periodic (step + 1) or terminal (step)
+        return AutoResumeSelection(payload_path, ckpt, nxt) if cursor_ok else None
+    except _UNUSABLE:
         return None
-    except _CORRUPT:
-        return None
-    return AutoResumeSelection(absolute, ckpt, nxt)
 
 
-def _highest_valid(store: Store) -> Optional[AutoResumeSelection]:
-    for _step, key in reversed(_numbered(store)):
-        sel = _validated(store, key)
-        if sel is not None:
-            return sel
+def _newest_valid(store: Store) -> Optional[AutoResumeSelection]:
+    for _, key in reversed(_steps(store)):
+        chosen = _verify(store, key)
+        if chosen is not None:
+            return chosen
     return None
 
 
 def highest_valid_published(location: Location) -> Optional[str]:
-    sel = _highest_valid(checkpoint_store(location))
-    return None if sel is None else sel.path
+    chosen = _newest_valid(checkpoint_store(location))
+    return chosen.path if chosen else None
 
 
 latest_valid = highest_valid_published
 
 
-def resolve_auto_resume(location: Location) -> Optional[tuple[str, Dict[str, Any]]]:
+def resolve_auto_resume(location: Location) -> Optional[tuple]:
     """``(path, checkpoint)`` of the newest valid published checkpoint, or None."""
 
-    sel = _highest_valid(checkpoint_store(location))
-    return None if sel is None else (sel.path, sel.checkpoint)
+    chosen = _newest_valid(checkpoint_store(location))
+    return (chosen.path, chosen.checkpoint) if chosen else None
 
 
 def prune(store: Store, keep_last_k: int) -> None:
-    """Drop all but the newest ``keep_last_k`` numbered checkpoints, manifest first."""
+    """Keep the newest ``keep_last_k`` numbered checkpoints (manifest removed before its payload)."""
 
-    if keep_last_k <= 0:
-        return
-    for _step, key in _numbered(store)[:-keep_last_k]:
-        store.delete(key + PUBLICATION_SUFFIX)
-        store.delete(key)
+    if keep_last_k > 0:
+        for _, key in _steps(store)[:-keep_last_k]:
+            store.delete(key + PUBLICATION_SUFFIX)
+            store.delete(key)
 
 
 def publish(store: Store, name: str, data: bytes, *, keep_last_k: int = 3) -> str:
-    """Payload create-only, then manifest; replaces a same-named checkpoint (uncommitting it first)."""
+    """Put the payload create-only, then its manifest; a same-named checkpoint is uncommitted and replaced."""
 
     path = checkpoint_path(store, name)
-    mname = name + PUBLICATION_SUFFIX
-    if store.stat(name) is not None or store.stat(mname) is not None:
-        store.delete(mname)
+    manifest_key = name + PUBLICATION_SUFFIX
+    if store.stat(name) is not None or store.stat(manifest_key) is not None:
+        store.delete(manifest_key)  # uncommit first
         store.delete(name)
     info = store.put(name, data)
-    digest = info.sha256 if info.sha256 is not None else hashlib.sha256(data).hexdigest()
-    store.put(mname, _encode_manifest(_manifest(path, info.size, digest)))
+    manifest = _Manifest.for_payload(path, info.size, info.sha256 or hashlib.sha256(data).hexdigest())
+    store.put(manifest_key, manifest.encode())
     if isinstance(store, LocalStore) and store.publish == "link":
-        _refresh_latest_link(path)
+        _point_latest_at(path)
     prune(store, keep_last_k)
     return path
 
 
 def save(ckpt: Dict[str, Any], path: str, keep_last_k: int = 3) -> str:
-    directory = os.path.dirname(os.path.abspath(path)) or "."
-    publish(checkpoint_store(directory), os.path.basename(path), serialize(ckpt), keep_last_k=keep_last_k)
+    where = os.path.dirname(os.path.abspath(path)) or "."
+    publish(checkpoint_store(where), os.path.basename(path), serialize(ckpt), keep_last_k=keep_last_k)
     return path
 
 
 class BackgroundPublisher:
-    """One publication at a time on a background thread.
+    """Publishes one checkpoint at a time on a worker thread.
 
-    ``submit`` returns the path at once; ``poll``/``wait`` return ``(path, token)``
-    once committed and re-raise a failed publication on the caller's thread.
+    ``submit`` returns the future path at once; ``poll`` (non-blocking) and
+    ``wait`` hand back ``(path, token)`` once the manifest is written, and
+    re-raise a failed publication on the caller's thread.
     """
 
     def __init__(self, store: Store, *, keep_last_k: int) -> None:
         self.store = store
         self.keep_last_k = keep_last_k
-        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="koochak-checkpoint")
-        self._pending: Optional[Tuple[Future, Any]] = None
+        self._worker = ThreadPoolExecutor(max_workers=1, thread_name_prefix="koochak-checkpoint")
+        self._inflight: Optional[Tuple[Future, Any]] = None
 
     @property
     def pending(self) -> bool:
-        return self._pending is not None
+        return self._inflight is not None
 
     def submit(self, name: str, data: bytes, token: Any = None) -> str:
-        if self._pending is not None:
+        if self._inflight is not None:
             raise RuntimeError("a checkpoint publication is already pending; wait() for it first")
-        path = checkpoint_path(self.store, name)
-        self._pending = (self._pool.submit(publish, self.store, name, data, keep_last_k=self.keep_last_k), token)
-        return path
+        future = self._worker.submit(publish, self.store, name, data, keep_last_k=self.keep_last_k)
+        self._inflight = (future, token)
+        return checkpoint_path(self.store, name)
 
     def poll(self) -> Optional[Tuple[str, Any]]:
-        if self._pending is None or not self._pending[0].done():
-            return None
-        return self.wait()
+        return self.wait() if self._inflight is not None and self._inflight[0].done() else None
 
     def wait(self) -> Optional[Tuple[str, Any]]:
-        if self._pending is None:
+        if self._inflight is None:
             return None
-        fut, token = self._pending
-        self._pending = None
-        return fut.result(), token
+        future, token = self._inflight
+        self._inflight = None
+        return future.result(), token
 
     def close(self) -> None:
-        self._pool.shutdown(wait=True)
-        self._pending = None
+        self._worker.shutdown(wait=True)
+        self._inflight = None
 
 
 def load(path: str) -> Dict[str, Any]:
@@ -278,7 +293,7 @@ def load(path: str) -> Dict[str, Any]:
     return torch.load(path, weights_only=False, map_location="cpu")
 
 
-def _directory(location: Location) -> str:
+def _directory_of(location: Location) -> str:
     if isinstance(location, LocalStore):
         return location.root
     text = os.fspath(location)
@@ -291,37 +306,37 @@ def _directory(location: Location) -> str:
 
 
 def latest(location: Location) -> Optional[str]:
-    return fs_utils.latest(_directory(location), pattern=_STEP_RE.pattern)
+    return fs_utils.latest(_directory_of(location), pattern=_STEP_PATTERN)
 
 
 def best(location: Location, key: str = "val_loss") -> Optional[str]:
-    return fs_utils.best(_directory(location), key=key, pattern=_STEP_RE.pattern)
+    return fs_utils.best(_directory_of(location), key=key, pattern=_STEP_PATTERN)
 
 
-def _all_prefixed(sd: Dict[str, Any]) -> bool:
-    keys = list(sd.keys())
-    return bool(keys) and all(isinstance(k, str) and k.startswith("module.") for k in keys)
+_PREFIX = "module."
+
+
+def _prefixed(key: Any) -> bool:
+    return isinstance(key, str) and key.startswith(_PREFIX)
 
 
 def strip_module_prefix(sd: Dict[str, Any]) -> "OrderedDict[str, Any]":
-    return OrderedDict((k[7:] if isinstance(k, str) and k.startswith("module.") else k, v) for k, v in sd.items())
+    return OrderedDict((k[len(_PREFIX):] if _prefixed(k) else k, v) for k, v in sd.items())
 
 
 def add_module_prefix(sd: Dict[str, Any]) -> "OrderedDict[str, Any]":
-    return OrderedDict((f"module.{k}" if isinstance(k, str) and not k.startswith("module.") else k, v)
-                       for k, v in sd.items())
+    return OrderedDict((k if _prefixed(k) or not isinstance(k, str) else _PREFIX + k, v) for k, v in sd.items())
 
 
 def match_state_dict_to_model(model: Any, sd: Dict[str, Any]) -> "OrderedDict[str, Any]":
-    """Add or strip the DDP ``module.`` prefix so ``sd`` matches ``model``'s keys."""
+    """Add or strip the data-parallel ``module.`` prefix so ``sd``'s keys match ``model``'s."""
 
-    fn = getattr(model, "state_dict", None)
-    if fn is None:
+    if getattr(model, "state_dict", None) is None:
         return OrderedDict(sd)
-    wants = any(isinstance(k, str) and k.startswith("module.") for k in fn().keys())
-    has = _all_prefixed(sd)
-    if wants and not has:
+    model_wrapped = any(_prefixed(k) for k in model.state_dict().keys())
+    sd_wrapped = bool(sd) and all(_prefixed(k) for k in sd.keys())
+    if model_wrapped and not sd_wrapped:
         return add_module_prefix(sd)
-    if has and not wants:
+    if sd_wrapped and not model_wrapped:
         return strip_module_prefix(sd)
     return OrderedDict(sd)
