@@ -1,6 +1,6 @@
 """Collections: many files described by one manifest written last.
 
-(reference: koochak/storage/collection.py:205-411)
+(behaviour of reference koochak/storage/collection.py:205-411)
 
 Under one store prefix::
 
@@ -171,39 +171,51 @@ class PackRange:
     members: Tuple[FileEntry, ...]
 
 
+def _coalesce(members: List[FileEntry], merge_gap: int, max_range: int) -> Iterator[List[FileEntry]]:
+    """Runs of offset-sorted members that one read can cover (small gaps, bounded length)."""
+
+    run: List[FileEntry] = []
+    for f in members:
+        if run:
+            first, last = run[0], run[-1]
+            gap = f.offset - (last.offset + last.size)
+            span = f.offset + f.size - first.offset
+            if gap > merge_gap or span > max_range:
+                yield run
+                run = []
+        run.append(f)
+    if run:
+        yield run
+
+
 def pack_ranges(files: Iterable[FileEntry], packs: Sequence[PackEntry], *, merge_gap: int,
                 max_range: int) -> List[PackRange]:
-    """Cover packed files with few reads: neighbours share a read when the gap is small enough."""
+    """Cover the packed files with few reads: neighbours share a read when the gap is small enough."""
 
-    per_pack: Dict[int, List[FileEntry]] = {}
+    by_pack: Dict[int, List[FileEntry]] = {}
     for f in files:
         if f.pack is None:
             raise ValueError(f"{f.path} is a standalone object, not a pack member")
-        per_pack.setdefault(f.pack, []).append(f)
-    out: List[PackRange] = []
-    for idx in sorted(per_pack):
-        cur: List[FileEntry] = []
-        start = end = 0
-        for f in sorted(per_pack[idx], key=lambda e: e.offset):
-            f_end = f.offset + f.size
-            if cur and (f.offset - end > merge_gap or f_end - start > max_range):
-                out.append(PackRange(packs[idx], start, end - start, tuple(cur)))
-                cur = []
-            if not cur:
-                start = f.offset
-            cur.append(f)
-            end = f_end
-        if cur:
-            out.append(PackRange(packs[idx], start, end - start, tuple(cur)))
-    return out
+        by_pack.setdefault(f.pack, []).append(f)
+    ranges: List[PackRange] = []
+    for index in sorted(by_pack):
+        ordered = sorted(by_pack[index], key=lambda e: e.offset)
+        for run in _coalesce(ordered, merge_gap, max_range):
+            lo, hi = run[0].offset, run[-1].offset + run[-1].size
+            ranges.append(PackRange(packs[index], lo, hi - lo, tuple(run)))
+    return ranges
 
 
-def _split(part: PackRange, data: bytes, verify: bool) -> Dict[str, bytes]:
+def _members_of(part: PackRange, data: bytes, verify: bool) -> Dict[str, bytes]:
+    """Cut one range read into its member files (checking each digest when asked)."""
+
     if len(data) != part.length:
         raise ValueError(f"{part.pack.key} is shorter than its manifest says")
+    view = memoryview(data)
     out: Dict[str, bytes] = {}
     for f in part.members:
-        blob = data[f.offset - part.start: f.offset - part.start + f.size]
+        at = f.offset - part.start
+        blob = bytes(view[at:at + f.size])
         if verify and hashlib.sha256(blob).hexdigest() != f.sha256:
             raise ValueError(f"{f.path} in {part.pack.key} does not match its SHA256")
         out[f.path] = blob
@@ -211,27 +223,32 @@ def _split(part: PackRange, data: bytes, verify: bool) -> Dict[str, bytes]:
 
 
 def read_pack_range(store: Store, part: PackRange, *, verify: bool = True) -> Dict[str, bytes]:
-    return _split(part, store.get(part.pack.key, part.start, part.length), verify)
+    return _members_of(part, store.get(part.pack.key, part.start, part.length), verify)
 
 
 def read_pack_ranges(store: Store, parts: Sequence[PackRange], *, verify: bool = True) -> Dict[str, bytes]:
-    """Several ranges of one pack through one open handle (opens can cost more than reads)."""
+    """Several ranges of one pack through one open handle (on some mounts an open costs more than a read).
+
+    If the mount drops the handle with a transient error, the ranges not yet
+    read are fetched with ranged gets instead.
+    """
 
     if len({p.pack.key for p in parts}) != 1:
         raise ValueError("read_pack_ranges reads ranges of exactly one pack")
-    out: Dict[str, bytes] = {}
+    got: Dict[str, bytes] = {}
+    todo = sorted(parts, key=lambda r: r.start)
     try:
-        with store.open(parts[0].pack.key) as fh:
-            for p in sorted(parts, key=lambda r: r.start):
-                fh.seek(p.start)
-                out.update(_split(p, fh.read(p.length), verify))
+        with store.open(todo[0].pack.key) as fh:
+            while todo:
+                fh.seek(todo[0].start)
+                got.update(_members_of(todo[0], fh.read(todo[0].length), verify))
+                todo.pop(0)
     except OSError as err:
         if not transient_read_error(err):
             raise
-        for p in parts:  # the mount dropped the handle: finish with ranged gets
-            if any(m.path not in out for m in p.members):
-                out.update(read_pack_range(store, p, verify=verify))
-    return out
+        for p in todo:
+            got.update(read_pack_range(store, p, verify=verify))
+    return got
 
 
 def _canonical(value: Any) -> bytes:
@@ -274,50 +291,74 @@ def _totals(packs: Sequence[PackEntry], files: Sequence[FileEntry]) -> Dict[str,
             "objects": sum(1 for f in files if f.object is not None)}
 
 
-def write_collection(store: Store, *, layout: str, packs: Sequence[PackEntry], files: Iterable[FileEntry],
-                     metadata: Optional[Mapping[str, Any]] = None) -> Collection:
-    """Write the file table, then the manifest (the commit point)."""
+_MANIFEST_FIELDS = frozenset({"kind", "v", "layout", "files_table", "packs", "totals", "metadata"})
 
-    ordered = tuple(sorted(files, key=lambda f: f.path))
-    packs = tuple(packs)
-    _check(layout, packs, ordered)
-    table = gzip.compress(b"".join(_canonical(f.to_row()) for f in ordered), compresslevel=6, mtime=0)
-    put_once(store, FILES_KEY, table)
-    manifest = _canonical({
-        "kind": COLLECTION_KIND, "v": VERSION, "layout": layout,
+
+def _table_bytes(files: Sequence[FileEntry]) -> bytes:
+    """The gzip file table: canonical JSON rows sorted by path, gzip mtime 0 (deterministic)."""
+
+    return gzip.compress(b"".join(_canonical(f.to_row()) for f in files), compresslevel=6, mtime=0)
+
+
+def _manifest_doc(layout: str, table: bytes, packs: Sequence[PackEntry], files: Sequence[FileEntry],
+                  metadata: Mapping[str, Any]) -> Dict[str, Any]:
+    return {
+        "kind": COLLECTION_KIND,
+        "v": VERSION,
+        "layout": layout,
         "files_table": {"key": FILES_KEY, "size": len(table), "sha256": hashlib.sha256(table).hexdigest()},
         "packs": [{"key": p.key, "size": p.size, "sha256": p.sha256, "files": p.files} for p in packs],
-        "totals": _totals(packs, ordered), "metadata": dict(metadata or {}),
-    })
+        "totals": _totals(packs, files),
+        "metadata": dict(metadata),
+    }
+
+
+def write_collection(store: Store, *, layout: str, packs: Sequence[PackEntry], files: Iterable[FileEntry],
+                     metadata: Optional[Mapping[str, Any]] = None) -> Collection:
+    """Write the file table, then the manifest (the commit point); re-writing identical content is accepted."""
+
+    rows = tuple(sorted(files, key=lambda f: f.path))
+    pack_list = tuple(packs)
+    extra = dict(metadata or {})
+    _check(layout, pack_list, rows)
+    table = _table_bytes(rows)
+    put_once(store, FILES_KEY, table)
+    manifest = _canonical(_manifest_doc(layout, table, pack_list, rows, extra))
     put_once(store, MANIFEST_KEY, manifest)
-    return Collection(layout, packs, ordered, MappingProxyType(dict(metadata or {})),
-                      hashlib.sha256(manifest).hexdigest())
+    return Collection(layout, pack_list, rows, MappingProxyType(extra), hashlib.sha256(manifest).hexdigest())
+
+
+def _parse_manifest(raw: bytes) -> Dict[str, Any]:
+    try:
+        doc = json.loads(raw)
+    except (UnicodeDecodeError, json.JSONDecodeError) as exc:
+        raise ValueError("collection manifest is not valid JSON") from exc
+    if not isinstance(doc, dict) or set(doc) != _MANIFEST_FIELDS:
+        raise ValueError(f"collection manifest must contain exactly {sorted(_MANIFEST_FIELDS)}")
+    if (doc["kind"], doc["v"]) != (COLLECTION_KIND, VERSION):
+        raise ValueError("unsupported collection kind or version")
+    ref = doc["files_table"]
+    if not isinstance(ref, dict) or set(ref) != {"key", "size", "sha256"}:
+        raise ValueError("invalid files_table reference")
+    if not isinstance(doc["packs"], list) or not all(isinstance(p, dict) for p in doc["packs"]):
+        raise ValueError("manifest packs must be a list of objects")
+    if not isinstance(doc["metadata"], dict):
+        raise ValueError("manifest metadata must be an object")
+    return doc
 
 
 def load_collection(store: Store) -> Collection:
+    """Read and cross-check a collection: manifest, file table digest, pack bounds, totals."""
+
     raw = store.get(MANIFEST_KEY)
-    try:
-        m = json.loads(raw)
-    except (UnicodeDecodeError, json.JSONDecodeError) as exc:
-        raise ValueError("collection manifest is not valid JSON") from exc
-    keys = {"kind", "v", "layout", "files_table", "packs", "totals", "metadata"}
-    if not isinstance(m, dict) or set(m) != keys:
-        raise ValueError(f"collection manifest must contain exactly {sorted(keys)}")
-    if m["kind"] != COLLECTION_KIND or m["v"] != VERSION:
-        raise ValueError("unsupported collection kind or version")
-    ref = m["files_table"]
-    if not isinstance(ref, dict) or set(ref) != {"key", "size", "sha256"}:
-        raise ValueError("invalid files_table reference")
+    doc = _parse_manifest(raw)
+    ref = doc["files_table"]
     table = store.get(validate_key(ref["key"], "files table key"))
-    if len(table) != ref["size"] or hashlib.sha256(table).hexdigest() != ref["sha256"]:
+    if (len(table), hashlib.sha256(table).hexdigest()) != (ref["size"], ref["sha256"]):
         raise ValueError("file table does not match the manifest's size and SHA256")
     files = tuple(FileEntry.from_row(json.loads(line)) for line in gzip.decompress(table).splitlines())
-    if not isinstance(m["packs"], list) or not all(isinstance(p, dict) for p in m["packs"]):
-        raise ValueError("manifest packs must be a list of objects")
-    packs = tuple(PackEntry(**p) for p in m["packs"])
-    _check(m["layout"], packs, files)
-    if m["totals"] != _totals(packs, files):
+    packs = tuple(PackEntry(**p) for p in doc["packs"])
+    _check(doc["layout"], packs, files)
+    if doc["totals"] != _totals(packs, files):
         raise ValueError("manifest totals do not match the file table")
-    if not isinstance(m["metadata"], dict):
-        raise ValueError("manifest metadata must be an object")
-    return Collection(m["layout"], packs, files, MappingProxyType(m["metadata"]), hashlib.sha256(raw).hexdigest())
+    return Collection(doc["layout"], packs, files, MappingProxyType(doc["metadata"]), hashlib.sha256(raw).hexdigest())

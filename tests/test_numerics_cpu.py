@@ -92,8 +92,15 @@ def test_ema_closed_forms_and_state():
     assert {"decay", "profile", "gamma", "num_updates", "step_counter", "last_update_step_counter", "update_every",
             "compensate_update_every", "shadow", "dtype"} == set(st)
     power = EMA(model, decay=0.9, profile="power", gamma=6.94, offload_to_cpu=False)
-    power.update(model)
-    assert power._current_decay() == 0.0  # first update copies the parameter
+    with torch.no_grad():
+        model.weight.fill_(3.0)
+    power.update(model)  # the power profile's first update (t = 1) has decay 0: it copies the parameter
+    assert torch.equal(power.shadow["weight"], torch.full((1, 3), 3.0))
+    with torch.no_grad():
+        model.weight.fill_(5.0)
+    power.update(model)  # t = 2: decay (1/2) ** (gamma + 1)
+    d = 0.5 ** 7.94
+    assert torch.allclose(power.shadow["weight"], torch.full((1, 3), 3.0 * d + 5.0 * (1 - d)))
     assert abs(srel_from_gamma(gamma_from_srel(0.1)) - 0.1) < 1e-6
     a, b = ls_coeffs_for_power_profile(100, 5.0, 10.0, 5.0)
     assert abs(a - 1.0) < 1e-6 and abs(b) < 1e-6
