@@ -1,6 +1,6 @@
 """Write-once dataset shards, their index, and the dealing of shards to workers.
 
-(reference: koochak/data/shards.py:134-569)
+(behaviour of reference koochak/data/shards.py:134-569)
 
 A dataset is a set of large immutable shard objects plus one small index
 written last. The index (``kind: koochak.shard_index``, ``v: 1``) lists every
@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import hashlib
 import io
+import itertools
 import json
 import posixpath
 import re
@@ -262,6 +263,26 @@ TAR = ShardFormat(".tar", encode_tar_sample, decode_tar_samples, trailer=b"\0" *
 
 # ----------------------------------------------------------------------------- writer
 
+class _OpenShard:
+    """The records of the shard being filled: encoded pieces, their running size and digest."""
+
+    def __init__(self) -> None:
+        self.pieces: List[bytes] = []
+        self.size = 0
+        self.count = 0
+        self.digest = hashlib.sha256()
+
+    def append(self, encoded: bytes) -> None:
+        self.pieces.append(encoded)
+        self.digest.update(encoded)
+        self.size += len(encoded)
+        self.count += 1
+
+    def seal(self, key: str, trailer: bytes) -> Tuple[Shard, List[bytes]]:
+        self.digest.update(trailer)
+        return Shard(key, self.size + len(trailer), self.digest.hexdigest(), self.count), self.pieces + [trailer]
+
+
 class ShardWriter:
     """Pack records into ``{prefix}/{name}-{n:06d}{suffix}`` shards of about ``target_bytes``; index last.
 
@@ -283,58 +304,51 @@ class ShardWriter:
         self.index_name = _leaf(index_name, "index_name")
         self.metadata = dict(metadata or {})
         self.index: Optional[ShardIndex] = None
-        self._done: List[Shard] = []
-        self._reset()
+        self._written: List[Shard] = []
+        self._current = _OpenShard()
         self._state = "open"
-
-    def _reset(self) -> None:
-        self._parts: List[bytes] = []
-        self._bytes = 0
-        self._count = 0
-        self._hash = hashlib.sha256()
 
     def _key(self, leaf: str) -> str:
         return f"{self.prefix}/{leaf}" if self.prefix else leaf
 
-    def add(self, record: Any) -> None:
+    def _require_open(self) -> None:
         if self._state != "open":
             raise RuntimeError(f"ShardWriter is {self._state}")
-        enc = self.format.encode(record)
-        if not isinstance(enc, bytes):
-            raise TypeError(f"format.encode must return bytes, got {type(enc).__name__}")
-        self._parts.append(enc)
-        self._hash.update(enc)
-        self._bytes += len(enc)
-        self._count += 1
-        if self._bytes + len(self.format.trailer) >= self.target_bytes:
-            self._flush()
 
-    def _flush(self) -> None:
-        if not self._count:
+    def add(self, record: Any) -> None:
+        self._require_open()
+        encoded = self.format.encode(record)
+        if not isinstance(encoded, bytes):
+            raise TypeError(f"format.encode must return bytes, got {type(encoded).__name__}")
+        self._current.append(encoded)
+        if self._current.size + len(self.format.trailer) >= self.target_bytes:
+            self._emit()
+
+    def _emit(self) -> None:
+        if self._current.count == 0:
             return
-        self._hash.update(self.format.trailer)
-        shard = Shard(self._key(f"{self.name}-{len(self._done):06d}{self.format.suffix}"),
-                      self._bytes + len(self.format.trailer), self._hash.hexdigest(), self._count)
+        name = self._key(f"{self.name}-{len(self._written):06d}{self.format.suffix}")
+        shard, body = self._current.seal(name, self.format.trailer)
         try:
-            self.store.put(shard.key, [*self._parts, self.format.trailer])
+            self.store.put(shard.key, body)
         except FileExistsError as exc:
+            # A rerun of an interrupted build: the same bytes are fine, anything else is not.
             if _digest_object(self.store, shard.key) != (shard.size_bytes, shard.sha256):
                 raise FileExistsError(f"{shard.key} already exists with different content; delete the "
                                       "uncommitted shards or choose a new prefix") from exc
-        self._done.append(shard)
-        self._reset()
+        self._written.append(shard)
+        self._current = _OpenShard()
 
     def close(self) -> ShardIndex:
         if self._state == "closed":
             assert self.index is not None
             return self.index
-        if self._state != "open":
-            raise RuntimeError(f"ShardWriter is {self._state}")
+        self._require_open()
         try:
-            self._flush()
-            if not self._done:
+            self._emit()
+            if not self._written:
                 raise ValueError("no records were added; refusing to commit an empty dataset")
-            self.index = write_index(self.store, self._key(self.index_name), self._done, metadata=self.metadata)
+            self.index = write_index(self.store, self._key(self.index_name), self._written, metadata=self.metadata)
         except BaseException:
             self._state = "aborted"
             raise
@@ -344,16 +358,13 @@ class ShardWriter:
     def abort(self) -> None:
         if self._state == "open":
             self._state = "aborted"
-            self._parts = []
+            self._current = _OpenShard()
 
     def __enter__(self) -> "ShardWriter":
         return self
 
     def __exit__(self, exc_type, exc, tb) -> None:
-        if exc_type is None:
-            self.close()
-        else:
-            self.abort()
+        self.close() if exc_type is None else self.abort()
 
 
 # ----------------------------------------------------------------------------- planning
@@ -361,12 +372,21 @@ class ShardWriter:
 ShardsLike = Union[ShardIndex, Sequence[Shard]]
 
 
-def _order_key(seed: int, epoch: int, key: str) -> bytes:
+def _shuffle_rank(seed: int, epoch: int, key: str) -> bytes:
+    """Sort key of a shard for one (seed, epoch): a hash, so every process computes the same order."""
+
     return hashlib.sha256(f"{seed}\x00{epoch}\x00{key}".encode("utf-8")).digest()
 
 
 def plan_shards(shards: ShardsLike, *, num_workers: int, epoch: int = 0, seed: int = 0,
                 shuffle: bool = True) -> Tuple[Tuple[Shard, ...], ...]:
+    """Deal whole shards to ``num_workers`` workers (a pure function: every process gets the same plan).
+
+    Shards are ordered by ``_shuffle_rank`` (or kept in index order), laid
+    end to end on the record axis, and each goes to the worker whose equal
+    slice of that axis contains the shard's midpoint.
+    """
+
     _int(num_workers, "num_workers", 1)
     _int(epoch, "epoch", 0)
     _int(seed, "seed")
@@ -376,19 +396,19 @@ def plan_shards(shards: ShardsLike, *, num_workers: int, epoch: int = 0, seed: i
     if len(items) < num_workers:
         raise ValueError(f"{len(items)} shards cannot feed {num_workers} workers; write smaller shards or use "
                          "fewer workers")
-    order = sorted(items, key=lambda s: _order_key(seed, epoch, s.key)) if shuffle else list(items)
-    total = sum(s.records for s in order)
-    owners: List[List[Shard]] = [[] for _ in range(num_workers)]
-    seen = 0
-    for s in order:
-        # midpoint (seen + records/2) of this shard, scaled to a worker, in exact integers
-        owners[(2 * seen + s.records) * num_workers // (2 * total)].append(s)
-        seen += s.records
-    idle = [w for w, o in enumerate(owners) if not o]
-    if idle:
+    ordered = sorted(items, key=lambda sh: _shuffle_rank(seed, epoch, sh.key)) if shuffle else list(items)
+    counts = [sh.records for sh in ordered]
+    starts = [0, *itertools.accumulate(counts)][:-1]
+    total = starts[-1] + counts[-1]
+    hands: List[List[Shard]] = [[] for _ in range(num_workers)]
+    for shard, start, n in zip(ordered, starts, counts):
+        # midpoint start + n/2 scaled to [0, num_workers), in exact integer arithmetic
+        hands[(2 * start + n) * num_workers // (2 * total)].append(shard)
+    empty = [w for w, hand in enumerate(hands) if not hand]
+    if empty:
         raise ValueError(f"shard record counts are too uneven to give all {num_workers} workers a shard "
-                         f"(idle workers include {idle[:8]}); write smaller shards or use fewer workers")
-    return tuple(tuple(o) for o in owners)
+                         f"(idle workers include {empty[:8]}); write smaller shards or use fewer workers")
+    return tuple(tuple(hand) for hand in hands)
 
 
 def assign_shards(shards: ShardsLike, *, worker: int, num_workers: int, epoch: int = 0, seed: int = 0,
