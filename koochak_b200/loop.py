@@ -1,40 +1,43 @@
-"""``training_loop``: the function-first training runtime (reference: koochak/loop.py:437-1739).
+"""``training_loop``: the function-first training runtime.
 
-The public contract matches the reference: the caller supplies a model, a
-dataset, ``step_fn(model, batch, ctx) -> {"loss": tensor, ...}``, an
-optimizer and a ``train`` config; the loop owns micro-batching and gradient
-accumulation, AMP and the GradScaler, the gradient gate (unscale, finite
-check, clipping), the optimizer/EMA/scheduler update, data parallelism, hooks
-and logging, periodic/async/terminal checkpoints in the published ``.pt`` +
-``.ready.json`` format, auto-resume, OOM skip/restart, SIGUSR1 evacuation and
-the background GPU-health watchdog.
+(public contract of reference koochak/loop.py:437-476: the same keyword
+signature, hook names and payloads, config keys, checkpoint format, exit
+codes)
 
-What runs differently on CUDA:
+The caller supplies a model, a dataset, ``step_fn(model, batch, ctx) ->
+{"loss": tensor, ...}``, an optimizer and the ``train`` config. The run is
+assembled from parts, most of them in ``koochak_b200.runtime``:
 
-* gradient gate: one native pass computes the finite flag, per-tensor norms
-  and the clip coefficient (and unscales for fp16); the host reads three
-  numbers once; fused optimizers apply the coefficient when they read the
-  gradients;
-* update: optimizers from this package fuse the GPU-resident EMA into their
-  parameter-update kernels;
-* data parallelism (``ddp: true``): :class:`koochak_b200.parallel.ddp.DataParallel`
-  with bucketed reductions overlapped with backward (NCCL, or the native
-  P2P path with ``comm.transport: p2p``);
-* optional device timing (``device_timing: true``): CUDA events bracket every
-  update; ``on_update_end`` logs carry ``step_device_ms``.
+* ``LoopSettings`` / ``EmaSettings`` -- the ``train.*`` keys, read once;
+* ``_Profiler`` -- optional per-phase wall time (and NVTX ranges), reported
+  as ``profile_loop_*_time_s``;
+* ``_MicroSteps`` -- gradient accumulation: ``no_sync`` on all but the last
+  micro-batch, autocast, ``step_fn``, scaled backward (on the native
+  data-parallel path backward launches the bucket reductions from gradient
+  hooks);
+* ``GradientGate`` -- unscale, finite check and clip, from the fused
+  reduction's statistics when there are any (one 16-byte read per step);
+* the update -- EMA snapshot wait, optimizer (the fused optimizers take the
+  clip coefficient and the GPU EMA into their own kernels), scaler, EMA,
+  scheduler;
+* ``CheckpointKeeper`` -- every rank collects (optimizer state gathered from
+  its owners), rank 0 publishes ``stepNNNNNNNNN.pt`` + ``.ready.json``;
+* ``_StopControl`` -- after every update, one small cross-rank reduction
+  agrees on evacuation (SIGUSR1 / the runner's request file) and GPU-health
+  failures; an agreed stop checkpoints and exits 75 or 42;
+* ``_OomGuard`` -- opt-in recovery from CUDA out-of-memory inside a step.
 """
 
 from __future__ import annotations
 
 import json
-import math
 import os
 import statistics
 import time
 import warnings
 from contextlib import ExitStack, nullcontext
 from dataclasses import dataclass, field
-from typing import Any, Callable, Dict, Iterable, Iterator, Mapping, Optional, Sequence
+from typing import Any, Callable, Dict, Iterable, Iterator, List, Mapping, Optional, Sequence, Tuple
 
 import torch
 import torch.nn as nn
@@ -45,22 +48,21 @@ from torch.optim.lr_scheduler import _LRScheduler
 from . import oom as oom_lib
 from .core import dist as dist_lib
 from .core import hooks as hooks_lib
-from .core.precision import Scaler as make_scaler
-from .core.precision import FusedGradScaler, autocast_context, prepare_compile_backend
+from .core.precision import FusedGradScaler, Scaler as make_scaler, autocast_context, prepare_compile_backend
 from .data.iterable import prefetch, to_device
 from .data.sharding import shard_dataset, warn_if_unsharded
 from .health.background import BackgroundGpuHealth
 from .health.gpu import summarize_failures_for_stdout
 from .interruption import EVACUATION_EXIT_CODE, OOM_RESTART_EXIT_CODE, EvacuationController
-from .optim.grad_clip import GradientClipStats, clip_grad_norm_, fused_grad_gate
+from .runtime.checkpoints import CheckpointKeeper, EmaBuilder, restore_ema, restore_training_state
+from .runtime.gate import GradientGate
+from .runtime.settings import EmaSettings, LoopSettings, shard_mode
 from .storage import checkpoint as checkpoint_lib
 from .utils import config as config_lib
 from .utils import flags as flags_lib
 from .utils.collector import WarmFreeze
 from .utils.device import ensure_process_device, get_device, get_lr
 from .utils.ema import EMA
-from .utils.paths import canonical_dir
-from .utils.seed import get_rng_state, set_rng_state
 
 __all__ = ["training_loop", "StepFn", "EvalFn", "BatchPrepareFn"]
 
@@ -68,307 +70,10 @@ StepFn = Callable[[nn.Module, Any, Mapping[str, Any]], Dict[str, Any]]
 EvalFn = Callable[[nn.Module, Iterable, Mapping[str, Any]], Dict[str, float]]
 BatchPrepareFn = Callable[[Any], Any]
 
-_TIMING_KEYS = ("batch_wait_s", "step_compute_s", "total_step_s")
-_ROOT_SIBLINGS = ("data", "optim", "logging", "wandb", "entry")
-_EMA_FLAT_KEYS = {
-    "enabled": "ema_enabled", "decay": "ema_decay", "decay_init": "ema_decay_init",
-    "warmup_steps": "ema_warmup_steps", "schedule": "ema_schedule", "profile": "ema_profile",
-    "gamma": "ema_gamma", "srel": "ema_srel", "offload_to_cpu": "ema_offload_to_cpu",
-    "pin_memory": "ema_pin_memory", "update_every": "ema_update_every",
-    "compensate_update_every": "ema_compensate_update_every", "eval_with_ema": "ema_eval",
-}
-_EMA_RAMPS = frozenset({"linear", "ramp", "warmup", "cosine"})
-_WRAPS_ONLY = frozenset({"wraps", "wraps-only", "merge-wraps", "merge_wraps"})
-_FULL = frozenset({"full", "full-model", "full_model"})
-
-
-def _emit(hooks, event: str, *args, suppress_exceptions: bool = True, **kwargs) -> None:
-    hooks_lib.emit(hooks, event, *args, suppress_exceptions=suppress_exceptions, **kwargs)
-
-
-def _parameter_counts(module: nn.Module) -> Dict[str, int]:
-    base = getattr(module, "module", module)
-    total = sum(p.numel() for p in base.parameters())
-    trainable = sum(p.numel() for p in base.parameters() if p.requires_grad)
-    return {"total": int(total), "trainable": int(trainable), "frozen": int(total - trainable)}
-
-
-def _batch_total(batch: Any, key: str) -> float:
-    if not isinstance(batch, Mapping) or key not in batch:
-        return 0.0
-    v = batch[key]
-    if isinstance(v, torch.Tensor):
-        return float(v.detach().to(torch.float32).sum().item())
-    if isinstance(v, (list, tuple)):
-        return float(sum(float(x) for x in v)) if v else 0.0
-    return float(v)
-
-
-def _skip_counts(batch: Any) -> Dict[str, float]:
-    if not isinstance(batch, Mapping):
-        return {}
-    return {str(k): _batch_total(batch, str(k)) for k in batch.keys() if str(k).endswith("_skip_count")}
-
-
-def _timing_fragment(entries: list, key: str) -> str:
-    if not entries:
-        return f"{key}=n/a"
-    ordered = sorted((float(e.get(key, 0.0)), int(e.get("rank", 0))) for e in entries)
-    vals = [v for v, _ in ordered]
-    slow, slow_rank = ordered[-1]
-    return (f"{key}={ordered[0][0]:.3f}/{statistics.median(vals):.3f}/{slow:.3f}@r{slow_rank} "
-            f"span={slow - ordered[0][0]:.3f}")
-
-
-def _format_rank_timing(entries: list, step: int, extra_keys: Sequence[str] = ()) -> str:
-    return f"[rank-timing] step={step} " + " ".join(_timing_fragment(entries, k) for k in (*_TIMING_KEYS, *extra_keys))
-
-
-def _looks_like_root_config(cfg: Any) -> bool:
-    if isinstance(cfg, Mapping):
-        return "train" in cfg and any(k in cfg for k in _ROOT_SIBLINGS)
-    return all(hasattr(cfg, k) for k in ("train",) + _ROOT_SIBLINGS)
-
-
-def _resolve_train_config(train_cfg: Any, config_json: Optional[Mapping[str, Any]]):
-    if _looks_like_root_config(train_cfg):
-        warnings.warn("training_loop now expects train_cfg only; passing the full root config is deprecated.",
-                      DeprecationWarning)
-        config_json = config_json or train_cfg
-        train_cfg = config_lib.get(train_cfg, "train", {})
-    return train_cfg or {}, config_json
-
-
-def _shard_mode(enabled: bool, mode: Any, label: str) -> Optional[str]:
-    if not enabled:
-        return None
-    if mode is None:
-        raise ValueError(f"train.{label}_mode must be set when train.{label}=true")
-    key = str(mode).lower()
-    if key not in ("iterable", "map"):
-        raise ValueError(f"Invalid train.{label}_mode: {mode!r} (expected 'iterable' or 'map')")
-    return key
-
-
-@dataclass
-class _TrainSettings:
-    ddp_enabled: bool
-    shard_dataset_enabled: bool
-    shard_dataset_mode: Optional[str]
-    shard_eval_dataset_enabled: bool
-    shard_eval_dataset_mode: Optional[str]
-    warn_unsharded: bool
-    amp_mode: str
-    grad_accum: int
-    grad_clip_norm: Optional[float]
-    nonfinite_grad_check_every: int
-    scheduler_step_policy: str
-    max_steps: int
-    log_every: int
-    eval_every: int
-    eval_at_step_zero: bool
-    ckpt_every: int
-    intervals_use_completed_steps: bool
-    rank_timing_every: int
-    rank_timing_extra_keys: tuple
-    out_dir: str
-    keep_last_k: int
-    checkpoint_dir: str
-    checkpoint_async: bool
-    prefetch_batches: int
-    prefetch_pipeline: str
-    prefetch_threaded: bool
-    autocast_in_step_fn: bool
-    scalarize_loss_every_step: bool
-    profile_step_timing: bool
-    profile_step_cuda_sync: bool
-    find_unused_parameters: bool
-    ddp_static_graph: bool
-    ddp_gradient_as_bucket_view: bool
-    ddp_bucket_cap_mb: Optional[int]
-    ddp_bucket_cap_mb_list: Optional[tuple]
-    ddp_broadcast_buffers: bool
-    device_timing: bool = False
-    comm_transport: str = "auto"
-    profile_nvtx: bool = False
-
-    @classmethod
-    def from_cfg(cls, cfg: Any) -> "_TrainSettings":
-        g = config_lib.get
-        cap, cap_list = g(cfg, "ddp_bucket_cap_mb", None), g(cfg, "ddp_bucket_cap_mb_list", None)
-        if cap is not None and cap_list is not None:
-            raise ValueError("Set only one of train.ddp_bucket_cap_mb and train.ddp_bucket_cap_mb_list")
-        caps = tuple(int(v) for v in cap_list) if cap_list is not None else None
-        if caps is not None and (not caps or any(v <= 0 for v in caps)):
-            raise ValueError("train.ddp_bucket_cap_mb_list must contain positive values")
-        out_dir = canonical_dir(g(cfg, "out_dir", "./runs/exp0"))
-        ckpt_dir = g(cfg, "checkpoint_dir", None)
-        if ckpt_dir is None:
-            ckpt_dir = out_dir
-        elif "://" not in str(ckpt_dir):
-            ckpt_dir = canonical_dir(ckpt_dir)
-        return cls(
-            ddp_enabled=bool(g(cfg, "ddp", False)),
-            shard_dataset_enabled=bool(g(cfg, "shard_dataset", False)),
-            shard_dataset_mode=g(cfg, "shard_dataset_mode", None),
-            shard_eval_dataset_enabled=bool(g(cfg, "shard_eval_dataset", False)),
-            shard_eval_dataset_mode=g(cfg, "shard_eval_dataset_mode", None),
-            warn_unsharded=bool(g(cfg, "warn_unsharded", True)),
-            amp_mode=str(g(cfg, "amp", "fp32")),
-            grad_accum=int(g(cfg, "grad_accum", 1)),
-            grad_clip_norm=g(cfg, "grad_clip_norm", None),
-            nonfinite_grad_check_every=int(g(cfg, "nonfinite_grad_check_every", 0)),
-            scheduler_step_policy=str(g(cfg, "scheduler_step", "step")),
-            max_steps=int(g(cfg, "max_steps", 100_000)),
-            log_every=int(g(cfg, "log_every", 100)),
-            eval_every=int(g(cfg, "eval_every", 5_000)),
-            eval_at_step_zero=bool(g(cfg, "eval_at_step_zero", True)),
-            ckpt_every=int(g(cfg, "ckpt_every", 5_000)),
-            intervals_use_completed_steps=bool(g(cfg, "intervals_use_completed_steps", False)),
-            rank_timing_every=int(g(cfg, "rank_timing_every", 0)),
-            rank_timing_extra_keys=tuple(str(k) for k in (g(cfg, "rank_timing_keys", ()) or ())),
-            out_dir=out_dir,
-            keep_last_k=int(g(cfg, "keep_last_k", 3)),
-            checkpoint_dir=str(ckpt_dir),
-            checkpoint_async=bool(g(cfg, "checkpoint_async", False)),
-            prefetch_batches=int(g(cfg, "prefetch_batches", 0)),
-            prefetch_pipeline=str(g(cfg, "prefetch_pipeline", "single")),
-            prefetch_threaded=bool(g(cfg, "prefetch_threaded", False)),
-            autocast_in_step_fn=bool(g(cfg, "autocast_in_step_fn", False)),
-            scalarize_loss_every_step=bool(g(cfg, "scalarize_loss_every_step", True)),
-            profile_step_timing=bool(g(cfg, "profile_step_fn_timing", False)),
-            profile_step_cuda_sync=bool(g(cfg, "profile_step_fn_cuda_sync", True)),
-            find_unused_parameters=bool(g(cfg, "find_unused_parameters", False)),
-            ddp_static_graph=bool(g(cfg, "ddp_static_graph", False)),
-            ddp_gradient_as_bucket_view=bool(g(cfg, "ddp_gradient_as_bucket_view", False)),
-            ddp_bucket_cap_mb=int(cap) if cap is not None else None,
-            ddp_bucket_cap_mb_list=caps,
-            ddp_broadcast_buffers=bool(g(cfg, "ddp_broadcast_buffers", True)),
-            device_timing=bool(g(cfg, "device_timing", False)),
-            comm_transport=str(g(cfg, "comm_transport", "auto")),
-            profile_nvtx=bool(g(cfg, "profile_nvtx", False)),
-        )
-
-
-@dataclass
-class _DualEmaSettings:
-    enabled: bool
-    gamma1: Optional[float]
-    gamma2: Optional[float]
-    srel1: Optional[float]
-    srel2: Optional[float]
-
-    @classmethod
-    def from_cfg(cls, ema_cfg: Any) -> "_DualEmaSettings":
-        d = config_lib.get(ema_cfg, "dual", {}) if ema_cfg is not None else {}
-        g = config_lib.get
-        return cls(bool(g(d, "enabled", False)), g(d, "gamma1", None), g(d, "gamma2", None), g(d, "srel1", None),
-                   g(d, "srel2", None))
-
-
-def _ema_getter(train_cfg: Any) -> Callable[[str, Any], Any]:
-    """Read ``train.ema.<key>``, falling back to the legacy flat ``train.ema_<key>``."""
-
-    ema_cfg = config_lib.get(train_cfg, "ema", {}) if train_cfg is not None else {}
-
-    def get(key: str, default: Any = None) -> Any:
-        if isinstance(ema_cfg, Mapping):
-            if key in ema_cfg:
-                v = config_lib.get(ema_cfg, key, default)
-                if v is not None:
-                    return v
-        else:
-            v = getattr(ema_cfg, key, None)
-            if v is not None:
-                return v
-        flat = _EMA_FLAT_KEYS.get(key)
-        if flat is None:
-            return default
-        v = config_lib.get(train_cfg, flat, default)
-        return default if v is None else v
-
-    return get
-
-
-@dataclass
-class _EmaSettings:
-    enabled: bool
-    profile: str
-    target_decay: Optional[float]
-    decay_init: Optional[float]
-    warmup_steps: int
-    schedule: str
-    gamma: Optional[float]
-    srel: Optional[float]
-    offload_to_cpu: bool
-    pin_memory: bool
-    update_every: int
-    compensate_update_every: bool
-    eval_with_ema: bool
-    dual: _DualEmaSettings
-
-    @classmethod
-    def from_cfg(cls, train_cfg: Any) -> "_EmaSettings":
-        get = _ema_getter(train_cfg)
-        ema_cfg = config_lib.get(train_cfg, "ema", {}) if train_cfg is not None else {}
-        flag = get("enabled", None)
-        if flag is None:
-            prof = get("profile", None)
-            enabled = get("decay", None) is not None or (prof is not None and str(prof).lower()
-                                                          not in ("", "none", "constant"))
-        else:
-            enabled = bool(flag)
-        target = float(get("decay", 0.999)) if enabled else None
-        return cls(
-            enabled=enabled,
-            profile=str(get("profile", "constant")).lower() if enabled else "constant",
-            target_decay=target,
-            decay_init=float(get("decay_init", min(0.9, target or 0.999))) if enabled else None,
-            warmup_steps=int(get("warmup_steps", 0)) if enabled else 0,
-            schedule=str(get("schedule", "constant")).lower() if enabled else "constant",
-            gamma=get("gamma", None),
-            srel=get("srel", None),
-            offload_to_cpu=bool(get("offload_to_cpu", True)),
-            pin_memory=bool(get("pin_memory", True)),
-            update_every=max(1, int(get("update_every", 1))),
-            compensate_update_every=bool(get("compensate_update_every", True)),
-            eval_with_ema=bool(get("eval_with_ema", False)) if enabled else False,
-            dual=_DualEmaSettings.from_cfg(ema_cfg),
-        )
-
-    def warmed_decay(self, step: int) -> float:
-        d = float(self.target_decay or 0.999)
-        if self.warmup_steps <= 0 or self.schedule not in _EMA_RAMPS:
-            return d
-        t = max(0.0, min(1.0, (step + 1) / float(self.warmup_steps)))
-        s = 0.5 * (1.0 - math.cos(math.pi * t)) if self.schedule == "cosine" else t
-        init = self.decay_init or d
-        return float(min(max(init + (d - init) * s, 0.0), 0.999999))
-
-    def _make(self, module: nn.Module, profile: str, gamma, srel) -> EMA:
-        return EMA(module, decay=float(self.target_decay or 0.999), profile=profile, gamma=gamma, srel=srel,
-                   update_every=self.update_every, offload_to_cpu=self.offload_to_cpu, pin_memory=self.pin_memory,
-                   compensate_update_every=self.compensate_update_every)
-
-    def build(self, module: nn.Module) -> EMA:
-        return self._make(module, self.profile, self.gamma, self.srel)
-
-    def build_dual(self, module: nn.Module) -> list:
-        if not self.dual.enabled:
-            return []
-        return [self._make(module, "power", self.dual.gamma1, self.dual.srel1),
-                self._make(module, "power", self.dual.gamma2, self.dual.srel2)]
-
-
-@dataclass
-class _MicroStats:
-    out: Optional[Dict[str, Any]] = None
-    total_loss: Optional[torch.Tensor] = None
-    total_loss_scalar: Optional[float] = None
-    batch_wait_s: float = 0.0
-    extra_timing_totals: Dict[str, float] = field(default_factory=dict)
-    profile_timing_totals: Dict[str, float] = field(default_factory=dict)
-    skip_count_totals: Dict[str, float] = field(default_factory=dict)
+_ROOT_SECTIONS = ("data", "optim", "logging", "wandb", "entry")
+_COMPILE_WRAPS_ONLY = frozenset({"wraps", "wraps-only", "merge-wraps", "merge_wraps"})
+_COMPILE_FULL = frozenset({"full", "full-model", "full_model"})
+_RANK_TIMING = ("batch_wait_s", "step_compute_s", "total_step_s")
 
 
 def training_loop(*, model: nn.Module, dataset: Iterable, step_fn: StepFn, optimizer: Optimizer,
@@ -381,34 +86,312 @@ def training_loop(*, model: nn.Module, dataset: Iterable, step_fn: StepFn, optim
                   evacuation: Optional[EvacuationController | bool] = None) -> Dict[str, Any]:
     """Train until ``train.max_steps`` or dataset exhaustion; return the final checkpoint dict."""
 
-    return _TrainLoop(model=model, dataset=dataset, step_fn=step_fn, optimizer=optimizer, scheduler=scheduler,
-                      train_cfg=train_cfg, config_json=config_json, checkpoint_dict=checkpoint_dict,
-                      eval_dataset=eval_dataset, eval_fn=eval_fn, prepare_batch_fn=prepare_batch_fn, hooks=hooks,
-                      resume=resume, auto_resume_path=auto_resume_path, evacuation=evacuation).run()
+    return _Run(model=model, dataset=dataset, step_fn=step_fn, optimizer=optimizer, scheduler=scheduler,
+                train_cfg=train_cfg, config_json=config_json, checkpoint_dict=checkpoint_dict,
+                eval_dataset=eval_dataset, eval_fn=eval_fn, prepare_batch_fn=prepare_batch_fn, hooks=hooks,
+                resume=resume, auto_resume_path=auto_resume_path, evacuation=evacuation).execute()
 
 
-class _TrainLoop:
-    """Orchestrator behind ``training_loop`` (not public API)."""
+# ----------------------------------------------------------------------------- small helpers
+
+
+def _split_root_config(train_cfg: Any, config_json: Optional[Mapping[str, Any]]):
+    """A whole root config passed as ``train_cfg`` is still accepted (deprecated): use its ``train`` part."""
+
+    is_root = (("train" in train_cfg and any(k in train_cfg for k in _ROOT_SECTIONS)) if isinstance(train_cfg, Mapping)
+               else all(hasattr(train_cfg, k) for k in ("train",) + _ROOT_SECTIONS))
+    if is_root:
+        warnings.warn("training_loop now expects train_cfg only; passing the full root config is deprecated.",
+                      DeprecationWarning)
+        return config_lib.get(train_cfg, "train", {}) or {}, config_json or train_cfg
+    return train_cfg or {}, config_json
+
+
+def _sum_of(value: Any) -> float:
+    if isinstance(value, torch.Tensor):
+        return float(value.detach().to(torch.float32).sum().item())
+    if isinstance(value, (list, tuple)):
+        return float(sum(float(x) for x in value))
+    return float(value)
+
+
+def _skip_counters(batch: Any) -> Dict[str, float]:
+    """``*_skip_count`` entries a dataset put into a dict batch, summed."""
+
+    if not isinstance(batch, Mapping):
+        return {}
+    return {str(k): _sum_of(v) for k, v in batch.items() if str(k).endswith("_skip_count")}
+
+
+def _rank_timing_line(entries: List[Dict[str, Any]], step: int, keys: Sequence[str]) -> str:
+    def part(key: str) -> str:
+        if not entries:
+            return f"{key}=n/a"
+        ranked = sorted((float(e.get(key, 0.0)), int(e.get("rank", 0))) for e in entries)
+        fastest, (slowest, who) = ranked[0][0], ranked[-1]
+        middle = statistics.median(v for v, _ in ranked)
+        return f"{key}={fastest:.3f}/{middle:.3f}/{slowest:.3f}@r{who} span={slowest - fastest:.3f}"
+
+    return f"[rank-timing] step={step} " + " ".join(part(k) for k in (*_RANK_TIMING, *keys))
+
+
+def _parameter_counts(module: nn.Module) -> Tuple[int, int]:
+    inner = getattr(module, "module", module)
+    total = sum(p.numel() for p in inner.parameters())
+    return total, sum(p.numel() for p in inner.parameters() if p.requires_grad)
+
+
+class _Profiler:
+    """Per-phase wall time (``profile_step_fn_timing``) with optional CUDA sync and NVTX ranges."""
+
+    def __init__(self, settings: LoopSettings, on_cuda: bool, device: torch.device) -> None:
+        self.timing = settings.profile_step_timing
+        self.sync = settings.profile_step_timing and settings.profile_step_cuda_sync and on_cuda
+        self.nvtx = settings.profile_nvtx and on_cuda
+        self.device = device
+        self._open = 0
+
+    def barrier(self) -> None:
+        if self.sync:
+            torch.cuda.synchronize(self.device)
+
+    def start(self, phase: Optional[str] = None) -> float:
+        self.barrier()
+        if self.nvtx and phase is not None:
+            torch.cuda.nvtx.range_push(f"koochak/{phase}")
+            self._open += 1
+        return time.perf_counter()
+
+    def stop(self, totals: Dict[str, float], key: str, began: float) -> float:
+        self.barrier()
+        if self._open:
+            torch.cuda.nvtx.range_pop()
+            self._open -= 1
+        took = time.perf_counter() - began
+        if self.timing:
+            totals[key] = totals.get(key, 0.0) + took
+        return took
+
+    def run(self, totals: Dict[str, float], key: str, thunk: Callable[[], Any]) -> Any:
+        began = self.start(key[len("profile_loop_"):-len("_time_s")])
+        try:
+            return thunk()
+        finally:
+            self.stop(totals, key, began)
+
+
+@dataclass
+class _StepRecord:
+    """What one update produced for logs and rank timing."""
+
+    out: Optional[Dict[str, Any]] = None
+    loss: Optional[torch.Tensor] = None
+    loss_value: Optional[float] = None
+    batch_wait_s: float = 0.0
+    extra_timing: Dict[str, float] = field(default_factory=dict)
+    timings: Dict[str, float] = field(default_factory=dict)
+    skip_counts: Dict[str, float] = field(default_factory=dict)
+
+
+class _MicroSteps:
+    """Gradient accumulation over ``grad_accum`` micro-batches."""
+
+    def __init__(self, run: "_Run") -> None:
+        self.run_ = run
+
+    def __call__(self, step: int, batches: Iterator[Any], *, want_rank_timing: bool) -> _StepRecord:
+        r = self.run_
+        s = r.settings
+        rec = _StepRecord()
+        prof = r.profiler
+        count = s.grad_accum
+        prefetching = r.on_cuda and s.prefetch_batches > 0
+        can_defer_sync = hasattr(r.model, "no_sync")
+        for micro in range(count):
+            defer = r.model.no_sync() if can_defer_sync and micro < count - 1 else nullcontext()
+            cast = r.autocast() if not s.autocast_in_step_fn else nullcontext()
+            with defer, cast:
+                r.micro_position = (micro, "fetch")
+                began = prof.start("batch_wait")
+                batch = next(batches) if prefetching else to_device(next(batches), r.device)
+                rec.batch_wait_s += prof.stop(rec.timings, "profile_loop_batch_wait_time_s", began)
+                for k, v in _skip_counters(batch).items():
+                    rec.skip_counts[k] = rec.skip_counts.get(k, 0.0) + v
+                r.micro_position = (micro, "step_fn")
+                out = prof.run(rec.timings, "profile_loop_step_fn_time_s",
+                               lambda: r.step_fn(r.model, batch, r.step_ctx(step)))
+                if want_rank_timing and isinstance(out, Mapping):
+                    for key in s.rank_timing_extra_keys:
+                        if out.get(key) is not None:
+                            v = out[key]
+                            rec.extra_timing[key] = rec.extra_timing.get(key, 0.0) + float(
+                                v.detach() if isinstance(v, torch.Tensor) else v)
+                if not isinstance(out, Mapping) or "loss" not in out:
+                    raise RuntimeError("step_fn must return a dict containing a 'loss' Tensor")
+                if not isinstance(out["loss"], torch.Tensor):
+                    raise RuntimeError("step_fn returned a 'loss' that is not a torch.Tensor")
+                loss = out["loss"] / count
+            r.micro_position = (micro, "backward")
+            prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
+            part = loss.detach()
+            rec.loss = part if rec.loss is None else rec.loss + part
+            if s.scalarize_loss_every_step:
+                rec.loss_value = float(rec.loss)
+            rec.out = out
+        return rec
+
+
+class _StopControl:
+    """Per-update agreement on stopping (evacuation, GPU health) and what an agreed stop does."""
+
+    def __init__(self, run: "_Run") -> None:
+        self.run_ = run
+
+    def reconcile(self, step: int) -> None:
+        r = self.run_
+        r.health.update_step(step)
+        local = r.health.failures()
+        evacuate, unhealthy = r.evacuation.reconcile_requests(bool(local))
+        r.evacuation_requested = evacuate
+        r.ctx["evacuation_requested"] = evacuate
+        if unhealthy:
+            everyone = [local]
+            if dist_lib.is_initialized():
+                everyone = [None] * r.world_size
+                torch.distributed.all_gather_object(everyone, local)
+            self._stop_for_health(step, [f for per_rank in everyone for f in per_rank])
+
+    def _stop_for_health(self, step: int, failures: list) -> None:
+        r = self.run_
+        h = r.health
+        h.close()
+        completed = step + 1
+        bad_nodes = h.bad_nodes_from_failures(failures)
+        metrics = {"gpu_health": {"event": "gpu_health_shutdown", "failures": failures, "bad_nodes": bad_nodes,
+                                  "slurm_action": h.slurm_action, "slurm_disabled": h.slurm_disabled}}
+        path, ckpt = r.checkpoint(completed, next_step=completed, metrics=metrics, gather_rng=True, announce=False)
+        r.final_ckpt = ckpt
+        dist_lib.barrier()
+        if r.is_rank0:
+            r.emit("on_checkpoint", path, ckpt, r.step_ctx(completed))
+            summary = h.write_failure_summary(step=completed, failures=failures, checkpoint_path=path)
+            print(f"[gpu-health] FAIL step={step} {summarize_failures_for_stdout(failures)}", flush=True)
+            print(f"[gpu-health] checkpoint={path} summary={summary} slurm_action={h.slurm_action} "
+                  f"bad_nodes={','.join(bad_nodes)}", flush=True)
+        dist_lib.barrier()
+        if r.is_rank0:
+            results = h.perform_slurm_recovery(failures)
+            if results:
+                print(f"[gpu-health] slurm_results={json.dumps(results, sort_keys=True)}", flush=True)
+        elif os.environ.get("SLURM_JOB_ID") and not h.slurm_disabled and h.slurm_action in {"requeue", "cancel"}:
+            time.sleep(30.0)  # rank 0 mutates the Slurm job before the job is torn down
+        raise SystemExit(h.exit_code)
+
+
+class _OomGuard:
+    """Opt-in survival of CUDA OOMs raised while a step fetches, runs ``step_fn`` or backward."""
+
+    def __init__(self, run: "_Run", settings: oom_lib.OomRecoverySettings) -> None:
+        self.run_ = run
+        self.settings = settings
+        self.catches: tuple = (oom_lib.OutOfMemoryError,) if settings.enabled else ()
+        self.skipped: set = set()
+
+    def load_records(self, start: int) -> None:
+        """Learn the steps earlier attempts recorded as OOM (rank 0 reads, everyone receives)."""
+
+        r = self.run_
+        steps = sorted(oom_lib.recorded_steps(r.keeper.store)) if r.is_rank0 else None
+        if r.world_size > 1 and dist_lib.is_initialized():
+            box = [steps]
+            torch.distributed.broadcast_object_list(box, src=0)
+            steps = box[0]
+        self.skipped = set(steps or ())
+        upcoming = [s for s in sorted(self.skipped) if start <= s < r.settings.max_steps]
+        if upcoming and r.is_rank0:
+            shown = ", ".join(map(str, upcoming[:20])) + (", ..." if len(upcoming) > 20 else "")
+            print(f"[oom] {len(upcoming)} step(s) recorded as OOM-skipped by earlier attempts will be skipped: {shown}",
+                  flush=True)
+
+    def record(self, step: int, exc: BaseException) -> Dict[str, Any]:
+        r = self.run_
+        micro, phase = r.micro_position
+        verdict = oom_lib.decide(self.settings, self.skipped, step, distributed=r.world_size > 1,
+                                 during_fetch=phase == "fetch")
+        memory, summary = oom_lib.memory_report(r.device)
+        rec = {"v": 1, "step": step, "rank": r.rank, "world_size": r.world_size, "phase": phase,
+               "micro_step": micro, "grad_accum": r.settings.grad_accum, "action": verdict.action,
+               "reason": verdict.reason, "consecutive": verdict.consecutive,
+               "max_consecutive": self.settings.max_consecutive, "skipped_total": verdict.skipped_total,
+               "error_type": type(exc).__name__, "message": oom_lib.short_message(exc), "memory": memory,
+               "memory_summary": summary, "wall_time": time.time()}
+        print(oom_lib.format_record(rec), flush=True)
+        return rec
+
+    def recover(self, step: int, batches: Iterator[Any], rec: Dict[str, Any]) -> bool:
+        r = self.run_
+        r.optimizer.zero_grad(set_to_none=True)
+        oom_lib.release_memory(r.device)
+        oom_lib.write_record(r.keeper.store, rec)  # durable before anything else can fail
+        self.skipped.add(step)
+        r.emit("on_oom", rec, r.step_ctx(step))
+        if r.world_size > 1:
+            print(f"[oom] rank={r.rank} exiting with code {OOM_RESTART_EXIT_CODE}; resubmit with resume=auto to "
+                  "continue from the last checkpoint", flush=True)
+            raise SystemExit(OOM_RESTART_EXIT_CODE)
+        consumed = 0 if rec["phase"] == "fetch" else int(rec["micro_step"]) + 1
+        if rec["phase"] != "fetch" and not self._discard(batches, r.settings.grad_accum - consumed):
+            return False
+        r.step_scheduler()
+        if rec["action"] == oom_lib.RESTART:
+            completed = step + 1
+            path, r.final_ckpt = r.checkpoint(completed, next_step=completed, gather_rng=True, announce=False)
+            r.emit("on_checkpoint", path, r.final_ckpt, r.step_ctx(completed))
+            print(f"[oom] checkpoint={path} next_step={completed}; exiting with code {OOM_RESTART_EXIT_CODE} so a "
+                  "resubmit starts with a fresh CUDA allocator", flush=True)
+            raise SystemExit(OOM_RESTART_EXIT_CODE)
+        return r.after_update(step, {})
+
+    def replay_skip(self, step: int, batches: Iterator[Any]) -> bool:
+        r = self.run_
+        if not self._discard(batches, r.settings.grad_accum):
+            return False
+        r.step_scheduler()
+        if r.is_rank0:
+            print(f"[oom] step={step} skipped: recorded as OOM by an earlier attempt", flush=True)
+        return r.after_update(step, {})
+
+    @staticmethod
+    def _discard(batches: Iterator[Any], n: int) -> bool:
+        for _ in range(n):
+            try:
+                next(batches)
+            except StopIteration:
+                return False
+        return True
+
+
+# ----------------------------------------------------------------------------- the run
+
+
+class _Run:
+    """One call of ``training_loop`` (not public API)."""
 
     def __init__(self, *, model, dataset, step_fn, optimizer, scheduler, train_cfg, config_json, checkpoint_dict,
                  eval_dataset, eval_fn, prepare_batch_fn, hooks, resume, auto_resume_path, evacuation) -> None:
-        train_config, config_json = _resolve_train_config(train_cfg, config_json)
-        self.train_cfg = train_config
-        self.settings = _TrainSettings.from_cfg(train_config)
-        self._nvtx_open = 0
-        self.ema_settings = _EmaSettings.from_cfg(train_config)
-        self.step_fn = step_fn
-        self.optimizer = optimizer
-        self.scheduler = scheduler
-        self.dataset = dataset
-        self.eval_dataset = eval_dataset
-        self.eval_fn = eval_fn
+        train_cfg, config_json = _split_root_config(train_cfg, config_json)
+        self.train_cfg = train_cfg
+        self.settings = s = LoopSettings.from_cfg(train_cfg)
+        self.ema_settings = EmaSettings.from_cfg(train_cfg)
+        self.step_fn, self.optimizer, self.scheduler = step_fn, optimizer, scheduler
+        self.dataset, self.eval_dataset, self.eval_fn = dataset, eval_dataset, eval_fn
         self.prepare_batch_fn = prepare_batch_fn
         self.hooks = hooks
-        if self.settings.checkpoint_async and hooks and hooks.get("on_checkpoint_all_ranks"):
+        all_rank_hooks = bool(hooks and hooks.get("on_checkpoint_all_ranks"))
+        if s.checkpoint_async and all_rank_hooks:
             raise ValueError("All-rank checkpoint hooks require synchronous publication")
         self.checkpoint_dict = checkpoint_dict
-        self.resume_mode = str(resume if resume is not None else config_lib.get(train_config, "resume", "none")).lower()
+        self.resume_mode = str(resume if resume is not None else config_lib.get(train_cfg, "resume", "none")).lower()
         if self.resume_mode not in {"none", "auto"}:
             raise ValueError("resume must be 'none' or 'auto'")
         if auto_resume_path is not None and self.resume_mode != "auto":
@@ -416,165 +399,174 @@ class _TrainLoop:
         if auto_resume_path is not None and checkpoint_dict is None:
             raise ValueError("auto_resume_path requires a preloaded checkpoint")
         self.auto_resume_path = auto_resume_path
-        if evacuation is None:
-            self.evacuation = EvacuationController(bool(config_lib.get(train_config, "evacuation_enabled", False)),
-                                                   signal_name=config_lib.get(train_config, "evacuation_signal", "USR1"))
+        if isinstance(evacuation, EvacuationController):
+            self.evacuation = evacuation
         elif isinstance(evacuation, bool):
             self.evacuation = EvacuationController(evacuation)
         else:
-            self.evacuation = evacuation
+            self.evacuation = EvacuationController(bool(config_lib.get(train_cfg, "evacuation_enabled", False)),
+                                                   signal_name=config_lib.get(train_cfg, "evacuation_signal", "USR1"))
         self.evacuation_requested = False
-        self.oom_recovery = oom_lib.OomRecoverySettings.from_cfg(train_config)
-        self._oom_errors: tuple = (oom_lib.OutOfMemoryError,) if self.oom_recovery.enabled else ()
-        self.oom_skipped_steps: set[int] = set()
-        self._micro_position: tuple = (0, "fetch")
-        self.collector = WarmFreeze()
-        self._gather_checkpoint_rng = False
+        self.micro_position: Tuple[int, str] = (0, "fetch")
+        self.freezer = WarmFreeze()
 
-        self.device = ensure_process_device(get_device(train_config))
+        self.device = ensure_process_device(get_device(train_cfg))
         model.to(self.device)
         self.model: nn.Module = model
-        self.rank = dist_lib.rank()
-        self.world_size = dist_lib.world_size()
-        self.is_rank0 = dist_lib.rank0()
-        self.checkpoint_store = checkpoint_lib.checkpoint_store(self.settings.checkpoint_dir)
-        self.checkpoint_publisher = (checkpoint_lib.BackgroundPublisher(self.checkpoint_store,
-                                                                        keep_last_k=self.settings.keep_last_k)
-                                     if self.settings.checkpoint_async and self.is_rank0 else None)
-        self.scaler = make_scaler(self.settings.amp_mode)
-        self.cfg_json = config_lib.as_dict(config_json if config_json is not None else train_config)
+        self.rank, self.world_size, self.is_rank0 = dist_lib.rank(), dist_lib.world_size(), dist_lib.rank0()
+        self.on_cuda = getattr(self.device, "type", "cpu") == "cuda"
+        self.keeper = CheckpointKeeper(location=s.checkpoint_dir, keep_last_k=s.keep_last_k,
+                                       background=s.checkpoint_async, is_rank0=self.is_rank0,
+                                       world_size=self.world_size, emit=self.emit, has_all_rank_hooks=all_rank_hooks)
+        self.scaler = make_scaler(s.amp_mode)
+        self.cfg_json = config_lib.as_dict(config_json if config_json is not None else train_cfg)
         self.ctx: Dict[str, Any] = {
-            "device": self.device, "rank": self.rank, "world_size": self.world_size,
-            "autocast": self._autocast_factory, "scaler": self.scaler, "config": self.cfg_json,
-            "config_json": self.cfg_json, "train_cfg": train_config, "model": self.model,
-            "evacuation_requested": False, "resume_mode": self.resume_mode, "auto_resume_selected": False,
+            "device": self.device, "rank": self.rank, "world_size": self.world_size, "autocast": self.autocast,
+            "scaler": self.scaler, "config": self.cfg_json, "config_json": self.cfg_json, "train_cfg": train_cfg,
+            "model": self.model, "evacuation_requested": False, "resume_mode": self.resume_mode,
+            "auto_resume_selected": False,
         }
         self.ema: Optional[EMA] = None
-        self.ema_dual: list[EMA] = []
-        self._ema_fused_this_step = False
+        self.ema_dual: List[EMA] = []
+        self._ema_in_optimizer = False
         self.final_ckpt: Optional[Dict[str, Any]] = checkpoint_dict
-        self.gpu_health = BackgroundGpuHealth(device=self.device, out_dir=self.settings.out_dir, rank=self.rank,
-                                              world_size=self.world_size)
-        self._events: Optional[tuple] = None
+        self.health = BackgroundGpuHealth(device=self.device, out_dir=s.out_dir, rank=self.rank,
+                                          world_size=self.world_size)
+        self.profiler = _Profiler(s, self.on_cuda, self.device)
+        self.gate = GradientGate(max_norm=s.grad_clip_norm, check_every=s.nonfinite_grad_check_every,
+                                 scaler=self.scaler, profile=lambda key, thunk: thunk())
+        self.micro_steps = _MicroSteps(self)
+        self.stops = _StopControl(self)
+        self.oom = _OomGuard(self, oom_lib.OomRecoverySettings.from_cfg(train_cfg))
 
-    # ------------------------------------------------------------------ helpers
-    def _autocast_factory(self):
+    # ------------------------------------------------------------------ shared helpers
+    def emit(self, event: str, *args, suppress_exceptions: bool = True, **kwargs) -> None:
+        hooks_lib.emit(self.hooks, event, *args, suppress_exceptions=suppress_exceptions, **kwargs)
+
+    def autocast(self):
         return autocast_context(self.settings.amp_mode, self.device)
 
-    def _step_ctx(self, step: int) -> Dict[str, Any]:
+    def step_ctx(self, step: int) -> Dict[str, Any]:
         return {**self.ctx, "step": step, "optimizer": self.optimizer, "ema": self.ema}
 
-    def _module_for_state(self) -> nn.Module:
+    def unwrapped(self) -> nn.Module:
         return getattr(self.model, "module", self.model)
 
-    def _on_cuda(self) -> bool:
-        return getattr(self.device, "type", "cpu") == "cuda"
+    def checkpoint(self, step: int, *, next_step: int, metrics=None, gather_rng: bool = False, announce: bool = True,
+                   background: bool = False) -> Tuple[str, Dict[str, Any]]:
+        """Every rank collects the checkpoint; rank 0 publishes it. Returns (path, dict) on every rank."""
 
-    # ------------------------------------------------------------------ setup stages
-    def _shard_datasets(self) -> None:
+        ckpt = self.keeper.collect(step=step, next_step=next_step, module=self.unwrapped(), optimizer=self.optimizer,
+                                   scheduler=self.scheduler, scaler=self.scaler, config=self.cfg_json, ema=self.ema,
+                                   dual=self.ema_dual, oom_skipped=self.oom.skipped, metrics=metrics,
+                                   gather_rng=gather_rng)
+        if not self.is_rank0:
+            return self.keeper.path_of(step), ckpt
+        tell = (lambda path: self.emit("on_checkpoint", path, ckpt, self.step_ctx(step))) if announce else None
+        return self.keeper.publish(step, ckpt, announce=tell, background=background), ckpt
+
+    def step_scheduler(self) -> None:
+        if self.scheduler is not None and self.settings.scheduler_step_policy == "step":
+            try:
+                self.scheduler.step()
+            except TypeError:
+                pass  # a scheduler that steps on a metric after eval
+
+    # ------------------------------------------------------------------ setup
+    def _shard_inputs(self) -> None:
         s = self.settings
-        mode = _shard_mode(s.shard_dataset_enabled, s.shard_dataset_mode, "shard_dataset")
-        eval_mode = _shard_mode(s.shard_eval_dataset_enabled, s.shard_eval_dataset_mode, "shard_eval_dataset")
-        if s.ddp_enabled and mode is not None:
+        mode = shard_mode(s.shard_dataset_enabled, s.shard_dataset_mode, "shard_dataset")
+        eval_mode = shard_mode(s.shard_eval_dataset_enabled, s.shard_eval_dataset_mode, "shard_eval_dataset")
+        if not s.ddp_enabled:
+            return
+        if mode is not None:
             self.dataset = shard_dataset(self.dataset, rank=self.rank, world_size=self.world_size, mode=mode)
-        if s.ddp_enabled and self.eval_dataset is not None and eval_mode is not None:
+        if self.eval_dataset is not None and eval_mode is not None:
             self.eval_dataset = shard_dataset(self.eval_dataset, rank=self.rank, world_size=self.world_size,
                                               mode=eval_mode)
-        if s.ddp_enabled and s.warn_unsharded and self.is_rank0:
+        if s.warn_unsharded and self.is_rank0:
             warn_if_unsharded(self.dataset, enabled=True, name="train dataset")
             warn_if_unsharded(self.eval_dataset, enabled=True, name="eval dataset")
 
-    @staticmethod
-    def _parse_compile_cfg(compile_cfg: Any) -> tuple:
+    def _compile(self) -> None:
+        """Opt-in ``torch.compile`` of the model before data-parallel wrapping (never on the native hot path)."""
+
+        setting = config_lib.get(self.train_cfg, "compile", None)
+        if not setting:
+            return
         kwargs: Dict[str, Any] = {}
         enabled, preset = True, None
-        if isinstance(compile_cfg, Mapping):
-            enabled = bool(compile_cfg.get("enabled", True))
-            preset = compile_cfg.get("preset", None)
-            kwargs = {k: v for k, v in compile_cfg.items() if k not in ("enabled", "preset")}
-        elif isinstance(compile_cfg, str):
-            preset = compile_cfg
-        elif isinstance(compile_cfg, bool):
-            enabled = compile_cfg
-        return enabled, (str(preset) if preset is not None else None), kwargs
-
-    def _apply_compile(self) -> None:
-        """Optional ``torch.compile`` of the model, before data-parallel wrapping (opt-in only)."""
-
-        compile_cfg = config_lib.get(self.train_cfg, "compile", None)
-        if not compile_cfg:
-            return
-        enabled, preset, kwargs = self._parse_compile_cfg(compile_cfg)
+        if isinstance(setting, Mapping):
+            enabled, preset = bool(setting.get("enabled", True)), setting.get("preset")
+            kwargs = {k: v for k, v in setting.items() if k not in ("enabled", "preset")}
+        elif isinstance(setting, str):
+            preset = setting
+        elif isinstance(setting, bool):
+            enabled = setting
         if not enabled:
             return
+        preset = None if preset is None else str(preset)
         if preset is not None:
-            kwargs.setdefault("mode", "max-autotune" if preset.lower() in _FULL else preset)
-        wraps_only = preset is not None and preset.lower() in _WRAPS_ONLY
-        disabled, unwrapped = [], []
+            kwargs.setdefault("mode", "max-autotune" if preset.lower() in _COMPILE_FULL else preset)
+        wraps_only = preset is not None and preset.lower() in _COMPILE_WRAPS_ONLY
+        undo: List[Callable[[], None]] = []
+        was_enabled = flags_lib.get_compile_wrap_enabled()
         if wraps_only:
-            disabled = self._disable_non_wrapped_forwards()
-        prev = flags_lib.get_compile_wrap_enabled()
-        if not wraps_only:
+            undo += self._dynamo_skip_unwrapped()
+        else:
             flags_lib.set_compile_wrap_enabled(False)
-            unwrapped = self._unwrap_compile_wrap_methods()
+            undo += self._strip_compile_wraps()
         try:
             prepare_compile_backend()
             self.model = torch.compile(self.model, **kwargs)
             self.ctx["model"] = self.model
         except Exception as exc:
-            for mod, fwd in disabled:
-                mod.forward = fwd
-            for cls, desc in unwrapped:
-                setattr(cls, "forward", desc)
-            flags_lib.set_compile_wrap_enabled(prev)
+            for restore in undo:
+                restore()
+            flags_lib.set_compile_wrap_enabled(was_enabled)
             if self.is_rank0:
                 warnings.warn(f"torch.compile failed; falling back to eager: {exc}", RuntimeWarning)
 
-    def _disable_non_wrapped_forwards(self) -> list:
-        out = []
+    def _dynamo_skip_unwrapped(self) -> List[Callable[[], None]]:
+        undo: List[Callable[[], None]] = []
 
-        def visit(mod: nn.Module, inside: bool) -> None:
-            now = inside or isinstance(getattr(type(mod), "forward", None), flags_lib.compile_wrap)
-            if mod is not self.model and not now:
-                fwd = mod.forward
-                mod.forward = torch._dynamo.disable(mod.forward)
-                out.append((mod, fwd))
-            for child in mod.children():
-                visit(child, now)
+        def walk(module: nn.Module, covered: bool) -> None:
+            covered = covered or isinstance(getattr(type(module), "forward", None), flags_lib.compile_wrap)
+            if module is not self.model and not covered:
+                original = module.forward
+                module.forward = torch._dynamo.disable(module.forward)
+                undo.append(lambda m=module, f=original: setattr(m, "forward", f))
+            for child in module.children():
+                walk(child, covered)
 
-        visit(self.model, False)
-        return out
+        walk(self.model, False)
+        return undo
 
-    def _unwrap_compile_wrap_methods(self) -> list:
-        changed, seen = [], set()
-        for mod in self.model.modules():
-            cls = type(mod)
-            if cls in seen:
-                continue
-            seen.add(cls)
-            desc = getattr(cls, "forward", None)
-            if isinstance(desc, flags_lib.compile_wrap):
-                setattr(cls, "forward", desc.function)
-                changed.append((cls, desc))
-        return changed
+    def _strip_compile_wraps(self) -> List[Callable[[], None]]:
+        undo: List[Callable[[], None]] = []
+        for cls in {type(m) for m in self.model.modules()}:
+            wrapped = getattr(cls, "forward", None)
+            if isinstance(wrapped, flags_lib.compile_wrap):
+                setattr(cls, "forward", wrapped.function)
+                undo.append(lambda c=cls, w=wrapped: setattr(c, "forward", w))
+        return undo
 
-    def _wrap_ddp(self) -> None:
-        if not (self.settings.ddp_enabled and self.world_size > 1):
+    def _wrap_data_parallel(self) -> None:
+        s = self.settings
+        if not (s.ddp_enabled and self.world_size > 1):
             return
         assert dist_lib.is_initialized()
-        s = self.settings
-        if self._on_cuda() and str(torch.distributed.get_backend()).lower() == "nccl":
+        if self.on_cuda and str(torch.distributed.get_backend()).lower() == "nccl":
             from .parallel.ddp import DataParallel
 
-            caps = ([float(s.ddp_bucket_cap_mb)] if s.ddp_bucket_cap_mb is not None else
-                    [float(c) for c in s.ddp_bucket_cap_mb_list] if s.ddp_bucket_cap_mb_list else [25.0])
             owners, shard_rest = {}, False
             commit = getattr(self.optimizer, "kb_commit_gradient_plan", None)
-            if str(s.comm_transport).lower() in ("fused", "p2p") and callable(commit):
+            if s.comm_transport.lower() in ("fused", "p2p") and callable(commit):
                 owners, shard_rest = commit(self.world_size)
-            self.model = DataParallel(self.model, bucket_cap_mb=caps, broadcast_buffers=s.ddp_broadcast_buffers,
-                                      transport=s.comm_transport, find_unused_parameters=s.find_unused_parameters,
-                                      owners=owners, shard_rest=shard_rest)
+            self.model = DataParallel(self.model, bucket_cap_mb=s.bucket_caps_mb(),
+                                      broadcast_buffers=s.ddp_broadcast_buffers, transport=s.comm_transport,
+                                      find_unused_parameters=s.find_unused_parameters, owners=owners,
+                                      shard_rest=shard_rest)
             if isinstance(self.scaler, FusedGradScaler) and self.model.transport == "fused":
                 scaler = self.scaler
                 self.model.grad_scale_fn = lambda: scaler._scale
@@ -589,786 +581,305 @@ class _TrainLoop:
                 kw["bucket_cap_mb"] = s.ddp_bucket_cap_mb
             if s.ddp_bucket_cap_mb_list is not None:
                 kw["bucket_cap_mb_list"] = list(s.ddp_bucket_cap_mb_list)
-            if self._on_cuda():
+            if self.on_cuda:
                 kw["device_ids"] = [torch.cuda.current_device()]
             self.model = DistributedDataParallel(self.model, **kw)
         self.ctx["model"] = self.model
 
-    # ------------------------------------------------------------------ resume
-    def _resume_from_checkpoint(self) -> int:
-        ckpt = self.checkpoint_dict
-        if not (ckpt and isinstance(ckpt, dict)):
-            return 0
-        sd = ckpt.get("model")
-        if sd is not None:
-            self.model.load_state_dict(checkpoint_lib.match_state_dict_to_model(self.model, sd), strict=True)
-        for key, target, label in (("optimizer", self.optimizer, "optimizer"),
-                                   ("scheduler", self.scheduler, "scheduler")):
-            state = ckpt.get(key)
-            if target is not None and state is not None:
-                try:
-                    target.load_state_dict(state)
-                except (ValueError, RuntimeError, KeyError) as exc:
-                    warnings.warn(f"Failed to restore {label} state from checkpoint: {exc}", RuntimeWarning)
-        sc = ckpt.get("scaler")
-        if sc is not None and isinstance(self.scaler, GradScaler):
-            try:
-                self.scaler.load_state_dict(sc)
-            except (ValueError, RuntimeError, KeyError) as exc:
-                warnings.warn(f"Failed to restore grad-scaler state from checkpoint: {exc}", RuntimeWarning)
-        self._restore_ema(ckpt.get("ema"), ckpt.get("ema_dual"))
-        rng = ckpt.get("rng")
-        if isinstance(rng, Mapping) and "per_rank" in rng:
-            states = rng.get("per_rank")
-            if isinstance(states, Sequence) and self.rank < len(states):
-                rng = states[self.rank]
-        if isinstance(rng, Mapping):
-            try:
-                set_rng_state(dict(rng))
-            except (RuntimeError, TypeError, ValueError, KeyError) as exc:
-                warnings.warn(f"Failed to restore RNG state from checkpoint: {exc}", RuntimeWarning)
-        try:
-            if "next_step" in ckpt:
-                return int(ckpt["next_step"])
-            saved = int(ckpt.get("step", 0))
-            conf = ckpt.get("config", {})
-            max_steps = int(conf.get("train", conf).get("max_steps", -1))
-            # Old terminal checkpoints stored the completed count; periodic ones the last index.
-            return saved if saved == max_steps else saved + 1
-        except (AttributeError, TypeError, ValueError):
-            return 0
-
-    def _load_auto_resume(self) -> Optional[str]:
+    def _pick_resume(self) -> Optional[str]:
         if self.resume_mode != "auto":
             return None
         if self.checkpoint_dict is not None:
-            if self.auto_resume_path is not None:
-                self.ctx["auto_resume_selected"] = True
-                return self.auto_resume_path
+            if self.auto_resume_path is None:
+                return None
+            self.ctx["auto_resume_selected"] = True
+            return self.auto_resume_path
+        found = checkpoint_lib.resolve_auto_resume(self.keeper.store)
+        if found is None:
             return None
-        sel = checkpoint_lib.resolve_auto_resume(self.checkpoint_store)
-        if sel is None:
-            return None
-        path, self.checkpoint_dict = sel
+        path, self.checkpoint_dict = found
         self.ctx["auto_resume_selected"] = True
         return path
 
-    def _restore_one_ema(self, state: Mapping[str, Any], *, fallback_profile: str, fallback_gamma) -> EMA:
-        ref = self._module_for_state()
-        s = self.ema_settings
-        decay = float(state.get("decay", s.target_decay or 0.999))
-        prof = str(state.get("profile", fallback_profile)).lower()
-        gamma = state.get("gamma", fallback_gamma)
-        ema = EMA(ref, decay=decay, profile=prof, gamma=gamma, update_every=s.update_every,
-                  offload_to_cpu=s.offload_to_cpu, pin_memory=s.pin_memory,
-                  compensate_update_every=s.compensate_update_every)
-        shadow = state.get("shadow", {})
-        try:
-            mapped = checkpoint_lib.match_state_dict_to_model(ref, shadow)
-        except (TypeError, AttributeError):
-            mapped = shadow
-        ema.load_state_dict({
-            "decay": decay, "profile": prof, "gamma": gamma, "shadow": mapped,
-            "num_updates": state.get("num_updates", 0),
-            "step_counter": state.get("step_counter", state.get("num_updates", 0)),
-            "update_every": state.get("update_every", s.update_every),
-            "compensate_update_every": state.get("compensate_update_every", s.compensate_update_every),
-        })
-        return ema
+    def _resume(self) -> int:
+        ckpt = self.checkpoint_dict
+        if not (ckpt and isinstance(ckpt, dict)):
+            return 0
+        start = restore_training_state(ckpt, model=self.model, optimizer=self.optimizer, scheduler=self.scheduler,
+                                       scaler=self.scaler, rank=self.rank)
+        self.ema, self.ema_dual = restore_ema(self.unwrapped(), self.ema_settings, ckpt.get("ema"),
+                                              ckpt.get("ema_dual"))
+        return start
 
-    def _restore_ema(self, ema_ckpt, dual_ckpt=None) -> None:
-        ref = self._module_for_state()
-        s = self.ema_settings
-        if ema_ckpt is not None:
-            try:
-                self.ema = self._restore_one_ema(ema_ckpt, fallback_profile=s.profile, fallback_gamma=s.gamma)
-            except (TypeError, ValueError, RuntimeError) as exc:
-                warnings.warn(f"Failed to restore EMA from checkpoint: {exc}", RuntimeWarning)
-                self.ema = None
-        elif s.enabled:
-            self.ema = s.build(ref)
-        self.ema_dual = []
-        if isinstance(dual_ckpt, Sequence) and not isinstance(dual_ckpt, (str, bytes)):
-            for i, st in enumerate(dual_ckpt):
-                if not isinstance(st, Mapping):
-                    continue
-                try:
-                    self.ema_dual.append(self._restore_one_ema(
-                        st, fallback_profile="power", fallback_gamma=s.dual.gamma1 if i == 0 else s.dual.gamma2))
-                except (TypeError, ValueError, RuntimeError) as exc:
-                    warnings.warn(f"Failed to restore dual EMA #{i} from checkpoint: {exc}", RuntimeWarning)
-        elif s.dual.enabled:
-            self.ema_dual = s.build_dual(ref)
-
-    # ------------------------------------------------------------------ checkpoints
-    def _optimizer_state(self) -> Dict[str, Any]:
-        gather = getattr(self.optimizer, "gathered_state_dict", None)
-        return gather() if callable(gather) else self.optimizer.state_dict()
-
-    def _build_checkpoint(self, step: int, *, next_step: Optional[int] = None,
-                          metrics: Optional[Dict[str, Any]] = None) -> Dict[str, Any]:
-        module = self._module_for_state()
-        try:
-            rng: Any = get_rng_state()
-            if (self._gather_checkpoint_rng and torch.distributed.is_available() and torch.distributed.is_initialized()
-                    and self.world_size > 1):
-                gathered: list = [None] * self.world_size
-                torch.distributed.all_gather_object(gathered, rng)
-                rng = {"per_rank": gathered}
-        except RuntimeError:
-            if self._gather_checkpoint_rng:
-                raise
-            rng = None
-        ckpt: Dict[str, Any] = {
-            "step": step,
-            "next_step": step + 1 if next_step is None else int(next_step),
-            "model": module.state_dict(),
-            "optimizer": self._optimizer_state(),
-            "scheduler": self.scheduler.state_dict() if self.scheduler is not None else None,
-            "scaler": self.scaler.state_dict() if isinstance(self.scaler, GradScaler) else None,
-            "config": self.cfg_json,
-            "rng": rng,
-            "wall_time": time.time(),
-            "metrics": dict(metrics or {}),
-        }
-        if self.ema is not None:
-            ckpt["ema"] = self.ema.state_dict()
-        if self.ema_dual:
-            ckpt["ema_dual"] = [e.state_dict() for e in self.ema_dual]
-        skipped = sorted(s for s in self.oom_skipped_steps if s < ckpt["next_step"])
-        if skipped:
-            ckpt["oom_skipped_steps"] = skipped
-        return ckpt
-
-    def _save_checkpoint(self, step: int, *, next_step: Optional[int] = None, metrics=None, emit_hook: bool = True,
-                         background: bool = False) -> tuple:
-        ckpt = self._build_checkpoint(step, next_step=next_step, metrics=metrics)
-        os.makedirs(self.settings.out_dir, exist_ok=True)
-        name = f"step{step:09d}.pt"
-        data = checkpoint_lib.serialize(ckpt)
-        self._drain_checkpoint()
-        if background and self.checkpoint_publisher is not None:
-            return self.checkpoint_publisher.submit(name, data, (ckpt, step, emit_hook)), ckpt
-        path = checkpoint_lib.publish(self.checkpoint_store, name, data, keep_last_k=self.settings.keep_last_k)
-        if emit_hook:
-            _emit(self.hooks, "on_checkpoint", path, ckpt, self._step_ctx(step))
-        return path, ckpt
-
-    def _announce(self, finished) -> None:
-        if finished is None:
-            return
-        path, (ckpt, step, emit_hook) = finished
-        if emit_hook:
-            _emit(self.hooks, "on_checkpoint", path, ckpt, self._step_ctx(step))
-
-    def _checkpoint_all_ranks(self, path: str, ckpt: Dict[str, Any], step: int) -> None:
-        if not self.hooks or not self.hooks.get("on_checkpoint_all_ranks"):
-            return
-        dist_lib.barrier()
-        _emit(self.hooks, "on_checkpoint_all_ranks", path, ckpt, self._step_ctx(step), suppress_exceptions=False)
-        dist_lib.barrier()
-
-    def _poll_checkpoint(self) -> None:
-        if self.checkpoint_publisher is not None:
-            self._announce(self.checkpoint_publisher.poll())
-
-    def _drain_checkpoint(self) -> None:
-        if self.checkpoint_publisher is not None:
-            self._announce(self.checkpoint_publisher.wait())
-
-    # ------------------------------------------------------------------ inner loop
-    def _make_iterator(self) -> Iterator[Any]:
-        if self._on_cuda() and self.settings.prefetch_batches > 0:
-            return prefetch(iter(self.dataset), self.device, prefetch=self.settings.prefetch_batches,
-                            prepare_fn=self.prepare_batch_fn, threaded=self.settings.prefetch_threaded,
-                            pipeline=self.settings.prefetch_pipeline)
+    def _batches(self) -> Iterator[Any]:
+        s = self.settings
+        if self.on_cuda and s.prefetch_batches > 0:
+            return prefetch(iter(self.dataset), self.device, prefetch=s.prefetch_batches,
+                            prepare_fn=self.prepare_batch_fn, threaded=s.prefetch_threaded,
+                            pipeline=s.prefetch_pipeline)
         return iter(self.dataset)
 
-    def _profile_sync(self) -> None:
-        if self.settings.profile_step_timing and self.settings.profile_step_cuda_sync and self._on_cuda():
-            torch.cuda.synchronize(self.device)
+    # ------------------------------------------------------------------ one update
+    def _update_parameters(self, step: int, rec: _StepRecord) -> None:
+        prof, t = self.profiler, rec.timings
 
-    def _profile_start(self, phase: Optional[str] = None) -> float:
-        self._profile_sync()
-        if self.settings.profile_nvtx and phase is not None and self._on_cuda():
-            torch.cuda.nvtx.range_push(f"koochak/{phase}")
-            self._nvtx_open += 1
-        return time.perf_counter()
+        def wait_for_ema_snapshots() -> None:
+            for e in ([self.ema] if self.ema is not None else []) + self.ema_dual:
+                e.wait_before_param_mutation()
 
-    def _profile_add(self, totals: Dict[str, float], key: str, start: float) -> float:
-        self._profile_sync()
-        if self._nvtx_open:
-            torch.cuda.nvtx.range_pop()
-            self._nvtx_open -= 1
-        elapsed = time.perf_counter() - start
-        if self.settings.profile_step_timing:
-            totals[key] = totals.get(key, 0.0) + elapsed
-        return elapsed
+        prof.run(t, "profile_loop_ema_wait_time_s", wait_for_ema_snapshots)
+        self._hand_ema_to_optimizer(step)
+        prof.run(t, "profile_loop_optimizer_step_time_s", lambda: self.scaler.step(self.optimizer))
+        prof.run(t, "profile_loop_scaler_update_time_s", self.scaler.update)
+        prof.run(t, "profile_loop_ema_update_time_s", lambda: self._update_ema(step))
+        prof.run(t, "profile_loop_scheduler_time_s", self.step_scheduler)
 
-    def _run_micro_steps(self, step: int, it: Iterator[Any], *, collect_rank_timing: bool) -> _MicroStats:
-        stats = _MicroStats()
-        autocast_factory = self.ctx.get("autocast")
-        use_prefetch = self._on_cuda() and self.settings.prefetch_batches > 0
-        n = self.settings.grad_accum
-        for micro in range(n):
-            sync_cm = self.model.no_sync() if (hasattr(self.model, "no_sync") and micro < n - 1) else nullcontext()
-            ac = autocast_factory() if (callable(autocast_factory) and not self.settings.autocast_in_step_fn) \
-                else nullcontext()
-            with sync_cm, ac:
-                self._micro_position = (micro, "fetch")
-                t0 = self._profile_start("batch_wait")
-                batch = next(it) if use_prefetch else to_device(next(it), self.device)
-                stats.batch_wait_s += self._profile_add(stats.profile_timing_totals, "profile_loop_batch_wait_time_s",
-                                                        t0)
-                for k, v in _skip_counts(batch).items():
-                    stats.skip_count_totals[k] = stats.skip_count_totals.get(k, 0.0) + float(v)
-                self._micro_position = (micro, "step_fn")
-                t0 = self._profile_start("step_fn")
-                out = self.step_fn(self.model, batch, self._step_ctx(step))
-                self._profile_add(stats.profile_timing_totals, "profile_loop_step_fn_time_s", t0)
-                if collect_rank_timing and isinstance(out, Mapping):
-                    for key in self.settings.rank_timing_extra_keys:
-                        v = out.get(key)
-                        if v is None:
-                            continue
-                        if isinstance(v, torch.Tensor):
-                            v = float(v.detach())
-                        stats.extra_timing_totals[key] = stats.extra_timing_totals.get(key, 0.0) + float(v)
-                if not isinstance(out, Mapping) or "loss" not in out:
-                    raise RuntimeError("step_fn must return a dict containing a 'loss' Tensor")
-                if not isinstance(out["loss"], torch.Tensor):
-                    raise RuntimeError("step_fn returned a 'loss' that is not a torch.Tensor")
-                loss = out["loss"] / n
-            self._micro_position = (micro, "backward")
-            t0 = self._profile_start("backward")
-            self.scaler.scale(loss).backward()
-            self._profile_add(stats.profile_timing_totals, "profile_loop_backward_time_s", t0)
-            d = loss.detach()
-            stats.total_loss = d if stats.total_loss is None else stats.total_loss + d
-            if self.settings.scalarize_loss_every_step:
-                stats.total_loss_scalar = float(stats.total_loss)
-            stats.out = out
-        return stats
+    def _hand_ema_to_optimizer(self, step: int) -> None:
+        """Let a fused single-process optimizer apply this step's EMA update inside its own kernels."""
 
-    def _nonfinite_names(self) -> list:
-        bad = []
-        for name, p in self.model.named_parameters():
-            if p.grad is not None and torch.is_floating_point(p.grad) and not torch.isfinite(p.grad).all():
-                bad.append(name)
-        return bad
-
-    def _check_nonfinite_grads(self, step: int) -> None:
-        every = self.settings.nonfinite_grad_check_every
-        if every <= 0 or step % every != 0:
+        self._ema_in_optimizer = False
+        if self.ema is None or self.ema_dual or isinstance(self.scaler, GradScaler) or not self.ema.fusable():
             return
-        bad = self._nonfinite_names()
-        if bad:
-            raise FloatingPointError("Gradient entries contain NaN or infinity; optimizer step stopped: "
-                                     + ", ".join(bad))
-
-    def _native_grads(self) -> Optional[list]:
-        if not self._on_cuda():
-            return None
-        grads = []
-        for p in self.model.parameters():
-            if p.grad is None:
-                continue
-            g = p.grad
-            if not (g.is_cuda and g.dtype == torch.float32 and g.is_contiguous() and g.layout == torch.strided):
-                return None
-            grads.append(g)
-        if not grads:
-            return None
-        from .ops._ext import available
-
-        return grads if available() else None
-
-    def _gradient_gate(self, step: int, stats: _MicroStats) -> None:
-        """Unscale -> optional finite check -> optional clip (reference: koochak/loop.py:1612-1637)."""
-
-        s = self.settings
-        clip = s.grad_clip_norm is not None
-        grads = self._native_grads()
-        fused_opt = bool(getattr(self.optimizer, "kb_fused", False)) or bool(
-            getattr(getattr(self.optimizer, "inner", None), "kb_fused", False))
-
-        t0 = self._profile_start("unscale")
-        gate_stats = None
-        dp = self.model if getattr(self.model, "fused_gate_available", None) is not None else None
-        if dp is not None and grads is not None and dp.fused_gate_available():
-            # The fused all-reduce already averaged, unscaled and measured the
-            # gradients: the gate is one small kernel and one host read.
-            gate_stats = dp.fused_gate(s.grad_clip_norm)
-            if isinstance(self.scaler, FusedGradScaler):
-                self.scaler.mark_unscaled(self.optimizer, gate_stats)
-        elif isinstance(self.scaler, FusedGradScaler) and grads is not None:
-            self.scaler.unscale_(self.optimizer, max_norm=s.grad_clip_norm)
-            gate_stats = self.scaler.last_stats
-        elif isinstance(self.scaler, GradScaler):
-            self.scaler.unscale_(self.optimizer)
-        self._profile_add(stats.profile_timing_totals, "profile_loop_unscale_time_s", t0)
-
-        t0 = self._profile_start("nonfinite_grad_check")
-        self._check_nonfinite_grads(step)
-        self._profile_add(stats.profile_timing_totals, "profile_loop_nonfinite_grad_check_time_s", t0)
-
-        t0 = self._profile_start("grad_clip")
-        if clip:
-            if grads is None:
-                clipping = clip_grad_norm_(self.model.parameters(), float(s.grad_clip_norm))
-            elif gate_stats is not None:
-                clipping = self._clip_from_stats(gate_stats, grads, fused_opt)
-            else:
-                res = fused_grad_gate(grads, max_norm=float(s.grad_clip_norm), check_finite=True)
-                clipping = res.stats
-                if res.coef_tensor is not None:
-                    self._apply_coef(res.coef_tensor, grads, fused_opt)
-            if isinstance(clipping, GradientClipStats):
-                if stats.out is None:
-                    stats.out = {}
-                stats.out.update(grad_norm=clipping.norm, grad_clip_coefficient=clipping.coefficient,
-                                 grad_clip_scaled_norm=int(clipping.used_scaled_norm))
-        self._profile_add(stats.profile_timing_totals, "profile_loop_grad_clip_time_s", t0)
-
-    @staticmethod
-    def _raise_if_comm_failed(gate_stats: torch.Tensor) -> None:
-        if float(gate_stats[3]) != 0.0:
-            from .ops._ext import check_status
-
-            check_status(int(gate_stats.device.index or 0))
-            raise RuntimeError(f"gradient all-reduce reported device status {int(float(gate_stats[3]))}")
-
-    def _apply_coef(self, coef: torch.Tensor, grads: list, fused_opt: bool) -> None:
-        if fused_opt:
-            self.optimizer.kb_grad_scale = coef
-        else:
-            torch._foreach_mul_(grads, coef)
-
-    def _clip_from_stats(self, out: torch.Tensor, grads: list, fused_opt: bool) -> GradientClipStats:
-        vals = out.tolist()
-        norm, coef, bad = (float(v) for v in vals[:3])
-        if len(vals) > 3 and vals[3] != 0.0:
-            self._raise_if_comm_failed(out)
-        if bad or not math.isfinite(norm) or 0.0 < coef < torch.finfo(torch.float32).tiny:
-            # fp16 overflow or huge values: the reference path decides (and raises on inf/nan).
-            return clip_grad_norm_(self.model.parameters(), float(self.settings.grad_clip_norm))
-        self._apply_coef(out[1:2], grads, fused_opt)
-        return GradientClipStats(norm, coef, False)
-
-    def _maybe_fuse_ema(self, step: int) -> None:
-        self._ema_fused_this_step = False
-        if self.ema is None or self.ema_dual or isinstance(self.scaler, GradScaler):
-            return
-        opt = self.optimizer
-        target = opt if getattr(opt, "kb_fused", False) else getattr(opt, "inner", None)
-        if target is None or not getattr(target, "kb_fused", False) or not self.ema.fusable():
+        target = self.optimizer if getattr(self.optimizer, "kb_fused", False) else getattr(self.optimizer, "inner",
+                                                                                           None)
+        if target is None or not getattr(target, "kb_fused", False):
             return
         if self.world_size > 1 and getattr(target, "_distributed", False):
             return
-        s = self.ema_settings
-        decay = None if s.profile == "power" else s.warmed_decay(step)
-        target.kb_ema = self.ema.begin_fused_update(self._module_for_state(), decay)
-        self._ema_fused_this_step = True
+        es = self.ema_settings
+        target.kb_ema = self.ema.begin_fused_update(self.unwrapped(), None if es.profile == "power"
+                                                    else es.warmed_decay(step))
+        self._ema_in_optimizer = True
 
     def _update_ema(self, step: int) -> None:
-        s = self.ema_settings
-        all_ranks = bool(self.hooks and self.hooks.get("on_checkpoint_all_ranks"))
-        if self.ema is None and s.enabled and (self.is_rank0 or all_ranks):
-            self.ema = s.build(self._module_for_state())
-        if not self.ema_dual and s.dual.enabled and (self.is_rank0 or all_ranks):
-            self.ema_dual = s.build_dual(self._module_for_state())
-        module = self._module_for_state()
-        if self.ema is not None and not self._ema_fused_this_step:
-            if s.profile == "power":
+        es = self.ema_settings
+        keeps_ema = self.is_rank0 or self.keeper.all_rank_hooks
+        module = self.unwrapped()
+        if keeps_ema and self.ema is None and es.enabled:
+            self.ema = EmaBuilder(es).single(module)
+        if keeps_ema and not self.ema_dual and es.dual.enabled:
+            self.ema_dual = EmaBuilder(es).pair(module)
+        if self.ema is not None and not self._ema_in_optimizer:
+            if es.profile == "power":
                 self.ema.update(module)
             else:
-                self.ema.update(module, decay=s.warmed_decay(step))
+                self.ema.update(module, decay=es.warmed_decay(step))
         for e in self.ema_dual:
             e.update(module)
-        self._ema_fused_this_step = False
+        self._ema_in_optimizer = False
 
-    def _step_scheduler(self) -> None:
-        if self.scheduler is None or self.settings.scheduler_step_policy != "step":
-            return
-        try:
-            self.scheduler.step()
-        except TypeError:
-            pass  # schedulers that need a metric step after eval
-
-    def _emit_rank_timing(self, step: int, stats: _MicroStats, step_time_s: float) -> None:
-        payload: Dict[str, Any] = {"rank": self.rank, "batch_wait_s": float(stats.batch_wait_s),
-                                   "step_compute_s": float(max(0.0, step_time_s - stats.batch_wait_s)),
-                                   "total_step_s": float(step_time_s)}
-        for k in self.settings.rank_timing_extra_keys:
-            payload[k] = float(stats.extra_timing_totals.get(k, stats.profile_timing_totals.get(k, 0.0)))
-        gathered: list = [None] * self.world_size
-        torch.distributed.all_gather_object(gathered, payload)
-        if self.is_rank0:
-            print(_format_rank_timing([g for g in gathered if isinstance(g, dict)], step,
-                                      self.settings.rank_timing_extra_keys))
-
-    def _build_logs(self, step: int, stats: _MicroStats, step_time_s: float) -> tuple:
-        loss_value: Any = stats.total_loss_scalar
-        if loss_value is None:
-            loss_value = stats.total_loss if stats.total_loss is not None else 0.0
-        minimal: Dict[str, Any] = {"loss": loss_value, "lr": get_lr(self.optimizer), "step_time_s": step_time_s,
-                                   "step": step}
+    def _logs(self, step: int, rec: _StepRecord, seconds: float) -> Tuple[Optional[Dict[str, Any]], Dict[str, Any]]:
+        lr = get_lr(self.optimizer)
+        loss: Any = rec.loss_value if rec.loss_value is not None else (rec.loss if rec.loss is not None else 0.0)
+        minimal: Dict[str, Any] = {"loss": loss, "lr": lr, "step_time_s": seconds, "step": step}
         if not (self.is_rank0 and step % self.settings.log_every == 0):
             return None, minimal
-        loss_scalar = (float(stats.total_loss) if stats.total_loss_scalar is None and stats.total_loss is not None
-                       else float(stats.total_loss_scalar or 0.0))
-        stats.total_loss_scalar = loss_scalar
-        extra = {}
-        for k, v in (stats.out or {}).items():
-            if k == "loss":
-                continue
-            extra[k] = float(v.detach()) if isinstance(v, torch.Tensor) else v
-        prof = {k: float(v) for k, v in stats.profile_timing_totals.items() if k.startswith("profile_loop_")}
-        full = {"loss": loss_scalar, "lr": get_lr(self.optimizer), "step_time_s": step_time_s,
-                **{k: float(v) for k, v in stats.skip_count_totals.items()}, **extra, **prof, "step": step}
+        value = float(rec.loss_value if rec.loss_value is not None else (rec.loss if rec.loss is not None else 0.0))
+        rec.loss_value = value
+        extras = {k: (float(v.detach()) if isinstance(v, torch.Tensor) else v)
+                  for k, v in (rec.out or {}).items() if k != "loss"}
+        profiled = {k: float(v) for k, v in rec.timings.items() if k.startswith("profile_loop_")}
+        full = {"loss": value, "lr": lr, "step_time_s": seconds, **rec.skip_counts, **extras, **profiled, "step": step}
         return full, full
 
-    # ------------------------------------------------------------------ health
-    def _handle_health_failure(self, step: int, failures: list) -> None:
-        self.gpu_health.close()
-        completed = step + 1
-        bad_nodes = self.gpu_health.bad_nodes_from_failures(failures)
-        metrics = {"gpu_health": {"event": "gpu_health_shutdown", "failures": failures, "bad_nodes": bad_nodes,
-                                  "slurm_action": self.gpu_health.slurm_action,
-                                  "slurm_disabled": self.gpu_health.slurm_disabled}}
-        self._gather_checkpoint_rng = True
+    def _rank_timing(self, step: int, rec: _StepRecord, seconds: float) -> None:
+        mine: Dict[str, Any] = {"rank": self.rank, "batch_wait_s": float(rec.batch_wait_s),
+                                "step_compute_s": float(max(0.0, seconds - rec.batch_wait_s)),
+                                "total_step_s": float(seconds)}
+        for key in self.settings.rank_timing_extra_keys:
+            mine[key] = float(rec.extra_timing.get(key, rec.timings.get(key, 0.0)))
+        everyone: list = [None] * self.world_size
+        torch.distributed.all_gather_object(everyone, mine)
+        if self.is_rank0:
+            print(_rank_timing_line([e for e in everyone if isinstance(e, dict)], step,
+                                    self.settings.rank_timing_extra_keys))
+
+    def _one_update(self, step: int, batches: Iterator[Any]) -> bool:
+        if step in self.oom.skipped:
+            return self.oom.replay_skip(step, batches)
+        s, prof = self.settings, self.profiler
+        began = prof.start()
+        timer = self._start_device_timer()
+        prelude: Dict[str, float] = {}
+
+        def reset() -> None:
+            self.model.train()
+            self.optimizer.zero_grad(set_to_none=True)
+
+        prof.run(prelude, "profile_loop_setup_zero_grad_time_s", reset)
+        want_timing = (s.ddp_enabled and self.world_size > 1 and s.rank_timing_every > 0
+                       and step % s.rank_timing_every == 0)
+        oom_rec = None
         try:
-            if self.is_rank0:
-                path, ckpt = self._save_checkpoint(completed, next_step=completed, metrics=metrics, emit_hook=False)
-            else:
-                ckpt = self._build_checkpoint(completed, next_step=completed, metrics=metrics)
-                path = checkpoint_lib.checkpoint_path(self.checkpoint_store, f"step{completed:09d}.pt")
-        finally:
-            self._gather_checkpoint_rng = False
-        self.final_ckpt = ckpt
-        dist_lib.barrier()
-        if self.is_rank0:
-            _emit(self.hooks, "on_checkpoint", path, ckpt, self._step_ctx(completed))
-            summary = self.gpu_health.write_failure_summary(step=completed, failures=failures, checkpoint_path=path)
-            print(f"[gpu-health] FAIL step={step} {summarize_failures_for_stdout(failures)}", flush=True)
-            print(f"[gpu-health] checkpoint={path} summary={summary} slurm_action={self.gpu_health.slurm_action} "
-                  f"bad_nodes={','.join(bad_nodes)}", flush=True)
-        dist_lib.barrier()
-        if self.is_rank0:
-            results = self.gpu_health.perform_slurm_recovery(failures)
-            if results:
-                print(f"[gpu-health] slurm_results={json.dumps(results, sort_keys=True)}", flush=True)
-        elif (os.environ.get("SLURM_JOB_ID") and not self.gpu_health.slurm_disabled
-              and self.gpu_health.slurm_action in {"requeue", "cancel"}):
-            time.sleep(30.0)  # give rank 0 time to mutate the Slurm job before teardown
-        raise SystemExit(self.gpu_health.exit_code)
-
-    def _reconcile_stop_requests(self, step: int) -> None:
-        self.gpu_health.update_step(step)
-        local = self.gpu_health.failures()
-        evacuate, health = self.evacuation.reconcile_requests(bool(local))
-        self.evacuation_requested = evacuate
-        self.ctx["evacuation_requested"] = evacuate
-        if health:
-            gathered = [local]
-            if dist_lib.is_initialized():
-                gathered = [None] * self.world_size
-                torch.distributed.all_gather_object(gathered, local)
-            self._handle_health_failure(step, [f for rank_failures in gathered for f in rank_failures])
-
-    # ------------------------------------------------------------------ OOM
-    def _load_oom_records(self, start_step: int) -> None:
-        steps = sorted(oom_lib.recorded_steps(self.checkpoint_store)) if self.is_rank0 else None
-        if self.world_size > 1 and dist_lib.is_initialized():
-            box = [steps]
-            torch.distributed.broadcast_object_list(box, src=0)
-            steps = box[0]
-        self.oom_skipped_steps = set(steps or ())
-        pending = [s for s in sorted(self.oom_skipped_steps) if start_step <= s < self.settings.max_steps]
-        if pending and self.is_rank0:
-            shown = ", ".join(str(s) for s in pending[:20]) + (", ..." if len(pending) > 20 else "")
-            print(f"[oom] {len(pending)} step(s) recorded as OOM-skipped by earlier attempts will be skipped: {shown}",
-                  flush=True)
-
-    def _oom_record(self, step: int, exc: BaseException) -> Dict[str, Any]:
-        micro, phase = self._micro_position
-        decision = oom_lib.decide(self.oom_recovery, self.oom_skipped_steps, step, distributed=self.world_size > 1,
-                                  during_fetch=phase == "fetch")
-        memory, summary = oom_lib.memory_report(self.device)
-        record = {"v": 1, "step": step, "rank": self.rank, "world_size": self.world_size, "phase": phase,
-                  "micro_step": micro, "grad_accum": self.settings.grad_accum, "action": decision.action,
-                  "reason": decision.reason, "consecutive": decision.consecutive,
-                  "max_consecutive": self.oom_recovery.max_consecutive, "skipped_total": decision.skipped_total,
-                  "error_type": type(exc).__name__, "message": oom_lib.short_message(exc), "memory": memory,
-                  "memory_summary": summary, "wall_time": time.time()}
-        print(oom_lib.format_record(record), flush=True)
-        return record
-
-    def _recover_from_oom(self, step: int, it: Iterator[Any], record: Dict[str, Any]) -> bool:
-        self.optimizer.zero_grad(set_to_none=True)
-        oom_lib.release_memory(self.device)
-        oom_lib.write_record(self.checkpoint_store, record)  # durable before anything that can fail
-        self.oom_skipped_steps.add(step)
-        _emit(self.hooks, "on_oom", record, self._step_ctx(step))
-        if self.world_size > 1:
-            print(f"[oom] rank={self.rank} exiting with code {OOM_RESTART_EXIT_CODE}; resubmit with resume=auto to "
-                  "continue from the last checkpoint", flush=True)
-            raise SystemExit(OOM_RESTART_EXIT_CODE)
-        if record["phase"] != "fetch":
-            if not self._drain_micro_batches(it, self.settings.grad_accum - (int(record["micro_step"]) + 1)):
-                return False
-        self._step_scheduler()
-        if record["action"] == oom_lib.RESTART:
-            self._checkpoint_and_exit_after_oom(step)
-        return self._finish_step(step, {})
-
-    def _replay_oom_skip(self, step: int, it: Iterator[Any]) -> bool:
-        if not self._drain_micro_batches(it, self.settings.grad_accum):
+            rec = self.micro_steps(step, batches, want_rank_timing=want_timing)
+        except StopIteration:
             return False
-        self._step_scheduler()
-        if self.is_rank0:
-            print(f"[oom] step={step} skipped: recorded as OOM by an earlier attempt", flush=True)
-        return self._finish_step(step, {})
+        except self.oom.catches as exc:
+            oom_rec = self.oom.record(step, exc)
+            if oom_rec["action"] == oom_lib.FAIL:
+                raise
+        if oom_rec is not None:
+            return self.oom.recover(step, batches, oom_rec)
+        for k, v in prelude.items():
+            rec.timings[k] = rec.timings.get(k, 0.0) + v
+
+        self.gate.profile = lambda key, thunk: prof.run(rec.timings, key, thunk)
+        clip = self.gate.run(self.model, self.optimizer, step, self.on_cuda)
+        if clip:
+            rec.out = {} if rec.out is None else rec.out
+            rec.out.update(clip)
+        self._update_parameters(step, rec)
+
+        prof.barrier()
+        seconds = time.perf_counter() - began
+        device_ms = self._stop_device_timer(timer)
+        if want_timing:
+            self._rank_timing(step, rec, seconds)
+        mark = prof.start("log_build")
+        full, minimal = self._logs(step, rec, seconds)
+        if device_ms is not None:
+            for d in (minimal, full):
+                if d is not None:
+                    d["step_device_ms"] = device_ms
+        built = prof.stop(rec.timings, "profile_loop_log_build_time_s", mark)
+        if s.profile_step_timing:
+            for d in (minimal, full):
+                if d is not None:
+                    d["profile_loop_log_build_time_s"] = built
+        mark = prof.start("log_emit")
+        ctx = self.step_ctx(step)
+        self.emit("on_update_end", minimal, ctx)
+        if full is not None:
+            self.emit("on_log", full, ctx)
+        self.emit("on_step_end", minimal, ctx)
+        prof.stop(rec.timings, "profile_loop_log_emit_time_s", mark)
+        self.freezer.update()
+        return self.after_update(step, rec.timings)
+
+    def _start_device_timer(self):
+        if not (self.settings.device_timing and self.on_cuda):
+            return None
+        pair = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        pair[0].record()
+        return pair
 
     @staticmethod
-    def _drain_micro_batches(it: Iterator[Any], count: int) -> bool:
-        for _ in range(count):
-            try:
-                next(it)
-            except StopIteration:
-                return False
+    def _stop_device_timer(pair) -> Optional[float]:
+        if pair is None:
+            return None
+        pair[1].record()
+        pair[1].synchronize()
+        return float(pair[0].elapsed_time(pair[1]))
+
+    def after_update(self, step: int, timings: Dict[str, float]) -> bool:
+        """Stop agreement, eval, periodic checkpoint -- after every update (also skipped ones)."""
+
+        s, prof = self.settings, self.profiler
+        prof.run(timings, "profile_loop_health_check_time_s", lambda: self.stops.reconcile(step))
+        prof.run(timings, "profile_loop_eval_time_s", lambda: self._maybe_eval(step))
+        if self.evacuation_requested:
+            return True
+        mark = prof.start("checkpoint")
+        at = step + int(s.intervals_use_completed_steps)
+        terminal_next = s.intervals_use_completed_steps and at == s.max_steps
+        if at > 0 and at % s.ckpt_every == 0 and not terminal_next:
+            path, ckpt = self.checkpoint(at, next_step=step + 1, gather_rng=True, background=s.checkpoint_async)
+            if self.is_rank0:
+                self.final_ckpt = ckpt
+            if not s.checkpoint_async:
+                dist_lib.barrier()  # peers wait until rank 0 has published
+            self.keeper.all_rank_hooks_run(path, ckpt, self.step_ctx(at))
+        self.keeper.poll()
+        prof.stop(timings, "profile_loop_checkpoint_time_s", mark)
         return True
 
-    def _checkpoint_and_exit_after_oom(self, step: int) -> None:
-        completed = step + 1
-        self._gather_checkpoint_rng = True
-        try:
-            path, self.final_ckpt = self._save_checkpoint(completed, next_step=completed, emit_hook=False)
-        finally:
-            self._gather_checkpoint_rng = False
-        _emit(self.hooks, "on_checkpoint", path, self.final_ckpt, self._step_ctx(completed))
-        print(f"[oom] checkpoint={path} next_step={completed}; exiting with code {OOM_RESTART_EXIT_CODE} so a "
-              "resubmit starts with a fresh CUDA allocator", flush=True)
-        raise SystemExit(OOM_RESTART_EXIT_CODE)
-
-    # ------------------------------------------------------------------ eval
-    def _maybe_run_eval(self, step: int) -> None:
-        if self.eval_fn is None or self.eval_dataset is None or self.settings.eval_every <= 0:
+    def _maybe_eval(self, step: int) -> None:
+        s = self.settings
+        if self.eval_fn is None or self.eval_dataset is None or s.eval_every <= 0:
             return
-        at = step + int(self.settings.intervals_use_completed_steps)
-        if at == 0 and not self.settings.eval_at_step_zero:
-            return
-        if at % self.settings.eval_every != 0:
+        at = step + int(s.intervals_use_completed_steps)
+        if (at == 0 and not s.eval_at_step_zero) or at % s.eval_every != 0:
             return
         if self.ema is not None and self.ema_settings.eval_with_ema:
-            metrics = self._eval_with_ema(step)
-        else:
-            metrics = self.eval_fn(self.model, self.eval_dataset, self._step_ctx(step))
-        if self.scheduler is not None and self.settings.scheduler_step_policy == "eval":
-            self.scheduler.step(metrics.get("val_loss", None))
-        if self.is_rank0:
-            _emit(self.hooks, "on_eval_end", metrics, self._step_ctx(step))
-
-    def _eval_with_ema(self, step: int) -> Dict[str, float]:
-        assert self.ema is not None and self.eval_fn is not None
-        module = self._module_for_state()
-        try:
+            module = self.unwrapped()
             self.ema.store(module)
             self.ema.copy_to(module)
-            return self.eval_fn(self.model, self.eval_dataset, self._step_ctx(step))
-        finally:
-            self.ema.restore(module)
+            try:
+                metrics = self.eval_fn(self.model, self.eval_dataset, self.step_ctx(step))
+            finally:
+                self.ema.restore(module)
+        else:
+            metrics = self.eval_fn(self.model, self.eval_dataset, self.step_ctx(step))
+        if self.scheduler is not None and s.scheduler_step_policy == "eval":
+            self.scheduler.step(metrics.get("val_loss", None))
+        if self.is_rank0:
+            self.emit("on_eval_end", metrics, self.step_ctx(step))
 
-    # ------------------------------------------------------------------ orchestration
-    def run(self) -> Dict[str, Any]:
-        it: Optional[Iterator[Any]] = None
+    # ------------------------------------------------------------------ the whole run
+    def execute(self) -> Dict[str, Any]:
+        batches: Optional[Iterator[Any]] = None
         try:
             self.evacuation.install()
             if self.evacuation.already_evacuated:
                 print("[evacuation] run already evacuated; exiting before training", flush=True)
                 raise SystemExit(EVACUATION_EXIT_CODE)
-            self.gpu_health.start()
-            self._shard_datasets()
-            resume_path = self._load_auto_resume()
-            _emit(self.hooks, "on_train_start", self.ctx, suppress_exceptions=False)
-            self._apply_compile()
-            self._wrap_ddp()
+            self.health.start()
+            self._shard_inputs()
+            resume_path = self._pick_resume()
+            self.emit("on_train_start", self.ctx, suppress_exceptions=False)
+            self._compile()
+            self._wrap_data_parallel()
             if self.is_rank0:
-                c = _parameter_counts(self.model)
-                print(f"[training] Model parameters — total: {c['total']:,} | trainable: {c['trainable']:,} | "
-                      f"frozen: {c['frozen']:,}")
-            start = self._resume_from_checkpoint()
-            if self.oom_recovery.enabled:
-                self._load_oom_records(start)
+                total, trainable = _parameter_counts(self.model)
+                print(f"[training] Model parameters — total: {total:,} | trainable: {trainable:,} | "
+                      f"frozen: {total - trainable:,}")
+            start = self._resume()
+            if self.oom.settings.enabled:
+                self.oom.load_records(start)
             if resume_path is not None and self.is_rank0:
-                _emit(self.hooks, "on_resume_checkpoint", resume_path, self.checkpoint_dict, self._step_ctx(start))
-            next_step = start
-            it = self._make_iterator()
-            interrupted = False
+                self.emit("on_resume_checkpoint", resume_path, self.checkpoint_dict, self.step_ctx(start))
+            batches = self._batches()
+            done, stopped = start, False
             for step in range(start, self.settings.max_steps):
-                if not self._run_step(step, it):
+                if not self._one_update(step, batches):
                     break
-                next_step = step + 1
+                done = step + 1
                 if self.evacuation_requested:
-                    interrupted = True
+                    stopped = True
                     break
-            self.gpu_health.close()
-            self._reconcile_stop_requests(next_step - 1)
-            interrupted = interrupted or self.evacuation_requested
-            # Terminal checkpoint: a completed-update cursor (step == next_step).
-            self._gather_checkpoint_rng = True
-            terminal = checkpoint_lib.checkpoint_path(self.checkpoint_store, f"step{next_step:09d}.pt")
-            if self.is_rank0:
-                terminal, self.final_ckpt = self._save_checkpoint(next_step, next_step=next_step, emit_hook=False)
-            else:
-                self.final_ckpt = self._build_checkpoint(next_step, next_step=next_step)
-            self._gather_checkpoint_rng = False
-            if torch.distributed.is_available() and torch.distributed.is_initialized():
-                dist_lib.barrier()
-            if self.is_rank0:
-                _emit(self.hooks, "on_checkpoint", terminal, self.final_ckpt, self._step_ctx(next_step))
-            self._checkpoint_all_ranks(terminal, self.final_ckpt, next_step)
-            if interrupted:
-                if self.is_rank0:
-                    _emit(self.hooks, "on_evacuation", terminal, self.final_ckpt, self._step_ctx(next_step))
-                _emit(self.hooks, "on_train_end", self.ctx)
-                if torch.distributed.is_available() and torch.distributed.is_initialized():
-                    dist_lib.barrier()
-                self.evacuation.mark_evacuated()
-                raise SystemExit(EVACUATION_EXIT_CODE)
-            _emit(self.hooks, "on_train_end", self.ctx)
+            self._finish(done, stopped)
         except Exception as exc:
-            _emit(self.hooks, "on_exception", exc, self.ctx)
+            self.emit("on_exception", exc, self.ctx)
             raise
         finally:
-            close_it = getattr(it, "close", None) if it is not None else None
             with ExitStack() as cleanup:
-                if callable(close_it):
-                    cleanup.callback(close_it)
-                if self.checkpoint_publisher is not None:
-                    cleanup.callback(self.checkpoint_publisher.close)
+                closer = getattr(batches, "close", None)
+                if callable(closer):
+                    cleanup.callback(closer)
+                cleanup.callback(self.keeper.close)
                 cleanup.callback(self.evacuation.uninstall)
-                cleanup.callback(self.gpu_health.close)
+                cleanup.callback(self.health.close)
         assert self.final_ckpt is not None
         return self.final_ckpt
 
-    def _device_timer_start(self) -> None:
-        if self.settings.device_timing and self._on_cuda():
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            start.record()
-            self._events = (start, end)
+    def _finish(self, done: int, stopped: bool) -> None:
+        """Last stop agreement, terminal checkpoint (cursor == step), evacuation exit if asked."""
 
-    def _device_timer_stop(self) -> Optional[float]:
-        if self._events is None:
-            return None
-        start, end = self._events
-        end.record()
-        end.synchronize()
-        self._events = None
-        return float(start.elapsed_time(end))
-
-    def _run_step(self, step: int, it: Iterator[Any]) -> bool:
-        if step in self.oom_skipped_steps:
-            return self._replay_oom_skip(step, it)
-        step_start = self._profile_start()
-        self._device_timer_start()
-        totals: Dict[str, float] = {}
-        t0 = self._profile_start("setup_zero_grad")
-        self.model.train()
-        self.optimizer.zero_grad(set_to_none=True)
-        self._profile_add(totals, "profile_loop_setup_zero_grad_time_s", t0)
-        collect = (self.settings.ddp_enabled and self.world_size > 1 and self.settings.rank_timing_every > 0
-                   and step % self.settings.rank_timing_every == 0)
-        oom = None
-        try:
-            stats = self._run_micro_steps(step, it, collect_rank_timing=collect)
-        except StopIteration:
-            return False
-        except self._oom_errors as exc:
-            oom = self._oom_record(step, exc)
-            if oom["action"] == oom_lib.FAIL:
-                raise
-        if oom is not None:
-            return self._recover_from_oom(step, it, oom)
-        for k, v in totals.items():
-            stats.profile_timing_totals[k] = stats.profile_timing_totals.get(k, 0.0) + v
-
-        self._gradient_gate(step, stats)
-
-        t0 = self._profile_start("ema_wait")
-        if self.ema is not None:
-            self.ema.wait_before_param_mutation()
-        for e in self.ema_dual:
-            e.wait_before_param_mutation()
-        self._profile_add(stats.profile_timing_totals, "profile_loop_ema_wait_time_s", t0)
-
-        self._maybe_fuse_ema(step)
-        t0 = self._profile_start("optimizer_step")
-        self.scaler.step(self.optimizer)
-        self._profile_add(stats.profile_timing_totals, "profile_loop_optimizer_step_time_s", t0)
-        t0 = self._profile_start("scaler_update")
-        self.scaler.update()
-        self._profile_add(stats.profile_timing_totals, "profile_loop_scaler_update_time_s", t0)
-        t0 = self._profile_start("ema_update")
-        self._update_ema(step)
-        self._profile_add(stats.profile_timing_totals, "profile_loop_ema_update_time_s", t0)
-        t0 = self._profile_start("scheduler")
-        self._step_scheduler()
-        self._profile_add(stats.profile_timing_totals, "profile_loop_scheduler_time_s", t0)
-
-        self._profile_sync()
-        step_time_s = time.perf_counter() - step_start
-        device_ms = self._device_timer_stop()
-        if collect:
-            self._emit_rank_timing(step, stats, step_time_s)
-        t0 = self._profile_start("log_build")
-        full, minimal = self._build_logs(step, stats, step_time_s)
-        if device_ms is not None:
-            minimal["step_device_ms"] = device_ms
-            if full is not None:
-                full["step_device_ms"] = device_ms
-        built = self._profile_add(stats.profile_timing_totals, "profile_loop_log_build_time_s", t0)
-        if self.settings.profile_step_timing:
-            if full is not None:
-                full["profile_loop_log_build_time_s"] = built
-            minimal["profile_loop_log_build_time_s"] = built
-        t0 = self._profile_start("log_emit")
-        _emit(self.hooks, "on_update_end", minimal, self._step_ctx(step))
-        if full is not None:
-            _emit(self.hooks, "on_log", full, self._step_ctx(step))
-        _emit(self.hooks, "on_step_end", minimal, self._step_ctx(step))
-        self._profile_add(stats.profile_timing_totals, "profile_loop_log_emit_time_s", t0)
-        self.collector.update()
-        return self._finish_step(step, stats.profile_timing_totals)
-
-    def _finish_step(self, step: int, totals: Dict[str, float]) -> bool:
-        t0 = self._profile_start("health_check")
-        self._reconcile_stop_requests(step)
-        self._profile_add(totals, "profile_loop_health_check_time_s", t0)
-        t0 = self._profile_start("eval")
-        self._maybe_run_eval(step)
-        self._profile_add(totals, "profile_loop_eval_time_s", t0)
-        if self.evacuation_requested:
-            return True
-        t0 = self._profile_start("checkpoint")
-        at = step + int(self.settings.intervals_use_completed_steps)
-        terminal_due = self.settings.intervals_use_completed_steps and at == self.settings.max_steps
-        if at > 0 and at % self.settings.ckpt_every == 0 and not terminal_due:
-            self._gather_checkpoint_rng = True
-            try:
-                if self.is_rank0:
-                    path, ckpt = self._save_checkpoint(at, next_step=step + 1,
-                                                       background=self.settings.checkpoint_async)
-                    self.final_ckpt = ckpt
-                else:
-                    ckpt = self._build_checkpoint(at, next_step=step + 1)
-                    path = checkpoint_lib.checkpoint_path(self.checkpoint_store, f"step{at:09d}.pt")
-            finally:
-                self._gather_checkpoint_rng = False
-            if not self.settings.checkpoint_async:
-                dist_lib.barrier()  # keep peers out of the next step until rank 0 has published
-            self._checkpoint_all_ranks(path, ckpt, at)
-        self._poll_checkpoint()
-        self._profile_add(totals, "profile_loop_checkpoint_time_s", t0)
-        return True
+        self.health.close()
+        self.stops.reconcile(done - 1)
+        stopped = stopped or self.evacuation_requested
+        path, self.final_ckpt = self.checkpoint(done, next_step=done, gather_rng=True, announce=False)
+        if dist_lib.is_initialized():
+            dist_lib.barrier()
+        if self.is_rank0:
+            self.emit("on_checkpoint", path, self.final_ckpt, self.step_ctx(done))
+        self.keeper.all_rank_hooks_run(path, self.final_ckpt, self.step_ctx(done))
+        if stopped:
+            if self.is_rank0:
+                self.emit("on_evacuation", path, self.final_ckpt, self.step_ctx(done))
+            self.emit("on_train_end", self.ctx)
+            if dist_lib.is_initialized():
+                dist_lib.barrier()
+            self.evacuation.mark_evacuated()
+            raise SystemExit(EVACUATION_EXIT_CODE)
+        self.emit("on_train_end", self.ctx)

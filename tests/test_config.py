@@ -1,7 +1,7 @@
 import pytest
 
 from koochak_b200 import config as config_lib
-from koochak_b200.loop import _TrainSettings
+from koochak_b200.runtime.settings import LoopSettings as _TrainSettings
 
 
 def test_load_config_layering(tmp_path):
