@@ -481,6 +481,10 @@ int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
 //   * the first call on each device resolves the array's device address with
 //     cudaGetSymbolAddress (the host-side name of a __device__ array is not a
 //     device address); make that first call before any stream capture.
+//   * the resolved address is remembered per device ordinal for the rest of
+//     the process. It assumes the device is not reset in between: after a
+//     cudaDeviceReset in the same process the remembered address is stale,
+//     so do not use this entry point across a device reset.
 //   * no cudaMalloc, cudaFree or allocating library routine is called.
 //
 // Types: dy bf16 [M, C]; x, w, mean, rstd, dx, dw, db fp32; all contiguous,
@@ -533,18 +537,21 @@ extern "C" __attribute__((visibility("default"))) int kb_layernorm_backward_noal
   const int smem = norm_bwd_smem_bytes(C);
   const bool sacc = norm_bwd_smem_acc(C);
   bool launched = false;
+  cudaError_t setup = cudaSuccess;
   with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
     auto kern = sacc ? norm_bwd_kernel<V, float, __nv_bfloat16, float, false, true>
                      : norm_bwd_kernel<V, float, __nv_bfloat16, float, false, false>;
     if (smem > 48 * 1024) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
+      setup = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (setup != cudaSuccess) return;
     }
     kern<<<(unsigned)grid, 32 * kNormWarps, smem, stream>>>(static_cast<const __nv_bfloat16*>(dy), x, w, mean, rstd,
                                                              nullptr, dx, nullptr, dw_part, db_part, M, C);
     launched = true;
   });
-  if (!launched) return (int)cudaErrorInvalidConfiguration;
+  if (setup != cudaSuccess) return (int)setup;  // the attribute call's own error
+  if (!launched) return (int)cudaErrorInvalidConfiguration;  // no kernel instance for this row width
   err = cudaGetLastError();
   if (err != cudaSuccess) return (int)err;
   column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw, (int)grid, C, 0);

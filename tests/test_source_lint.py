@@ -35,13 +35,33 @@ _BULK = "cp.async." + "bulk"
 _FANOUT = "multi" + "cast"
 
 
+def _joined_literals(code: str) -> str:
+    """Code with adjacent string literals merged ("a" "b" -> "ab"), so a PTX
+    statement split over several literals or lines reads as one."""
+
+    return re.sub(r'"\s*\n?\s*"', "", code)
+
+
 def test_no_cluster_fanout_bulk_copies():
+    # One PTX statement runs to its ';': look for the fan-out qualifier
+    # anywhere between a bulk copy's opcode and that ';', across lines.
+    statement = re.compile(re.escape(_BULK) + r"[^;]*" + _FANOUT, re.S)
     bad = []
     for p in SOURCES:
-        for ln, line in enumerate(_code(p).splitlines(), 1):
-            if _BULK in line and _FANOUT in line:
-                bad.append(f"{p.name}:{ln}: {line.strip()}")
+        code = _joined_literals(_code(p))
+        for m in statement.finditer(code):
+            ln = code.count("\n", 0, m.start()) + 1
+            bad.append(f"{p.name}:{ln}: {m.group(0)[:120]!r}")
     assert not bad, "bulk copies fanned out over a cluster are not allowed:\n" + "\n".join(bad)
+
+
+def test_fanout_lint_sees_split_statements():
+    split = ('asm volatile("' + _BULK + '.tensor.2d.shared::cluster.global"\n'
+             '             ".' + _FANOUT + '::cluster [%0], [%1];");')
+    statement = re.compile(re.escape(_BULK) + r"[^;]*" + _FANOUT, re.S)
+    assert statement.search(_joined_literals(split))
+    allowed = 'asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.' + _FANOUT + '::cluster.b64 [%0];");'
+    assert not statement.search(_joined_literals(allowed))
 
 
 def test_no_batched_memcpy_entry_points():

@@ -4,6 +4,8 @@ The entry point ``kb_layernorm_backward_noalloc`` is called through its
 exported C symbol (ctypes), not through the Python bindings, and its results
 are compared against the regular ``norm_backward`` binding on two calls in a
 row (the second call reuses the shared static scratch left by the first).
+Around the second call the test also checks that PyTorch's allocator served
+no allocation: the entry point takes its scratch from its own static array.
 """
 
 import ctypes
@@ -49,9 +51,13 @@ def test_noalloc_layernorm_backward_matches(M, C):
         dx = torch.full_like(x, float("nan"))
         dw = torch.full((C,), float("nan"), device=dev)
         db = torch.full((C,), float("nan"), device=dev)
-        rc = _call(fn, dy, x, w, mean, rstd, dx, dw, db, M, C)
-        assert rc == 0, f"entry point returned {rc}"
         torch.cuda.synchronize()
+        before = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
+        rc = _call(fn, dy, x, w, mean, rstd, dx, dw, db, M, C)
+        torch.cuda.synchronize()
+        after = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
+        assert rc == 0, f"entry point returned {rc}"
+        assert after == before, f"the call allocated through PyTorch ({after - before} allocations)"
         torch.testing.assert_close(dx, dx_ref, rtol=1e-5, atol=1e-5)
         torch.testing.assert_close(dw, dw_ref, rtol=1e-4, atol=1e-3)
         torch.testing.assert_close(db, db_ref, rtol=1e-4, atol=1e-3)
