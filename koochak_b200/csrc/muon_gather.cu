@@ -76,7 +76,7 @@ __device__ __forceinline__ T* shifted(T* p, long long bytes) {
 template <bool MULTIMEM>
 __global__ void __launch_bounds__(256)
     muon_update_gather_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X, float lr,
-                              float wd, float scale, int transpose) {
+                              float wd, float scale, int transpose, const float* __restrict__ row_scale) {
   const int i = blockIdx.z;
   const int R = mm.R, C = mm.C;
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -112,11 +112,12 @@ __global__ void __launch_bounds__(256)
     float* p = mm.p[i] + idx;
     const float4 old = *reinterpret_cast<const float4*>(p);
     const float decay = 1.f - lr * wd;
+    const float f = row_scale ? row_scale[(long long)i * R + r] : scale;
     float4 pn;
-    pn.x = old.x * decay - lr * (scale * u[0]);
-    pn.y = old.y * decay - lr * (scale * u[1]);
-    pn.z = old.z * decay - lr * (scale * u[2]);
-    pn.w = old.w * decay - lr * (scale * u[3]);
+    pn.x = old.x * decay - lr * (f * u[0]);
+    pn.y = old.y * decay - lr * (f * u[1]);
+    pn.z = old.z * decay - lr * (f * u[2]);
+    pn.w = old.w * decay - lr * (f * u[3]);
     if constexpr (MULTIMEM) {
       mm_st_v4(shifted(p, mm.mc_delta), pn);
     } else {
@@ -144,7 +145,7 @@ constexpr int kGatherFlatPerCta = 256 * kGatherFlatVecs;  // float4 per CTA
 template <bool MULTIMEM>
 __global__ void __launch_bounds__(256)
     muon_update_gather_flat_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X,
-                                   float lr, float wd, float scale) {
+                                   float lr, float wd, float scale, const float* __restrict__ row_scale) {
   const int i = blockIdx.y;
   const long long n4 = (long long)mm.R * mm.C / 4;
   float4* p = reinterpret_cast<float4*>(mm.p[i]);
@@ -168,11 +169,12 @@ __global__ void __launch_bounds__(256)
     if (j < n4) {
       const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&xv[k].x);
       const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&xv[k].y);
+      const float f = row_scale ? row_scale[(long long)i * mm.R + (4 * j) / mm.C] : scale;  // C % 4 == 0
       float4 pn;
-      pn.x = pv[k].x * decay - lr * (scale * __low2float(lo));
-      pn.y = pv[k].y * decay - lr * (scale * __high2float(lo));
-      pn.z = pv[k].z * decay - lr * (scale * __low2float(hi));
-      pn.w = pv[k].w * decay - lr * (scale * __high2float(hi));
+      pn.x = pv[k].x * decay - lr * (f * __low2float(lo));
+      pn.y = pv[k].y * decay - lr * (f * __high2float(lo));
+      pn.z = pv[k].z * decay - lr * (f * __low2float(hi));
+      pn.w = pv[k].w * decay - lr * (f * __high2float(hi));
       if constexpr (MULTIMEM) {
         mm_st_v4(shifted(reinterpret_cast<float*>(p + j), mm.mc_delta), pn);
       } else {
@@ -199,7 +201,8 @@ __global__ void __launch_bounds__(256)
 // bases: every rank's slab base address; mc_base: multicast alias or 0.
 void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor& X,
                         const std::vector<at::Tensor>& shadow, double lr, double wd, double scale, bool transpose,
-                        const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank, int64_t slab_bytes) {
+                        const std::vector<int64_t>& bases, int64_t mc_base, int64_t rank, int64_t slab_bytes,
+                        const c10::optional<at::Tensor>& row_scale) {
   const size_t n = params.size();
   if (n == 0) return;
   const int world = (int)bases.size();
@@ -214,6 +217,13 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
   KB_CHECK(X.scalar_type() == at::kBFloat16 && X.is_contiguous() && X.numel() >= (int64_t)n * R * C,
            "muon_update_gather: X must be contiguous bf16 [n, R*C]");
   KB_CHECK(reinterpret_cast<uintptr_t>(X.data_ptr()) % 8 == 0, "muon_update_gather: X must be 8-byte aligned");
+  const float* rs_all = nullptr;
+  if (row_scale.has_value() && row_scale->defined()) {
+    KB_CHECK(row_scale->scalar_type() == at::kFloat && row_scale->is_contiguous() &&
+                 row_scale->numel() >= (int64_t)n * R,
+             "muon_update_gather: row_scale must be fp32 [n, rows]");
+    rs_all = row_scale->data_ptr<float>();
+  }
   for (int q = 0; q < world; ++q) KB_CHECK(bases[q] != 0 && bases[q] % 16 == 0, "muon_update_gather: bad slab base");
   KB_CHECK(mc_base % 16 == 0, "muon_update_gather: multicast base must be 16-byte aligned");
   for (size_t base = 0; base < n; base += kGatherMats) {
@@ -241,22 +251,24 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
                "muon_update_gather: shadow must be a contiguous 8-byte aligned bf16 copy of the parameter");
     }
     const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(X.data_ptr()) + (int64_t)base * R * C;
+    const float* rs = rs_all ? rs_all + (int64_t)base * R : nullptr;
     if (!transpose) {  // C % 4 == 0, params 16-byte and X / shadows 8-byte aligned (checked above)
       const long long n4 = (long long)R * C / 4;
       dim3 fgrid((unsigned)((n4 + kGatherFlatPerCta - 1) / kGatherFlatPerCta), count);
       if (mc_base != 0) {
-        muon_update_gather_flat_kernel<true><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale);
+        muon_update_gather_flat_kernel<true><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, rs);
       } else {
-        muon_update_gather_flat_kernel<false><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale);
+        muon_update_gather_flat_kernel<false><<<fgrid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, rs);
       }
       KB_LAUNCHED();
       continue;
     }
     dim3 grid((C + 31) / 32, (R + 31) / 32, count);
     if (mc_base != 0) {
-      muon_update_gather_kernel<true><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose);
+      muon_update_gather_kernel<true><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose, rs);
     } else {
-      muon_update_gather_kernel<false><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose);
+      muon_update_gather_kernel<false><<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose,
+                                                           rs);
     }
     KB_LAUNCHED();
   }
@@ -436,7 +448,7 @@ void register_muon_gather_ops(pybind11::module& m) {
         "owner's Muon update written into every rank's parameter copy (P2P or multimem stores)", pybind11::arg("params"),
         pybind11::arg("X"), pybind11::arg("shadow"), pybind11::arg("lr"), pybind11::arg("wd"), pybind11::arg("scale"),
         pybind11::arg("transpose"), pybind11::arg("bases"), pybind11::arg("mc_base"), pybind11::arg("rank"),
-        pybind11::arg("slab_bytes"));
+        pybind11::arg("slab_bytes"), pybind11::arg("row_scale") = pybind11::none());
   m.def("adam_shard_gather", &adam_shard_gather,
         "AdamW on this rank's shard of each tensor, new values written into every rank's copy (P2P or multimem)");
 }

@@ -14,6 +14,8 @@
 //    optional transpose + Frobenius sum of squares; normalisation; parameter
 //    update with weight decay, fused EMA and bf16 shadow).
 //  * ema_update: shadow = d * shadow + (1 - d) * param for a tensor list.
+//  * normuon_row_scale: NorMuon's per-row second moments and update scales.
+//  * hyperball_project: each matrix scaled back to its radius after a step.
 //
 // Tensor lists are passed by value in the kernel parameter block (<= 32 KB)
 // together with a block table, so a call is one launch and no host-to-device
@@ -384,7 +386,7 @@ __global__ void muon_scale_kernel(__nv_bfloat16* __restrict__ X, const float* __
 // p = p * (1 - lr*wd) - lr * scale * U  (U = X or X^T), then EMA and bf16 shadow.
 __global__ void __launch_bounds__(256)
     muon_epilogue_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr, float wd,
-                         float scale, int transpose, float ema_decay) {
+                         float scale, int transpose, float ema_decay, const float* __restrict__ row_scale) {
   const int i = blockIdx.z;
   const int R = mm.R, C = mm.C;
   __shared__ float tile[32][33];
@@ -410,7 +412,8 @@ __global__ void __launch_bounds__(256)
     if (r < R && c < C) {
       const long long idx = (long long)r * C + c;
       const float u = transpose ? tile[tx][ty + 8 * k] : __bfloat162float(x[idx]);
-      const float pn = p[idx] * decay - lr * (scale * u);
+      const float f = row_scale ? row_scale[(long long)i * R + r] : scale;
+      const float pn = p[idx] * decay - lr * (f * u);
       p[idx] = pn;
       if (e) e[idx] = e[idx] * ema_decay + (1.f - ema_decay) * pn;
       if (sh) sh[idx] = __float2bfloat16_rn(pn);
@@ -492,7 +495,7 @@ __global__ void __launch_bounds__(256)
 
 __global__ void __launch_bounds__(256)
     muon_epilogue_flat_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr,
-                              float wd, float scale, float ema_decay) {
+                              float wd, float scale, float ema_decay, const float* __restrict__ row_scale) {
   const int i = blockIdx.y;
   const long long n4 = (long long)mm.R * mm.C / 4;
   float4* p = reinterpret_cast<float4*>(mm.p[i]);
@@ -516,11 +519,13 @@ __global__ void __launch_bounds__(256)
     const long long j = j0 + k * 256;
     if (j < n4) {
       const float4 u = unpack_bf16x4(xv[k]);
+      // C % 4 == 0 on this path, so a float4 never straddles two rows.
+      const float f = row_scale ? row_scale[(long long)i * mm.R + (4 * j) / mm.C] : scale;
       float4 pn;
-      pn.x = pv[k].x * decay - lr * (scale * u.x);
-      pn.y = pv[k].y * decay - lr * (scale * u.y);
-      pn.z = pv[k].z * decay - lr * (scale * u.z);
-      pn.w = pv[k].w * decay - lr * (scale * u.w);
+      pn.x = pv[k].x * decay - lr * (f * u.x);
+      pn.y = pv[k].y * decay - lr * (f * u.y);
+      pn.z = pv[k].z * decay - lr * (f * u.z);
+      pn.w = pv[k].w * decay - lr * (f * u.w);
       p[j] = pn;
       if (e) {
         const float4 ev = e[j];
@@ -600,31 +605,272 @@ void muon_scale(at::Tensor& X, const at::Tensor& sumsq, int64_t n) {
 
 void muon_epilogue(const std::vector<at::Tensor>& params, const at::Tensor& X, const std::vector<at::Tensor>& ema,
                    const std::vector<at::Tensor>& shadow, double lr, double wd, double scale, bool transpose,
-                   double ema_decay) {
+                   double ema_decay, const c10::optional<at::Tensor>& row_scale) {
   const size_t n = params.size();
   if (n == 0) return;
   const c10::cuda::CUDAGuard guard(params[0].device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
   const int R = (int)params[0].size(0);
   const int C = (int)(params[0].numel() / R);
+  const float* rs_all = nullptr;
+  if (row_scale.has_value() && row_scale->defined()) {
+    KB_CHECK(row_scale->scalar_type() == at::kFloat && row_scale->is_contiguous() &&
+                 row_scale->numel() >= (int64_t)n * R,
+             "muon_epilogue: row_scale must be fp32 [n, rows]");
+    rs_all = row_scale->data_ptr<float>();
+  }
   for (size_t base = 0; base < n; base += kMuonMax) {
     const int count = (int)std::min<size_t>(kMuonMax, n - base);
     MuonMats mm = make_mats({}, {}, params, ema, shadow, base, count);
     const __nv_bfloat16* xb = (const __nv_bfloat16*)X.data_ptr() + (int64_t)base * R * C;
+    const float* rs = rs_all ? rs_all + (int64_t)base * R : nullptr;
     bool flat = !transpose && ((int64_t)R * C) % 4 == 0 && aligned(xb, 8);
     for (int j = 0; j < count && flat; ++j)
       flat = aligned(mm.p[j], 16) && aligned(mm.ema[j], 16) && aligned(mm.shadow[j], 8);
     if (flat) {
       const long long n4 = (long long)R * C / 4;
       dim3 grid((unsigned)((n4 + kFlatVecsPerCta - 1) / kFlatVecsPerCta), count);
-      muon_epilogue_flat_kernel<<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, (float)ema_decay);
+      muon_epilogue_flat_kernel<<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, (float)ema_decay,
+                                                     rs);
     } else {
       dim3 grid((C + 31) / 32, (R + 31) / 32, count);
       muon_epilogue_kernel<<<grid, 256, 0, s>>>(mm, xb, (float)lr, (float)wd, (float)scale, transpose ? 1 : 0,
-                                                (float)ema_decay);
+                                                (float)ema_decay, rs);
     }
     KB_LAUNCHED();
   }
+}
+
+// ------------------------------------------------------------ NorMuon
+//
+// NorMuon rescales the orthogonalised update U (rows x cols in the
+// parameter's own orientation; X holds U transposed when rows > cols) row by
+// row (reference koochak/optim/muon.py:56-74):
+//   v_r = mean_c U[r, c]^2,  m2_r <- m2_r + (1 - beta2) (v_r - m2_r)
+//   A   = U / (sqrt(m2_r) + 1e-10),  B = A * |U| / (|A| + 1e-10),
+//   final update = B * sqrt(max(1, rows / cols)).
+// normuon_row_stats: per matrix, the row sums of squares of U.
+// normuon_finish:    per matrix (one CTA), the m2 update and one factor per
+//                    row, 1/(sqrt(m2_r)+1e-10) * |U|/(|A|+1e-10) *
+//                    sqrt(max(1, rows/cols)), which the Muon update kernels
+//                    apply in place of the scalar Muon scale.
+
+// Non-transposed: a warp per row of X (contiguous). Transposed (X = U^T,
+// [cols, rows]): a thread per U row = X column, walking the X rows, so a warp
+// reads 32 consecutive columns of one X row at a time.
+__global__ void __launch_bounds__(256)
+    normuon_row_stats_kernel(const __nv_bfloat16* __restrict__ X, int R, int C, int transpose,
+                             float* __restrict__ rowsq) {
+  const int i = blockIdx.y;
+  const __nv_bfloat16* x = X + (long long)i * R * C;
+  float* out = rowsq + (long long)i * R;
+  if (!transpose) {
+    const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+    for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < R; r += gridDim.x * warps) {
+      const __nv_bfloat16* row = x + (long long)r * C;
+      float acc = 0.f;
+      for (int c = lane; c < C; c += 32) {
+        const float u = __bfloat162float(row[c]);
+        acc += u * u;
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) out[r] = acc;
+    }
+    return;
+  }
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < R; r += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int c = 0; c < C; ++c) {
+      const float u = __bfloat162float(x[(long long)c * R + r]);
+      acc += u * u;
+    }
+    out[r] = acc;
+  }
+}
+
+constexpr int kNormuonThreads = 512;
+
+struct NormuonMoments {
+  float* m[kMuonMax];  // each matrix's second-moment buffer (R values)
+};
+
+__global__ void __launch_bounds__(kNormuonThreads)
+    normuon_finish_kernel(const float* __restrict__ rowsq, int R, int C, float beta2,
+                          const __grid_constant__ NormuonMoments m2, float* __restrict__ row_scale) {
+  const int i = blockIdx.x;
+  const float* sq = rowsq + (long long)i * R;
+  float* m = m2.m[i];
+  float* scale = row_scale + (long long)i * R;
+  __shared__ float red[2][kNormuonThreads / 32];
+  float total = 0.f, rescaled = 0.f;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    const float v = sq[r] / (float)C;
+    const float mr = m[r] + (1.f - beta2) * (v - m[r]);
+    m[r] = mr;
+    const float inv = 1.f / (sqrtf(mr) + 1e-10f);
+    scale[r] = inv;
+    total += sq[r];
+    rescaled += sq[r] * inv * inv;
+  }
+  total = warp_sum(total);
+  rescaled = warp_sum(rescaled);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    red[0][warp] = total;
+    red[1][warp] = rescaled;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float a = lane < kNormuonThreads / 32 ? red[0][lane] : 0.f;
+    float b = lane < kNormuonThreads / 32 ? red[1][lane] : 0.f;
+    a = warp_sum(a);
+    b = warp_sum(b);
+    if (lane == 0) {
+      red[0][0] = a;
+      red[1][0] = b;
+    }
+  }
+  __syncthreads();
+  const float ratio = sqrtf(red[0][0]) / (sqrtf(red[1][0]) + 1e-10f);
+  const float shape = sqrtf(fmaxf(1.f, (float)R / (float)C));
+  for (int r = threadIdx.x; r < R; r += blockDim.x) scale[r] = scale[r] * ratio * shape;
+}
+
+// X: bf16 [n, r, c] orthogonalised batch (U^T when transpose); R, C: the
+// parameter shape; second_moments: n fp32 tensors of R values (updated in
+// place); rowsq, row_scale: fp32 [n, R] scratch / output.
+void normuon_row_scale(const at::Tensor& X, int64_t R, int64_t C, bool transpose,
+                       const std::vector<at::Tensor>& second_moments, double beta2, at::Tensor& rowsq,
+                       at::Tensor& row_scale) {
+  const int64_t n = (int64_t)second_moments.size();
+  if (n == 0) return;
+  KB_CHECK(X.scalar_type() == at::kBFloat16 && X.is_contiguous() && X.numel() >= n * R * C,
+           "normuon_row_scale: X must be contiguous bf16 [n, R*C]");
+  KB_CHECK(rowsq.scalar_type() == at::kFloat && rowsq.numel() >= n * R && row_scale.scalar_type() == at::kFloat &&
+               row_scale.numel() >= n * R,
+           "normuon_row_scale: rowsq / row_scale must be fp32 [n, R]");
+  for (int64_t i = 0; i < n; ++i) {
+    const at::Tensor& m = second_moments[i];
+    KB_CHECK(m.scalar_type() == at::kFloat && m.is_contiguous() && m.numel() == R,
+             "normuon_row_scale: second moments must be contiguous fp32 with one value per row");
+  }
+  const c10::cuda::CUDAGuard guard(X.device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  const int grid = transpose ? (int)std::min<int64_t>((R + 255) / 256, 64) : (int)std::min<int64_t>((R + 7) / 8, 128);
+  normuon_row_stats_kernel<<<dim3(grid, (unsigned)n), 256, 0, s>>>((const __nv_bfloat16*)X.data_ptr(), (int)R, (int)C,
+                                                                   transpose ? 1 : 0, rowsq.data_ptr<float>());
+  KB_LAUNCHED();
+  for (int64_t base = 0; base < n; base += kMuonMax) {
+    const int count = (int)std::min<int64_t>(kMuonMax, n - base);
+    NormuonMoments mom{};
+    for (int j = 0; j < count; ++j) mom.m[j] = second_moments[base + j].data_ptr<float>();
+    normuon_finish_kernel<<<(unsigned)count, kNormuonThreads, 0, s>>>(rowsq.data_ptr<float>() + base * R, (int)R,
+                                                                      (int)C, (float)beta2, mom,
+                                                                      row_scale.data_ptr<float>() + base * R);
+    KB_LAUNCHED();
+  }
+}
+
+// ------------------------------------------------------------ hyperball projection
+//
+// After the inner optimizer's step, each listed matrix is pulled back to its
+// radius r (reference koochak/optim/muon.py:158-168):
+//   s = r / max(|p|, eps)            (sphere)
+//   s = min(1, r / max(|p|, eps))    (ball)
+//   p <- p * s   (and its bf16 copy, when the model keeps one)
+// Two launches for any number of matrices: per-tensor sums of squares
+// (atomics into an fp64 accumulator), then the scaling pass, which forms s
+// from the finished sum itself.
+
+struct ProjectArgs {
+  int n;
+  float* p[kMaxT];
+  void* shadow[kMaxT];   // bf16 copy or null
+  long long numel[kMaxT];
+  int index[kMaxT];      // slot of the tensor in the sums / radii arrays
+};
+
+__global__ void __launch_bounds__(256)
+    tensor_sumsq_kernel(const __grid_constant__ ProjectArgs a, const __grid_constant__ BlockTable bt,
+                        double* __restrict__ sumsq) {
+  const int ti = bt.tensor[blockIdx.x];
+  const long long n = a.numel[ti];
+  const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
+  const long long end = min(n, start + kChunk);
+  const float* p = a.p[ti];
+  float acc = 0.f;
+  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) acc += p[i] * p[i];
+  acc = warp_sum(acc);
+  __shared__ float part[8];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int k = 0; k < 8; ++k) t += part[k];
+    atomicAdd(sumsq + a.index[ti], t);
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    project_radius_kernel(const __grid_constant__ ProjectArgs a, const __grid_constant__ BlockTable bt,
+                          const double* __restrict__ sumsq, const float* __restrict__ radii, float eps, int ball) {
+  const int ti = bt.tensor[blockIdx.x];
+  const long long n = a.numel[ti];
+  const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
+  const long long end = min(n, start + kChunk);
+  const int slot = a.index[ti];
+  const float norm = (float)sqrt(sumsq[slot]);
+  float s = radii[slot] / fmaxf(norm, eps);
+  if (ball) s = fminf(s, 1.f);
+  float* p = a.p[ti];
+  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(a.shadow[ti]);
+  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = p[i] * s;
+    p[i] = v;
+    if (sh) sh[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// params: fp32 contiguous matrices; radii: fp32 [n] on the same device;
+// shadow: bf16 copies or empty placeholders (possibly an empty list).
+void hyperball_project(const std::vector<at::Tensor>& params, const at::Tensor& radii,
+                       const std::vector<at::Tensor>& shadow, double eps, bool ball) {
+  const size_t n = params.size();
+  if (n == 0) return;
+  KB_CHECK(radii.scalar_type() == at::kFloat && radii.is_contiguous() && radii.numel() == (int64_t)n,
+           "hyperball_project: radii must be fp32 [n]");
+  KB_CHECK(shadow.empty() || shadow.size() == n, "hyperball_project: shadow list length");
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
+  std::vector<int64_t> numels;
+  for (const auto& p : params) {
+    KB_CHECK(p.scalar_type() == at::kFloat && p.is_contiguous() && p.is_cuda(),
+             "hyperball_project: fp32 contiguous CUDA tensors required");
+    numels.push_back(p.numel());
+  }
+  at::Tensor sums = at::zeros({(int64_t)n}, params[0].options().dtype(at::kDouble));
+  auto fill = [&](const std::vector<int>& tensors) {
+    ProjectArgs a{};
+    a.n = (int)tensors.size();
+    for (int j = 0; j < a.n; ++j) {
+      const int k = tensors[j];
+      a.p[j] = params[k].data_ptr<float>();
+      const bool has = !shadow.empty() && shadow[k].numel() == params[k].numel();
+      a.shadow[j] = has ? shadow[k].data_ptr() : nullptr;
+      a.numel[j] = params[k].numel();
+      a.index[j] = k;
+    }
+    return a;
+  };
+  for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
+    tensor_sumsq_kernel<<<bt.n_blocks, 256, 0, s>>>(fill(tensors), bt, sums.data_ptr<double>());
+    KB_LAUNCHED();
+  });
+  for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
+    project_radius_kernel<<<bt.n_blocks, 256, 0, s>>>(fill(tensors), bt, sums.data_ptr<double>(),
+                                                      radii.data_ptr<float>(), (float)eps, ball ? 1 : 0);
+    KB_LAUNCHED();
+  });
 }
 
 void register_optim_ops(pybind11::module& m) {
@@ -633,7 +879,12 @@ void register_optim_ops(pybind11::module& m) {
   m.def("ema_update", &ema_update);
   m.def("muon_prologue", &muon_prologue);
   m.def("muon_scale", &muon_scale);
-  m.def("muon_epilogue", &muon_epilogue);
+  m.def("muon_epilogue", &muon_epilogue, "Muon parameter update (scalar or per-row scale), EMA and bf16 copy",
+        pybind11::arg("params"), pybind11::arg("X"), pybind11::arg("ema"), pybind11::arg("shadow"), pybind11::arg("lr"),
+        pybind11::arg("wd"), pybind11::arg("scale"), pybind11::arg("transpose"), pybind11::arg("ema_decay"),
+        pybind11::arg("row_scale") = pybind11::none());
+  m.def("normuon_row_scale", &normuon_row_scale, "NorMuon second-moment update and per-row update scales");
+  m.def("hyperball_project", &hyperball_project, "scale each matrix back to its radius (sphere or ball)");
 }
 
 }  // namespace kb

@@ -128,31 +128,41 @@ def _profile_range(name: str):
         yield
 
 
+_PROJECTIONS = ("sphere", "ball")
+
+
 class HyperballOptimizer:
-    """Wraps an optimizer; after each step projects selected matrices back to their initial Frobenius radii."""
+    """Wraps an optimizer; after each step, pulls chosen matrices back to their starting Frobenius radius.
+
+    (behaviour of reference koochak/optim/muon.py:106-192)
+
+    Each trainable matrix (``ndim >= 2``) with a non-negligible norm keeps the
+    radius ``radius_scale * |p_0|``. ``sphere`` rescales it to exactly that
+    radius after every step, ``ball`` only shrinks it back when it grew past
+    it. On CUDA fp32 matrices the projection is two native launches for all
+    matrices together (``hyperball_project``), which also refresh the models'
+    bf16 copies; elsewhere it runs as PyTorch ops.
+    """
 
     def __init__(self, inner: torch.optim.Optimizer, params: Iterable[torch.nn.Parameter], *, eps: float = 1.0e-8,
                  radius_scale: float = 1.0, projection: str = "sphere") -> None:
-        self.inner = inner
-        self.eps = float(eps)
-        self.radius_scale = float(radius_scale)
-        if self.radius_scale <= 0.0:
+        kind = str(projection).lower()
+        if float(radius_scale) <= 0.0:
             raise ValueError("radius_scale must be positive")
-        self.projection = str(projection).lower()
-        if self.projection not in {"sphere", "ball"}:
+        if kind not in _PROJECTIONS:
             raise ValueError("projection must be 'sphere' or 'ball'")
+        self.inner = inner
+        self.eps, self.radius_scale, self.projection = float(eps), float(radius_scale), kind
         self.params: List[torch.nn.Parameter] = []
         self.radii: List[torch.Tensor] = []
-        seen = set()
-        for p in params:
-            if id(p) in seen or not p.requires_grad or p.ndim < 2:
+        for p in dict.fromkeys(params):  # first occurrence of each parameter, in order
+            if not (p.requires_grad and p.ndim >= 2):
                 continue
-            seen.add(id(p))
-            r = p.detach().float().norm()
-            if float(r) <= self.eps:
-                continue
-            self.params.append(p)
-            self.radii.append((r * self.radius_scale).detach())
+            start = p.detach().float().norm()
+            if float(start) > self.eps:
+                self.params.append(p)
+                self.radii.append((start * self.radius_scale).detach())
+        self._radius_table: Optional[torch.Tensor] = None
 
     @property
     def param_groups(self):
@@ -176,17 +186,34 @@ class HyperballOptimizer:
         else:
             object.__setattr__(self, name, value)
 
+    def _native_projection(self) -> bool:
+        if not self.params or not _native_ready(self.params):
+            return False
+        dev = self.params[0].device
+        return all(p.device == dev for p in self.params)
+
     @torch.no_grad()
     def _project(self) -> None:
-        for i, (p, r) in enumerate(zip(self.params, self.radii)):
-            norm = p.detach().float().norm()
-            if r.device != p.device or r.dtype != torch.float32:
-                r = r.to(device=p.device, dtype=torch.float32)
-                self.radii[i] = r.detach()
-            scale = r / norm.clamp_min(self.eps)
+        if self._native_projection():
+            from ..ops._ext import native
+
+            dev = self.params[0].device
+            table = self._radius_table
+            if table is None or table.device != dev:
+                table = torch.stack([r.to(device=dev, dtype=torch.float32) for r in self.radii])
+                self._radius_table = table
+            native().hyperball_project(self.params, table, _shadow_list(self.params), self.eps,
+                                       self.projection == "ball")
+            _mark_shadows(self.params)
+            return
+        for i, p in enumerate(self.params):
+            radius = self.radii[i]
+            if radius.device != p.device or radius.dtype != torch.float32:
+                radius = self.radii[i] = radius.to(device=p.device, dtype=torch.float32).detach()
+            factor = radius / p.detach().float().norm().clamp_min(self.eps)
             if self.projection == "ball":
-                scale = torch.minimum(scale, torch.ones_like(scale))
-            p.mul_(scale.to(dtype=p.dtype))
+                factor = torch.minimum(factor, torch.ones_like(factor))
+            p.mul_(factor.to(dtype=p.dtype))
 
     def step(self, closure=None):
         with _profile_range("optimizer.hyperball.inner_step"):
@@ -205,9 +232,10 @@ class HyperballOptimizer:
             self.inner.load_state_dict(state_dict)
             return
         self.inner.load_state_dict(state_dict["inner"])
-        radii = state_dict.get("hyperball_radii")
-        if radii is not None and len(radii) == len(self.radii):
-            self.radii = [torch.as_tensor(r).detach().clone() for r in radii]
+        saved = state_dict.get("hyperball_radii")
+        if saved is not None and len(saved) == len(self.radii):
+            self.radii = [torch.as_tensor(r).detach().clone() for r in saved]
+            self._radius_table = None
 
 
 # ----------------------------------------------------------------------------- reference-path group steps
@@ -436,17 +464,20 @@ def _muon_buckets(params: Sequence[torch.nn.Parameter]) -> Dict[Tuple[int, int],
 
 def _native_muon_bucket(optimizer, group, parts: List[Tuple[int, int, List[torch.nn.Parameter]]],
                         slab=None) -> None:
-    """Muon on matrices that orthogonalise as one batch.
+    """Muon (or NorMuon) on matrices that orthogonalise as one batch.
 
     ``parts`` lists (R, C, params) groups whose shapes agree up to a
     transpose (all [R, C] or [C, R]): the prologue writes each matrix in its
     wide orientation [min, max] into one bf16 batch, Newton-Schulz runs once
     over the whole batch (fewer, fuller GEMM launches), and each part's
-    epilogue transposes back as needed.
+    epilogue transposes back as needed. For NorMuon each part's per-row
+    second moments and update scales come from ``normuon_row_scale`` and the
+    update kernels apply one scale per row instead of Muon's scalar.
     """
 
     from ..ops._ext import native
 
+    normuon = bool(getattr(optimizer, "_normuon", False))
     n = sum(len(ps) for _, _, ps in parts)
     dev = parts[0][2][0].device
     r, c = min(parts[0][0], parts[0][1]), max(parts[0][0], parts[0][1])
@@ -460,6 +491,8 @@ def _native_muon_bucket(optimizer, group, parts: List[Tuple[int, int, List[torch
             st = optimizer.state[p]
             if "momentum_buffer" not in st:
                 st["momentum_buffer"] = torch.zeros_like(p)
+            if normuon and "second_momentum_buffer" not in st:
+                st["second_momentum_buffer"] = torch.zeros((p.shape[0], 1), dtype=p.dtype, device=p.device)
             g = p.grad
             if g.dtype != torch.float32 or not g.is_contiguous():
                 g = g.float().contiguous()
@@ -476,15 +509,23 @@ def _native_muon_bucket(optimizer, group, parts: List[Tuple[int, int, List[torch
         k = len(params)
         Xi = X[base:base + k]
         base += k
+        row_scale = None
+        if normuon:
+            row_scale = torch.empty((k, R), device=dev, dtype=torch.float32)
+            rowsq = torch.empty((k, R), device=dev, dtype=torch.float32)
+            native().normuon_row_scale(Xi, R, C, R > C,
+                                       [optimizer.state[p]["second_momentum_buffer"].view(-1) for p in params],
+                                       float(group["beta2"]), rowsq, row_scale)
+        scale = 0.2 * math.sqrt(max(R, C))
         if slab is not None:
             ws = slab.ws
             native().muon_update_gather(params, Xi, _shadow_list(params), float(group["lr"]),
-                                        float(group["weight_decay"]), 0.2 * math.sqrt(max(R, C)), R > C, ws.bases,
-                                        ws.mc_base, ws.rank, ws.nbytes)
+                                        float(group["weight_decay"]), scale, R > C, ws.bases, ws.mc_base, ws.rank,
+                                        ws.nbytes, row_scale)
         else:
             ema, d = _ema_list(optimizer, params)
             native().muon_epilogue(params, Xi, ema, _shadow_list(params), float(group["lr"]),
-                                   float(group["weight_decay"]), 0.2 * math.sqrt(max(R, C)), R > C, d)
+                                   float(group["weight_decay"]), scale, R > C, d, row_scale)
         _mark_shadows(params)
 
 
@@ -513,7 +554,7 @@ def _muon_path(group: Dict[str, Any], normuon: bool, distributed: bool) -> str:
     """How a Muon group is stepped: 'ref' (PyTorch ops), 'native', 'slab' (native + peer stores) or 'nccl'."""
 
     params = list(group["params"])
-    if normuon or not _native_ready(params):
+    if not _native_ready(params) or any(p.dim() < 2 for p in params):
         return "ref"
     if not distributed:
         return "native"
