@@ -16,25 +16,27 @@ import torch.nn.functional as F
 
 
 class _Attn(nn.Module):
-    def __init__(self, d: int, h: int) -> None:
+    def __init__(self, d: int, h: int, causal: bool = True) -> None:
         super().__init__()
         self.h = h
+        self.causal = causal
         self.c_attn = nn.Linear(d, 3 * d)
         self.c_proj = nn.Linear(d, d)
 
     def forward(self, x):
         B, S, C = x.shape
         q, k, v = self.c_attn(x).view(B, S, 3, self.h, C // self.h).unbind(2)
-        y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+        y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           is_causal=self.causal)
         return self.c_proj(y.transpose(1, 2).reshape(B, S, C))
 
 
 class _Block(nn.Module):
-    def __init__(self, d: int, h: int) -> None:
+    def __init__(self, d: int, h: int, causal: bool = True, eps: float = 1e-5) -> None:
         super().__init__()
-        self.ln_1 = nn.LayerNorm(d)
-        self.attn = _Attn(d, h)
-        self.ln_2 = nn.LayerNorm(d)
+        self.ln_1 = nn.LayerNorm(d, eps=eps)
+        self.attn = _Attn(d, h, causal)
+        self.ln_2 = nn.LayerNorm(d, eps=eps)
         self.c_fc = nn.Linear(d, 4 * d)
         self.c_proj = nn.Linear(4 * d, d)
 
@@ -149,3 +151,35 @@ class PlainLlama(nn.Module):
         if targets is None:
             return logits
         return F.cross_entropy(logits.float().view(-1, logits.size(-1)), targets.reshape(-1))
+
+
+class PlainViT(nn.Module):
+    """ViT-B/16 by default: 224 x 224 x 3 images, 16 x 16 patches + class token, 12 pre-LN blocks of width 768
+    with 12 heads and MLP 3072, 1000 classes (non-causal attention)."""
+
+    def __init__(self, image_size: int = 224, patch: int = 16, dim: int = 768, depth: int = 12, heads: int = 12,
+                 num_classes: int = 1000) -> None:
+        super().__init__()
+        tokens = (image_size // patch) ** 2 + 1
+        self.patch_embed = nn.Conv2d(3, dim, patch, stride=patch)
+        self.cls_token = nn.Parameter(torch.zeros(1, 1, dim))
+        self.pos_embed = nn.Parameter(torch.randn(1, tokens, dim) * 0.02)
+        self.blocks = nn.ModuleList([_Block(dim, heads, causal=False, eps=1e-6) for _ in range(depth)])
+        self.norm = nn.LayerNorm(dim, eps=1e-6)
+        self.head = nn.Linear(dim, num_classes)
+        for m in self.modules():
+            if isinstance(m, nn.Linear):
+                nn.init.trunc_normal_(m.weight, std=0.02)
+                if m.bias is not None:
+                    nn.init.zeros_(m.bias)
+
+    def forward(self, images, labels=None):
+        B = images.shape[0]
+        x = self.patch_embed(images).flatten(2).transpose(1, 2)
+        x = torch.cat([self.cls_token.expand(B, -1, -1), x], dim=1) + self.pos_embed
+        for blk in self.blocks:
+            x = blk(x)
+        logits = self.head(self.norm(x)[:, 0])
+        if labels is None:
+            return logits
+        return F.cross_entropy(logits.float(), labels)

@@ -1,7 +1,8 @@
 """Optimizer and scheduler factories from config (reference: koochak/optim/build.py:52-243).
 
-Names: ``adamw`` / ``adam`` / ``sgd`` (PyTorch optimizers; CUDA AdamW uses
-PyTorch's fused implementation), ``muon`` / ``normuon`` and the Hyperball
+Names: ``adamw`` (on CUDA fp32 parameters the native multi-tensor
+``FusedAdamW``, elsewhere ``torch.optim.AdamW``), ``adam`` / ``sgd`` (PyTorch
+optimizers), ``muon`` / ``normuon`` and the Hyperball
 variants ``muonh`` / ``normuonh`` (aliases ``hyperball-muon`` ...). Muon
 needs the model (or param groups with ``use_muon``); the distributed class is
 chosen iff a process group is initialised. Schedulers: ``cosine``,
@@ -19,7 +20,7 @@ from torch.optim import SGD, Adam, AdamW, Optimizer
 from torch.optim.lr_scheduler import CosineAnnealingLR, LambdaLR, ReduceLROnPlateau, SequentialLR, StepLR, _LRScheduler
 
 from ..utils.nn_utils import prepare_param_groups_for_muon
-from .muon import HyperballOptimizer, MuonWithAuxAdam, NorMuonWithAuxAdam, SingleDeviceMuonWithAuxAdam, \
+from .muon import FusedAdamW, HyperballOptimizer, MuonWithAuxAdam, NorMuonWithAuxAdam, SingleDeviceMuonWithAuxAdam, \
     SingleDeviceNorMuonWithAuxAdam
 
 __all__ = ["build_optimizer", "build_scheduler"]
@@ -83,6 +84,17 @@ def _build_muon(params, *, name: str, lr: float, weight_decay: float, muon_lr: O
                               projection=str(hyperball_projection))
 
 
+def _native_adamw_ok(plist) -> bool:
+    tensors = [p for p in plist if isinstance(p, torch.Tensor)]
+    if not tensors or len(tensors) != len(plist):
+        return False
+    if not all(p.is_cuda and p.dtype == torch.float32 for p in tensors):
+        return False
+    from ..ops._ext import available
+
+    return available()
+
+
 def build_optimizer(params, cfg: Optional[Mapping[str, Any]]) -> Optimizer:
     cfg = cfg or {}
     name = str(cfg.get("name", "adamw")).lower()
@@ -92,11 +104,10 @@ def build_optimizer(params, cfg: Optional[Mapping[str, Any]]) -> Optimizer:
         betas = tuple(cfg.get("betas", (0.9, 0.999)))
         eps = float(cfg.get("eps", 1e-8))
         plist = list(_params_of(params))
-        kw: dict = {}
-        if plist and all(isinstance(p, torch.Tensor) and p.is_cuda for p in plist):
-            kw["fused"] = True
+        if name == "adamw" and _native_adamw_ok(plist):
+            return FusedAdamW(plist, lr=lr, betas=betas, eps=eps, weight_decay=wd)
         cls = AdamW if name == "adamw" else Adam
-        return cls(plist, lr=lr, betas=betas, eps=eps, weight_decay=wd, **kw)
+        return cls(plist, lr=lr, betas=betas, eps=eps, weight_decay=wd)
     if name == "sgd":
         return SGD(_params_of(params), lr=lr, momentum=float(cfg.get("momentum", 0.9)), weight_decay=wd,
                    nesterov=bool(cfg.get("nesterov", False)))

@@ -952,3 +952,26 @@ class SingleDeviceNorMuonWithAuxAdam(_KbOptimizer):
     def __init__(self, param_groups):
         _init_groups(param_groups, with_beta2=True, sort_muon=False)
         super().__init__(param_groups, dict())
+
+
+class FusedAdamW(_KbOptimizer):
+    """AdamW (decoupled weight decay, bias-corrected moments) on the native multi-tensor kernel.
+
+    The update is ``torch.optim.AdamW``'s (reference koochak/optim/build.py:174-177
+    builds that class): ``p *= 1 - lr * wd``, then ``p -= lr * m_hat /
+    (sqrt(v_hat) + eps)``. All tensors of a group are updated by one launch,
+    which also applies a clip coefficient handed over as a device scalar and
+    the fused EMA. Under data parallelism the gradient sync may reduce-scatter
+    the gradients and the step then updates this rank's shard and publishes
+    it to the peers (the sharded Adam path). The state dict has
+    ``torch.optim.AdamW``'s keys (``step``, ``exp_avg``, ``exp_avg_sq``).
+    """
+
+    _distributed = True
+
+    def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 1e-2):
+        params = list(params)
+        groups = params if params and isinstance(params[0], dict) else [{"params": params}]
+        for g in groups:
+            g["use_muon"] = False
+        super().__init__(groups, dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay))

@@ -109,3 +109,31 @@ def test_hyperball_native_matches_torch(projection):
     twin_opt.step()
     for p, q in zip(ps, twin):
         torch.testing.assert_close(p.detach().cpu(), q.detach(), rtol=2e-6, atol=1e-7)
+
+
+def test_fused_adamw_matches_torch_adamw():
+    """build_optimizer('adamw') on CUDA is the native multi-tensor AdamW; three steps against torch.optim.AdamW."""
+
+    from koochak_b200.optim import FusedAdamW, build_optimizer
+
+    torch.manual_seed(3)
+    shapes = [(768, 768), (3072,), (1, 197, 768), (1000, 768)]
+    ours = [torch.nn.Parameter(torch.randn(s, device="cuda") * 0.02) for s in shapes]
+    theirs = [torch.nn.Parameter(p.detach().clone()) for p in ours]
+    opt = build_optimizer(ours, {"name": "adamw", "lr": 1e-3, "weight_decay": 0.05})
+    assert isinstance(opt, FusedAdamW)
+    ref = torch.optim.AdamW(theirs, lr=1e-3, weight_decay=0.05)
+    for step in range(3):
+        for p, q in zip(ours, theirs):
+            g = torch.randn_like(p) * (10.0 ** -step)
+            p.grad = g.clone()
+            q.grad = g.clone()
+        opt.step()
+        ref.step()
+    for p, q in zip(ours, theirs):
+        torch.testing.assert_close(p.detach(), q.detach(), rtol=1e-5, atol=1e-7)
+        torch.testing.assert_close(opt.state[p]["exp_avg_sq"], ref.state[q]["exp_avg_sq"], rtol=1e-5, atol=1e-12)
+    # The state dict loads into torch.optim.AdamW (same keys per parameter).
+    twin = torch.optim.AdamW(theirs, lr=1e-3, weight_decay=0.05)
+    twin.load_state_dict(opt.state_dict())
+    assert int(twin.state[theirs[0]]["step"]) == 3
