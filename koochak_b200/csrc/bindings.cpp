@@ -29,6 +29,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_set_debug", &kb::gemm_set_debug,
         "diagnostic GEMM modes for timing studies: bit 0 skips operand loads, bit 1 skips the epilogue (0: off)");
   m.def("read_and_clear_status", &kb::read_and_clear_status, "read and clear the device status word");
+  m.def("read_debug_bounds_detail", &kb::read_debug_bounds_detail,
+        "(site, index, extent) of the last debug-bounds failure on a device (cleared on read)");
+  m.def(
+      "debug_bounds_enabled",
+      []() {
+#ifdef KB_DEBUG_BOUNDS
+        return true;
+#else
+        return false;
+#endif
+      },
+      "whether this library was built with the KB_DEBUG_BOUNDS checks");
+  m.def(
+      "set_debug_extent_slack", [](int64_t n) { kb::debug_extent_slack().store(n); },
+      "elements subtracted from every declared extent (tests use it to make the bounds checks fire)");
   m.def("num_sms", &kb::num_sms, "streaming multiprocessor count of a device");
   m.def("set_sm_reserve", [](int64_t n) { kb::sm_reserve().store((int)std::max<int64_t>(0, n)); },
         "SMs kept free of persistent GEMM / attention grids (for kernels overlapped beside them)");

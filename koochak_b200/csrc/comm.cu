@@ -69,6 +69,7 @@ struct SyncArgs {
   int n_chunks;
   int n_tensors;
   int* status;
+  long long ws_bytes;                  // KB_DEBUG_BOUNDS: declared workspace size (bytes)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
@@ -189,6 +190,9 @@ __global__ void __launch_bounds__(kCommThreads) grad_sync_kernel(const SyncArgs 
     float ss = 0.f;
     bool bad = false;
     const long long off = a.data_off + start * 4;  // bytes; start is a multiple of 4 elements
+    if (!debug_bounds_ok(a.status, kSiteCommChunk, off + 4LL * len - 1, a.ws_bytes) ||
+        !debug_bounds_ok(a.status, kSiteCommChunk, tid, a.n_tensors))
+      continue;  // the same decision in every thread of the block
     const int n4 = len >> 2;
     // kUnroll float4 per thread per pass, every rank's loads issued before
     // the first use, so each thread keeps kUnroll * world loads in flight.
@@ -332,7 +336,7 @@ static SyncArgs make_args(const std::vector<int64_t>& bases, int64_t mc_base, in
 
 void comm_grad_sync(const std::vector<int64_t>& bases, int64_t mc_base, int64_t flags_off, int64_t stats_off,
                     int64_t data_off, const at::Tensor& chunks, int64_t n_tensors, int64_t rank, int64_t epoch,
-                    const c10::optional<at::Tensor>& scale, int64_t blocks, double timeout_s) {
+                    const c10::optional<at::Tensor>& scale, int64_t blocks, double timeout_s, int64_t ws_bytes) {
   check_cuda_tensor(chunks, "chunks");
   KB_CHECK(chunks.scalar_type() == at::kLong && chunks.is_contiguous() && chunks.dim() == 2 && chunks.size(1) == 4,
            "comm: chunks must be int64 [n, 4]");
@@ -343,6 +347,7 @@ void comm_grad_sync(const std::vector<int64_t>& bases, int64_t mc_base, int64_t 
   a.chunks = reinterpret_cast<const long long*>(chunks.data_ptr<int64_t>());
   a.n_chunks = (int)chunks.size(0);
   a.n_tensors = (int)n_tensors;
+  a.ws_bytes = ws_bytes > 0 ? ws_bytes - 4 * debug_extent_slack().load() : (long long)INT64_MAX;
   if (scale.has_value() && scale->defined()) {
     KB_CHECK(scale->scalar_type() == at::kFloat && scale->numel() == 1, "comm: scale must be an fp32 scalar");
     a.scale = scale->data_ptr<float>();
@@ -394,7 +399,8 @@ void register_comm_ops(pybind11::module& m) {
         "fused bucket reduction (+unscale, finite flag, sumsq); per chunk to every rank or to this rank only",
         pybind11::arg("bases"), pybind11::arg("mc_base"), pybind11::arg("flags_off"), pybind11::arg("stats_off"),
         pybind11::arg("data_off"), pybind11::arg("chunks"), pybind11::arg("n_tensors"), pybind11::arg("rank"),
-        pybind11::arg("epoch"), pybind11::arg("scale"), pybind11::arg("blocks"), pybind11::arg("timeout_s"));
+        pybind11::arg("epoch"), pybind11::arg("scale"), pybind11::arg("blocks"), pybind11::arg("timeout_s"),
+        pybind11::arg("ws_bytes") = 0);
   m.def("comm_barrier", &comm_barrier, "cross-GPU arrival barrier with a bounded wait", pybind11::arg("bases"),
         pybind11::arg("flags_off"), pybind11::arg("rank"), pybind11::arg("epoch"), pybind11::arg("blocks"),
         pybind11::arg("timeout_s"), pybind11::arg("device"));

@@ -58,6 +58,9 @@ struct GemmParams {
   // waiting for a full accumulator (summed over warps), [4] producer role
   // total, [5] tiles issued by the MMA thread.
   unsigned long long* prof;
+  // Extents (elements from the base pointer) of C, D and aux that a
+  // KB_DEBUG_BOUNDS build checks every epilogue tile against.
+  long long dbg_c_extent, dbg_d_extent, dbg_aux_extent;
   // Diagnostic modes (0 in normal use): bit 0 skips the operand loads (MMAs
   // read whatever the ring holds), bit 1 skips the epilogue's math and
   // stores, bit 2 keeps only the epilogue's TMEM loads (32 columns each; with
@@ -65,6 +68,25 @@ struct GemmParams {
   // of interest.
   int debug;
 };
+
+// KB_DEBUG_BOUNDS: the last element of rows [row0, row0 + 32) x columns
+// [col0, col1) of batch b, clipped to M x N, must lie inside C (and D, aux).
+__device__ __forceinline__ bool debug_tile_ok(const GemmParams& p, int b, int row0, int col0, int col1) {
+  if constexpr (!kDebugBounds) {
+    return true;
+  } else {
+    const int r1 = min(row0 + 32, p.M), c1 = min(col1, p.N);
+    if (row0 >= r1 || col0 >= c1) return true;  // nothing of this slice is written
+    const long long r = r1 - 1, c = c1 - 1;
+    bool ok = debug_bounds_ok(p.status, kSiteGemmC, (long long)b * p.strideC + r * p.ldc + c, p.dbg_c_extent);
+    if (p.D != nullptr)
+      ok = ok && debug_bounds_ok(p.status, kSiteGemmD, (long long)b * p.strideD + r * p.ldd + c, p.dbg_d_extent);
+    if (p.aux != nullptr)
+      ok = ok && debug_bounds_ok(p.status, kSiteGemmAux, (long long)b * p.strideAux + r * p.ldaux + c,
+                                 p.dbg_aux_extent);
+    return ok;
+  }
+}
 
 __device__ __forceinline__ bool prof_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                           int code, bool on, long long& acc) {
@@ -612,7 +634,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
-      if (!(p.debug & 2))
+      if (!(p.debug & 2) && debug_tile_ok(p, b, m_blk * kBM + q * 32, n_blk * BN + half * (BN / 2),
+                                          n_blk * BN + (half + 1) * (BN / 2)))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
                                m_blk * kBM + q * 32, b, n_blk * BN, kb0 == 0 ? 0 : 1, half * (BN / 2), (half + 1) * (BN / 2), vec,
                                use_tma);
@@ -864,7 +887,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int r = ts - b * tiles_per_batch;
       const int n_blk = r / num_m;
       const int m_blk = r - n_blk * num_m;
-      if (!(p.debug & 2))
+      if (!(p.debug & 2) && debug_tile_ok(p, b, m_blk * 256 + (int)rank * 128 + q * 32, n_blk * BN + half * (BN / 2),
+                                          n_blk * BN + (half + 1) * (BN / 2)))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
                                m_blk * 256 + (int)rank * 128 + q * 32, b, n_blk * BN, kb0 == 0 ? 0 : 1, half * (BN / 2),
                                (half + 1) * (BN / 2), vec, use_tma);
@@ -1068,6 +1092,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   p.b_mn_major = b_mn_major;
   p.fp16_inputs = a.scalar_type() == at::kHalf;
   p.C = c.data_ptr();
+  p.dbg_c_extent = declared_extent(c);
   p.ldc = c.stride(-2);
   p.strideC = batched ? c.stride(0) : 0;
   p.alpha = (float)alpha;
@@ -1076,6 +1101,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   if (d.has_value() && d->defined()) {
     KB_CHECK(d->scalar_type() == ct && d->size(-2) == M && d->size(-1) == N && d->stride(-1) == 1, "D mismatch");
     p.D = d->data_ptr();
+    p.dbg_d_extent = declared_extent(*d);
     p.ldd = d->stride(-2);
     p.strideD = batched ? d->stride(0) : 0;
     vec = vec && (p.ldd % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.D) & 15) == 0) && (!batched || p.strideD % 8 == 0);
@@ -1089,6 +1115,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     KB_CHECK(aux->scalar_type() == aux_t && aux->size(-2) == M && aux->size(-1) == N,
              "aux must be [.., M, N] in the output's 16-bit type (bf16 for fp32 outputs)");
     p.aux = aux->data_ptr();
+    p.dbg_aux_extent = declared_extent(*aux);
     p.ldaux = aux->stride(-2);
     p.strideAux = batched ? aux->stride(0) : 0;
     vec = vec && (p.ldaux % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.aux) & 15) == 0);

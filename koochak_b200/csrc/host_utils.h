@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <array>
 #include <atomic>
+#include <tuple>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -149,6 +150,26 @@ inline std::atomic<long long>& launch_counter() {
 // the life of the process. Kernels with bounded waits record timeouts here.
 int* device_status_ptr(int device);
 int read_and_clear_status(int device);
+// Site, index and extent recorded with a kStatusDebugBounds failure (cleared on read).
+std::tuple<int, long long, long long> read_debug_bounds_detail(int device);
+
+// Elements a kernel may touch from ``t``'s data pointer to the end of its
+// storage: the extent a KB_DEBUG_BOUNDS build checks indices against. The
+// debug slack (0 unless a test sets it) is subtracted, so a test can declare
+// a buffer shorter than it is and see the check fire without any access
+// leaving the real allocation.
+inline std::atomic<long long>& debug_extent_slack() {
+  static std::atomic<long long> n{0};
+  return n;
+}
+
+inline long long declared_extent(const at::Tensor& t) {
+  const long long es = (long long)t.element_size();
+  const long long total = (long long)t.storage().nbytes() / es - (long long)t.storage_offset();
+  return total - debug_extent_slack().load();
+}
+
+inline long long declared_extent_bytes(const at::Tensor& t) { return declared_extent(t) * (long long)t.element_size(); }
 
 inline int num_sms(int device) {
   static int cached[64] = {0};

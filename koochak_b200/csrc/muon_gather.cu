@@ -294,6 +294,8 @@ struct AdamShard {
   float bc1[kShardT], bc2[kShardT];
   long long delta[kGatherRanks];
   long long mc_delta;
+  long long ext[kShardT];     // KB_DEBUG_BOUNDS: elements every tensor of i is declared to hold
+  int* status;
 };
 
 template <bool MULTIMEM>
@@ -337,6 +339,7 @@ __global__ void __launch_bounds__(256)
     while (a.first[i + 1] <= w) ++i;
     const long long s0 = a.lo[i] + (w - a.first[i]) * kShardChunk;
     const long long s1 = min(a.hi[i], s0 + kShardChunk);
+    if (!debug_bounds_ok(a.status, kSiteAdamShard, s1 - 1, a.ext[i])) continue;  // uniform over the block
     const float inv_bc1 = 1.f / a.bc1[i], inv_bc2 = 1.f / a.bc2[i];
     float* p = a.p[i];
     const float* g = a.g[i];
@@ -404,6 +407,7 @@ void adam_shard_gather(const std::vector<at::Tensor>& params, const std::vector<
     a.world = world;
     for (int q = 0; q < world; ++q) a.delta[q] = bases[q] - bases[rank];
     a.mc_delta = mc_base ? mc_base - bases[rank] : 0;
+    a.status = device_status_ptr(params[0].get_device());
     a.first[0] = 0;
     for (int j = 0; j < count; ++j) {
       const size_t k = base + j;
@@ -426,6 +430,8 @@ void adam_shard_gather(const std::vector<at::Tensor>& params, const std::vector<
       a.v[j] = exp_avg_sq[k].data_ptr<float>();
       a.lo[j] = lo[k];
       a.hi[j] = hi[k];
+      a.ext[j] = std::min({declared_extent(p), declared_extent(grads[k]), declared_extent(exp_avg[k]),
+                           declared_extent(exp_avg_sq[k])});
       a.first[j + 1] = a.first[j] + (hi[k] - lo[k] + kShardChunk - 1) / kShardChunk;
       a.bc1[j] = (float)(1.0 - std::pow(beta1, (double)steps[k]));
       a.bc2[j] = (float)(1.0 - std::pow(beta2, (double)steps[k]));

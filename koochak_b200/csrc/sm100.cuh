@@ -32,7 +32,46 @@ enum StatusCode : int {
   kStatusTimeoutDrain = 4,      // drain at exit did not complete
   kStatusTimeoutPeer = 5,       // cross-GPU flag wait ran out
   kStatusBadArgs = 6,
+  kStatusDebugBounds = 7,       // KB_DEBUG_BOUNDS build: an index fell outside its declared extent
 };
+
+// Bounds checks of the KB_DEBUG_BOUNDS build. Kernels compare the last
+// element a tile, shard or chunk will touch against the extent the host
+// declared for that buffer (elements or bytes from the base pointer to the
+// end of its allocation). A failed check skips the access and records, in the
+// status block, kStatusDebugBounds (word 0), the site (word 1), the offending
+// index (bytes 8..15) and the extent (bytes 16..23); the first failure wins.
+// In other builds the checks compile away.
+#ifdef KB_DEBUG_BOUNDS
+constexpr bool kDebugBounds = true;
+#else
+constexpr bool kDebugBounds = false;
+#endif
+
+enum DebugSite : int {
+  kSiteGemmC = 1,
+  kSiteGemmD = 2,
+  kSiteGemmAux = 3,
+  kSiteAttnO = 4,
+  kSiteCommChunk = 5,
+  kSiteAdamShard = 6,
+  kSiteMuonGather = 7,
+};
+
+__device__ __forceinline__ bool debug_bounds_ok(int* status, int site, long long index, long long extent) {
+  if constexpr (!kDebugBounds) {
+    return true;
+  } else {
+    if (index >= 0 && index < extent) return true;
+    if (status != nullptr && atomicCAS(status, 0, kStatusDebugBounds) == 0) {
+      status[1] = site;
+      reinterpret_cast<long long*>(status)[1] = index;
+      reinterpret_cast<long long*>(status)[2] = extent;
+      __threadfence();
+    }
+    return false;
+  }
+}
 
 // 4 seconds: far longer than any legitimate barrier wait inside one kernel.
 constexpr unsigned long long kWaitBudgetNs = 4000000000ull;

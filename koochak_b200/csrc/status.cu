@@ -37,4 +37,13 @@ int read_and_clear_status(int device) {
   return value;
 }
 
+std::tuple<int, long long, long long> read_debug_bounds_detail(int device) {
+  int* p = device_status_ptr(device);
+  long long words[3] = {0, 0, 0};  // [0]: status word and site; [1]: index; [2]: extent
+  KB_CUDA_CHECK(cudaMemcpy(words, p, sizeof(words), cudaMemcpyDeviceToHost));
+  KB_CUDA_CHECK(cudaMemset(reinterpret_cast<char*>(p) + 4, 0, sizeof(words) - 4));
+  const int site = reinterpret_cast<const int*>(words)[1];
+  return std::make_tuple(site, words[1], words[2]);
+}
+
 }  // namespace kb

@@ -218,7 +218,7 @@ class FusedGradReducer:
         nb = min(int(blocks), 148) if blocks else self.blocks
         self._C.comm_grad_sync(self.ws.bases, self.ws.mc_base, self.flags_off, self.stats_off[self.parity],
                                self.bucket_off[b], self.chunks[b], self.n_tensors, self.rank, self._next_epoch(),
-                               scale, nb, self.timeout_s)
+                               scale, nb, self.timeout_s, self.ws.nbytes)
 
     def barrier(self) -> None:
         self._C.comm_barrier(self.ws.bases, self.flags_off, self.rank, self._next_epoch(), 1, self.timeout_s,

@@ -63,33 +63,73 @@ def test_newton_schulz_batched_model_shapes(n, r, c):
     assert rel(ours) <= 1.25 * rel(theirs) + 2e-3, f"native {rel(ours):.4f} vs torch bf16 {rel(theirs):.4f}"
 
 
+def _normuon_fp32(grad, momentum, second, beta=0.95, beta2=0.95):
+    """NorMuon's update (reference koochak/optim/muon.py:50-74) with the Newton-Schulz iteration in fp32."""
+
+    momentum.lerp_(grad, 1 - beta)
+    update = grad.lerp_(momentum, beta)
+    rows, cols = update.shape
+    X = update.float()
+    if rows > cols:
+        X = X.mT
+    X = X / (X.norm() + 1e-7)
+    X = _ns_fp32(X)
+    if rows > cols:
+        X = X.mT
+    vnorm = X.norm()
+    second.lerp_((X * X).mean(dim=-1, keepdim=True), 1 - beta2)
+    X = X / (second.sqrt() + 1e-10)
+    X = X * (vnorm / (X.norm() + 1e-10))
+    return X * max(1, rows / cols) ** 0.5
+
+
 @pytest.mark.parametrize("shape", [(256, 768), (768, 256), (512, 1376)])
 def test_normuon_native_matches_reference_formula(shape):
+    """Native NorMuon against the formula with an fp32 Newton-Schulz (the oracle), over two steps.
+
+    The Newton-Schulz iteration in bf16 is only accurate to a few percent per
+    element, so the native result (tcgen05 bf16 iteration) must be as close to
+    the oracle as the reference's own bf16 arithmetic (``normuon_update`` run
+    with PyTorch ops) is, with a margin -- for the parameters and for the
+    row second moments.
+    """
+
     from koochak_b200.optim.muon import SingleDeviceNorMuonWithAuxAdam, normuon_update
 
     torch.manual_seed(1)
     mats = [torch.randn(shape, device="cuda") * 0.02 for _ in range(3)]
     native_p = [torch.nn.Parameter(m.clone()) for m in mats]
     opt = SingleDeviceNorMuonWithAuxAdam([dict(params=native_p, use_muon=True, lr=0.02, weight_decay=0.01)])
-    ref_p = [m.clone() for m in mats]
-    mom = [torch.zeros_like(m) for m in mats]
-    second = [torch.zeros((shape[0], 1), device="cuda") for _ in mats]
+    arms = {}
+    for arm in ("oracle", "torch_bf16"):
+        arms[arm] = dict(p=[m.clone() for m in mats], mom=[torch.zeros_like(m) for m in mats],
+                         second=[torch.zeros((shape[0], 1), device="cuda") for _ in mats])
     for step in range(2):
         g = torch.Generator(device="cpu").manual_seed(10 + step)
         grads = [torch.randn(shape, generator=g).cuda() for _ in mats]
         for p, gr in zip(native_p, grads):
             p.grad = gr.clone()
         opt.step()
-        for i, gr in enumerate(grads):
-            upd = normuon_update(gr.clone(), mom[i], second[i], beta=0.95, beta2=0.95)
-            ref_p[i].mul_(1 - 0.02 * 0.01)
-            ref_p[i].add_(upd.reshape(shape), alpha=-0.02)
+        for arm, st in arms.items():
+            fn = _normuon_fp32 if arm == "oracle" else normuon_update
+            for i, gr in enumerate(grads):
+                upd = fn(gr.clone(), st["mom"][i], st["second"][i], beta=0.95, beta2=0.95)
+                st["p"][i].mul_(1 - 0.02 * 0.01)
+                st["p"][i].add_(upd.reshape(shape), alpha=-0.02)
+
+    def rel(a, b):
+        return float((a - b).norm() / b.norm())
+
+    oracle, theirs = arms["oracle"], arms["torch_bf16"]
     for i in range(len(mats)):
-        moved = (ref_p[i] - mats[i]).norm()
-        diff = (native_p[i].detach() - ref_p[i]).norm()
-        assert float(diff) <= 0.03 * float(moved), f"matrix {i}: |native - formula| / |update| = {diff / moved:.4f}"
-        st = opt.state[native_p[i]]
-        torch.testing.assert_close(st["second_momentum_buffer"], second[i], rtol=3e-2, atol=1e-8)
+        moved = oracle["p"][i] - mats[i]
+        ours_err = rel(native_p[i].detach() - mats[i], moved)
+        ref_err = rel(theirs["p"][i] - mats[i], moved)
+        assert ours_err <= 1.5 * ref_err + 0.01, f"matrix {i}: update error {ours_err:.4f} vs bf16 torch {ref_err:.4f}"
+        sec = opt.state[native_p[i]]["second_momentum_buffer"]
+        ours_err = rel(sec, oracle["second"][i])
+        ref_err = rel(theirs["second"][i], oracle["second"][i])
+        assert ours_err <= 1.5 * ref_err + 0.01, f"matrix {i}: second moment {ours_err:.4f} vs bf16 torch {ref_err:.4f}"
 
 
 @pytest.mark.parametrize("projection", ["sphere", "ball"])
