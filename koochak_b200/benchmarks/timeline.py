@@ -82,14 +82,17 @@ def _merge(intervals: List[Tuple[float, float]]) -> List[Tuple[float, float]]:
 def analyse(events, gap_us: float) -> Dict[str, Any]:
     """Kernel busy time, idle gaps with causes, and per-kernel totals from profiler events (times in us)."""
 
-    kernels, runtime = [], []
+    kernels, runtime, ops = [], [], []
     for e in events:
         dev = str(getattr(e, "device_type", ""))
         start, end = float(e.time_range.start), float(e.time_range.end)
         if dev.endswith("CUDA"):
-            kernels.append((start, end, e.name))
+            if not getattr(e, "is_user_annotation", False) and "#" not in e.name:
+                kernels.append((start, end, e.name))
         elif e.name.startswith(("cuda", "cu")):
             runtime.append((start, end, e.name))
+        else:
+            ops.append((start, end, e.name))
     if not kernels:
         return {"error": "no kernel events recorded"}
     kernels.sort()
@@ -105,24 +108,41 @@ def analyse(events, gap_us: float) -> Dict[str, Any]:
     gap_rows = []
     for gs, ge in gaps:
         # The runtime call that ended last before the GPU resumed and overlapped the gap the most.
-        best, best_ov = "host launch latency", 0.0
+        best, best_ov, best_call = "host launch latency", 0.0, None
         for rs, re_, name in runtime:
             if re_ < gs or rs > ge:
                 continue
             ov = min(re_, ge) - max(rs, gs)
             if name.startswith(_SYNC_CALLS) and ov > best_ov:
-                best, best_ov = name, ov
+                best, best_ov, best_call = name, ov, (rs, re_)
+        if best_call is not None:
+            # The host operators enclosing that call, innermost first (e.g. aten::item < gate code).
+            rs, re_ = best_call
+            enclosing = sorted((o for o in ops if o[0] <= rs and o[1] >= re_), key=lambda o: o[1] - o[0])
+            names = [o[2] for o in enclosing if not o[2].startswith("ProfilerStep")][:3]
+            if names:
+                best = best + " in " + " < ".join(names)
         causes[best][0] += 1
         causes[best][1] += ge - gs
         before = max((k for k in kernels if k[1] <= gs + 0.5), key=lambda k: k[1], default=None)
         after = min((k for k in kernels if k[0] >= ge - 0.5), key=lambda k: k[0], default=None)
         gap_rows.append((ge - gs, best, before[2] if before else "-", after[2] if after else "-"))
+    # Host operators running while the GPU was idle (nested operators each count their own overlap).
+    host_in_gaps: Dict[str, float] = collections.defaultdict(float)
+    ops.sort()
+    for gs, ge in gaps:
+        for os_, oe, name in ops:
+            if os_ >= ge:
+                break
+            if oe > gs:
+                host_in_gaps[name] += min(oe, ge) - max(os_, gs)
     per_kernel: Dict[str, List[float]] = collections.defaultdict(lambda: [0, 0.0])
     for s, e, name in kernels:
         per_kernel[name][0] += 1
         per_kernel[name][1] += e - s
     return {"window_us": t1 - t0, "busy_us": busy_us, "idle_us": (t1 - t0) - busy_us, "n_kernels": len(kernels),
-            "causes": dict(causes), "gaps": sorted(gap_rows, reverse=True), "per_kernel": dict(per_kernel)}
+            "causes": dict(causes), "gaps": sorted(gap_rows, reverse=True), "per_kernel": dict(per_kernel),
+            "host_in_gaps": dict(host_in_gaps)}
 
 
 def report(res: Dict[str, Any], steps: int, top: int = 40) -> str:
@@ -136,11 +156,15 @@ def report(res: Dict[str, Any], steps: int, top: int = 40) -> str:
     lines.append("")
     lines.append("idle gaps by cause (count, total ms):")
     for name, (n, us) in sorted(res["causes"].items(), key=lambda x: -x[1][1]):
-        lines.append(f"  {us / 1e3:9.3f} ms  {int(n):6d}  {name}")
+        lines.append(f"  {us / 1e3:9.3f} ms  {int(n):6d}  {name[:150]}")
     lines.append("")
     lines.append(f"largest gaps (us, cause, kernel before -> kernel after):")
     for us, cause, before, after in res["gaps"][:top]:
-        lines.append(f"  {us:9.1f}  {cause:24s} {before[:60]} -> {after[:60]}")
+        lines.append(f"  {us:9.1f}  {cause[:90]:90s} {before[:50]} -> {after[:50]}")
+    lines.append("")
+    lines.append("host operators running during those gaps (ms of overlap; nested operators each counted):")
+    for name, us in sorted(res.get("host_in_gaps", {}).items(), key=lambda x: -x[1])[:top]:
+        lines.append(f"  {us / 1e3:9.3f} ms  {name[:120]}")
     lines.append("")
     lines.append("kernels as they ran (total ms, launches, share of busy time):")
     for name, (n, us) in sorted(res["per_kernel"].items(), key=lambda x: -x[1][1])[:top]:
@@ -159,6 +183,8 @@ def main(argv=None) -> int:
     from torch.profiler import ProfilerActivity, profile
 
     from koochak_b200.loop import training_loop
+
+    os.environ.setdefault("KAVEH_PROFILE_RANGES", "1")  # the optimizer's named host ranges
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)

@@ -36,6 +36,7 @@
 // free halves of the score columns); other head sizes use the mma.sync kernel.
 #include "host_utils.h"
 #include "sm100.cuh"
+#include "softmax_exp.cuh"
 
 #include <cstring>
 
@@ -490,7 +491,8 @@ __global__ void __launch_bounds__(kBwThreads, 1)
                 const float2 x = fma2(make_float2(__uint_as_float(sv[32 * c + t + 2 * e]),
                                                   __uint_as_float(sv[32 * c + t + 2 * e + 1])),
                                       sc2, l2);
-                p[e] = make_float2(bw_ex2(x.x), bw_ex2(x.y));
+                // Half of the exponentials on the MUFU unit, half on the FMA pipe (softmax_exp.cuh).
+                p[e] = e == 0 ? make_float2(bw_ex2(x.x), bw_ex2(x.y)) : ex2_fma2(x);
                 if (need_mask) {
                   const int q = q0 + 32 * c + t + 2 * e;
                   if (q >= a.Sq || (CAUSAL && q < kg)) p[e].x = 0.f;

@@ -391,6 +391,35 @@ void cast_multi(const std::vector<at::Tensor>& src, const std::vector<at::Tensor
 // ------------------------------------------------------------ SwiGLU
 
 // h[m, j] = silu(gu[m, j]) * gu[m, F + j]  (gate and up packed side by side)
+// Eight consecutive values (one 16-byte access for 16-bit types, two for fp32)
+// to and from fp32 registers. The address must be 16-byte aligned.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 q;
+    T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = from_f32<T>(v[i]);
+    *reinterpret_cast<uint4*>(p) = q;
+  }
+}
+
 template <typename T>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ h, long long M, int F) {
   const long long total = M * F;
@@ -421,19 +450,82 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gu, const T* __restrict_
   }
 }
 
+// Vectorised SwiGLU: one thread per 8 consecutive outputs of a row (F % 8 == 0
+// and 16-byte aligned rows), so every access is 16 bytes wide and the index
+// arithmetic runs once per 8 values. The arithmetic per value is the scalar
+// kernels'.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    swiglu_fwd_vec_kernel(const T* __restrict__ gu, T* __restrict__ h, long long M, int F) {
+  const int F8 = F >> 3;
+  const long long total = M * F8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long m = v / F8;
+    const int j = (int)(v - m * F8) << 3;
+    const T* row = gu + m * 2 * F;
+    float g[8], u[8], o[8];
+    load8<T>(row + j, g);
+    load8<T>(row + F + j, u);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) o[t] = g[t] / (1.f + __expf(-g[t])) * u[t];
+    store8<T>(h + m * F + j, o);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    swiglu_bwd_vec_kernel(const T* __restrict__ gu, const T* __restrict__ dh, T* __restrict__ dgu, long long M,
+                          int F) {
+  const int F8 = F >> 3;
+  const long long total = M * F8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long m = v / F8;
+    const int j = (int)(v - m * F8) << 3;
+    const T* row = gu + m * 2 * F;
+    float g[8], u[8], d[8], dg[8], du[8];
+    load8<T>(row + j, g);
+    load8<T>(row + F + j, u);
+    load8<T>(dh + m * F + j, d);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float sig = 1.f / (1.f + __expf(-g[t]));
+      const float silu = g[t] * sig;
+      dg[t] = d[t] * u[t] * (sig + silu * (1.f - sig));
+      du[t] = d[t] * silu;
+    }
+    T* out = dgu + m * 2 * F;
+    store8<T>(out + j, dg);
+    store8<T>(out + F + j, du);
+  }
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 void swiglu_forward(const at::Tensor& gu, at::Tensor& h) {
   const int F = (int)h.size(-1);
   const long long M = h.numel() / F;
   const c10::cuda::CUDAGuard guard(gu.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
-  const int blocks = (int)std::min<long long>((M * F + 255) / 256, num_sms(gu.get_device()) * 16LL);
   KB_CHECK(gu.scalar_type() == h.scalar_type(), "swiglu dtype mismatch");
-  if (gu.scalar_type() == at::kBFloat16)
-    swiglu_fwd_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)h.data_ptr(), M, F);
-  else if (gu.scalar_type() == at::kHalf)
-    swiglu_fwd_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)gu.data_ptr(), (__half*)h.data_ptr(), M, F);
-  else
-    swiglu_fwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
+  const bool vec = F % 8 == 0 && aligned16(gu.data_ptr()) && aligned16(h.data_ptr());
+  const long long work = vec ? M * (F / 8) : M * F;
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, num_sms(gu.get_device()) * 16LL));
+  if (gu.scalar_type() == at::kBFloat16) {
+    auto* in = (const __nv_bfloat16*)gu.data_ptr();
+    auto* out = (__nv_bfloat16*)h.data_ptr();
+    if (vec) swiglu_fwd_vec_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+    else swiglu_fwd_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+  } else if (gu.scalar_type() == at::kHalf) {
+    auto* in = (const __half*)gu.data_ptr();
+    auto* out = (__half*)h.data_ptr();
+    if (vec) swiglu_fwd_vec_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+    else swiglu_fwd_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+  } else {
+    if (vec) swiglu_fwd_vec_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
+    else swiglu_fwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
+  }
   KB_LAUNCHED();
 }
 
@@ -442,15 +534,29 @@ void swiglu_backward(const at::Tensor& gu, const at::Tensor& dh, at::Tensor& dgu
   const long long M = dh.numel() / F;
   const c10::cuda::CUDAGuard guard(gu.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
-  const int blocks = (int)std::min<long long>((M * F + 255) / 256, num_sms(gu.get_device()) * 16LL);
-  if (gu.scalar_type() == at::kBFloat16)
-    swiglu_bwd_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)gu.data_ptr(), (const __nv_bfloat16*)dh.data_ptr(),
-                                                            (__nv_bfloat16*)dgu.data_ptr(), M, F);
-  else if (gu.scalar_type() == at::kHalf)
-    swiglu_bwd_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)gu.data_ptr(), (const __half*)dh.data_ptr(),
-                                                     (__half*)dgu.data_ptr(), M, F);
-  else
-    swiglu_bwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(), dgu.data_ptr<float>(), M, F);
+  const bool vec = F % 8 == 0 && aligned16(gu.data_ptr()) && aligned16(dh.data_ptr()) && aligned16(dgu.data_ptr());
+  const long long work = vec ? M * (F / 8) : M * F;
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, num_sms(gu.get_device()) * 16LL));
+  if (gu.scalar_type() == at::kBFloat16) {
+    auto* g = (const __nv_bfloat16*)gu.data_ptr();
+    auto* d = (const __nv_bfloat16*)dh.data_ptr();
+    auto* o = (__nv_bfloat16*)dgu.data_ptr();
+    if (vec) swiglu_bwd_vec_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+    else swiglu_bwd_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+  } else if (gu.scalar_type() == at::kHalf) {
+    auto* g = (const __half*)gu.data_ptr();
+    auto* d = (const __half*)dh.data_ptr();
+    auto* o = (__half*)dgu.data_ptr();
+    if (vec) swiglu_bwd_vec_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+    else swiglu_bwd_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+  } else {
+    if (vec)
+      swiglu_bwd_vec_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(),
+                                                          dgu.data_ptr<float>(), M, F);
+    else
+      swiglu_bwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(),
+                                                      dgu.data_ptr<float>(), M, F);
+  }
   KB_LAUNCHED();
 }
 
@@ -480,24 +586,73 @@ __global__ void rope_kernel(T* __restrict__ x, const float* __restrict__ cosb, c
   }
 }
 
+// Vectorised RoPE: one thread per 8 consecutive pairs (x1[j..j+8), x2[j..j+8))
+// of one head of one token, with 16-byte accesses to x and to the fp32
+// cos/sin rows. Requires D % 16 == 0 and 16-byte aligned heads; the
+// arithmetic per pair is the scalar kernel's.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    rope_vec_kernel(T* __restrict__ x, const float* __restrict__ cosb, const float* __restrict__ sinb,
+                    long long tokens, int S, int H, int D, long long row_stride, int inverse) {
+  const int half = D >> 1, groups = half >> 3;
+  const long long total = tokens * H * groups;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const int gq = (int)(v % groups);
+    const long long th = v / groups;
+    const int h = (int)(th % H);
+    const long long t = th / H;
+    const int pos = (int)(t % S);
+    T* p = x + t * row_stride + (long long)h * D + gq * 8;
+    const float* cp = cosb + (long long)pos * half + gq * 8;
+    const float* sp = sinb + (long long)pos * half + gq * 8;
+    float a[8], b[8], c[8], sn[8], o1[8], o2[8];
+    load8<T>(p, a);
+    load8<T>(p + half, b);
+    load8<float>(cp, c);
+    load8<float>(sp, sn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float si = inverse ? -sn[i] : sn[i];
+      o1[i] = a[i] * c[i] - b[i] * si;
+      o2[i] = b[i] * c[i] + a[i] * si;
+    }
+    store8<T>(p, o1);
+    store8<T>(p + half, o2);
+  }
+}
+
 void rope_apply(at::Tensor& x, const at::Tensor& cosb, const at::Tensor& sinb, int64_t S, int64_t H, int64_t D,
                 bool inverse) {
+  KB_CHECK(x.dim() == 4 && x.stride(-1) == 1 && x.stride(-2) == D, "rope: x must be [B, S, H, D] with dense heads");
+  KB_CHECK(x.stride(0) == S * x.stride(1), "rope: tokens must be evenly strided");
+  KB_CHECK(cosb.is_contiguous() && sinb.is_contiguous() && cosb.scalar_type() == at::kFloat &&
+               sinb.scalar_type() == at::kFloat && cosb.numel() >= S * (D / 2) && sinb.numel() >= S * (D / 2),
+           "rope: cos/sin must be contiguous fp32 [S, D/2]");
   const long long row_stride = x.stride(-3);
-  const long long tokens = x.numel() / x.size(-3) / x.size(-2) / x.size(-1) * x.size(-3);
-  (void)tokens;
   const long long T = x.size(0) * x.size(1);
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
-  const int blocks = (int)std::min<long long>((T * H * (D / 2) + 255) / 256, num_sms(x.get_device()) * 16LL);
-  if (x.scalar_type() == at::kBFloat16)
-    rope_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((__nv_bfloat16*)x.data_ptr(), cosb.data_ptr<float>(),
-                                                      sinb.data_ptr<float>(), T, (int)S, (int)H, (int)D, row_stride, inverse);
-  else if (x.scalar_type() == at::kHalf)
-    rope_kernel<__half><<<blocks, 256, 0, s>>>((__half*)x.data_ptr(), cosb.data_ptr<float>(), sinb.data_ptr<float>(), T,
-                                               (int)S, (int)H, (int)D, row_stride, inverse);
-  else
-    rope_kernel<float><<<blocks, 256, 0, s>>>(x.data_ptr<float>(), cosb.data_ptr<float>(), sinb.data_ptr<float>(), T,
-                                              (int)S, (int)H, (int)D, row_stride, inverse);
+  const int es = (int)x.element_size();
+  const bool vec = D % 16 == 0 && aligned16(x.data_ptr()) && (row_stride * es) % 16 == 0 &&
+                   aligned16(cosb.data_ptr()) && aligned16(sinb.data_ptr());
+  const long long work = vec ? T * H * (D / 16) : T * H * (D / 2);
+  const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, num_sms(x.get_device()) * 16LL));
+  const float* c = cosb.data_ptr<float>();
+  const float* sn = sinb.data_ptr<float>();
+  if (x.scalar_type() == at::kBFloat16) {
+    auto* p = (__nv_bfloat16*)x.data_ptr();
+    if (vec) rope_vec_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+    else rope_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+  } else if (x.scalar_type() == at::kHalf) {
+    auto* p = (__half*)x.data_ptr();
+    if (vec) rope_vec_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+    else rope_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+  } else {
+    float* p = x.data_ptr<float>();
+    if (vec) rope_vec_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+    else rope_kernel<<<blocks, 256, 0, s>>>(p, c, sn, T, (int)S, (int)H, (int)D, row_stride, inverse);
+  }
   KB_LAUNCHED();
 }
 

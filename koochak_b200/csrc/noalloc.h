@@ -11,9 +11,9 @@
 // partials; the grid shrinks to fit). Rows wider than 4096 are rejected.
 // All calls share that array: overlapping calls race and must be serialised
 // by the caller. The first call on each device resolves the array's address
-// with cudaGetSymbolAddress, so make it before any stream capture. That
-// address is then remembered per device for the life of the process, which
-// assumes the device is not reset (cudaDeviceReset) in between.
+// with cudaGetSymbolAddress; that address is then remembered per device for
+// the life of the process, which assumes the device is not reset
+// (cudaDeviceReset) in between.
 //
 // dy: bf16 [M, C]; x, w, mean, rstd, dx, dw, db: fp32, contiguous.
 // Returns 0 on success, -1 for bad arguments, -2 when C > 4096, otherwise

@@ -289,6 +289,114 @@ __global__ void __launch_bounds__(32 * kNormWarps)
   }
 }
 
+// RMSNorm backward for wide rows (C a multiple of 256, above 1024 values):
+//   dx = rstd * (w*dy - xhat * mean(w*dy*xhat)) + dres,  dw += dy * xhat.
+// Two passes over each row instead of holding it in registers: the first
+// reads x and dy and forms the row sum and the dw contributions (summed per
+// warp in shared memory), the second re-reads x and dy -- the row was just
+// read, so these come from L2 -- and writes dx (and its 16-bit copy). With a
+// handful of registers per lane and 72 KB of shared memory per CTA at
+// C = 2048, three CTAs (24 rows) are resident per SM, against one CTA of the
+// register-resident kernel. Lane l owns columns [8 l + 256 k, 8 l + 256 k + 8).
+template <typename TIn, typename TG, typename TDx>
+__global__ void __launch_bounds__(32 * kNormWarps)
+    rms_bwd_wide_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
+                        const float* __restrict__ rstd_in, const TDx* __restrict__ dres, TDx* __restrict__ dx,
+                        TG* __restrict__ dx_lp, float* __restrict__ dw_part, int M, int C) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ float red[];
+  float* sdw = red + warp * C;         // [kNormWarps][C] per-warp dw sums
+  float* sw = red + kNormWarps * C;    // [C] weights
+  for (int c = lane * 4; c < C; c += 128) *reinterpret_cast<float4*>(sdw + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = threadIdx.x * 4; c < C; c += blockDim.x * 4)
+    *reinterpret_cast<float4*>(sw + c) = *reinterpret_cast<const float4*>(w + c);
+  __syncthreads();
+  const int chunks = C >> 8;
+  for (int row = blockIdx.x * kNormWarps + warp; row < M; row += gridDim.x * kNormWarps) {
+    const TIn* xr = x + (long long)row * C;
+    const TG* gr = dy + (long long)row * C;
+    const float rstd = rstd_in[row];
+    float s2 = 0.f;
+    // pass 1: two chunks in flight per step
+    for (int k = 0; k < chunks; k += 2) {
+      float xa[2][8], ga[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int col = ((k + u) << 8) + lane * 8;
+        if (k + u < chunks) {
+          load4<TIn>(xr + col, *reinterpret_cast<float(*)[4]>(&xa[u][0]));
+          load4<TIn>(xr + col + 4, *reinterpret_cast<float(*)[4]>(&xa[u][4]));
+          load4<TG>(gr + col, *reinterpret_cast<float(*)[4]>(&ga[u][0]));
+          load4<TG>(gr + col + 4, *reinterpret_cast<float(*)[4]>(&ga[u][4]));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (k + u >= chunks) break;
+        const int col = ((k + u) << 8) + lane * 8;
+        float dv[8], wv[8];
+        *reinterpret_cast<float4*>(&dv[0]) = *reinterpret_cast<const float4*>(sdw + col);
+        *reinterpret_cast<float4*>(&dv[4]) = *reinterpret_cast<const float4*>(sdw + col + 4);
+        *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(sw + col);
+        *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(sw + col + 4);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float xh = xa[u][t] * rstd;
+          s2 += wv[t] * ga[u][t] * xh;
+          dv[t] += ga[u][t] * xh;
+        }
+        *reinterpret_cast<float4*>(sdw + col) = *reinterpret_cast<const float4*>(&dv[0]);
+        *reinterpret_cast<float4*>(sdw + col + 4) = *reinterpret_cast<const float4*>(&dv[4]);
+      }
+    }
+    s2 = warp_sum(s2) / C;
+    // pass 2
+    const TDx* rr = dres ? dres + (long long)row * C : nullptr;
+    TDx* dxr = dx + (long long)row * C;
+    TG* lpr = dx_lp ? dx_lp + (long long)row * C : nullptr;
+    for (int k = 0; k < chunks; ++k) {
+      const int col = (k << 8) + lane * 8;
+      float xa[8], ga[8], ra[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, o[8];
+      load4<TIn>(xr + col, *reinterpret_cast<float(*)[4]>(&xa[0]));
+      load4<TIn>(xr + col + 4, *reinterpret_cast<float(*)[4]>(&xa[4]));
+      load4<TG>(gr + col, *reinterpret_cast<float(*)[4]>(&ga[0]));
+      load4<TG>(gr + col + 4, *reinterpret_cast<float(*)[4]>(&ga[4]));
+      if (rr) {
+        load4<TDx>(rr + col, *reinterpret_cast<float(*)[4]>(&ra[0]));
+        load4<TDx>(rr + col + 4, *reinterpret_cast<float(*)[4]>(&ra[4]));
+      }
+      float wv[8];
+      *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(sw + col);
+      *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(sw + col + 4);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) o[t] = rstd * (wv[t] * ga[t] - xa[t] * rstd * s2) + ra[t];
+      store4<TDx>(dxr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
+      store4<TDx>(dxr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
+      if (lpr) {
+        store4<TG>(lpr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
+        store4<TG>(lpr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormWarps; ++k) a += red[k * C + c];
+    dw_part[(long long)blockIdx.x * C + c] = a;
+  }
+}
+
+static inline bool rms_bwd_wide(bool rms, int C) { return rms && C > 1024 && C % 256 == 0 && C <= 4096; }
+static inline int rms_bwd_wide_smem(int C) { return (kNormWarps + 1) * C * (int)sizeof(float); }
+
+// CTAs of the backward grid (persistent; the partial-sum workspace holds one
+// row of C per CTA, two rows for LayerNorm's dgamma and dbeta).
+static inline int norm_bwd_grid(int M, int C, bool rms, int dev) {
+  const int per_sm = rms_bwd_wide(rms, C) ? std::max(1, (227 * 1024) / (rms_bwd_wide_smem(C) + 1024)) : 2;
+  return std::max(1, std::min(num_sms(dev) * per_sm, (M + kNormWarps - 1) / kNormWarps));
+}
+
 // Whether norm_bwd_kernel keeps its column sums in shared memory for this row
 // width, and the dynamic shared memory it then needs.
 static inline bool norm_bwd_smem_acc(int C) { return C <= 2560; }
@@ -392,7 +500,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
   const int dev = x.get_device();
-  const int grid = std::max(1, std::min(num_sms(dev) * 2, (M + kNormWarps - 1) / kNormWarps));
+  const int grid = norm_bwd_grid(M, C, rms, dev);
   KB_CHECK(workspace.scalar_type() == at::kFloat && workspace.numel() >= 2LL * grid * C, "norm bwd: workspace too small");
   float* dw_part = workspace.data_ptr<float>();
   float* db_part = rms ? nullptr : dw_part + (long long)grid * C;
@@ -403,7 +511,30 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   if (has_res) KB_CHECK(dres->scalar_type() == dx.scalar_type() && dres->is_contiguous(), "dres must match dx");
   const int smem = norm_bwd_smem_bytes(C);
   const bool sacc = norm_bwd_smem_acc(C);
-  with_vpt(C, [&](auto vpt) {
+  const bool wide = rms_bwd_wide(rms, C);
+  if (wide) {
+    with_type(x.scalar_type(), [&](auto tin) {
+      using TIn = decltype(tin);
+      with_lp_type(dy.scalar_type(), [&](auto tg) {
+        using TG = decltype(tg);
+        using TDx = TIn;
+        TG* lp = nullptr;
+        if (dx_lp.has_value() && dx_lp->defined()) {
+          KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
+                   "dx_lp must be contiguous, of dy's dtype and dx's size");
+          lp = (TG*)dx_lp->data_ptr();
+        }
+        const int wsmem = rms_bwd_wide_smem(C);
+        auto kern = rms_bwd_wide_kernel<TIn, TG, TDx>;
+        KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, wsmem));
+        kern<<<grid, 32 * kNormWarps, wsmem, stream>>>((const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(),
+                                                       w.data_ptr<float>(), rstd.data_ptr<float>(),
+                                                       has_res ? (const TDx*)dres->data_ptr() : nullptr,
+                                                       (TDx*)dx.data_ptr(), lp, dw_part, M, C);
+      });
+    });
+  }
+  if (!wide) with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
     with_type(x.scalar_type(), [&](auto tin) {
       using TIn = decltype(tin);
@@ -450,7 +581,9 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
 }
 
 int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
-  const int grid = std::max<int64_t>(1, std::min<int64_t>(num_sms((int)device) * 2, (M + kNormWarps - 1) / kNormWarps));
+  // Sized for the larger of the two grids (RMSNorm's wide kernel runs more CTAs).
+  const int grid = std::max(norm_bwd_grid((int)M, (int)C, true, (int)device),
+                            norm_bwd_grid((int)M, (int)C, false, (int)device));
   return 2LL * grid * C;
 }
 
@@ -462,9 +595,7 @@ int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
 // The regular norm_backward above takes its partial-sum scratch from the
 // caller (the Python layer allocates it through PyTorch's caching allocator).
 // Some callers cannot allocate device memory at the point where they need
-// this op: code running while a stream is being captured into a CUDA graph
-// (an allocation made there is not part of the graph and breaks replay),
-// engines that own a fixed device-memory arena and forbid any other
+// this op: engines that own a fixed device-memory arena and forbid any other
 // allocation, and plain C callers that link this library without PyTorch and
 // therefore have no allocator to hand over. For them this variant keeps its
 // scratch in a file-scope device array of fixed size:
@@ -480,7 +611,7 @@ int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
 //     array and must be serialised by the caller.
 //   * the first call on each device resolves the array's device address with
 //     cudaGetSymbolAddress (the host-side name of a __device__ array is not a
-//     device address); make that first call before any stream capture.
+//     device address).
 //   * the resolved address is remembered per device ordinal for the rest of
 //     the process. It assumes the device is not reset in between: after a
 //     cudaDeviceReset in the same process the remembered address is stale,

@@ -148,6 +148,9 @@ class _Profiler:
         self.timing = settings.profile_step_timing
         self.sync = settings.profile_step_timing and settings.profile_step_cuda_sync and on_cuda
         self.nvtx = settings.profile_nvtx and on_cuda
+        # Named host ranges for torch.profiler (the reference's KAVEH_PROFILE_RANGES switch).
+        self.ranges = os.environ.get("KAVEH_PROFILE_RANGES", "").lower() in {"1", "true", "yes", "on"}
+        self._ranges: List[Any] = []
         self.device = device
         self._open = 0
 
@@ -160,6 +163,10 @@ class _Profiler:
         if self.nvtx and phase is not None:
             torch.cuda.nvtx.range_push(f"koochak/{phase}")
             self._open += 1
+        if self.ranges and phase is not None:  # every stop() pairs with a start() that named its phase
+            rf = torch.autograd.profiler.record_function(f"loop.{phase}")
+            rf.__enter__()
+            self._ranges.append(rf)
         return time.perf_counter()
 
     def stop(self, totals: Dict[str, float], key: str, began: float) -> float:
@@ -167,6 +174,8 @@ class _Profiler:
         if self._open:
             torch.cuda.nvtx.range_pop()
             self._open -= 1
+        if self._ranges:
+            self._ranges.pop().__exit__(None, None, None)
         took = time.perf_counter() - began
         if self.timing:
             totals[key] = totals.get(key, 0.0) + took

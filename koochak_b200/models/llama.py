@@ -135,8 +135,7 @@ class _LayerFn(torch.autograd.Function):
         h1, _, r1 = kf.norm_forward(x2, w_in, None, eps, rms=True, out_dtype=cdt)
         qkv = kf.gemm(h1, qkv_w16)
         q5 = qkv.view(B, S, 3, H, D)
-        kf.rope_apply_(q5[:, :, 0], cos, sin)
-        kf.rope_apply_(q5[:, :, 1], cos, sin)
+        kf.rope_apply_(q5[:, :, :2].view(B, S, 2 * H, D), cos, sin)  # q and k heads: one launch
         a, lse = kf.flash_attention_forward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], causal=True)
         a2 = a.view(M, C)
         x_mid = kf.gemm(a2, o_w16, d=x2, beta=1.0, out_dtype=torch.float32)
@@ -174,8 +173,7 @@ class _LayerFn(torch.autograd.Function):
         dqkv = torch.empty((B, S, 3, H, D), device=qkv.device, dtype=cdt)
         kf.flash_attention_backward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], a2.view(B, S, H, D), da.view(B, S, H, D),
                                     lse, causal=True, dq=dqkv[:, :, 0], dk=dqkv[:, :, 1], dv=dqkv[:, :, 2])
-        kf.rope_apply_(dqkv[:, :, 0], cos, sin, inverse=True)
-        kf.rope_apply_(dqkv[:, :, 1], cos, sin, inverse=True)
+        kf.rope_apply_(dqkv[:, :, :2].view(B, S, 2 * H, D), cos, sin, inverse=True)
         dqkv2 = dqkv.view(M, 3 * C)
         dh1 = kf.gemm(dqkv2, qkv_w16, b_mn_major=True)
         d_qkv = kf.gemm(dqkv2, h1, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)

@@ -9,15 +9,17 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-LINE = "0, {mhz}, 1965, 900.0, 0x4, Not Active, Not Active, Not Active, {cap}"
+
+def _sample(t, mhz, cap):
+    return (t, float(mhz), 1965.0, frozenset({"sw_power_cap"}) if cap else frozenset())
 
 
 def test_clock_sampler_keeps_the_timed_window():
     import bench
 
     c = bench.ClockSampler(0)
-    c.lines = [(1.0, LINE.format(mhz=1100, cap="Not Active")), (2.2, LINE.format(mhz=1800, cap="Active")),
-               (2.6, LINE.format(mhz=1700, cap="Active")), (4.0, LINE.format(mhz=600, cap="Not Active"))]
+    c.samples = [_sample(1.0, 1100, False), _sample(2.2, 1800, True), _sample(2.6, 1700, True),
+                 _sample(4.0, 600, False)]
     out = c.stop(2.0, 3.0)
     assert out["samples"] == 2 and out["sm_mhz"] == 1750.0 and out["window"] == "timed"
     assert out["reasons"] == ["sw_power_cap"] and out["sm_max_mhz"] == 1965.0
@@ -27,7 +29,7 @@ def test_clock_sampler_falls_back_to_the_end_of_warmup():
     import bench
 
     c = bench.ClockSampler(0)
-    c.lines = [(0.5, LINE.format(mhz=900, cap="Not Active")), (1.7, LINE.format(mhz=1850, cap="Active"))]
+    c.samples = [_sample(0.5, 900, False), _sample(1.7, 1850, True)]
     out = c.stop(2.0, 2.1)  # timed region shorter than the sampling period
     assert out["samples"] == 1 and out["sm_mhz"] == 1850.0 and out["window"] == "last second of warm-up"
 

@@ -73,7 +73,7 @@ def test_gemm_epilogues_and_batch():
     assert _rel(c, ref) < 1e-4
 
 
-@pytest.mark.parametrize("C", [64, 768, 1000, 2048])
+@pytest.mark.parametrize("C", [64, 768, 1000, 1280, 2048, 4096])
 @pytest.mark.parametrize("rms", [False, True])
 def test_norm_forward_backward(C, rms):
     kf = _kf()
@@ -165,26 +165,39 @@ def test_cross_entropy_and_embedding():
     assert _rel(kf.bias_grad(gbias), gbias.float().sum(0)) < 1e-4
 
 
-def test_swiglu_and_rope():
+@pytest.mark.parametrize("F", [96, 100, 5504])
+def test_swiglu(F):
+    """Vectorised (F % 8 == 0) and scalar (F = 100) SwiGLU against the fp32 formula."""
+
     kf = _kf()
     torch.manual_seed(5)
-    gu = torch.randn(100, 2 * 96, device=DEV).bfloat16()
+    gu = torch.randn(37, 2 * F, device=DEV).bfloat16()
     assert _rel(kf.swiglu_forward(gu), kf.swiglu_ref(gu)) < 1e-2
     gr = gu.float().requires_grad_(True)
-    dh = torch.randn(100, 96, device=DEV).bfloat16()
+    dh = torch.randn(37, F, device=DEV).bfloat16()
     kf.swiglu_ref(gr).backward(dh.float())
     assert _rel(kf.swiglu_backward(gu, dh), gr.grad) < 2e-2
-    B, S, H, D = 2, 32, 3, 64
-    x = torch.randn(B, S, H, D, device=DEV).bfloat16()
+
+
+@pytest.mark.parametrize("D", [64, 128, 24])
+def test_rope(D):
+    """RoPE in place, forward and inverse; D = 24 takes the scalar kernel. The q and k heads of a fused
+    [B, S, 3, H, D] projection are rotated by one call on their [B, S, 2H, D] view, as the Llama layer does."""
+
+    kf = _kf()
+    torch.manual_seed(5)
+    B, S, H = 2, 32, 3
+    qkv = torch.randn(B, S, 3, H, D, device=DEV).bfloat16()
     pos = torch.arange(S, device=DEV).float()[:, None]
     inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=DEV).float() / D))
     cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
-    ref = kf.rope_ref(x, cos, sin)
-    y = x.clone()
-    kf.rope_apply_(y, cos, sin)
-    assert _rel(y, ref) < 1e-2
-    kf.rope_apply_(y, cos, sin, inverse=True)
-    assert _rel(y, x) < 2e-2
+    ref_q, ref_k = kf.rope_ref(qkv[:, :, 0], cos, sin), kf.rope_ref(qkv[:, :, 1], cos, sin)
+    y = qkv.clone()
+    kf.rope_apply_(y[:, :, :2].view(B, S, 2 * H, D), cos, sin)
+    assert _rel(y[:, :, 0], ref_q) < 1e-2 and _rel(y[:, :, 1], ref_k) < 1e-2
+    assert torch.equal(y[:, :, 2], qkv[:, :, 2])
+    kf.rope_apply_(y[:, :, :2].view(B, S, 2 * H, D), cos, sin, inverse=True)
+    assert _rel(y, qkv) < 2e-2
 
 
 def test_optimizer_kernels_match_reference():
@@ -354,3 +367,20 @@ def test_gemm_two_sm(M, N, K, a_mn, b_mn, block_n):
     g = kf.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, aux=aux, act=kf.ACT_GELU, block_n=block_n)
     rg, rpre = kf.gemm_ref(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, act=kf.ACT_GELU)
     assert _rel(g, rg) < 1e-2 and _rel(aux, rpre) < 1e-2
+
+
+def test_exp2_on_fma_pipe_error_bound():
+    """The attention kernels' FMA-pipe 2^x: relative error below 1e-4 against exp2 over the softmax range,
+    and exactly 0 below -125 (masked scores are -inf)."""
+
+    from koochak_b200.ops import native
+
+    x = torch.cat([torch.linspace(-125.0, 8.0, 1_000_001, device=DEV),
+                   torch.tensor([-125.5, -200.0, float("-inf"), 0.0, 0.5, -0.5, 1.0], device=DEV)])
+    y = torch.empty_like(x)
+    native().exp2_fma(x, y)
+    ref = torch.exp2(x.double())
+    live = x >= -125.0
+    rel = ((y[live].double() - ref[live]) / ref[live]).abs().max().item()
+    assert rel < 1e-4, rel
+    assert torch.all(y[~live] == 0)

@@ -20,14 +20,16 @@ def test_gaps_are_merged_and_attributed():
         _ev("cudaLaunchKernel", 395, 440, "DeviceType.CPU"),
         _ev("rope", 450, 460, "DeviceType.CUDA"),       # 50 us gap, launch latency only
         _ev("aten::add", 0, 10, "DeviceType.CPU"),
+        _ev("aten::item", 105, 305, "DeviceType.CPU"),  # encloses the synchronisation
+        _ev("Optimizer.step#X.step", 0, 400, "DeviceType.CUDA"),  # a GPU user annotation, not a kernel
     ]
     res = analyse(events, gap_us=20.0)
     assert res["window_us"] == 460
     assert res["busy_us"] == 120 + 100 + 10
     assert res["idle_us"] == 460 - 230
-    assert res["causes"]["cudaStreamSynchronize"] == [1, 180.0]
+    assert res["causes"]["cudaStreamSynchronize in aten::item"] == [1, 180.0]
     assert res["causes"]["host launch latency"] == [1, 50.0]
-    assert res["gaps"][0][:2] == (180.0, "cudaStreamSynchronize")
+    assert res["gaps"][0][:2] == (180.0, "cudaStreamSynchronize in aten::item")
     assert res["gaps"][0][2:] == ("norm", "attn")
     assert res["per_kernel"]["gemm"] == [1, 100.0]
     text = report(res, steps=1)
