@@ -116,6 +116,7 @@ class FusedGradScaler(GradScaler):
     def unscale_(self, optimizer, *, max_norm: Optional[float] = None) -> None:  # type: ignore[override]
         from torch.amp.grad_scaler import OptState
 
+        self.last_stats = None
         if not self._enabled:
             return
         self._check_scale_growth_tracker("unscale_")

@@ -37,6 +37,7 @@
 // store to a peer lands at the same offset of that peer's slab.
 // No TMA and no cluster multicast: plain and multimem stores only.
 #include "host_utils.h"
+#include "step_guard.h"
 #include "sm100.cuh"
 
 #include <torch/extension.h>
@@ -58,6 +59,7 @@ struct GatherMats {
   __nv_bfloat16* shadow[kGatherMats];  // bf16 compute copy on this rank, or null
   long long delta[kGatherRanks];       // bytes from this rank's slab to rank r's
   long long mc_delta;                  // bytes from this rank's slab to the multicast alias (0: none)
+  const float* skip;                   // device skip flag (step_guard.h) or null
 };
 
 __device__ __forceinline__ void mm_st_v4(float* mc, float4 v) {
@@ -77,6 +79,7 @@ template <bool MULTIMEM>
 __global__ void __launch_bounds__(256)
     muon_update_gather_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X, float lr,
                               float wd, float scale, int transpose, const float* __restrict__ row_scale) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.z;
   const int R = mm.R, C = mm.C;
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
@@ -146,6 +149,7 @@ template <bool MULTIMEM>
 __global__ void __launch_bounds__(256)
     muon_update_gather_flat_kernel(const __grid_constant__ GatherMats mm, const __nv_bfloat16* __restrict__ X,
                                    float lr, float wd, float scale, const float* __restrict__ row_scale) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.y;
   const long long n4 = (long long)mm.R * mm.C / 4;
   float4* p = reinterpret_cast<float4*>(mm.p[i]);
@@ -229,6 +233,7 @@ void muon_update_gather(const std::vector<at::Tensor>& params, const at::Tensor&
   for (size_t base = 0; base < n; base += kGatherMats) {
     const int count = (int)std::min<size_t>(kGatherMats, n - base);
     GatherMats mm{};
+    mm.skip = step_skip_ptr();
     mm.R = R;
     mm.C = C;
     mm.world = world;
@@ -399,7 +404,8 @@ void adam_shard_gather(const std::vector<at::Tensor>& params, const std::vector<
   const c10::cuda::CUDAGuard guard(params[0].device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
   const float* cp = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
-  const float* sp = (skip.has_value() && skip->defined()) ? skip->data_ptr<float>() : nullptr;
+  // An explicit flag, else the one of the step being enqueued (step_guard.h).
+  const float* sp = (skip.has_value() && skip->defined()) ? skip->data_ptr<float>() : step_skip_ptr();
   for (size_t base = 0; base < n; base += kShardT) {
     const int count = (int)std::min<size_t>(kShardT, n - base);
     AdamShard a{};

@@ -21,6 +21,7 @@
 // together with a block table, so a call is one launch and no host-to-device
 // copy.
 #include "host_utils.h"
+#include "step_guard.h"
 #include "sm100.cuh"
 
 #include <torch/extension.h>
@@ -187,12 +188,14 @@ struct AdamArgs {
   long long numel[kMaxT];
   float bc1[kMaxT];        // 1 - beta1^step
   float bc2[kMaxT];        // 1 - beta2^step
+  const float* skip;       // device skip flag (step_guard.h) or null
 };
 
 __global__ void __launch_bounds__(256)
     adamw_kernel(const __grid_constant__ AdamArgs a, const __grid_constant__ BlockTable bt,
                  const float* __restrict__ coef_ptr, float lr, float beta1, float beta2, float eps, float wd,
                  float ema_decay) {
+  if (step_skipped(a.skip)) return;
   const int ti = bt.tensor[blockIdx.x];
   const long long n = a.numel[ti];
   const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
@@ -246,6 +249,7 @@ void adamw_step(const std::vector<at::Tensor>& params, const std::vector<at::Ten
   const float* cp = (coef.has_value() && coef->defined()) ? coef->data_ptr<float>() : nullptr;
   for_each_launch(numels, [&](const std::vector<int>& tensors, const BlockTable& bt) {
     AdamArgs a{};
+    a.skip = step_skip_ptr();
     a.n = (int)tensors.size();
     for (int i = 0; i < a.n; ++i) {
       const int k = tensors[i];
@@ -321,6 +325,7 @@ struct MuonMats {
   float* p[kMuonMax];
   float* ema[kMuonMax];
   void* shadow[kMuonMax];
+  const float* skip;  // device skip flag (step_guard.h) or null
 };
 
 // X[i] = bf16(nesterov(momentum update)) stored [R, C] or transposed [C, R];
@@ -328,6 +333,7 @@ struct MuonMats {
 __global__ void __launch_bounds__(256)
     muon_prologue_kernel(const __grid_constant__ MuonMats mm, __nv_bfloat16* __restrict__ X, float* __restrict__ sumsq,
                          const float* __restrict__ coef_ptr, float beta, int nesterov, int transpose) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.z;
   const int R = mm.R, C = mm.C;
   const float coef = coef_ptr ? *coef_ptr : 1.f;
@@ -387,6 +393,7 @@ __global__ void muon_scale_kernel(__nv_bfloat16* __restrict__ X, const float* __
 __global__ void __launch_bounds__(256)
     muon_epilogue_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr, float wd,
                          float scale, int transpose, float ema_decay, const float* __restrict__ row_scale) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.z;
   const int R = mm.R, C = mm.C;
   __shared__ float tile[32][33];
@@ -446,6 +453,7 @@ __device__ __forceinline__ float4 unpack_bf16x4(uint2 r) {
 __global__ void __launch_bounds__(256)
     muon_prologue_flat_kernel(const __grid_constant__ MuonMats mm, __nv_bfloat16* __restrict__ X,
                               float* __restrict__ sumsq, const float* __restrict__ coef_ptr, float beta, int nesterov) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.y;
   const long long n4 = (long long)mm.R * mm.C / 4;
   const float coef = coef_ptr ? *coef_ptr : 1.f;
@@ -496,6 +504,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     muon_epilogue_flat_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr,
                               float wd, float scale, float ema_decay, const float* __restrict__ row_scale) {
+  if (step_skipped(mm.skip)) return;
   const int i = blockIdx.y;
   const long long n4 = (long long)mm.R * mm.C / 4;
   float4* p = reinterpret_cast<float4*>(mm.p[i]);
@@ -543,6 +552,7 @@ static MuonMats make_mats(const std::vector<at::Tensor>& grads, const std::vecto
                           const std::vector<at::Tensor>& params, const std::vector<at::Tensor>& ema,
                           const std::vector<at::Tensor>& shadow, size_t base, int count) {
   MuonMats mm{};
+  mm.skip = step_skip_ptr();
   mm.n = count;
   const auto& p0 = params.empty() ? grads[base] : params[base];
   mm.R = (int)p0.size(0);
@@ -692,11 +702,13 @@ constexpr int kNormuonThreads = 512;
 
 struct NormuonMoments {
   float* m[kMuonMax];  // each matrix's second-moment buffer (R values)
+  const float* skip;   // device skip flag (step_guard.h) or null
 };
 
 __global__ void __launch_bounds__(kNormuonThreads)
     normuon_finish_kernel(const float* __restrict__ rowsq, int R, int C, float beta2,
                           const __grid_constant__ NormuonMoments m2, float* __restrict__ row_scale) {
+  if (step_skipped(m2.skip)) return;
   const int i = blockIdx.x;
   const float* sq = rowsq + (long long)i * R;
   float* m = m2.m[i];
@@ -763,6 +775,7 @@ void normuon_row_scale(const at::Tensor& X, int64_t R, int64_t C, bool transpose
   for (int64_t base = 0; base < n; base += kMuonMax) {
     const int count = (int)std::min<int64_t>(kMuonMax, n - base);
     NormuonMoments mom{};
+    mom.skip = step_skip_ptr();
     for (int j = 0; j < count; ++j) mom.m[j] = second_moments[base + j].data_ptr<float>();
     normuon_finish_kernel<<<(unsigned)count, kNormuonThreads, 0, s>>>(rowsq.data_ptr<float>() + base * R, (int)R,
                                                                       (int)C, (float)beta2, mom,
@@ -788,6 +801,7 @@ struct ProjectArgs {
   void* shadow[kMaxT];   // bf16 copy or null
   long long numel[kMaxT];
   int index[kMaxT];      // slot of the tensor in the sums / radii arrays
+  const float* skip;     // device skip flag (step_guard.h) or null
 };
 
 __global__ void __launch_bounds__(256)
@@ -814,6 +828,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     project_radius_kernel(const __grid_constant__ ProjectArgs a, const __grid_constant__ BlockTable bt,
                           const double* __restrict__ sumsq, const float* __restrict__ radii, float eps, int ball) {
+  if (step_skipped(a.skip)) return;
   const int ti = bt.tensor[blockIdx.x];
   const long long n = a.numel[ti];
   const long long start = (long long)bt.chunk[blockIdx.x] * kChunk;
@@ -851,6 +866,7 @@ void hyperball_project(const std::vector<at::Tensor>& params, const at::Tensor& 
   at::Tensor sums = at::zeros({(int64_t)n}, params[0].options().dtype(at::kDouble));
   auto fill = [&](const std::vector<int>& tensors) {
     ProjectArgs a{};
+    a.skip = step_skip_ptr();
     a.n = (int)tensors.size();
     for (int j = 0; j < a.n; ++j) {
       const int k = tensors[j];
@@ -873,7 +889,26 @@ void hyperball_project(const std::vector<at::Tensor>& params, const at::Tensor& 
   });
 }
 
+static const float* g_step_skip = nullptr;
+const float* step_skip_ptr() { return g_step_skip; }
+void set_step_skip_ptr(const float* p) { g_step_skip = p; }
+
+// Python: set (a one-element fp32 CUDA tensor, kept alive by the caller for the
+// step) or clear (None) the device skip flag of the optimizer step being enqueued.
+static void set_step_skip(const c10::optional<at::Tensor>& flag) {
+  if (!flag.has_value() || !flag->defined()) {
+    g_step_skip = nullptr;
+    return;
+  }
+  KB_CHECK(flag->is_cuda() && flag->scalar_type() == at::kFloat && flag->numel() >= 1,
+           "step skip flag must be a CUDA fp32 tensor");
+  g_step_skip = flag->data_ptr<float>();
+}
+
 void register_optim_ops(pybind11::module& m) {
+  m.def("set_step_skip", &set_step_skip,
+        "device flag (non-zero: skip) read by the optimizer kernels of the step being enqueued; None clears it",
+        pybind11::arg("flag"));
   m.def("grad_stats", &grad_stats);
   m.def("adamw_step", &adamw_step);
   m.def("ema_update", &ema_update);

@@ -639,6 +639,12 @@ class _Run:
         prof.run(t, "profile_loop_ema_wait_time_s", wait_for_ema_snapshots)
         self._hand_ema_to_optimizer(step)
         prof.run(t, "profile_loop_optimizer_step_time_s", lambda: self.scaler.step(self.optimizer))
+        # The gate's outcome: read now that the step is enqueued (a rejected step was skipped on the device
+        # and raises here under clipping, before the EMA, the scheduler or any hook sees it).
+        clip = self.gate.finish(self.model, self.optimizer)
+        if clip:
+            rec.out = {} if rec.out is None else rec.out
+            rec.out.update(clip)
         prof.run(t, "profile_loop_scaler_update_time_s", self.scaler.update)
         prof.run(t, "profile_loop_ema_update_time_s", lambda: self._update_ema(step))
         prof.run(t, "profile_loop_scheduler_time_s", self.step_scheduler)
@@ -733,10 +739,7 @@ class _Run:
             rec.timings[k] = rec.timings.get(k, 0.0) + v
 
         self.gate.profile = lambda key, thunk: prof.run(rec.timings, key, thunk)
-        clip = self.gate.run(self.model, self.optimizer, step, self.on_cuda)
-        if clip:
-            rec.out = {} if rec.out is None else rec.out
-            rec.out.update(clip)
+        self.gate.begin(self.model, self.optimizer, step, self.on_cuda)
         self._update_parameters(step, rec)
 
         prof.barrier()

@@ -90,6 +90,7 @@ class GateResult(NamedTuple):
     stats: Optional[GradientClipStats]   # None when clipping is off
     coef_tensor: Optional[torch.Tensor]  # device scalar to apply on read (None: nothing to apply)
     nonfinite: bool
+    device_stats: Optional[torch.Tensor] = None  # fp32 [norm, coefficient, found_inf] on the device
 
 
 @torch.no_grad()
@@ -113,7 +114,7 @@ def fused_grad_gate(grads: Sequence[torch.Tensor], *, max_norm: Optional[float],
     native().grad_stats(list(grads), inv_scale, float(max_norm or 0.0), clip, scratch, out, None)
     coef_t = out[1:2]
     if not (clip or check_finite) or not sync:
-        return GateResult(None, coef_t if clip else None, False)
+        return GateResult(None, coef_t if clip else None, False, out)
     norm, coef, bad = (float(v) for v in out.tolist())
     nonfinite = bad != 0.0
     if not clip:

@@ -216,10 +216,24 @@ class HyperballOptimizer:
             p.mul_(factor.to(dtype=p.dtype))
 
     def step(self, closure=None):
+        skip = getattr(self.inner, "kb_skip", None)  # read before the inner step consumes it
         with _profile_range("optimizer.hyperball.inner_step"):
             loss = self.inner.step(closure)
         with _profile_range("optimizer.hyperball.project"):
-            self._project()
+            if skip is not None and not self._native_projection():
+                if float(skip.sum()) != 0.0:
+                    return loss  # the inner step was skipped: nothing to project
+                skip = None
+            from ..ops._ext import native
+
+            C = native() if skip is not None else None
+            if C is not None:
+                C.set_step_skip(skip.float().reshape(-1)[:1].contiguous())
+            try:
+                self._project()
+            finally:
+                if C is not None:
+                    C.set_step_skip(None)
         return loss
 
     def state_dict(self) -> dict[str, Any]:
@@ -671,7 +685,8 @@ def _optimizer_slab(optimizer, params: List[torch.nn.Parameter]):
     return slab
 
 
-def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) -> None:
+def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool,
+                skip: Optional[torch.Tensor] = None) -> None:
     plan = getattr(optimizer, "_kb_plan", None) if distributed else None
     shard_adam = bool(plan and plan["shard_rest"])
     paths = []
@@ -690,7 +705,28 @@ def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) 
     if shard_adam and "ref" in [p for g, p in zip(optimizer.param_groups, paths) if not g.get("use_muon", True)]:
         raise RuntimeError("the gradient sync reduce-scattered the Adam tensors, but an Adam group cannot take "
                            "the sharded native path")
+    if skip is not None and "ref" in paths:
+        # The PyTorch paths cannot skip on the device: read the flag on the host.
+        if float(skip.sum()) != 0.0:
+            return
+        skip = None
     slab = _optimizer_slab(optimizer, slab_params) if slab_params else None
+    from ..ops._ext import native
+
+    C = native() if skip is not None else None
+    if C is not None:
+        C.set_step_skip(skip)
+    try:
+        _run_paths(optimizer, muon_fn, distributed, paths, slab)
+    finally:
+        if C is not None:
+            C.set_step_skip(None)
+    if slab is not None:
+        slab.barrier()  # every rank's peer stores of this step have landed
+
+
+def _run_paths(optimizer, muon_fn: Callable, distributed: bool, paths: List[str], slab) -> None:
+    ran = getattr(optimizer, "_kb_adam_ran", None)
     for group, path in zip(optimizer.param_groups, paths):
         params = group["params"]
         if group.get("use_muon", True):
@@ -707,8 +743,8 @@ def _run_groups(optimizer, muon_fn: Callable, normuon: bool, distributed: bool) 
                     _native_adam_group(optimizer, group)
                 else:
                     _ref_adam_group(optimizer, group)
-    if slab is not None:
-        slab.barrier()  # every rank's peer stores of this step have landed
+            if ran is not None and path != "ref":
+                ran.append(group)
 
 
 def gradient_plan(optimizer, world: int) -> Tuple[Dict[int, int], bool]:
@@ -768,25 +804,65 @@ def _closure(closure):
 
 
 class _KbOptimizer(torch.optim.Optimizer):
-    """Base: fused-path hooks (clip coefficient, fused EMA) consumed by one step, and sharded-state handling."""
+    """Base: fused-path hooks consumed by one step, device-side skip, and sharded-state handling.
+
+    Hooks set before ``step`` and cleared by it: ``kb_grad_scale`` (clip
+    coefficient, a device scalar applied when each gradient is read),
+    ``kb_ema`` (a GPU EMA update fused into the update kernels) and
+    ``kb_skip`` (a device flag; non-zero makes every kernel of the step
+    return before touching any state). ``GradScaler.step`` hands over its
+    found-inf flag the same way (``_step_supports_amp_scaling``: it sets
+    ``found_inf`` / ``grad_scale`` instead of reading found-inf on the host),
+    so a skipped step costs no host synchronisation. A step skipped on the
+    device still advanced the host-side Adam step counters;
+    ``kb_rollback_step`` undoes that once the caller has read the flag.
+    """
 
     kb_fused = True
     _normuon = False
     _distributed = False
+    _step_supports_amp_scaling = True
 
     def _distributed_now(self) -> bool:
         return self._distributed and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+    def _skip_flag(self) -> Optional[torch.Tensor]:
+        flags = [f for f in (getattr(self, "kb_skip", None), getattr(self, "found_inf", None)) if f is not None]
+        if not flags:
+            return None
+        flag = flags[0].float().reshape(-1)[:1]
+        for f in flags[1:]:
+            flag = flag + f.float().reshape(-1)[:1]
+        return flag.contiguous()
 
     @torch.no_grad()
     def step(self, closure=None):
         loss = _closure(closure)
         fn = _normuon_param_update if self._normuon else _muon_param_update
+        skip = self._skip_flag()
+        grad_scale = getattr(self, "grad_scale", None)  # GradScaler: gradients not unscaled yet
+        if grad_scale is not None:
+            inv = grad_scale.double().reciprocal().float().reshape(1)
+            coef = getattr(self, "kb_grad_scale", None)
+            self.kb_grad_scale = inv if coef is None else coef * inv
+        self._kb_adam_ran: List[Dict[str, Any]] = []
         try:
-            _run_groups(self, fn, self._normuon, self._distributed_now())
+            _run_groups(self, fn, self._normuon, self._distributed_now(), skip)
         finally:
             self.kb_grad_scale = None
             self.kb_ema = None
+            self.kb_skip = None
         return loss
+
+    def kb_rollback_step(self) -> None:
+        """Undo the host-side step counters of the last step, which its kernels skipped on the device."""
+
+        for group in getattr(self, "_kb_adam_ran", []):
+            for p in group["params"]:
+                st = self.state.get(p)
+                if st and "step" in st:
+                    st["step"] = int(st["step"]) - 1
+        self._kb_adam_ran = []
 
     def kb_commit_gradient_plan(self, world: int) -> Tuple[Dict[int, int], bool]:
         """Fix where reduced gradients must arrive (see ``gradient_plan``); later steps rely on it."""

@@ -177,3 +177,111 @@ def test_fused_adamw_matches_torch_adamw():
     twin = torch.optim.AdamW(theirs, lr=1e-3, weight_decay=0.05)
     twin.load_state_dict(opt.state_dict())
     assert int(twin.state[theirs[0]]["step"]) == 3
+
+
+def _snapshot(opt, params):
+    st = {id(p): {k: (v.clone() if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in params
+          if p in opt.state}
+    return [p.detach().clone() for p in params], st
+
+
+@pytest.mark.parametrize("kind", ["adamw", "muon", "normuon"])
+def test_device_skip_leaves_state_untouched(kind):
+    """A step whose device skip flag is set changes no parameter or optimizer state; the host counters roll back."""
+
+    from koochak_b200.optim import FusedAdamW
+    from koochak_b200.optim.muon import SingleDeviceMuonWithAuxAdam, SingleDeviceNorMuonWithAuxAdam
+
+    torch.manual_seed(4)
+    mats = [torch.nn.Parameter(torch.randn(s, device="cuda") * 0.02) for s in [(256, 768), (768, 256)]]
+    vecs = [torch.nn.Parameter(torch.randn(s, device="cuda") * 0.02) for s in [(768,), (1000, 64)]]
+    if kind == "adamw":
+        opt = FusedAdamW(mats + vecs, lr=1e-3, weight_decay=0.05)
+    else:
+        cls = SingleDeviceMuonWithAuxAdam if kind == "muon" else SingleDeviceNorMuonWithAuxAdam
+        opt = cls([dict(params=mats, use_muon=True, lr=0.02, weight_decay=0.01),
+                   dict(params=vecs, use_muon=False, lr=1e-3, weight_decay=0.0)])
+    params = mats + vecs
+    for p in params:
+        p.grad = torch.randn_like(p)
+    opt.step()  # state exists from here on
+    before, st_before = _snapshot(opt, params)
+    for p in params:
+        p.grad = torch.randn_like(p)
+    opt.kb_skip = torch.ones(1, device="cuda")
+    opt.step()
+    torch.cuda.synchronize()
+    for p, b in zip(params, before):
+        assert torch.equal(p.detach(), b)
+    for p in params:
+        for k, v in st_before.get(id(p), {}).items():
+            if torch.is_tensor(v):
+                assert torch.equal(opt.state[p][k], v), k
+    opt.kb_rollback_step()
+    for p in params:
+        if "step" in st_before.get(id(p), {}):
+            assert int(opt.state[p]["step"]) == int(st_before[id(p)]["step"])
+    # GradScaler's hand-over (found_inf attribute) skips the same way
+    opt.found_inf = torch.ones((), device="cuda")
+    opt.step()
+    del opt.found_inf
+    torch.cuda.synchronize()
+    for p, b in zip(params, before):
+        assert torch.equal(p.detach(), b)
+
+
+def test_deferred_gate_matches_synchronous_gate_and_raises_like_the_reference():
+    """The two-phase gate (optimizer enqueued before the statistics are read) gives the synchronous gate's
+    parameters bit for bit; with a non-finite gradient under clipping it raises FloatingPointError and leaves
+    parameters and Adam step counters as they were."""
+
+    from koochak_b200.core.precision import NoOpScaler
+    from koochak_b200.models import GPT2
+    from koochak_b200.optim import build_optimizer
+    from koochak_b200.runtime.gate import GradientGate
+
+    def make():
+        torch.manual_seed(0)
+        m = GPT2(n_layer=2, n_head=4, n_embd=256, vocab_size=512, block_size=128).cuda()
+        return m, build_optimizer(m, {"name": "muon", "lr": 6e-4, "muon_lr": 0.02})
+
+    idx = torch.randint(0, 512, (4, 128), device="cuda")
+    results = []
+    for defer in (True, False):
+        m, opt = make()
+        gate = GradientGate(max_norm=0.5, check_every=0, scaler=NoOpScaler(), profile=lambda k, f: f())
+        for _ in range(3):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = m(idx, idx)
+            loss.backward()
+            gate.begin(m, opt, 0, True, defer=defer)
+            opt.step()
+            out = gate.finish(m, opt)
+            assert 0.0 < out["grad_norm"] and 0.0 < out["grad_clip_coefficient"] <= 1.0
+        results.append([p.detach().clone() for p in m.parameters()])
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+
+    m, opt = make()
+    gate = GradientGate(max_norm=0.5, check_every=0, scaler=NoOpScaler(), profile=lambda k, f: f())
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        m(idx, idx).backward()
+    gate.begin(m, opt, 0, True)
+    opt.step()
+    gate.finish(m, opt)
+    before = [p.detach().clone() for p in m.parameters()]
+    steps = {id(p): int(st["step"]) for p, st in opt.state.items() if "step" in st}
+    opt.zero_grad(set_to_none=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        m(idx, idx).backward()
+    next(iter(m.parameters())).grad[0, 0] = float("inf")
+    gate.begin(m, opt, 1, True)
+    opt.step()
+    with pytest.raises(FloatingPointError):
+        gate.finish(m, opt)
+    for p, b in zip(m.parameters(), before):
+        assert torch.equal(p.detach(), b)
+    for p, st in opt.state.items():
+        if "step" in st:
+            assert int(st["step"]) == steps[id(p)]
