@@ -92,7 +92,7 @@ def analyse(events, gap_us: float) -> Dict[str, Any]:
         elif e.name.startswith(("cuda", "cu")):
             runtime.append((start, end, e.name))
         else:
-            ops.append((start, end, e.name))
+            ops.append((start, end, e.name, tuple(getattr(e, "stack", None) or ())))
     if not kernels:
         return {"error": "no kernel events recorded"}
     kernels.sort()
@@ -105,6 +105,7 @@ def analyse(events, gap_us: float) -> Dict[str, Any]:
             gaps.append((e0, s1))
     runtime.sort()
     causes: Dict[str, List[float]] = collections.defaultdict(lambda: [0, 0.0])
+    stacks: Dict[str, set] = collections.defaultdict(set)
     gap_rows = []
     for gs, ge in gaps:
         # The runtime call that ended last before the GPU resumed and overlapped the gap the most.
@@ -122,6 +123,9 @@ def analyse(events, gap_us: float) -> Dict[str, Any]:
             names = [o[2] for o in enclosing if not o[2].startswith("ProfilerStep")][:3]
             if names:
                 best = best + " in " + " < ".join(names)
+            frames = next((o[3] for o in enclosing if o[3]), ())
+            if frames:
+                stacks[best].add(" <- ".join(f for f in frames[:6]))
         causes[best][0] += 1
         causes[best][1] += ge - gs
         before = max((k for k in kernels if k[1] <= gs + 0.5), key=lambda k: k[1], default=None)
@@ -131,18 +135,24 @@ def analyse(events, gap_us: float) -> Dict[str, Any]:
     host_in_gaps: Dict[str, float] = collections.defaultdict(float)
     ops.sort()
     for gs, ge in gaps:
-        for os_, oe, name in ops:
+        for os_, oe, name, _stack in ops:
             if os_ >= ge:
                 break
             if oe > gs:
                 host_in_gaps[name] += min(oe, ge) - max(os_, gs)
+    # Host time of the loop's named phases (the loop.* ranges): where the host spends each step.
+    host_phases: Dict[str, float] = collections.defaultdict(float)
+    for os_, oe, name, _stack in ops:
+        if name.startswith("loop."):
+            host_phases[name] += oe - os_
     per_kernel: Dict[str, List[float]] = collections.defaultdict(lambda: [0, 0.0])
     for s, e, name in kernels:
         per_kernel[name][0] += 1
         per_kernel[name][1] += e - s
     return {"window_us": t1 - t0, "busy_us": busy_us, "idle_us": (t1 - t0) - busy_us, "n_kernels": len(kernels),
             "causes": dict(causes), "gaps": sorted(gap_rows, reverse=True), "per_kernel": dict(per_kernel),
-            "host_in_gaps": dict(host_in_gaps)}
+            "host_in_gaps": dict(host_in_gaps), "stacks": {k: sorted(v) for k, v in stacks.items()},
+            "host_phases": dict(host_phases)}
 
 
 def report(res: Dict[str, Any], steps: int, top: int = 40) -> str:
@@ -162,6 +172,18 @@ def report(res: Dict[str, Any], steps: int, top: int = 40) -> str:
     for us, cause, before, after in res["gaps"][:top]:
         lines.append(f"  {us:9.1f}  {cause[:90]:90s} {before[:50]} -> {after[:50]}")
     lines.append("")
+    if res.get("host_phases"):
+        lines.append("host time of the loop's phases per step (ms):")
+        for name, us in sorted(res["host_phases"].items(), key=lambda x: -x[1]):
+            lines.append(f"  {us / 1e3 / steps:9.3f} ms  {name}")
+        lines.append("")
+    if res.get("stacks"):
+        lines.append("Python stacks of the synchronising calls (innermost frame first):")
+        for cause, frames in res["stacks"].items():
+            lines.append(f"  {cause[:100]}")
+            for f in frames[:4]:
+                lines.append(f"      {f[:300]}")
+        lines.append("")
     lines.append("host operators running during those gaps (ms of overlap; nested operators each counted):")
     for name, us in sorted(res.get("host_in_gaps", {}).items(), key=lambda x: -x[1])[:top]:
         lines.append(f"  {us / 1e3:9.3f} ms  {name[:120]}")
@@ -179,6 +201,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--gap-us", type=float, default=10.0)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--stacks", action="store_true", help="record Python stacks (slower host) to locate syncs")
     args = ap.parse_args(argv)
     from torch.profiler import ProfilerActivity, profile
 
@@ -189,7 +212,8 @@ def main(argv=None) -> int:
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     model, opt, sched, batch, step_fn, extra = _workload(args.model, device)
-    prof = profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=False)
+    prof = profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=False,
+                   with_stack=bool(args.stacks))
     first, last = args.warmup, args.warmup + args.steps - 1
 
     def hook(log, ctx):

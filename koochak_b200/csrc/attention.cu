@@ -571,7 +571,6 @@ bool flash_attention_forward_tc(const at::Tensor& q, const at::Tensor& k, const 
 // 0: tcgen05 forward where the shape allows it (default); 1: the mma.sync kernels.
 static int g_attn_impl = 0;
 void attention_set_impl(int64_t impl) { g_attn_impl = (int)impl; }
-void exp2_fma(const at::Tensor& x, at::Tensor& y);
 extern int g_attn_bwd_debug;
 void attention_set_debug(int64_t bits) { g_attn_bwd_debug = (int)bits; }
 extern long long* g_attn_bwd_trace;
@@ -691,7 +690,6 @@ void register_attention_ops(pybind11::module& m) {
         "Diagnostics for the tcgen05 attention backward (bit 0: skip dQ reductions, bit 1: skip elementwise math)");
   m.def("attention_set_trace", &attention_set_trace,
         "Diagnostics: device address of an int64[168] buffer for clock64 stamps of one backward CTA (0 = off)");
-  m.def("exp2_fma", &exp2_fma, "the attention kernels' FMA-pipe 2^x, elementwise (for numerics tests)");
   m.def("attention_set_impl", &attention_set_impl,
         "attention forward implementation: 0 = tcgen05 (default), 1 = mma.sync kernels");
   m.def("flash_attention_forward", &flash_attention_forward);

@@ -28,7 +28,8 @@
 // execute in order. At D = 64 it also goes ahead of dQ_i (dS is double
 // buffered in shared memory; the completion of S^T_{i+2} covers dQ_i), so
 // step i+1's elementwise work overlaps dQ_i. At D = 128 dQ_i uses the upper
-// score columns, so S^T_{i+1} waits until dQ_i has been read out.
+// score columns, so S^T_{i+1} waits until dQ_i has been read out; dQ_i is
+// issued before dV / dK there, so that readout overlaps their MMAs.
 //
 // Every mbarrier wait is bounded; a wait that runs out records a status code,
 // raises the CTA abort flag, and the kernel drains its copies and MMAs, frees
@@ -36,7 +37,6 @@
 // free halves of the score columns); other head sizes use the mma.sync kernel.
 #include "host_utils.h"
 #include "sm100.cuh"
-#include "softmax_exp.cuh"
 
 #include <cstring>
 
@@ -361,6 +361,23 @@ __global__ void __launch_bounds__(kBwThreads, 1)
           bw_stamp(a, 8 + 16 * step + 2);
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQ + st * Cfg::kTile), do_addr = smem_u32(sDO + st * Cfg::kTile);
+          const uint32_t ds_addr = smem_u32(sDS + (Cfg::kDsBuffers == 2 ? (step & 1) * Cfg::kDsBytes : 0));
+          auto issue_dq = [&]() {
+#pragma unroll
+            for (int h2 = 0; h2 < D / 64; ++h2)
+#pragma unroll
+              for (int kk = 0; kk < kBwBK / 16; ++kk)
+                umma_f16_ss(tmem + Cfg::dq_col(h2), sw128_desc(ds_addr + kk * 2048, 128 * 128, 1024),
+                            sw128_desc(k_addr + h2 * (128 * 128) + kk * 2048, 128 * 128, 1024), idesc_q,
+                            kk != 0 ? 1u : 0u);
+            umma_commit(dq_full);
+            bw_stamp(a, 8 + 16 * step + 4);
+          };
+          // D = 128: dQ goes first; its commit covers only the dQ MMAs, so the
+          // dQ warps read it out while the tensor cores run dV / dK, and the
+          // next step's scores (which reuse dQ's columns) are not held up by
+          // the readout.
+          if (Cfg::kDqInScores) issue_dq();
 #pragma unroll
           for (int kk = 0; kk < kBwBQ / 16; ++kk) {
             const uint32_t acc = (st_i | kk) != 0 ? 1u : 0u;
@@ -376,21 +393,14 @@ __global__ void __launch_bounds__(kBwThreads, 1)
             ok = false;
             break;
           }
-          if (!Cfg::kDqInScores && !mbar_wait(dq_empty, (step & 1) ^ 1, abort_flag, a.status, kStatusTimeoutMma)) {
-            ok = false;
-            break;
+          if (!Cfg::kDqInScores) {
+            if (!mbar_wait(dq_empty, (step & 1) ^ 1, abort_flag, a.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_dq();
           }
-          tc_fence_after();
-          const uint32_t ds_addr = smem_u32(sDS + (Cfg::kDsBuffers == 2 ? (step & 1) * Cfg::kDsBytes : 0));
-#pragma unroll
-          for (int h2 = 0; h2 < D / 64; ++h2)
-#pragma unroll
-            for (int kk = 0; kk < kBwBK / 16; ++kk)
-              umma_f16_ss(tmem + Cfg::dq_col(h2), sw128_desc(ds_addr + kk * 2048, 128 * 128, 1024),
-                          sw128_desc(k_addr + h2 * (128 * 128) + kk * 2048, 128 * 128, 1024), idesc_q,
-                          kk != 0 ? 1u : 0u);
-          umma_commit(dq_full);
-          bw_stamp(a, 8 + 16 * step + 4);
           umma_commit(&q_empty[st]);
           if (Cfg::kDqInScores && more && !issue_sdp(step + 1)) {
             ok = false;
@@ -491,8 +501,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
                 const float2 x = fma2(make_float2(__uint_as_float(sv[32 * c + t + 2 * e]),
                                                   __uint_as_float(sv[32 * c + t + 2 * e + 1])),
                                       sc2, l2);
-                // Half of the exponentials on the MUFU unit, half on the FMA pipe (softmax_exp.cuh).
-                p[e] = e == 0 ? make_float2(bw_ex2(x.x), bw_ex2(x.y)) : ex2_fma2(x);
+                p[e] = make_float2(bw_ex2(x.x), bw_ex2(x.y));
                 if (need_mask) {
                   const int q = q0 + 32 * c + t + 2 * e;
                   if (q >= a.Sq || (CAUSAL && q < kg)) p[e].x = 0.f;

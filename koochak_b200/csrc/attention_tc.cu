@@ -18,9 +18,7 @@
 //               rescaled when the row maximum grows by more than 2^8 over the
 //               maximum the exponentials were taken against (the rescale reads
 //               and rewrites O_t in TMEM). Probabilities up to 2^8 are exact in
-//               the 16-bit P, and O / l is unchanged by the choice of m. Half
-//               of the exponentials run on the FMA pipe (softmax_exp.cuh),
-//               half with ex2.approx.
+//               the 16-bit P, and O / l is unchanged by the choice of m.
 // TMEM (512 columns): S_0, S_1 at columns 0 and 128; O_0, O_1 at 256 and 256+D.
 // The S MMA of step j+1 for a tile is issued after the P V MMA of step j that
 // reads P from the same columns; tcgen05 MMAs issued by one thread execute in
@@ -33,7 +31,6 @@
 // log-sum-exp of the scaled scores, as the backward kernels expect.
 #include "host_utils.h"
 #include "sm100.cuh"
-#include "softmax_exp.cuh"
 
 #include <torch/extension.h>
 
@@ -127,9 +124,8 @@ __device__ __forceinline__ void softmax_step(uint32_t s_tm, uint32_t o_tm, int k
     for (int i = 0; i < 32; i += 4) {
       const float2 x0 = fma2(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sc2, mn2);
       const float2 x1 = fma2(make_float2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])), sc2, mn2);
-      // Half of the exponentials on the MUFU unit, half on the FMA pipe (softmax_exp.cuh).
       const float2 p0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
-      const float2 p1 = ex2_fma2(x1);
+      const float2 p1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
       rs0 = add2(rs0, p0);
       rs1 = add2(rs1, p1);
       pk[i / 2] = pack_pair<F16>(p0.x, p0.y);
@@ -502,30 +498,6 @@ bool flash_attention_forward_tc(const at::Tensor& q, const at::Tensor& k, const 
   }
 #undef KB_TC
   return true;
-}
-
-// The FMA-pipe 2^x of softmax_exp.cuh, elementwise over an fp32 tensor (numerics
-// tests compare it with exp2).
-__global__ void exp2_fma_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
-  for (long long i = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < n;
-       i += 2LL * gridDim.x * blockDim.x) {
-    const float2 v = ex2_fma2(make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f));
-    y[i] = v.x;
-    if (i + 1 < n) y[i + 1] = v.y;
-  }
-}
-
-void exp2_fma(const at::Tensor& x, at::Tensor& y) {
-  check_cuda_tensor(x, "x");
-  KB_CHECK(x.scalar_type() == at::kFloat && y.scalar_type() == at::kFloat && x.is_contiguous() && y.is_contiguous() &&
-               x.numel() == y.numel(),
-           "exp2_fma: contiguous fp32 tensors of one size");
-  const c10::cuda::CUDAGuard guard(x.device());
-  const long long n = x.numel();
-  const int grid = (int)std::max<long long>(1, std::min<long long>((n / 2 + 255) / 256, 4096));
-  exp2_fma_kernel<<<grid, 256, 0, c10::cuda::getCurrentCUDAStream().stream()>>>(x.data_ptr<float>(),
-                                                                                 y.data_ptr<float>(), n);
-  KB_LAUNCHED();
 }
 
 }  // namespace kb

@@ -1130,22 +1130,46 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   const int64_t tiles = batch * ((M + rows_per_tile - 1) / rows_per_tile) * ((N + bn - 1) / bn);
   const int sms = pair_mode ? (sms_all / 2) : sms_all;  // concurrent tile slots
   const int64_t num_kb = (K + 63) / 64;
-  // Stream-K for fp32 outputs without an activation (weight gradients, long
-  // K) when whole tiles would leave part of the last wave idle: the K-blocks of
-  // all tiles are spread evenly over every worker and partial tiles are summed
-  // into C with fp32 atomics (C first set to beta * D, or zero).
+  // fp32 outputs without an activation (weight gradients, long K) whose whole
+  // tiles would leave part of the last wave idle are cut along K, and the
+  // partial tiles are summed into C with fp32 atomics (C first set to
+  // beta * D, or zero):
+  //  * split-K first: every tile cut at the same K boundaries, units of one
+  //    split handed to neighbouring workers, so the workers running at the
+  //    same time read the same K range of the operand panels and those stay
+  //    in L2 (cutting the K-iterations of all tiles evenly over the workers,
+  //    stream-K, puts every worker at a different K offset and, once the
+  //    operands outgrow L2, re-reads them from DRAM). The smallest split
+  //    count that fills the machine is taken, as long as its atomic traffic
+  //    (splits x the size of C) stays moderate;
+  //  * stream-K otherwise.
+  // With a D operand (a residual to add) the copy of D into C and the
+  // atomics cost more than a partly idle last wave, so those cut only when
+  // whole tiles would leave a quarter of the machine idle.
   int splits = 1;
   int stream_k = 0;
   if (ct == at::kFloat && act == ACT_NONE && num_kb >= 8) {
-    const int64_t waves = (tiles + sms - 1) / sms;
-    const double filled = double(tiles) / double(waves * sms);
-    if (filled < 0.9) stream_k = 1;
+    auto fill = [&](int64_t units) {
+      const int64_t waves = (units + sms - 1) / sms;
+      return double(units) / double(waves * sms);
+    };
+    const bool has_d = p.D != nullptr && p.beta != 0.f;
+    if (fill(tiles) < (has_d ? 0.75 : 0.9)) {
+      const double c_bytes = double(batch) * double(M) * double(N) * 4.0;
+      for (int sp = 2; sp <= 8 && sp * 4 <= num_kb; ++sp) {
+        if (fill(tiles * sp) >= 0.9 && sp * c_bytes <= 96.0 * (1 << 20)) {
+          splits = sp;
+          break;
+        }
+      }
+      if (splits == 1) stream_k = 1;
+    }
   }
-  p.splits = 1;
-  p.kb_per_split = (int)num_kb;
+  p.splits = splits;
+  p.kb_per_split = (int)((num_kb + splits - 1) / splits);
   p.stream_k = stream_k;
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
-  if (stream_k) {
+  if (stream_k || splits > 1) {
     // C = beta * D (or 0); every split then adds its partial product.
     if (p.D != nullptr && p.beta != 0.f) {
       if (p.D != p.C || p.beta != 1.f) {
@@ -1164,7 +1188,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   std::memset(&maps, 0, sizeof(maps));
   {
     const int64_t esz = c.element_size();
-    bool ok = !stream_k && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+    bool ok = !stream_k && splits == 1 && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
               (!batched || (p.strideC * esz) % 16 == 0);
     if (ok && p.aux != nullptr)
       ok = (p.ldaux * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15) == 0 && (!batched || (p.strideAux * 2) % 16 == 0);
@@ -1182,7 +1206,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     }
   }
   if (pair_mode) {
-    const int grid2 = 2 * (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles, sms));
+    const int grid2 = 2 * (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles * splits, sms));
     if (bn == 256) {
       if (ct == at::kFloat) dispatch_act2<256, float>((int)act, ta, tb, p, maps, grid2, stream);
       else if (ct == at::kBFloat16) dispatch_act2<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid2, stream);
@@ -1194,7 +1218,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     }
     return;
   }
-  const int grid = (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles, sms));
+  const int grid = (int)(stream_k ? std::min<int64_t>(tiles * num_kb, sms) : std::min<int64_t>(tiles * splits, sms));
   if (bn == 256) {
     if (ct == at::kFloat) dispatch_act<256, float>((int)act, ta, tb, p, maps, grid, stream);
     else if (ct == at::kBFloat16) dispatch_act<256, __nv_bfloat16>((int)act, ta, tb, p, maps, grid, stream);
