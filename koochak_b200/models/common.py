@@ -113,3 +113,40 @@ def to_lp(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     out = torch.empty(t.shape, device=t.device, dtype=dtype)
     kf.cast_multi([t], [out])
     return out
+
+
+def accumulation_target(*params: torch.Tensor) -> Optional[torch.Tensor]:
+    """The existing fp32 gradient buffer of ``params`` that a backward may add into directly, or None.
+
+    Under gradient accumulation the second and later micro-steps would
+    otherwise produce a fresh weight gradient that autograd then adds into
+    ``.grad`` (one more read and write of every gradient). A backward may
+    instead accumulate into ``.grad`` itself (a GEMM with the old gradient as
+    its D operand) and return None for that weight, when nothing could
+    observe the difference: gradients are not being recorded, every
+    parameter already has a contiguous fp32 gradient of its own shape, no
+    hook is registered on the parameters (a hook expects to see the
+    accumulation), and -- for several parameters -- their gradients lie back
+    to back in one buffer (the layout autograd keeps when it adopted the
+    split views of one fused gradient on the first micro-step). Returns a
+    [sum of rows, cols] view over those gradients.
+    """
+
+    if torch.is_grad_enabled() or not params:
+        return None
+    grads = []
+    for p in params:
+        g = p.grad
+        if (g is None or g.dtype != torch.float32 or not g.is_contiguous() or g.shape != p.shape
+                or p._backward_hooks or getattr(p, "_post_accumulate_grad_hooks", None)):
+            return None
+        grads.append(g)
+    first = grads[0]
+    cols = first.numel() // first.shape[0]
+    rows = 0
+    for g in grads:
+        if (g.numel() // g.shape[0] != cols or g.untyped_storage().data_ptr() != first.untyped_storage().data_ptr()
+                or g.data_ptr() != first.data_ptr() + rows * cols * 4):
+            return None
+        rows += g.shape[0]
+    return first.as_strided((rows, cols), (cols, 1))

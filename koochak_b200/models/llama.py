@@ -35,8 +35,9 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..ops import functional as kf
+from ..ops._ext import native
 from ..utils.nn_utils import tag_param
-from .common import LowPrecisionShadows, compute_dtype, to_lp
+from .common import LowPrecisionShadows, accumulation_target, compute_dtype, to_lp
 from .gpt2 import _lp_copy_of, _with_lp_copy
 
 __all__ = ["LlamaConfig", "Llama", "rope_tables"]
@@ -123,6 +124,21 @@ class DecoderLayer(nn.Module):
                 m.up_proj.weight, m.down_proj.weight]
 
 
+def _wgrad(a: torch.Tensor, b: torch.Tensor, *weights: torch.Tensor) -> Optional[torch.Tensor]:
+    """fp32 weight gradient a^T b (both operands token-major) of ``weights`` (stacked by rows).
+
+    Added straight into the weights' ``.grad`` when ``accumulation_target``
+    allows it (later micro-steps of gradient accumulation; None is then
+    returned, so autograd adds nothing), else returned for autograd.
+    """
+
+    tgt = accumulation_target(*weights)
+    if tgt is not None:
+        kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out=tgt, d=tgt, beta=1.0)
+        return None
+    return kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+
+
 class _LayerFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_in, w_post, wq, wk, wv, wo, wg, wu, wd, lp, cos, sin, n_head, eps):
@@ -146,6 +162,7 @@ class _LayerFn(torch.autograd.Function):
         ctx.save_for_backward(x2, h1, r1, qkv, a2, lse, x_mid, h2, r2, gu, hs, w_in, w_post, qkv_w16, o_w16, gu_w16,
                               down_w16, cos, sin)
         ctx.dims = (B, S, C, H, D, Fd)
+        ctx.weights = (wq, wk, wv, wo, wg, wu, wd)
         return out.view(B, S, C)
 
     @staticmethod
@@ -159,16 +176,17 @@ class _LayerFn(torch.autograd.Function):
         dy = _lp_copy_of(dout, cdt)
         dy = dy.reshape(M, C) if dy is not None else to_lp(dout2, cdt)
         # MLP
+        wq, wk, wv, wo, wg, wu, wd = ctx.weights
         dhs = kf.gemm(dy, down_w16, b_mn_major=True)
-        d_down = kf.gemm(dy, hs, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+        d_down = _wgrad(dy, hs, wd)
         dgu = kf.swiglu_backward(gu, dhs)
         dh2 = kf.gemm(dgu, gu_w16, b_mn_major=True)
-        d_gu = kf.gemm(dgu, h2, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+        d_gu = _wgrad(dgu, h2, wg, wu)
         dx_mid, d_post, _, dmid = kf.norm_backward(dh2, x_mid, w_post, None, r2, rms=True, dres=dout2,
                                                    dx_dtype=torch.float32, want_lp=True)
         # attention
         da = kf.gemm(dmid, o_w16, b_mn_major=True)
-        d_o = kf.gemm(dmid, a2, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+        d_o = _wgrad(dmid, a2, wo)
         q5 = qkv.view(B, S, 3, H, D)
         dqkv = torch.empty((B, S, 3, H, D), device=qkv.device, dtype=cdt)
         kf.flash_attention_backward(q5[:, :, 0], q5[:, :, 1], q5[:, :, 2], a2.view(B, S, H, D), da.view(B, S, H, D),
@@ -176,11 +194,11 @@ class _LayerFn(torch.autograd.Function):
         kf.rope_apply_(dqkv[:, :, :2].view(B, S, 2 * H, D), cos, sin, inverse=True)
         dqkv2 = dqkv.view(M, 3 * C)
         dh1 = kf.gemm(dqkv2, qkv_w16, b_mn_major=True)
-        d_qkv = kf.gemm(dqkv2, h1, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+        d_qkv = _wgrad(dqkv2, h1, wq, wk, wv)
         dx, d_in, _, dx_lp = kf.norm_backward(dh1, x2, w_in, None, r1, rms=True, dres=dx_mid,
                                               dx_dtype=torch.float32, want_lp=True)
-        dq, dk, dv = d_qkv.split(C, dim=0)
-        dg, du = d_gu.split(Fd, dim=0)
+        dq, dk, dv = d_qkv.split(C, dim=0) if d_qkv is not None else (None, None, None)
+        dg, du = d_gu.split(Fd, dim=0) if d_gu is not None else (None, None)
         return (_with_lp_copy(dx.view(B, S, C), dx_lp), d_in, d_post, dq, dk, dv, d_o, dg, du, d_down,
                 None, None, None, None, None)
 
@@ -190,11 +208,16 @@ class _EmbedFn(torch.autograd.Function):
     def forward(ctx, idx, w):
         ctx.save_for_backward(idx)
         ctx.rows = w.shape[0]
+        ctx.weight = w
         return kf.embedding_forward(idx, w, None, idx.shape[1])
 
     @staticmethod
     def backward(ctx, dout):
         (idx,) = ctx.saved_tensors
+        tgt = accumulation_target(ctx.weight)
+        if tgt is not None:  # scatter-add straight into the existing gradient
+            native().embedding_backward(idx.contiguous(), dout.float().contiguous(), tgt, None, int(idx.shape[1]))
+            return None, None
         dw, _ = kf.embedding_backward(idx, dout.float().contiguous(), ctx.rows, 0, idx.shape[1], want_wpe=False)
         return None, dw
 
@@ -217,6 +240,7 @@ class _HeadFn(torch.autograd.Function):
         n_valid = (tgt != ignore_index).sum().clamp_min(1).to(torch.float32)
         ctx.save_for_backward(x2, h, r, logits, lse, tgt, n_valid, norm_w, head_w16)
         ctx.meta = (B, S, C, V, ignore_index, eps)
+        ctx.head_weight = head_w
         return loss_rows.sum() / n_valid
 
     @staticmethod
@@ -227,7 +251,7 @@ class _HeadFn(torch.autograd.Function):
                                    ignore_index)
         dlog = logits[:, :V]
         dh = kf.gemm(dlog, head_w16, b_mn_major=True)
-        dW = kf.gemm(dlog, h, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32)
+        dW = _wgrad(dlog, h, ctx.head_weight)
         dx, dnorm, _, dx_lp = kf.norm_backward(dh, x2, norm_w, None, r, rms=True, dx_dtype=torch.float32,
                                                want_lp=True)
         return _with_lp_copy(dx.view(B, S, C), dx_lp), dnorm, dW, None, None, None, None

@@ -349,6 +349,36 @@ def test_llama_native_matches_reference_path(head_dim):
         assert _rel(g_native[n], p.grad) < 0.08, n
 
 
+def test_llama_gradient_accumulation_in_place_matches_autograd():
+    """Later micro-steps add weight gradients straight into .grad (GEMM with the old gradient as D);
+    the result matches autograd's accumulation, which a hook on every parameter forces in the twin."""
+
+    from koochak_b200.models import Llama
+
+    def make():
+        torch.manual_seed(6)
+        return Llama(n_layer=2, n_head=4, dim=256, ffn_dim=688, vocab_size=1024, max_seq_len=128).to(DEV)
+
+    ours, twin = make(), make()
+    for p in twin.parameters():
+        p.register_post_accumulate_grad_hook(lambda _p: None)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    batches = [torch.randint(0, 1024, (2, 129), generator=g).to(DEV) for _ in range(3)]
+    first_ptr = None
+    for i, b in enumerate(batches):
+        for m in (ours, twin):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = m(b[:, :-1], b[:, 1:]) / 3
+            loss.backward()
+        wq = ours.model.layers[0].self_attn.q_proj.weight
+        if i == 0:
+            first_ptr = wq.grad.data_ptr()
+        else:
+            assert wq.grad.data_ptr() == first_ptr  # accumulated in place, not replaced
+    for (n, p), q in zip(ours.named_parameters(), twin.parameters()):
+        assert _rel(p.grad, q.grad) < 1e-3, n
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (520, 384, 200), (2048, 2304, 768), (1000, 776, 1024)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
 @pytest.mark.parametrize("block_n", [-128, -256])
