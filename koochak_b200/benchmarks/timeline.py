@@ -202,6 +202,8 @@ def main(argv=None) -> int:
     ap.add_argument("--gap-us", type=float, default=10.0)
     ap.add_argument("--out", default=None)
     ap.add_argument("--stacks", action="store_true", help="record Python stacks (slower host) to locate syncs")
+    ap.add_argument("--graph", action="store_true",
+                    help="capture forward + backward as a CUDA graph (train.cuda_graph_step; one micro-batch)")
     args = ap.parse_args(argv)
     from torch.profiler import ProfilerActivity, profile
 
@@ -231,6 +233,8 @@ def main(argv=None) -> int:
 
     cfg = {"max_steps": last + 1, "log_every": 10 ** 9, "eval_every": 0, "ckpt_every": 10 ** 9, "keep_last_k": 1,
            "ema": {"enabled": True, "decay": 0.999, "offload_to_cpu": False}, "warn_unsharded": False, **extra}
+    if args.graph:
+        cfg.update(cuda_graph_step=True, cuda_graph_warmup=max(1, args.warmup - 2))
     with tempfile.TemporaryDirectory(prefix="kb_timeline_") as out_dir:
         cfg["out_dir"] = out_dir
         training_loop(model=model, dataset=data(), step_fn=step_fn, optimizer=opt, scheduler=sched, train_cfg=cfg,

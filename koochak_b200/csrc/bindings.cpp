@@ -49,6 +49,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "SMs kept free of persistent GEMM / attention grids (for kernels overlapped beside them)");
   m.def("sm_reserve", []() { return kb::sm_reserve().load(); }, "current SM reserve");
   m.def("launch_count", []() { return kb::launch_counter().load(); }, "kernels launched by this library so far");
+  m.def(
+      "add_launches", [](int64_t n) { kb::launch_counter().fetch_add(n); },
+      "count kernels of this library launched by a CUDA-graph replay", pybind11::arg("n"));
   kb::register_norm_ops(m);
   kb::register_elementwise_ops(m);
   kb::register_attention_ops(m);

@@ -56,6 +56,7 @@ from .health.gpu import summarize_failures_for_stdout
 from .interruption import EVACUATION_EXIT_CODE, OOM_RESTART_EXIT_CODE, EvacuationController
 from .runtime.checkpoints import CheckpointKeeper, EmaBuilder, restore_ema, restore_training_state
 from .runtime.gate import GradientGate
+from .runtime.graphed_step import GraphedStep
 from .runtime.settings import EmaSettings, LoopSettings, shard_mode
 from .storage import checkpoint as checkpoint_lib
 from .utils import config as config_lib
@@ -113,6 +114,14 @@ def _sum_of(value: Any) -> float:
     if isinstance(value, (list, tuple)):
         return float(sum(float(x) for x in value))
     return float(value)
+
+
+def _checked(out: Any) -> Mapping[str, Any]:
+    if not isinstance(out, Mapping) or "loss" not in out:
+        raise RuntimeError("step_fn must return a dict containing a 'loss' Tensor")
+    if not isinstance(out["loss"], torch.Tensor):
+        raise RuntimeError("step_fn returned a 'loss' that is not a torch.Tensor")
+    return out
 
 
 def _skip_counters(batch: Any) -> Dict[str, float]:
@@ -216,9 +225,11 @@ class _MicroSteps:
         count = s.grad_accum
         prefetching = r.on_cuda and s.prefetch_batches > 0
         can_defer_sync = hasattr(r.model, "no_sync")
+        graphed = r.graphed_step if count == 1 else None
         for micro in range(count):
             defer = r.model.no_sync() if can_defer_sync and micro < count - 1 else nullcontext()
             cast = r.autocast() if not s.autocast_in_step_fn else nullcontext()
+            backward_done = False
             with defer, cast:
                 r.micro_position = (micro, "fetch")
                 began = prof.start("batch_wait")
@@ -227,21 +238,31 @@ class _MicroSteps:
                 for k, v in _skip_counters(batch).items():
                     rec.skip_counts[k] = rec.skip_counts.get(k, 0.0) + v
                 r.micro_position = (micro, "step_fn")
-                out = prof.run(rec.timings, "profile_loop_step_fn_time_s",
-                               lambda: r.step_fn(r.model, batch, r.step_ctx(step)))
+                if graphed is not None and graphed.wants(batch):
+                    def forward_backward(b):
+                        o = _checked(r.step_fn(r.model, b, r.step_ctx(step)))
+                        lo = o["loss"] / count
+                        r.scaler.scale(lo).backward()
+                        return o, lo
+
+                    out, loss = prof.run(rec.timings, "profile_loop_step_fn_time_s",
+                                         lambda: graphed.run(batch, forward_backward))
+                    backward_done = True
+                else:
+                    out = _checked(prof.run(rec.timings, "profile_loop_step_fn_time_s",
+                                            lambda: r.step_fn(r.model, batch, r.step_ctx(step))))
+                    if graphed is not None:
+                        graphed.note_eager()
+                    loss = out["loss"] / count
                 if want_rank_timing and isinstance(out, Mapping):
                     for key in s.rank_timing_extra_keys:
                         if out.get(key) is not None:
                             v = out[key]
                             rec.extra_timing[key] = rec.extra_timing.get(key, 0.0) + float(
                                 v.detach() if isinstance(v, torch.Tensor) else v)
-                if not isinstance(out, Mapping) or "loss" not in out:
-                    raise RuntimeError("step_fn must return a dict containing a 'loss' Tensor")
-                if not isinstance(out["loss"], torch.Tensor):
-                    raise RuntimeError("step_fn returned a 'loss' that is not a torch.Tensor")
-                loss = out["loss"] / count
             r.micro_position = (micro, "backward")
-            prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
+            if not backward_done:
+                prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
             part = loss.detach()
             rec.loss = part if rec.loss is None else rec.loss + part
             if s.scalarize_loss_every_step:
@@ -444,6 +465,9 @@ class _Run:
         self.profiler = _Profiler(s, self.on_cuda, self.device)
         self.gate = GradientGate(max_norm=s.grad_clip_norm, check_every=s.nonfinite_grad_check_every,
                                  scaler=self.scaler, profile=lambda key, thunk: thunk())
+        self.graphed_step: Optional[GraphedStep] = None
+        if s.cuda_graph_step and self.on_cuda and self.world_size == 1 and s.grad_accum == 1:
+            self.graphed_step = GraphedStep(model, warmup=s.cuda_graph_warmup)
         self.micro_steps = _MicroSteps(self)
         self.stops = _StopControl(self)
         self.oom = _OomGuard(self, oom_lib.OomRecoverySettings.from_cfg(train_cfg))

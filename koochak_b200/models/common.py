@@ -77,7 +77,15 @@ class LowPrecisionShadows:
 
         return self._fused[(index, dtype)]
 
+    def refresh(self) -> None:
+        """Bring every 16-bit copy handed out so far up to date with its parameter."""
+
+        for dtype in list(getattr(self, "_dtypes_seen", ())):
+            self.get(dtype)
+
     def get(self, dtype: torch.dtype) -> Dict[int, torch.Tensor]:
+        seen = self.__dict__.setdefault("_dtypes_seen", set())
+        seen.add(dtype)
         if self.fused_groups:
             self._ensure_fused(dtype)
         stale_src: List[torch.Tensor] = []

@@ -1,0 +1,136 @@
+"""Forward and backward of a training step captured once as a CUDA graph and replayed.
+
+A single-GPU step of the benchmark models launches a few hundred kernels for
+forward and backward; on B200 the host needs about as long to enqueue them
+as the GPU needs to run them, so the GPU idles wherever the host has a burst
+of work (the optimizer's preparation, logging). Captured into one CUDA graph,
+forward and backward become one launch and the host runs ahead.
+
+``GraphedStep`` (``train.cuda_graph_step: true``) runs the first
+``warmup`` updates eagerly (lazy initialisation of the native library, the
+allocator and the autograd graph happens there), captures the next one --
+``step_fn`` on static copies of the batch tensors, the loss scaling and
+``backward`` -- and replays the graph from then on. The gate, the optimizer,
+the EMA and everything else of the update stay eager. Preconditions, checked
+where they can be:
+
+* one process (a data-parallel wrapper reduces gradients from hooks, which
+  a replay does not run), one micro-batch per update (``grad_accum == 1``),
+  a CUDA device;
+* every batch a mapping of tensors with the captured shapes and dtypes (a
+  batch that differs runs eagerly);
+* ``step_fn`` behaves the same on every step: what it computes must not
+  depend on ``ctx`` or on host state (the forced-overflow benchmark step, for
+  instance, must run eagerly);
+* the model keeps its 16-bit weight copies in place (``LowPrecisionShadows``);
+  stale copies are refreshed eagerly before every replay, since the replay
+  skips the forward's Python code.
+
+Gradients: at capture autograd adopts the backward's gradient buffers as
+``.grad`` (they come from the graph's memory pool); every replay rewrites
+them, so after each replay those same tensors are put back as ``.grad``.
+Kernels of this library that the graph launches are added to the library's
+launch counter on every replay.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Callable, Dict, List, Mapping, Optional, Tuple
+
+import torch
+
+__all__ = ["GraphedStep"]
+
+
+def _signature(batch: Any) -> Optional[Tuple]:
+    if not isinstance(batch, Mapping):
+        return None
+    sig = []
+    for k in sorted(batch, key=str):
+        v = batch[k]
+        if not isinstance(v, torch.Tensor):
+            return None
+        sig.append((str(k), tuple(v.shape), v.dtype, v.device))
+    return tuple(sig)
+
+
+class GraphedStep:
+    def __init__(self, model: torch.nn.Module, *, warmup: int = 3) -> None:
+        self.model = model
+        self.warmup = max(1, int(warmup))
+        self.eager_steps = 0
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.sig: Optional[Tuple] = None
+        self.static: Dict[str, torch.Tensor] = {}
+        self.out: Optional[Mapping[str, Any]] = None
+        self.loss: Optional[torch.Tensor] = None
+        self.grads: List[Tuple[torch.nn.Parameter, torch.Tensor]] = []
+        self.kernels_per_replay = 0
+        self.disabled = False
+
+    # ------------------------------------------------------------------ helpers
+    def _refresh_shadows(self) -> None:
+        for m in self.model.modules():
+            shadows = getattr(m, "_shadows", None)
+            refresh = getattr(shadows, "refresh", None)
+            if callable(refresh):
+                refresh()
+
+    def _launch_count(self) -> int:
+        try:
+            from ..ops._ext import native
+
+            return int(native().launch_count())
+        except ImportError:
+            return 0
+
+    # ------------------------------------------------------------------ API
+    def wants(self, batch: Any) -> bool:
+        """Whether this update goes through the graph (capture or replay) instead of the eager path."""
+
+        if self.disabled:
+            return False
+        if self.graph is None:
+            return self.eager_steps >= self.warmup and _signature(batch) is not None
+        return _signature(batch) == self.sig
+
+    def note_eager(self) -> None:
+        self.eager_steps += 1
+
+    def run(self, batch: Mapping[str, torch.Tensor], forward_backward: Callable[[Mapping[str, torch.Tensor]],
+                                                                               Tuple[Mapping[str, Any], torch.Tensor]]
+            ) -> Tuple[Mapping[str, Any], torch.Tensor]:
+        """Forward and backward of ``batch``; returns (step_fn's output, the micro-step loss)."""
+
+        if self.graph is None:
+            self._capture(batch, forward_backward)  # counted once, at capture
+        else:
+            for k, v in batch.items():
+                self.static[str(k)].copy_(v, non_blocking=True)
+            self._refresh_shadows()
+            self.graph.replay()
+            if self.kernels_per_replay:
+                from ..ops._ext import native
+
+                native().add_launches(self.kernels_per_replay)
+        for p, g in self.grads:
+            p.grad = g
+        assert self.out is not None and self.loss is not None
+        return self.out, self.loss
+
+    def _capture(self, batch, forward_backward) -> None:
+        self.sig = _signature(batch)
+        self.static = {str(k): v.detach().clone() for k, v in batch.items()}
+        for p in self.model.parameters():
+            p.grad = None
+        self._refresh_shadows()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        before = self._launch_count()
+        with torch.cuda.graph(graph):
+            out, loss = forward_backward(self.static)
+        self.kernels_per_replay = self._launch_count() - before
+        self.graph = graph
+        self.out, self.loss = out, loss
+        self.grads = [(p, p.grad) for p in self.model.parameters() if p.grad is not None]
+        graph.replay()  # capture records the kernels without running them

@@ -67,6 +67,8 @@ _KEYS: Tuple[Tuple[str, str, Callable[[Any], Any], Any], ...] = (
     ("device_timing", "device_timing", bool, False),
     ("comm_transport", "comm_transport", str, "auto"),
     ("profile_nvtx", "profile_nvtx", bool, False),
+    ("cuda_graph_step", "cuda_graph_step", bool, False),
+    ("cuda_graph_warmup", "cuda_graph_warmup", int, 3),
 )
 
 
@@ -111,6 +113,8 @@ class LoopSettings:
     device_timing: bool = False
     comm_transport: str = "auto"
     profile_nvtx: bool = False
+    cuda_graph_step: bool = False
+    cuda_graph_warmup: int = 3
 
     @classmethod
     def from_cfg(cls, cfg: Any) -> "LoopSettings":
