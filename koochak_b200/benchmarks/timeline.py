@@ -232,6 +232,7 @@ def main(argv=None) -> int:
             yield dict(batch)
 
     cfg = {"max_steps": last + 1, "log_every": 10 ** 9, "eval_every": 0, "ckpt_every": 10 ** 9, "keep_last_k": 1,
+           "scalarize_loss_every_step": False,  # as in bench.py's device-timed phase
            "ema": {"enabled": True, "decay": 0.999, "offload_to_cpu": False}, "warn_unsharded": False, **extra}
     if args.graph:
         cfg.update(cuda_graph_step=True, cuda_graph_warmup=max(1, args.warmup - 2))

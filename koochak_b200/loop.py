@@ -242,8 +242,7 @@ class _MicroSteps:
                     def forward_backward(b):
                         o = _checked(r.step_fn(r.model, b, r.step_ctx(step)))
                         lo = o["loss"] / count
-                        r.scaler.scale(lo).backward()
-                        return o, lo
+                        return o, lo, r.scaler.scale(lo)
 
                     out, loss = prof.run(rec.timings, "profile_loop_step_fn_time_s",
                                          lambda: graphed.run(batch, forward_backward))
@@ -265,8 +264,6 @@ class _MicroSteps:
                 prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
             part = loss.detach()
             rec.loss = part if rec.loss is None else rec.loss + part
-            if s.scalarize_loss_every_step:
-                rec.loss_value = float(rec.loss)
             rec.out = out
         return rec
 
@@ -765,6 +762,10 @@ class _Run:
         self.gate.profile = lambda key, thunk: prof.run(rec.timings, key, thunk)
         self.gate.begin(self.model, self.optimizer, step, self.on_cuda)
         self._update_parameters(step, rec)
+        if s.scalarize_loss_every_step and rec.loss is not None:
+            # Read once per update, after the optimizer step is enqueued (the sum of the micro-step losses):
+            # a read after each micro-step would stall the GPU while the host enqueues the next one.
+            rec.loss_value = float(rec.loss)
 
         prof.barrier()
         seconds = time.perf_counter() - began

@@ -26,9 +26,9 @@ where they can be:
   stale copies are refreshed eagerly before every replay, since the replay
   skips the forward's Python code.
 
-Gradients: at capture autograd adopts the backward's gradient buffers as
-``.grad`` (they come from the graph's memory pool); every replay rewrites
-them, so after each replay those same tensors are put back as ``.grad``.
+Gradients: the captured backward returns them (``torch.autograd.grad``
+over the parameters) into buffers of the graph's memory pool; every replay
+rewrites them, and after each replay those tensors are set as ``.grad``.
 Kernels of this library that the graph launches are added to the library's
 launch counter on every replay.
 """
@@ -97,13 +97,17 @@ class GraphedStep:
     def note_eager(self) -> None:
         self.eager_steps += 1
 
-    def run(self, batch: Mapping[str, torch.Tensor], forward_backward: Callable[[Mapping[str, torch.Tensor]],
-                                                                               Tuple[Mapping[str, Any], torch.Tensor]]
+    def run(self, batch: Mapping[str, torch.Tensor],
+            forward: Callable[[Mapping[str, torch.Tensor]], Tuple[Mapping[str, Any], torch.Tensor, torch.Tensor]]
             ) -> Tuple[Mapping[str, Any], torch.Tensor]:
-        """Forward and backward of ``batch``; returns (step_fn's output, the micro-step loss)."""
+        """Forward and backward of ``batch``; returns (step_fn's output, the micro-step loss).
+
+        ``forward(batch)`` returns (step_fn's output, the micro-step loss, the
+        loss to differentiate -- the scaled one under a GradScaler).
+        """
 
         if self.graph is None:
-            self._capture(batch, forward_backward)  # counted once, at capture
+            self._capture(batch, forward)  # counted once, at capture
         else:
             for k, v in batch.items():
                 self.static[str(k)].copy_(v, non_blocking=True)
@@ -118,19 +122,27 @@ class GraphedStep:
         assert self.out is not None and self.loss is not None
         return self.out, self.loss
 
-    def _capture(self, batch, forward_backward) -> None:
+    def _capture(self, batch, forward) -> None:
         self.sig = _signature(batch)
         self.static = {str(k): v.detach().clone() for k, v in batch.items()}
-        for p in self.model.parameters():
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        for p in params:
             p.grad = None
         self._refresh_shadows()
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         before = self._launch_count()
-        with torch.cuda.graph(graph):
-            out, loss = forward_backward(self.static)
+        try:
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+                out, loss, scaled = forward(self.static)
+                # Gradients as outputs of the captured backward (autograd.grad, not backward(): the
+                # parameters' gradient-accumulation nodes of the eager updates belong to another stream).
+                grads = torch.autograd.grad(scaled, params, allow_unused=True)
+        except Exception:
+            self.disabled = True
+            raise
         self.kernels_per_replay = self._launch_count() - before
         self.graph = graph
         self.out, self.loss = out, loss
-        self.grads = [(p, p.grad) for p in self.model.parameters() if p.grad is not None]
+        self.grads = [(p, g) for p, g in zip(params, grads) if g is not None]
         graph.replay()  # capture records the kernels without running them
