@@ -229,43 +229,55 @@ class _MicroSteps:
         for micro in range(count):
             defer = r.model.no_sync() if can_defer_sync and micro < count - 1 else nullcontext()
             cast = r.autocast() if not s.autocast_in_step_fn else nullcontext()
-            backward_done = False
-            with defer, cast:
-                r.micro_position = (micro, "fetch")
-                began = prof.start("batch_wait")
-                batch = next(batches) if prefetching else to_device(next(batches), r.device)
-                rec.batch_wait_s += prof.stop(rec.timings, "profile_loop_batch_wait_time_s", began)
-                for k, v in _skip_counters(batch).items():
-                    rec.skip_counts[k] = rec.skip_counts.get(k, 0.0) + v
-                r.micro_position = (micro, "step_fn")
-                if graphed is not None and graphed.wants(batch):
-                    def forward_backward(b):
-                        o = _checked(r.step_fn(r.model, b, r.step_ctx(step)))
-                        lo = o["loss"] / count
-                        return o, lo, r.scaler.scale(lo)
-
-                    out, loss = prof.run(rec.timings, "profile_loop_step_fn_time_s",
-                                         lambda: graphed.run(batch, forward_backward))
-                    backward_done = True
-                else:
-                    out = _checked(prof.run(rec.timings, "profile_loop_step_fn_time_s",
-                                            lambda: r.step_fn(r.model, batch, r.step_ctx(step))))
-                    if graphed is not None:
-                        graphed.note_eager()
-                    loss = out["loss"] / count
-                if want_rank_timing and isinstance(out, Mapping):
-                    for key in s.rank_timing_extra_keys:
-                        if out.get(key) is not None:
-                            v = out[key]
-                            rec.extra_timing[key] = rec.extra_timing.get(key, 0.0) + float(
-                                v.detach() if isinstance(v, torch.Tensor) else v)
-            r.micro_position = (micro, "backward")
-            if not backward_done:
-                prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
+            # In graph mode forward and backward always run on the graph's own stream (eager updates too),
+            # so the autograd nodes of the parameters are made on the stream the capture uses.
+            side = graphed.on_side_stream() if graphed is not None else nullcontext()
+            with side:
+                out, loss = self._one(r, step, micro, count, batches, rec, graphed, defer, cast, prefetching,
+                                      want_rank_timing)
             part = loss.detach()
             rec.loss = part if rec.loss is None else rec.loss + part
             rec.out = out
         return rec
+
+    @staticmethod
+    def _one(r, step, micro, count, batches, rec, graphed, defer, cast, prefetching, want_rank_timing):
+        """One micro-batch: fetch, step_fn, backward (or the captured graph). Returns (output, loss)."""
+
+        s, prof = r.settings, r.profiler
+        backward_done = False
+        with defer, cast:
+            r.micro_position = (micro, "fetch")
+            began = prof.start("batch_wait")
+            batch = next(batches) if prefetching else to_device(next(batches), r.device)
+            rec.batch_wait_s += prof.stop(rec.timings, "profile_loop_batch_wait_time_s", began)
+            for k, v in _skip_counters(batch).items():
+                rec.skip_counts[k] = rec.skip_counts.get(k, 0.0) + v
+            r.micro_position = (micro, "step_fn")
+            if graphed is not None and graphed.wants(batch):
+                def forward(b):
+                    o = _checked(r.step_fn(r.model, b, r.step_ctx(step)))
+                    lo = o["loss"] / count
+                    return o, lo, r.scaler.scale(lo)
+
+                out, loss = prof.run(rec.timings, "profile_loop_step_fn_time_s", lambda: graphed.run(batch, forward))
+                backward_done = True
+            else:
+                out = _checked(prof.run(rec.timings, "profile_loop_step_fn_time_s",
+                                        lambda: r.step_fn(r.model, batch, r.step_ctx(step))))
+                if graphed is not None:
+                    graphed.note_eager()
+                loss = out["loss"] / count
+            if want_rank_timing and isinstance(out, Mapping):
+                for key in s.rank_timing_extra_keys:
+                    if out.get(key) is not None:
+                        v = out[key]
+                        rec.extra_timing[key] = rec.extra_timing.get(key, 0.0) + float(
+                            v.detach() if isinstance(v, torch.Tensor) else v)
+        r.micro_position = (micro, "backward")
+        if not backward_done:
+            prof.run(rec.timings, "profile_loop_backward_time_s", lambda: r.scaler.scale(loss).backward())
+        return out, loss
 
 
 class _StopControl:

@@ -35,6 +35,7 @@ launch counter on every replay.
 
 from __future__ import annotations
 
+import contextlib
 from typing import Any, Callable, Dict, List, Mapping, Optional, Tuple
 
 import torch
@@ -67,6 +68,7 @@ class GraphedStep:
         self.grads: List[Tuple[torch.nn.Parameter, torch.Tensor]] = []
         self.kernels_per_replay = 0
         self.disabled = False
+        self.stream: Optional[torch.cuda.Stream] = None
 
     # ------------------------------------------------------------------ helpers
     def _refresh_shadows(self) -> None:
@@ -96,6 +98,24 @@ class GraphedStep:
 
     def note_eager(self) -> None:
         self.eager_steps += 1
+
+    @contextlib.contextmanager
+    def on_side_stream(self):
+        """Run a micro-step's forward and backward on the graph's stream, ordered after earlier work.
+
+        The parameters' gradient-accumulation nodes are created on the stream
+        current at their first use and live as long as the module; running
+        the eager updates and the capture on one stream keeps them on it (a
+        capture that met nodes of the default stream would fail).
+        """
+
+        if self.stream is None:
+            self.stream = torch.cuda.Stream()
+        cur = torch.cuda.current_stream()
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            yield
+        cur.wait_stream(self.stream)
 
     def run(self, batch: Mapping[str, torch.Tensor],
             forward: Callable[[Mapping[str, torch.Tensor]], Tuple[Mapping[str, Any], torch.Tensor, torch.Tensor]]
@@ -133,10 +153,9 @@ class GraphedStep:
         graph = torch.cuda.CUDAGraph()
         before = self._launch_count()
         try:
-            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            with torch.cuda.graph(graph, stream=self.stream, capture_error_mode="thread_local"):
                 out, loss, scaled = forward(self.static)
-                # Gradients as outputs of the captured backward (autograd.grad, not backward(): the
-                # parameters' gradient-accumulation nodes of the eager updates belong to another stream).
+                # Gradients as outputs of the captured backward, in buffers of the graph's pool.
                 grads = torch.autograd.grad(scaled, params, allow_unused=True)
         except Exception:
             self.disabled = True
