@@ -1145,7 +1145,9 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   //  * stream-K otherwise.
   // With a D operand (a residual to add) the copy of D into C and the
   // atomics cost more than a partly idle last wave, so those cut only when
-  // whole tiles would leave a quarter of the machine idle.
+  // whole tiles would leave a quarter of the machine idle -- unless D is C
+  // itself with beta 1 (accumulation into an existing gradient), where the
+  // partial tiles are simply added into C.
   int splits = 1;
   int stream_k = 0;
   if (ct == at::kFloat && act == ACT_NONE && num_kb >= 8) {
@@ -1153,7 +1155,8 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
       const int64_t waves = (units + sms - 1) / sms;
       return double(units) / double(waves * sms);
     };
-    const bool has_d = p.D != nullptr && p.beta != 0.f;
+    // C += A B^T in place (D is C, beta 1) needs no copy of D: the cut costs what it costs without D.
+    const bool has_d = p.D != nullptr && p.beta != 0.f && !(p.D == p.C && p.beta == 1.f);
     if (fill(tiles) < (has_d ? 0.75 : 0.9)) {
       const double c_bytes = double(batch) * double(M) * double(N) * 4.0;
       for (int sp = 2; sp <= 8 && sp * 4 <= num_kb; ++sp) {

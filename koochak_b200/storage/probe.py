@@ -11,9 +11,11 @@ unclosed file is visible, and how long a closed file takes to read back with
 its exact bytes. From those it recommends ``LocalStore`` settings
 (``publish="link"`` when hard links work, else ``"exclusive"``;
 ``verify_readback`` and ``read_settle_seconds`` when read-after-close lags),
-then exercises the store API: small-object put/get/stat latency, listing,
-and single- and multi-stream throughput, from which it recommends a
-``StoreProfile``. Optional phases: a checkpoint-sized payload written as 1..N
+then exercises the store API: the contract (put/get/ranged get/stat/list
+agree, create-only puts, delete), small-object put/get/stat latency,
+listing, and large-object throughput -- one stream, ranged parallel reads of
+one object, many objects at once, each cold (page cache dropped where the
+filesystem allows) and warm -- from which it recommends a ``StoreProfile``. Optional phases: a checkpoint-sized payload written as 1..N
 concurrent parts and timed until every part reads back with its exact
 SHA-256; and a synthetic ``ShardWriter`` dataset read back with
 ``assign_shards``. Everything lives under a fresh ``koochak-probe-<id>``
@@ -147,32 +149,113 @@ def _recommend_local(posix: Dict[str, Any]) -> Dict[str, Any]:
     return rec
 
 
+def _semantics(store: Store, prefix: str, small: bytes) -> Dict[str, Any]:
+    """The store contract the checkpoint and dataset code relies on, checked on one small object."""
+
+    key = f"{prefix}/semantics"
+    info = store.put(key, small)
+    seen = store.stat(key)
+    out: Dict[str, Any] = {
+        "put_info_matches": info.size == len(small),
+        "get_matches": store.get(key) == small,
+        "range_get_matches": store.get(key, 1, 3) == small[1:4],
+        "stat_size_matches": seen is not None and seen.size == len(small),
+        "listed_after_put": key in store.list(f"{prefix}/"),
+    }
+    try:
+        store.put(key, small)
+        out["create_only"] = False
+    except FileExistsError:
+        out["create_only"] = True
+    store.delete(key)
+    out["absent_after_delete"] = store.stat(key) is None
+    out["ok"] = all(out.values())
+    return out
+
+
+def _evict(store: Store, key: str) -> bool:
+    """Best effort: drop a local file's cached pages, so the next read of it comes from the device."""
+
+    path = store.local_path(key)
+    fadvise = getattr(os, "posix_fadvise", None)
+    if path is None or fadvise is None:
+        return False
+    fd = os.open(path, os.O_RDONLY)
+    try:
+        fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+        return True
+    except OSError:
+        return False
+    finally:
+        os.close(fd)
+
+
+def _tagged(data: bytes, tag: int) -> bytes:
+    """``data`` with a distinct 16-byte head, so separate objects never share cached pages by content."""
+
+    return tag.to_bytes(16, "little") + data[16:]
+
+
 def _store_phase(store: Store, prefix: str, small: bytes, count: int, large: bytes,
                  streams: Sequence[int]) -> Dict[str, Any]:
-    puts, gets, stats = [], [], []
-    for i in range(count):
-        k = f"{prefix}/small/{i:05d}"
-        puts.append(_timed(lambda: store.put(k, small)))
-        gets.append(_timed(lambda: store.get(k)))
-        stats.append(_timed(lambda: store.stat(k)))
-    out: Dict[str, Any] = {"small_put": _pct(puts), "small_get": _pct(gets), "small_stat": _pct(stats)}
-    out["list_seconds"] = _timed(lambda: store.list(f"{prefix}/small"))
+    out: Dict[str, Any] = {"semantics": _semantics(store, prefix, small)}
+    keys = [f"{prefix}/small/{i:05d}" for i in range(count)]
+    out["small_put"] = _pct([_timed(lambda k=k: store.put(k, small)) for k in keys])
+    out["small_stat"] = _pct([_timed(lambda k=k: store.stat(k)) for k in keys])
+    out["small_get"] = _pct([_timed(lambda k=k: store.get(k)) for k in keys])
+    listed: List[str] = []
+    out["list_seconds"] = _timed(lambda: listed.extend(store.list(f"{prefix}/small/")))
+    out["list_complete"] = sorted(listed) == keys
+
+    # Large objects: a separate object for every cold measurement (reading warms what it touches).
+    n_max, size = max(streams), len(large)
+    single, ranged = f"{prefix}/large/single", f"{prefix}/large/ranged"
+    many = [f"{prefix}/large/{j:03d}" for j in range(n_max)]
+    put_one = _timed(lambda: store.put(single, _tagged(large, 0)))
+    with ThreadPoolExecutor(max_workers=n_max + 1) as pool:
+        put_all = _timed(lambda: list(pool.map(lambda jk: store.put(jk[1], _tagged(large, jk[0] + 1)),
+                                               enumerate([ranged, *many]))))
+    cold_ok = all([_evict(store, k) for k in (single, ranged, *many)])
+    cold = _timed(lambda: store.get(single))
+    warm = _timed(lambda: store.get(single))
+    out["large_single_stream"] = {"bytes": size, "put_mb_s": size / put_one / _MB, "cold_get_mb_s": size / cold / _MB,
+                                  "warm_get_mb_s": size / warm / _MB, "cold_is_cold": cold_ok}
+    part = -(-size // n_max)
+
+    def ranged_read() -> None:
+        with ThreadPoolExecutor(max_workers=n_max) as pool:
+            got = sum(pool.map(lambda off: len(store.get(ranged, off, min(part, size - off))), range(0, size, part)))
+        if got != size:
+            raise RuntimeError(f"ranged read returned {got} of {size} bytes")
+
+    cold = _timed(ranged_read)
+    warm = _timed(ranged_read)
+    out["large_ranged"] = {"ranges": n_max, "part_bytes": part, "cold_get_mb_s": size / cold / _MB,
+                           "warm_get_mb_s": size / warm / _MB}
+    conc: Dict[str, Any] = {"put_streams": n_max + 1, "put_mb_s": size * (n_max + 1) / put_all / _MB}
+    with ThreadPoolExecutor(max_workers=n_max) as pool:
+        t = _timed(lambda: list(pool.map(store.get, many)))
+    conc[f"cold_get_{n_max}_streams_mb_s"] = size * n_max / t / _MB
     for n in streams:
-        keys = [f"{prefix}/large-{n}-{j}" for j in range(n)]
         with ThreadPoolExecutor(max_workers=n) as pool:
-            tw = _timed(lambda: list(pool.map(lambda k: store.put(k, large), keys)))
-            tr = _timed(lambda: list(pool.map(store.get, keys)))
-        out[f"write_{n}_streams_mb_s"] = len(large) * n / tw / _MB
-        out[f"read_{n}_streams_mb_s"] = len(large) * n / tr / _MB
+            t = _timed(lambda: list(pool.map(store.get, many[:n])))
+        conc[f"warm_get_{n}_streams_mb_s"] = size * n / t / _MB
+        out[f"read_{n}_streams_mb_s"] = conc[f"warm_get_{n}_streams_mb_s"]
+    out["large_concurrent"] = conc
+    for k in (*keys, single, ranged, *many):
+        store.delete(k)
     return out
 
 
 def _recommend_profile(r: Dict[str, Any], streams: Sequence[int]) -> Dict[str, Any]:
-    one = r.get(f"read_{streams[0]}_streams_mb_s", 100.0)
+    one = r.get("large_single_stream", {}).get("cold_get_mb_s") or r.get(f"read_{streams[0]}_streams_mb_s", 100.0)
     best_n = max(streams, key=lambda n: r.get(f"read_{n}_streams_mb_s", 0.0))
+    ranged = r.get("large_ranged", {})
+    range_streams = ranged.get("ranges", 1) if ranged.get("cold_get_mb_s", 0.0) > 1.5 * one else 1
     req = r.get("small_get", {}).get("p50_ms", 1.0) / 1e3
-    return {"request_seconds": max(req, 1e-4), "stream_mb_s": one, "streams": int(best_n), "range_streams": 1,
-            "part_bytes": 64 * 1024 * 1024, "list_is_cheap": r.get("list_seconds", 1.0) < 0.5}
+    return {"request_seconds": max(req, 1e-4), "stream_mb_s": one, "streams": int(best_n),
+            "range_streams": int(range_streams), "part_bytes": 64 * 1024 * 1024,
+            "list_is_cheap": r.get("list_seconds", 1.0) < 0.5}
 
 
 def _checkpoint_phase(store: Store, prefix: str, total: int, parts: Sequence[int], settle: float) -> Dict[str, Any]:
