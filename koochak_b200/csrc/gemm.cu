@@ -88,6 +88,14 @@ __device__ __forceinline__ bool debug_tile_ok(const GemmParams& p, int b, int ro
   }
 }
 
+// Bulk reduce-add of a staged 3-D tile into global memory (fp32 add, per element).
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ bool prof_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                           int code, bool on, long long& acc) {
   if (!on) return mbar_wait(bar, parity, abort_flag, status, code);
@@ -338,7 +346,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = pre[j] = 0.f;  // rows past M: clipped by the TMA store
     }
-    if (atomic_out) {
+    if (atomic_out && !use_tma) {
       if (!row_ok) return;
       float* dst = reinterpret_cast<float*>(crow) + col0;
       if (vec && valid == 32) {
@@ -374,7 +382,11 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_3d(&maps.c, ctile, col0, row0, b);
+      // Partial tiles of split-K / stream-K are added into C by one bulk
+      // reduction per 32 x 32 tile (whole lines at the L2) instead of a
+      // per-row vector atomic from every thread.
+      if (atomic_out) tma_reduce_add_3d(&maps.c, ctile, col0, row0, b);
+      else tma_store_3d(&maps.c, ctile, col0, row0, b);
       if constexpr (ACT == ACT_GELU) {
         if (p.aux) tma_store_3d(&maps.aux, atile, col0, row0, b);
       }
@@ -1191,7 +1203,7 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   std::memset(&maps, 0, sizeof(maps));
   {
     const int64_t esz = c.element_size();
-    bool ok = !stream_k && splits == 1 && (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
+    bool ok = (p.ldc * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0 &&
               (!batched || (p.strideC * esz) % 16 == 0);
     if (ok && p.aux != nullptr)
       ok = (p.ldaux * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15) == 0 && (!batched || (p.strideAux * 2) % 16 == 0);
