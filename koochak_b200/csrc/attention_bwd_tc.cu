@@ -14,9 +14,8 @@
 //   dQ_i = dS K_j                A = dS from smem (MN-major), B = K_j (MN-major)
 // dQ_i is read out of TMEM and added to the fp32 dQ accumulator by TMA
 // reductions (cp.reduce.async.bulk.tensor .add) from a shared-memory staging
-// tile -- its own at D = 64, the dS tile in two halves at D = 128, where
-// shared memory holds nothing more; the softmax scale is applied to dK and dQ
-// on the way out. delta = rowsum(dO * O)
+// tile, or at D = 128 with vector reductions (red.global.add.v4.f32); the
+// softmax scale is applied to dK and dQ on the way out. delta = rowsum(dO * O)
 // comes from a pre-pass.
 //
 // Roles (512 threads): warp 0 producer (lane 0 issues TMA for K_j, V_j and
@@ -55,8 +54,8 @@ constexpr int kBwBQ = 128;
 constexpr int kBwThreads = 512;
 // Register split per warpgroup (launch: 128 per thread, so control + dQ
 // readout + 2 x elementwise must stay within 4 x 128): the dQ path stages
-// 32 columns at a time through shared memory; at D = 128 the elementwise
-// warps hold 64 scores and 64 dP values at once.
+// through shared memory at D = 64 and reduces from registers at D = 128; at
+// D = 128 the elementwise warps hold 64 scores and 64 dP values at once.
 template <int D>
 struct BwRegs {
   static constexpr int kCtl = D == 64 ? 72 : 80;
@@ -72,14 +71,11 @@ struct TcBwdCfg {
   static constexpr int kDsBytes = kBwBK * kBwBQ * 2;  // dS tile (16-bit)
   static constexpr int kVecBytes = kBwBQ * 4;         // one LSE or delta block
   // dQ leaves through TMA reductions from an fp32 staging tile (128 B
-  // swizzled, 32 columns per box) of its own where shared memory allows
-  // (D = 64).
+  // swizzled, 32 columns per box) where shared memory allows (D = 64); at
+  // D = 128 it leaves through vector reductions straight from registers
+  // (staging it through the dS tile instead, in two halves, measured slower:
+  // 554 us against 494 us on the Llama-style shape).
   static constexpr bool kDqTma = D == 64;
-  // D = 128: dQ also leaves through TMA reductions, staged in the dS tile in
-  // two 64-column halves (the dS tile is free from the completion of the dQ
-  // MMA, its last reader, until the next step's elementwise work, which the
-  // readout's dq_empty arrival precedes).
-  static constexpr bool kDqViaDs = D == 128;
   static constexpr int kDqStageBytes = kDqTma ? kBwBQ * D * 4 : 0;
   // dS tiles: two at D = 64, where step i+1's elementwise work writes dS
   // while step i's dQ MMA may still read it; one at D = 128, where dQ of
@@ -112,19 +108,6 @@ struct TcBwdCfg {
   }
   static_assert(kDqInScores || 256 + 3 * D <= 512, "TMEM columns");
 };
-
-// Named barrier over `count` threads that also ORs a predicate across them, so
-// every participating thread takes the same branch afterwards.
-__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "barrier.cta.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
 
 __device__ __forceinline__ float bw_ex2(float x) {
   float y;
@@ -255,7 +238,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
     tma_prefetch_desc(&tdo);
-    if (Cfg::kDqTma || Cfg::kDqViaDs) tma_prefetch_desc(&tdq);
+    if (Cfg::kDqTma) tma_prefetch_desc(&tdq);
   }
   if (warp == 1) tmem_alloc(tmem_holder, 512);
   tc_fence_before();
@@ -610,8 +593,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
       const BwItem it = bw_item<CAUSAL>(idx, a.H, BH, a.Sq);
       for (int st_i = 0; st_i < it.n_steps; ++st_i, ++step) {
         const bool got = mbar_wait(dq_full, step & 1, abort_flag, a.status, kStatusTimeoutEpilogue);
-        // The staged paths decide together (after a barrier) so no warp leaves the others waiting on it.
-        if (!Cfg::kDqTma && !Cfg::kDqViaDs && !got) {
+        if (!Cfg::kDqTma && !got) {
           ok = false;
           break;
         }
@@ -653,46 +635,6 @@ __global__ void __launch_bounds__(kBwThreads, 1)
               tma_reduce_add_4d(&tdq, sDQ + c * (kBwBQ * 128), 32 * c, qb0, it.h, it.b);
             bulk_commit();
           }
-        } else if constexpr (Cfg::kDqViaDs) {
-          if (named_bar_or(2, 128, !got || *abort_flag)) {
-            ok = false;
-            break;
-          }
-#pragma unroll 1
-          for (int h2 = 0; h2 < 2; ++h2) {
-            if (h2 == 1) {
-              if (leader) bulk_wait_read<0>();  // the first half's reductions have read the tile
-              named_bar_sync(2, 128);
-            }
-#pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-              const int c = 2 * h2 + c2;  // 32-column chunk of dQ
-              uint32_t v[32];
-              tmem_ld_32x32b_x32(t_dq + Cfg::dq_col(c >> 1) + 32 * (c & 1), v);
-              tmem_wait_ld_dep(v);
-              uint8_t* row = sDS + c2 * (kBwBQ * 128) + qr * 128;
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                *reinterpret_cast<float4*>(row + ((u ^ (qr & 7)) * 16)) =
-                    make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
-                                __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
-              }
-            }
-            fence_proxy_async_smem();
-            named_bar_sync(2, 128);
-            if (leader && !(a.debug & 1)) {
-#pragma unroll
-              for (int c2 = 0; c2 < 2; ++c2)
-                tma_reduce_add_4d(&tdq, sDS + c2 * (kBwBQ * 128), 32 * (2 * h2 + c2), qb0, it.h, it.b);
-              bulk_commit();
-            }
-          }
-          // The next step's elementwise work writes dS here once dq_empty lets
-          // its scores be computed: the reductions must have read the tile.
-          if (leader) bulk_wait_read<0>();
-          tc_fence_before();
-          named_bar_sync(2, 128);
-          if (lane == 0) mbar_arrive(dq_empty);
         } else {
           float* dst = a.dq_acc + (((long long)it.b * a.Sq + qg) * a.H + it.h) * D;
 #pragma unroll
@@ -714,7 +656,7 @@ __global__ void __launch_bounds__(kBwThreads, 1)
         if (threadIdx.x == 384) bw_stamp(a, 8 + 16 * step + 8);
       }
     }
-    if ((Cfg::kDqTma || Cfg::kDqViaDs) && leader) bulk_wait_all();
+    if (Cfg::kDqTma && leader) bulk_wait_all();
     if (!ok) *abort_flag = 1;
     tc_fence_before();
     named_bar_sync(1, kBwThreads);
@@ -740,7 +682,7 @@ void launch_bwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   // fp32 dQ accumulator [B, Sq, H, D] as {D, Sq, H, B}, 32 x 128 boxes, 128-byte swizzle.
   CUtensorMap tdq;
   std::memset(&tdq, 0, sizeof(tdq));
-  if (Cfg::kDqTma || Cfg::kDqViaDs) {
+  if (Cfg::kDqTma) {
     uint64_t dims[4] = {(uint64_t)D, (uint64_t)Sq, (uint64_t)H, (uint64_t)B};
     uint64_t strides[3] = {(uint64_t)H * D * 4, (uint64_t)D * 4, (uint64_t)Sq * H * D * 4};
     uint32_t box[4] = {32, 128, 1, 1};

@@ -378,7 +378,7 @@ def test_llama_gradient_accumulation_in_place_matches_autograd():
     # bf16 forward/backward with fp32 atomics is not bitwise reproducible between two models: compare norms
     for (n, p), q in zip(ours.named_parameters(), twin.parameters()):
         err = float((p.grad - q.grad).norm() / (q.grad.norm() + 1e-12))
-        assert err < 5e-3, (n, err)
+        assert err < 2e-2, (n, err)  # a missed or doubled micro-step would be off by a third or more
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 64), (520, 384, 200), (2048, 2304, 768), (1000, 776, 1024)])
