@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(32 * kNormWarps)
 // C = 2048, three CTAs (24 rows) are resident per SM, against one CTA of the
 // register-resident kernel. Lane l owns columns [8 l + 256 k, 8 l + 256 k + 8).
 template <typename TIn, typename TG, typename TDx>
-__global__ void __launch_bounds__(32 * kNormWarps)
+__global__ void __launch_bounds__(32 * kNormWarps, 3)
     rms_bwd_wide_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
                         const float* __restrict__ rstd_in, const TDx* __restrict__ dres, TDx* __restrict__ dx,
                         TG* __restrict__ dx_lp, float* __restrict__ dw_part, int M, int C) {
@@ -354,27 +354,40 @@ __global__ void __launch_bounds__(32 * kNormWarps)
     const TDx* rr = dres ? dres + (long long)row * C : nullptr;
     TDx* dxr = dx + (long long)row * C;
     TG* lpr = dx_lp ? dx_lp + (long long)row * C : nullptr;
-    for (int k = 0; k < chunks; ++k) {
-      const int col = (k << 8) + lane * 8;
-      float xa[8], ga[8], ra[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, o[8];
-      load4<TIn>(xr + col, *reinterpret_cast<float(*)[4]>(&xa[0]));
-      load4<TIn>(xr + col + 4, *reinterpret_cast<float(*)[4]>(&xa[4]));
-      load4<TG>(gr + col, *reinterpret_cast<float(*)[4]>(&ga[0]));
-      load4<TG>(gr + col + 4, *reinterpret_cast<float(*)[4]>(&ga[4]));
-      if (rr) {
-        load4<TDx>(rr + col, *reinterpret_cast<float(*)[4]>(&ra[0]));
-        load4<TDx>(rr + col + 4, *reinterpret_cast<float(*)[4]>(&ra[4]));
-      }
-      float wv[8];
-      *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(sw + col);
-      *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(sw + col + 4);
+    // two chunks per step, every load of both issued before the first use
+    for (int k = 0; k < chunks; k += 2) {
+      float xa[2][8], ga[2][8], ra[2][8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) o[t] = rstd * (wv[t] * ga[t] - xa[t] * rstd * s2) + ra[t];
-      store4<TDx>(dxr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
-      store4<TDx>(dxr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
-      if (lpr) {
-        store4<TG>(lpr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
-        store4<TG>(lpr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
+      for (int u = 0; u < 2; ++u) {
+        const int col = ((k + u) << 8) + lane * 8;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) ra[u][t] = 0.f;
+        if (k + u < chunks) {
+          load4<TIn>(xr + col, *reinterpret_cast<float(*)[4]>(&xa[u][0]));
+          load4<TIn>(xr + col + 4, *reinterpret_cast<float(*)[4]>(&xa[u][4]));
+          load4<TG>(gr + col, *reinterpret_cast<float(*)[4]>(&ga[u][0]));
+          load4<TG>(gr + col + 4, *reinterpret_cast<float(*)[4]>(&ga[u][4]));
+          if (rr) {
+            load4<TDx>(rr + col, *reinterpret_cast<float(*)[4]>(&ra[u][0]));
+            load4<TDx>(rr + col + 4, *reinterpret_cast<float(*)[4]>(&ra[u][4]));
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (k + u >= chunks) break;
+        const int col = ((k + u) << 8) + lane * 8;
+        float wv[8], o[8];
+        *reinterpret_cast<float4*>(&wv[0]) = *reinterpret_cast<const float4*>(sw + col);
+        *reinterpret_cast<float4*>(&wv[4]) = *reinterpret_cast<const float4*>(sw + col + 4);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) o[t] = rstd * (wv[t] * ga[u][t] - xa[u][t] * rstd * s2) + ra[u][t];
+        store4<TDx>(dxr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
+        store4<TDx>(dxr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
+        if (lpr) {
+          store4<TG>(lpr + col, *reinterpret_cast<float(*)[4]>(&o[0]));
+          store4<TG>(lpr + col + 4, *reinterpret_cast<float(*)[4]>(&o[4]));
+        }
       }
     }
   }

@@ -389,6 +389,23 @@ __global__ void muon_scale_kernel(__nv_bfloat16* __restrict__ X, const float* __
     x[j] = __float2bfloat16_rn(__bfloat162float(x[j]) * inv);
 }
 
+// The same scaling, eight values (one 16-byte access) per thread; needs
+// per_mat % 8 == 0 and a 16-byte aligned X.
+__global__ void muon_scale_vec_kernel(__nv_bfloat16* __restrict__ X, const float* __restrict__ sumsq,
+                                      long long per_mat) {
+  const int i = blockIdx.y;
+  const float inv = 1.f / (sqrtf(sumsq[i]) + 1e-7f);
+  uint4* x = reinterpret_cast<uint4*>(X + (long long)i * per_mat);
+  const long long n8 = per_mat >> 3;
+  for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += (long long)gridDim.x * blockDim.x) {
+    uint4 q = x[j];
+    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&q);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) e[t] = __float2bfloat16_rn(__bfloat162float(e[t]) * inv);
+    x[j] = q;
+  }
+}
+
 // p = p * (1 - lr*wd) - lr * scale * U  (U = X or X^T), then EMA and bf16 shadow.
 __global__ void __launch_bounds__(256)
     muon_epilogue_kernel(const __grid_constant__ MuonMats mm, const __nv_bfloat16* __restrict__ X, float lr, float wd,
@@ -608,8 +625,13 @@ void muon_scale(at::Tensor& X, const at::Tensor& sumsq, int64_t n) {
   const c10::cuda::CUDAGuard guard(X.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
   const long long per = X.numel() / X.size(0);
-  dim3 grid((unsigned)std::min<long long>((per + 255) / 256, 256), (unsigned)n);
-  muon_scale_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)X.data_ptr(), sumsq.data_ptr<float>(), per);
+  const bool vec = per % 8 == 0 && (reinterpret_cast<uintptr_t>(X.data_ptr()) & 15) == 0;
+  const long long work = vec ? per / 8 : per;
+  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>((work + 255) / 256, 256)), (unsigned)n);
+  if (vec)
+    muon_scale_vec_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)X.data_ptr(), sumsq.data_ptr<float>(), per);
+  else
+    muon_scale_kernel<<<grid, 256, 0, s>>>((__nv_bfloat16*)X.data_ptr(), sumsq.data_ptr<float>(), per);
   KB_LAUNCHED();
 }
 
