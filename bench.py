@@ -239,16 +239,34 @@ def step_fn(model, batch, ctx):
 
 
 class VitStep:
-    """step_fn for the ViT workload: mean cross-entropy, times 1e30 on the forced-overflow updates."""
+    """step_fn for the ViT workload: mean cross-entropy times a device scalar, 1 or 1e30.
+
+    The scalar is 1e30 on the forced-overflow updates (the fp16 backward then
+    overflows and the scaler sees inf gradients). It lives on the device and is
+    set by ``advance`` (an ``on_update_end`` hook) for the next update, so the
+    step_fn computes the same thing on every update and the step can be
+    replayed from a CUDA graph.
+    """
 
     def __init__(self, overflow_at):
         self.overflow_at = overflow_at  # step -> bool
+        self.mult = None
+
+    def _ensure(self, device):
+        import torch
+
+        if self.mult is None:
+            self.mult = torch.full((), 1e30 if self.overflow_at(0) else 1.0, device=device)
 
     def __call__(self, model, batch, ctx):
-        loss = model(batch["images"], batch["labels"])
-        if self.overflow_at(int(ctx["step"])):
-            loss = loss * 1e30  # the fp16 backward overflows; the scaler sees inf gradients
-        return {"loss": loss}
+        self._ensure(batch["images"].device)
+        return {"loss": model(batch["images"], batch["labels"]) * self.mult}
+
+    def advance(self, log, ctx):
+        """on_update_end: the multiplier of update ctx['step'] + 1."""
+
+        if self.mult is not None:
+            self.mult.fill_(1e30 if self.overflow_at(int(ctx["step"]) + 1) else 1.0)
 
 
 def vit_batches(n: int, micro: int, device, pinned: bool, seed: int):
@@ -313,9 +331,9 @@ def train_cfg_for(args, world: int, steps: int, out_dir: str, scalarize: bool, i
     vit = args.model == "vit"
     clip = (None if args.vit_clip == "none" else float(args.vit_clip)) if vit else 1.0
     # This framework's loop captures forward + backward as one CUDA graph on a single GPU with one
-    # micro-batch per update (the GPT-2 step; the ViT step varies per update and stays eager). The capture
-    # happens during warm-up, so every timed update replays it.
-    graph = (impl == "koochak_b200" and not vit and not args.no_graph)
+    # micro-batch per update (GPT-2 and ViT; the Llama step accumulates four micro-batches and stays eager).
+    # The capture happens during warm-up, so every timed update replays it.
+    graph = (impl == "koochak_b200" and not args.no_graph)
     return {
         **({"cuda_graph_step": True, "cuda_graph_warmup": max(1, args.warmup - 2)} if graph else {}),
         "max_steps": steps, "log_every": 10 ** 9, "eval_every": 0, "ckpt_every": 10 ** 9,
@@ -436,6 +454,8 @@ def run_phase(impl: str, args, world: int, rank: int, device, *, e2e: bool, samp
     with tempfile.TemporaryDirectory(prefix="kb_bench_") as out_dir:
         cfg = train_cfg_for(args, world, total + (1 if raise_variant else 0), out_dir, scalarize=e2e, impl=impl)
         hooks = ([NoGradSyncHook()] if no_grad_sync else []) + [timer, steps_counter]
+        if isinstance(fn, VitStep):
+            hooks.append(fn.advance)
         try:
             training_loop(model=model, dataset=CyclingDataset(pool), step_fn=fn, optimizer=opt, scheduler=sched,
                           train_cfg=cfg, hooks={"on_update_end": hooks})
@@ -552,7 +572,7 @@ def main() -> int:
                    "micro_batch_per_gpu": args.micro_batch, "grad_accum": args.grad_accum,
                    "seq_len": args.seq, "parallelism": f"dp{world}", "optimizer": optim,
                    "ema_decay": 0.999, "grad_clip": clip, "l2": l2,
-                   "fwd_bwd_cuda_graph": bool(args.impl == "koochak_b200" and not vit and not args.no_graph
+                   "fwd_bwd_cuda_graph": bool(args.impl == "koochak_b200" and not args.no_graph
                                               and world == 1 and args.grad_accum == 1)},
         "clocks": res["clocks"], "e2e": e2e,
     }
