@@ -74,8 +74,13 @@ def ns_cases(c: int, batch: int = 12, r: int = 768, block_n: int = 0):
     return {
         "XXt": (2.0 * batch * r * r * c, lambda: kf.gemm(X, X, block_n=block_n),
                 lambda: torch.bmm(X, X.transpose(1, 2))),
+        "XXt_sym": (2.0 * batch * r * r * c, lambda: kf.gemm(X, X, block_n=block_n, symmetric=True),
+                    lambda: torch.bmm(X, X.transpose(1, 2))),
         "AA": (2.0 * batch * r ** 3, lambda: kf.gemm(A, A, d=A, alpha=2.0, beta=-4.0, block_n=block_n),
                lambda: torch.bmm(A, A)),
+        "AA_sym": (2.0 * batch * r ** 3, lambda: kf.gemm(A, A, d=A, alpha=2.0, beta=-4.0, block_n=block_n,
+                                                          symmetric=True),
+                   lambda: torch.bmm(A, A)),
         "BX": (2.0 * batch * r * r * c, lambda: kf.gemm(A, X, b_mn_major=True, d=X, beta=3.0, block_n=block_n),
                lambda: torch.bmm(A, X)),
     }
@@ -106,7 +111,7 @@ def wait_profile(fn: Callable[[], object]) -> str:
 def main(argv: List[str] | None = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--case", default="all", help="linear layer name, 'ns<c>' (e.g. ns768) or 'all'")
-    ap.add_argument("--op", default="all", help="fwd | dgrad | wgrad | XXt | AA | BX | all")
+    ap.add_argument("--op", default="all", help="fwd | dgrad | wgrad | XXt | XXt_sym | AA | AA_sym | BX | all")
     ap.add_argument("--tokens", type=int, default=None, help="M (default 16384 for gpt2, 8192 for llama)")
     ap.add_argument("--model", choices=["gpt2", "llama"], default="gpt2",
                     help="which model's linear and Newton-Schulz shapes 'all' covers")
@@ -116,6 +121,10 @@ def main(argv: List[str] | None = None) -> None:
     ap.add_argument("--shape", default=None, help="M,N,K: one extra forward case of that shape (name 'custom')")
     ap.add_argument("--debug-mode", type=int, default=0,
                     help="diagnostic GEMM mode for timing studies: 1 skips operand loads, 2 skips the epilogue")
+    ap.add_argument("--group", type=int, default=-1,
+                    help="tile-column group width of the tile order (-1: the built-in rule; 0/1: plain order)")
+    ap.add_argument("--split", type=int, default=-1,
+                    help="K-cut of fp32 outputs: -1 the built-in rule, 0 none, 1 stream-K, s >= 2 split-K")
     ap.add_argument("--profile", action="store_true",
                     help="also report where each role of the GEMM waited (clock64 counters per CTA)")
     args = ap.parse_args(argv)
@@ -127,6 +136,14 @@ def main(argv: List[str] | None = None) -> None:
         m, n, k = (int(v) for v in args.shape.split(","))
         LINEAR["custom"] = (n, k)
         args.tokens = m
+    if args.group >= 0:
+        from koochak_b200.ops import native
+
+        native().gemm_set_group(args.group)
+    if args.split >= 0:
+        from koochak_b200.ops import native
+
+        native().gemm_set_split(args.split)
     if args.debug_mode:
         from koochak_b200.ops import native
 

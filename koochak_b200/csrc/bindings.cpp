@@ -6,7 +6,9 @@
 namespace kb {
 void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
                  const c10::optional<at::Tensor>& d, double alpha, double beta, const c10::optional<at::Tensor>& bias,
-                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n);
+                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n, int64_t flags);
+void gemm_set_group(int64_t g);
+void gemm_set_split(int64_t s);
 void gemm_set_profile(const c10::optional<at::Tensor>& buf);
 void gemm_set_debug(int64_t mode);
 void register_norm_ops(pybind11::module& m);
@@ -23,7 +25,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("a_mn_major"), pybind11::arg("b"), pybind11::arg("b_mn_major"), pybind11::arg("c"),
         pybind11::arg("d") = pybind11::none(), pybind11::arg("alpha") = 1.0, pybind11::arg("beta") = 0.0,
         pybind11::arg("bias") = pybind11::none(), pybind11::arg("aux") = pybind11::none(),
-        pybind11::arg("act") = 0, pybind11::arg("block_n") = 0);
+        pybind11::arg("act") = 0, pybind11::arg("block_n") = 0, pybind11::arg("flags") = 0);
+  m.def("gemm_set_group", &kb::gemm_set_group,
+        "tile-column group width of the GEMM tile order for timing studies (-1: the built-in rule)");
+  m.def("gemm_set_split", &kb::gemm_set_split,
+        "K-cut of fp32 GEMMs for timing studies: -1 built-in rule, 0 none, 1 stream-K, s >= 2 split-K");
   m.def("gemm_set_profile", &kb::gemm_set_profile,
         "route GEMM pipeline wait counters (int64, >= 4096 entries) to a buffer; None turns it off");
   m.def("gemm_set_debug", &kb::gemm_set_debug,

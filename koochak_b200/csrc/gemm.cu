@@ -51,6 +51,8 @@ struct GemmParams {
   int kb_per_split;  // 64-wide K blocks per split (every split non-empty)
   int tma_store;     // epilogue writes C (and aux) through staged TMA stores
   int stream_k;      // K-iterations of all tiles split evenly over the workers (fp32 atomics)
+  int group_n;       // tile order: > 1 takes the tile columns group_n at a time (see tile_mn)
+  int sym;           // symmetric output (M == N): only tiles touching the upper triangle, mirrored
   int* status;
   // Optional pipeline profile (null: off). Per CTA, 8 counters of clock64
   // cycles: [0] producer waiting for a free stage, [1] MMA waiting for
@@ -135,6 +137,54 @@ __device__ __forceinline__ bool work_unit(const GemmParams& p, int w, int nw, in
   return true;
 }
 
+// Symmetric products (X X^T, and A A or b A + c A A with A symmetric) compute
+// only the tiles that hold an element on or above the diagonal: in tile
+// column n_blk the first sym_rows(n_blk) row blocks. The epilogue writes each
+// such tile and, for its elements with column > row, the mirrored element.
+__device__ __forceinline__ int sym_rows(int n_blk, int num_m, int bm, int bn) {
+  return min(num_m, (n_blk * bn + bn - 1) / bm + 1);
+}
+
+__device__ __forceinline__ int tiles_in_batch(const GemmParams& p, int num_m, int num_n, int bm, int bn) {
+  if (!p.sym) return num_m * num_n;
+  int t = 0;
+  for (int n = 0; n < num_n; ++n) t += sym_rows(n, num_m, bm, bn);
+  return t;
+}
+
+// Output tile r of one batch as (m_blk, n_blk). Plain order: row blocks run
+// fastest down each tile column, so the tiles in flight together span few
+// columns and many row blocks (every A panel, few B panels). With group_n = G
+// the columns are taken G at a time and, inside a group, the G tiles of one
+// row block are consecutive: the tiles in flight then cover a patch about
+// (workers / G) x G, and read about that many A plus G B panels -- for long K
+// (weight gradients) that is what decides whether the panels stay in L2.
+__device__ __forceinline__ void tile_mn(const GemmParams& p, int r, int num_m, int num_n, int bm, int bn, int& m_blk,
+                                        int& n_blk) {
+  if (p.sym) {
+    int n = 0;
+    for (;; ++n) {
+      const int c = sym_rows(n, num_m, bm, bn);
+      if (r < c || n == num_n - 1) break;
+      r -= c;
+    }
+    n_blk = n;
+    m_blk = r;
+    return;
+  }
+  const int G = p.group_n <= 1 ? 1 : min(p.group_n, num_n);
+  if (G == 1) {
+    n_blk = r / num_m;
+    m_blk = r - n_blk * num_m;
+    return;
+  }
+  const int per_group = G * num_m;
+  const int g = r / per_group;
+  const int i = r - g * per_group;
+  const int w = min(G, num_n - g * G);  // the last group may be narrower
+  m_blk = i / w;
+  n_blk = g * G + (i - m_blk * w);
+}
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -346,6 +396,20 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiMaps
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = pre[j] = 0.f;  // rows past M: clipped by the TMA store
     }
+    if (p.sym && row_ok) {
+      // Mirror of the elements right of the diagonal: for each column j the
+      // warp's 32 rows are consecutive in the transposed row, one coalesced store.
+      OutT* cb = reinterpret_cast<OutT*>(p.C) + (long long)b * p.strideC;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = col0 + j;
+        if (j < valid && col > row) {
+          if constexpr (std::is_same<OutT, float>::value) cb[(long long)col * p.ldc + row] = v[j];
+          else if constexpr (std::is_same<OutT, __half>::value) cb[(long long)col * p.ldc + row] = __float2half_rn(v[j]);
+          else cb[(long long)col * p.ldc + row] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
     if (atomic_out && !use_tma) {
       if (!row_ok) return;
       float* dst = reinterpret_cast<float*>(crow) + col0;
@@ -488,7 +552,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int tiles_per_batch = num_m * num_n;
+  const int tiles_per_batch = tiles_in_batch(p, num_m, num_n, kBM, BN);
   const int tiles_per_split = tiles_per_batch * p.batch;
   const int total_tiles = tiles_per_split * p.splits;
   const int num_kb_total = (p.K + kBK - 1) / kBK;
@@ -509,8 +573,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ts = t - split * tiles_per_split;
         const int b = ts / tiles_per_batch;
         const int r = ts - b * tiles_per_batch;
-        const int n_blk = r / num_m;
-        const int m_blk = r - n_blk * num_m;
+        int m_blk, n_blk;
+        tile_mn(p, r, num_m, num_n, kBM, BN, m_blk, n_blk);
         const int m0 = m_blk * kBM;
         const int n0 = n_blk * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -644,8 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ts = t - split * tiles_per_split;
       const int b = ts / tiles_per_batch;
       const int r = ts - b * tiles_per_batch;
-      const int n_blk = r / num_m;
-      const int m_blk = r - n_blk * num_m;
+      int m_blk, n_blk;
+      tile_mn(p, r, num_m, num_n, kBM, BN, m_blk, n_blk);
       if (!(p.debug & 2) && debug_tile_ok(p, b, m_blk * kBM + q * 32, n_blk * BN + half * (BN / 2),
                                           n_blk * BN + (half + 1) * (BN / 2)))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
@@ -737,7 +801,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   const int num_m = (p.M + 255) / 256;
   const int num_n = (p.N + BN - 1) / BN;
-  const int tiles_per_batch = num_m * num_n;
+  const int tiles_per_batch = tiles_in_batch(p, num_m, num_n, 256, BN);
   const int tiles_per_split = tiles_per_batch * p.batch;
   const int total_tiles = tiles_per_split * p.splits;
   const int num_kb_total = (p.K + kBK - 1) / kBK;
@@ -761,8 +825,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int ts = t - split * tiles_per_split;
         const int b = ts / tiles_per_batch;
         const int r = ts - b * tiles_per_batch;
-        const int n_blk = r / num_m;
-        const int m_blk = r - n_blk * num_m;
+        int m_blk, n_blk;
+        tile_mn(p, r, num_m, num_n, 256, BN, m_blk, n_blk);
         const int m0 = m_blk * 256 + (int)rank * 128;
         const int n0 = n_blk * BN + (int)rank * BHALF;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -897,8 +961,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int ts = t - split * tiles_per_split;
       const int b = ts / tiles_per_batch;
       const int r = ts - b * tiles_per_batch;
-      const int n_blk = r / num_m;
-      const int m_blk = r - n_blk * num_m;
+      int m_blk, n_blk;
+      tile_mn(p, r, num_m, num_n, 256, BN, m_blk, n_blk);
       if (!(p.debug & 2) && debug_tile_ok(p, b, m_blk * 256 + (int)rank * 128 + q * 32, n_blk * BN + half * (BN / 2),
                                           n_blk * BN + (half + 1) * (BN / 2)))
       epilogue_rows<OutT, ACT>(p, maps, wstage, stage_pp, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN,
@@ -982,8 +1046,21 @@ static void dispatch_act2(int act, const CUtensorMap& ta, const CUtensorMap& tb,
 // when profiling is off. Set from Python for diagnostics only.
 static unsigned long long* g_gemm_prof = nullptr;
 static int g_gemm_debug = 0;
+// Tile-column group width override for timing studies (-1: the host's rule).
+static int g_gemm_group = -1;
+// K-cut override for fp32 outputs, for timing studies: -1 the host's rule,
+// 0 never cut, 1 stream-K, s >= 2 split-K into s parts.
+static int g_gemm_split = -1;
 
 void gemm_set_debug(int64_t mode) { g_gemm_debug = (int)mode; }
+void gemm_set_group(int64_t g) { g_gemm_group = (int)g; }
+void gemm_set_split(int64_t s) { g_gemm_split = (int)s; }
+
+static int64_t sym_tile_count(int64_t num_m, int64_t num_n, int64_t bm, int64_t bn) {
+  int64_t t = 0;
+  for (int64_t n = 0; n < num_n; ++n) t += std::min<int64_t>(num_m, (n * bn + bn - 1) / bm + 1);
+  return t;
+}
 
 void gemm_set_profile(const c10::optional<at::Tensor>& buf) {
   if (!buf.has_value() || !buf->defined()) {
@@ -1029,7 +1106,7 @@ static CUtensorMap operand_map(const at::Tensor& t, bool mn_major, int mn_extent
 // Public entry: see gemm() in bindings for argument meaning.
 void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool b_mn_major, at::Tensor& c,
                  const c10::optional<at::Tensor>& d, double alpha, double beta, const c10::optional<at::Tensor>& bias,
-                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n) {
+                 const c10::optional<at::Tensor>& aux, int64_t act, int64_t block_n, int64_t flags) {
   check_cuda_tensor(a, "a");
   check_cuda_tensor(b, "b");
   check_cuda_tensor(c, "c");
@@ -1051,6 +1128,14 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   KB_CHECK(ct == at::kFloat || ct == at::kBFloat16 || ct == at::kHalf, "C must be fp32, bf16 or fp16");
   KB_CHECK(ct == at::kFloat || ct == a.scalar_type(), "reduced-precision C must match the input dtype");
 
+  // flags bit 0: the product is symmetric (X X^T, or A A / b A + c A A with A
+  // and D symmetric); only tiles on or above the diagonal are computed.
+  const bool sym = (flags & 1) != 0;
+  KB_CHECK(!sym || (M == N && act == ACT_NONE && !(bias.has_value() && bias->defined()) &&
+                    !(aux.has_value() && aux->defined()) && ct != at::kFloat &&
+                    !(d.has_value() && d->defined() && d->data_ptr() == c.data_ptr())),
+           "symmetric GEMM: square 16-bit output without bias, aux or activation, D not C itself "
+           "(the mirrored stores would race with other tiles' reads of D)");
   const c10::cuda::CUDAGuard guard(a.device());
   const int dev = a.get_device();
   // Tile configuration: 1-SM 128 x {128, 256} or 2-SM 256 x {128, 256}.
@@ -1079,7 +1164,8 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
       const bool pm = cand_pair[i];
       if (pm && M < 256) continue;
       const int rows = pm ? 256 : 128;
-      const int64_t t = batch * ((M + rows - 1) / rows) * ((N + w - 1) / w);
+      const int64_t t = batch * (sym ? sym_tile_count((M + rows - 1) / rows, (N + w - 1) / w, rows, w)
+                                     : ((M + rows - 1) / rows) * ((N + w - 1) / w));
       const int64_t slots = pm ? sms_all / 2 : sms_all;
       // With stream-K available the work spreads evenly (plus a partial-tile
       // overhead); otherwise whole waves count.
@@ -1139,7 +1225,10 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
   p.debug = g_gemm_debug;
 
   const int rows_per_tile = pair_mode ? 256 : 128;
-  const int64_t tiles = batch * ((M + rows_per_tile - 1) / rows_per_tile) * ((N + bn - 1) / bn);
+  const int64_t num_m_tiles = (M + rows_per_tile - 1) / rows_per_tile, num_n_tiles = (N + bn - 1) / bn;
+  const int64_t tiles = batch * (sym ? sym_tile_count(num_m_tiles, num_n_tiles, rows_per_tile, bn)
+                                     : num_m_tiles * num_n_tiles);
+  p.sym = sym ? 1 : 0;
   const int sms = pair_mode ? (sms_all / 2) : sms_all;  // concurrent tile slots
   const int64_t num_kb = (K + 63) / 64;
   // fp32 outputs without an activation (weight gradients, long K) whose whole
@@ -1169,7 +1258,10 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
     };
     // C += A B^T in place (D is C, beta 1) needs no copy of D: the cut costs what it costs without D.
     const bool has_d = p.D != nullptr && p.beta != 0.f && !(p.D == p.C && p.beta == 1.f);
-    if (fill(tiles) < (has_d ? 0.75 : 0.9)) {
+    // (At a fill of 0.865 -- the Llama-style q/k/v and output-projection
+    // weight gradients -- whole tiles in the grouped order measured 7-9 %
+    // faster than stream-K, so the bar for cutting is 0.85.)
+    if (fill(tiles) < (has_d ? 0.75 : 0.85)) {
       const double c_bytes = double(batch) * double(M) * double(N) * 4.0;
       for (int sp = 2; sp <= 8 && sp * 4 <= num_kb; ++sp) {
         if (fill(tiles * sp) >= 0.9 && sp * c_bytes <= 96.0 * (1 << 20)) {
@@ -1179,10 +1271,21 @@ void gemm_launch(const at::Tensor& a, bool a_mn_major, const at::Tensor& b, bool
       }
       if (splits == 1) stream_k = 1;
     }
+    if (g_gemm_split >= 0) {
+      splits = g_gemm_split >= 2 ? (int)std::min<int64_t>(g_gemm_split, std::max<int64_t>(1, num_kb / 4)) : 1;
+      stream_k = g_gemm_split == 1 ? 1 : 0;
+    }
   }
   p.splits = splits;
   p.kb_per_split = (int)((num_kb + splits - 1) / splits);
   p.stream_k = stream_k;
+  // Tile order (measured on the GPT-2 and Llama-style shapes): columns taken
+  // 8 at a time where the operand panels of the tiles in flight would not
+  // stay in L2 in plain order -- long K (data and weight gradients, the LM
+  // head's gradients) and batched products (Newton-Schulz) -- 4-14 % faster
+  // there; plain order for short-K forward products, where grouping cost up
+  // to 4 %, and under stream-K, whose workers are spread over K anyway.
+  p.group_n = g_gemm_group >= 0 ? g_gemm_group : ((!stream_k && (batch > 1 || K >= 3072)) ? 8 : 0);
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(dev).stream();
   if (stream_k || splits > 1) {
     // C = beta * D (or 0); every split then adds its partial product.

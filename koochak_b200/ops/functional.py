@@ -37,6 +37,7 @@ def gemm(
     aux: Optional[torch.Tensor] = None,
     act: int = ACT_NONE,
     block_n: int = 0,
+    symmetric: bool = False,
 ) -> torch.Tensor:
     """``out = epilogue(alpha * A @ B^T)`` on tcgen05 tensor cores.
 
@@ -45,6 +46,13 @@ def gemm(
     Epilogue: ``+ bias[n]``; ``act=GELU`` stores the pre-activation to ``aux``
     and applies tanh-GELU; ``act=GELU_BWD`` multiplies by GELU'(d);
     otherwise ``+ beta * d``.
+
+    ``symmetric=True`` declares the result symmetric (``X X^T``, or ``A A``
+    plus ``beta * D`` with ``A`` and ``D`` symmetric; 16-bit output, no bias
+    or activation): only the tiles on or above the diagonal are computed and
+    the epilogue mirrors them, about half the work for large square outputs.
+    Elements next to the diagonal may be written from both sides; both
+    values are the same product up to rounding.
     """
 
     M = a.shape[-1] if a_mn_major else a.shape[-2]
@@ -52,7 +60,8 @@ def gemm(
     if out is None:
         shape = (*a.shape[:-2], M, N)
         out = torch.empty(shape, device=a.device, dtype=out_dtype or a.dtype)
-    native().gemm(a, a_mn_major, b, b_mn_major, out, d, float(alpha), float(beta), bias, aux, int(act), int(block_n))
+    native().gemm(a, a_mn_major, b, b_mn_major, out, d, float(alpha), float(beta), bias, aux, int(act), int(block_n),
+                  1 if symmetric else 0)
     return out
 
 

@@ -450,7 +450,14 @@ def _native_adam_group(optimizer, group) -> None:
 
 
 def newton_schulz_batched(X: torch.Tensor, steps: int = 5) -> torch.Tensor:
-    """In-place-style NS5 on a normalised bf16 batch [n, r, c] (r <= c) with tcgen05 GEMMs."""
+    """In-place-style NS5 on a normalised bf16 batch [n, r, c] (r <= c) with tcgen05 GEMMs.
+
+    ``X X^T`` and ``b A + c A A`` are symmetric, so those two GEMMs compute
+    only the tiles on or above the diagonal and mirror them, where the inner
+    dimension is long enough for the saved tiles to outweigh the mirrored
+    stores (measured: 1.2-1.7x faster at 2048 x 5504 and 768 x 3072, no gain
+    or a loss at 768 x 768).
+    """
 
     from ..ops import functional as kf
 
@@ -459,9 +466,10 @@ def newton_schulz_batched(X: torch.Tensor, steps: int = 5) -> torch.Tensor:
     A = torch.empty((n, r, r), device=X.device, dtype=torch.bfloat16)
     B = torch.empty_like(A)
     Y = torch.empty_like(X)
+    sym_xx, sym_aa = cols >= 1536, r >= 1024
     for _ in range(steps):
-        kf.gemm(X, X, out=A)                                 # A = X X^T
-        kf.gemm(A, A, out=B, d=A, alpha=c, beta=b)           # B = b A + c A A   (A symmetric)
+        kf.gemm(X, X, out=A, symmetric=sym_xx)                   # A = X X^T
+        kf.gemm(A, A, out=B, d=A, alpha=c, beta=b, symmetric=sym_aa)  # B = b A + c A A   (A symmetric)
         kf.gemm(B, X, b_mn_major=True, out=Y, d=X, beta=a)   # X' = a X + B X
         X, Y = Y, X
     return X

@@ -399,3 +399,51 @@ def test_gemm_two_sm(M, N, K, a_mn, b_mn, block_n):
     g = kf.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, aux=aux, act=kf.ACT_GELU, block_n=block_n)
     rg, rpre = kf.gemm_ref(a, b, a_mn_major=a_mn, b_mn_major=b_mn, bias=bias, act=kf.ACT_GELU)
     assert _rel(g, rg) < 1e-2 and _rel(aux, rpre) < 1e-2
+
+
+@pytest.mark.parametrize("n,r,c", [(3, 200, 136), (2, 768, 3072), (1, 520, 1000), (2, 2048, 512)])
+@pytest.mark.parametrize("block_n", [0, 128, 256, -128, -256])
+def test_gemm_symmetric(n, r, c, block_n):
+    """Symmetric products (upper tiles computed, mirrored in the epilogue) against the fp32 reference.
+
+    X X^T, and b A + c A A with A symmetric (the Newton-Schulz pair); the
+    result must also be symmetric up to bf16 rounding of one product.
+    """
+    kf = _kf()
+    torch.manual_seed(13)
+    if block_n < 0 and r < 256:
+        pytest.skip("2-SM tiles need 256 rows")
+    X = (torch.randn(n, r, c, device=DEV) / c ** 0.5).bfloat16()
+    A = kf.gemm(X, X, block_n=block_n, symmetric=True)
+    ref = kf.gemm_ref(X, X)
+    assert _rel(A, ref) < 1e-2
+    assert float((A.float() - A.float().transpose(1, 2)).abs().max()) <= 2e-2 * float(ref.abs().max())
+    As = ((A.float() + A.float().transpose(1, 2)) / 2).bfloat16()  # exactly symmetric operand
+    B = kf.gemm(As, As, d=As, alpha=2.0, beta=-4.0, block_n=block_n, symmetric=True)
+    refB = kf.gemm_ref(As, As, d=As, alpha=2.0, beta=-4.0)
+    assert _rel(B, refB) < 1e-2
+    # the plain GEMM on the same operands agrees
+    Bp = kf.gemm(As, As, d=As, alpha=2.0, beta=-4.0, block_n=block_n)
+    assert _rel(B, Bp.float()) < 1e-2
+
+
+@pytest.mark.parametrize("group", [0, 3, 8, 64])
+def test_gemm_grouped_tile_order(group):
+    """The grouped tile order (tile columns taken G at a time) gives the same products, 1-SM and 2-SM, fp32 split."""
+    kf = _kf()
+    from koochak_b200.ops import native
+
+    torch.manual_seed(14)
+    native().gemm_set_group(group)
+    try:
+        for M, N, K, bn in [(1000, 776, 520, 128), (2304, 1536, 768, -256), (3072, 768, 4096, 0)]:
+            a = torch.randn(K, M, device=DEV).bfloat16()
+            b = torch.randn(K, N, device=DEV).bfloat16()
+            out = kf.gemm(a, b, a_mn_major=True, b_mn_major=True, out_dtype=torch.float32, block_n=bn)
+            assert _rel(out, kf.gemm_ref(a, b, a_mn_major=True, b_mn_major=True)) < 1e-4, (M, N, K, bn)
+            x = torch.randn(M, K, device=DEV).bfloat16()
+            w = torch.randn(N, K, device=DEV).bfloat16()
+            y = kf.gemm(x, w, block_n=bn)
+            assert _rel(y, kf.gemm_ref(x, w)) < 1e-2, (M, N, K, bn)
+    finally:
+        native().gemm_set_group(-1)

@@ -5,7 +5,8 @@ eagerly and once with forward and backward captured after 3 eager updates:
 the losses and final parameters agree to a loose tolerance (weight gradients
 are summed with fp32 atomics, so two runs are not bitwise equal, and AdamW
 with a tiny eps turns such differences in near-zero gradients into steps of
-+-lr on a few elements; the key bias, whose exact gradient is zero, is left
++-lr on a few elements, and Muon's orthogonalisation lifts noise in weak
+gradient directions; the key bias, whose exact gradient is zero, is left
 out), the graph was captured once and replayed, and the
 library's launch counter keeps counting the replayed kernels.
 """
@@ -43,44 +44,6 @@ def _train(tmp_path, graph: bool):
     training_loop(model=model, dataset=iter(batches), step_fn=lambda m, b, c: {"loss": m(b["idx"], b["targets"])},
                   optimizer=opt, train_cfg=cfg, hooks={"on_update_end": [hook]})
     return model, losses, launches
-
-
-def test_graphed_step_matches_eager(tmp_path, monkeypatch):
-    from koochak_b200.runtime.graphed_step import GraphedStep
-
-    m_eager, l_eager, _ = _train(tmp_path, False)
-    calls = {"capture": 0, "replay": 0}
-    capture, run = GraphedStep._capture, GraphedStep.run
-
-    def counted_capture(self, *a, **k):
-        calls["capture"] += 1
-        return capture(self, *a, **k)
-
-    def counted_run(self, *a, **k):
-        calls["replay"] += 1
-        return run(self, *a, **k)
-
-    monkeypatch.setattr(GraphedStep, "_capture", counted_capture)
-    monkeypatch.setattr(GraphedStep, "run", counted_run)
-    m_graph, l_graph, launches = _train(tmp_path, True)
-    assert calls == {"capture": 1, "replay": 5}  # updates 3..7 through the graph
-    assert len(l_eager) == len(l_graph) == 8
-    for a, b in zip(l_eager, l_graph):
-        assert abs(a - b) <= 1e-2 * max(1.0, abs(a)), (l_eager, l_graph)
-    for (n, p), q in zip(m_eager.named_parameters(), m_graph.parameters()):
-        p, q = p.detach(), q.detach()
-        if n.endswith("attn.c_attn.bias"):
-            # The key third of the QKV bias gets a gradient that is zero in exact arithmetic (a shift of every
-            # key by one vector adds a constant to each softmax row); what it receives is fp32 rounding noise of
-            # random sign, which AdamW turns into steps of +-lr. Only the query and value thirds are compared.
-            C = p.numel() // 3
-            p, q = torch.cat([p[:C], p[2 * C:]]), torch.cat([q[:C], q[2 * C:]])
-        # AdamW parameters that start at zero (biases) stay small, so +-lr noise steps weigh heavily there
-        err = float((p - q).norm() / (p.norm() + 1e-6))
-        assert err < 5e-2, (n, err)
-    per_update = [b - a for a, b in zip(launches, launches[1:])]
-    # every replayed update still counts its kernels (forward/backward from the graph + the eager rest)
-    assert all(n > 0 for n in per_update) and max(per_update[4:]) >= 0.5 * max(per_update[:2])
 
 
 def _comparable(name: str, t: torch.Tensor) -> torch.Tensor:
@@ -122,11 +85,15 @@ def test_replayed_gradients_match_eager_gradients():
             scaled.backward()
         return float(loss), {n: p.grad.detach().clone() for n, p in named}
 
+    def rel(a, b):
+        return float((a - b).norm() / (b.norm() + 1e-12))
+
     eager(batch())
     step.note_eager()
     for i in range(4):  # capture, then three replays
         b = batch()
         ref_loss, ref = eager(b)
+        _, ref2 = eager(b)  # the same backward again: its spread is the run-to-run noise (fp32 atomics)
         model.zero_grad(set_to_none=True)
         with torch.autocast("cuda", dtype=torch.bfloat16), step.on_side_stream():
             _, loss = step.run(b, forward)
@@ -134,9 +101,52 @@ def test_replayed_gradients_match_eager_gradients():
         for n, p in named:
             assert p.grad is not None, n
             got, want = _comparable(n, p.grad.detach()), _comparable(n, ref[n])
-            err = float((got - want).norm() / (want.norm() + 1e-12))
-            assert err < 2e-2, (i, n, err)
+            noise = rel(_comparable(n, ref2[n]), want)
+            err = rel(got, want)
+            assert err < max(2e-2, 4 * noise), (i, n, err, noise)
         with torch.no_grad():  # an optimizer-like in-place change of every weight
             for _, p in named:
                 p.mul_(0.98).add_(0.01)
     assert step.graph is not None and not step.disabled
+
+
+def test_graphed_step_matches_eager(tmp_path, monkeypatch):
+    from koochak_b200.runtime.graphed_step import GraphedStep
+
+    m_eager, l_eager, _ = _train(tmp_path, False)
+    calls = {"capture": 0, "replay": 0}
+    capture, run = GraphedStep._capture, GraphedStep.run
+
+    def counted_capture(self, *a, **k):
+        calls["capture"] += 1
+        return capture(self, *a, **k)
+
+    def counted_run(self, *a, **k):
+        calls["replay"] += 1
+        return run(self, *a, **k)
+
+    monkeypatch.setattr(GraphedStep, "_capture", counted_capture)
+    monkeypatch.setattr(GraphedStep, "run", counted_run)
+    m_graph, l_graph, launches = _train(tmp_path, True)
+    assert calls == {"capture": 1, "replay": 5}  # updates 3..7 through the graph
+    assert len(l_eager) == len(l_graph) == 8
+    for a, b in zip(l_eager, l_graph):
+        assert abs(a - b) <= 1e-2 * max(1.0, abs(a)), (l_eager, l_graph)
+    for (n, p), q in zip(m_eager.named_parameters(), m_graph.parameters()):
+        p, q = p.detach(), q.detach()
+        if n.endswith("attn.c_attn.bias"):
+            # The key third of the QKV bias gets a gradient that is zero in exact arithmetic (a shift of every
+            # key by one vector adds a constant to each softmax row); what it receives is fp32 rounding noise of
+            # random sign, which AdamW turns into steps of +-lr. Only the query and value thirds are compared.
+            C = p.numel() // 3
+            p, q = torch.cat([p[:C], p[2 * C:]]), torch.cat([q[:C], q[2 * C:]])
+        # AdamW parameters that start at zero (biases) stay small, so +-lr noise steps weigh heavily there;
+        # Newton-Schulz gives every singular direction of a Muon update about the same size, so rounding noise
+        # in the weak directions of a gradient becomes a visible part of the update. The gradients themselves
+        # are compared tightly in test_replayed_gradients_match_eager_gradients.
+        err = float((p - q).norm() / (p.norm() + 1e-6))
+        assert err < 0.1, (n, err)
+    per_update = [b - a for a, b in zip(launches, launches[1:])]
+    # every replayed update still counts its kernels (forward/backward from the graph + the eager rest)
+    assert all(n > 0 for n in per_update) and max(per_update[4:]) >= 0.5 * max(per_update[:2])
+
