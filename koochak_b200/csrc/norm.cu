@@ -400,6 +400,135 @@ __global__ void __launch_bounds__(32 * kNormWarps, 3)
   }
 }
 
+// RMSNorm backward for rows of C = 256 * V (V = 8, 12, 16: C = 2048, 3072,
+// 4096), rows staged in shared memory by 1-D bulk copies.
+//
+// The register/shared-memory kernels above issue their row loads from the
+// threads and wait for them before the reductions; at C = 2048 that left the
+// wide kernel latency bound at 37 % of DRAM bandwidth (ncu: 18 long-scoreboard
+// stalls per issued instruction). Here one thread per CTA keeps kRowStages
+// rows (x, dy and the incoming residual gradient) in flight as bulk copies
+// while all 256 threads work on the oldest staged row: each thread owns V
+// consecutive columns for the CTA's whole life, so its share of dgamma stays
+// in registers, and a row costs one block-wide sum (one barrier). x and dy are
+// read from DRAM once; dx (+ the residual gradient) and its 16-bit copy are
+// written once.
+constexpr int kRowStages = 4;
+
+template <int V, typename TIn, typename TG, typename TDx>
+__global__ void __launch_bounds__(256, 2)
+    rms_bwd_staged_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
+                          const float* __restrict__ rstd_in, const TDx* __restrict__ dres, TDx* __restrict__ dx,
+                          TG* __restrict__ dx_lp, float* __restrict__ dw_part, int M, int* status) {
+  constexpr int C = 256 * V;
+  constexpr int kXB = C * (int)sizeof(TIn), kGB = C * (int)sizeof(TG), kRB = C * (int)sizeof(TDx);
+  constexpr int kStage = kXB + kGB + kRB;
+  extern __shared__ __align__(128) uint8_t smem_rows[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_rows + kRowStages * kStage);
+  float* red = reinterpret_cast<float*>(full + kRowStages);  // [2][8] per-warp partial sums, by row parity
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col = tid * V;
+  const int nrows = blockIdx.x < M ? (M - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const uint32_t row_bytes = (uint32_t)(kXB + kGB + (dres ? kRB : 0));
+
+  if (tid == 0) {
+    for (int s = 0; s < kRowStages; ++s) mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {  // thread 0: stage row i of this CTA
+    const long long row = (long long)blockIdx.x + (long long)i * gridDim.x;
+    uint8_t* st = smem_rows + (i % kRowStages) * kStage;
+    uint64_t* bar = &full[i % kRowStages];
+    mbar_arrive_expect_tx(bar, row_bytes);
+    bulk_load_1d(st, x + row * C, kXB, bar);
+    bulk_load_1d(st + kXB, dy + row * C, kGB, bar);
+    if (dres) bulk_load_1d(st + kXB + kGB, dres + row * C, kRB, bar);
+  };
+  int issued = 0;
+  if (tid == 0)
+    for (; issued < min(kRowStages, nrows); ++issued) issue(issued);
+
+  float wv[V], acc[V];
+#pragma unroll
+  for (int j = 0; j < V; j += 4) {
+    *reinterpret_cast<float4*>(&wv[j]) = *reinterpret_cast<const float4*>(w + col + j);
+    *reinterpret_cast<float4*>(&acc[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  int done = 0;
+  float rstd_next = nrows > 0 ? rstd_in[blockIdx.x] : 0.f;  // one row ahead: its latency hides behind a row
+  for (int i = 0; i < nrows; ++i) {
+    const long long row = (long long)blockIdx.x + (long long)i * gridDim.x;
+    const float rstd = rstd_next;
+    if (i + 1 < nrows) rstd_next = rstd_in[row + gridDim.x];
+    const uint8_t* st = smem_rows + (i % kRowStages) * kStage;
+    const bool ok = mbar_wait(&full[i % kRowStages], (uint32_t)(i / kRowStages) & 1u, abort_flag, status,
+                              kStatusTimeoutRowStage);
+    float xv[V], gv[V], rv[V];
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; j += 4) {
+      if (ok) {
+        load4<TIn>(reinterpret_cast<const TIn*>(st) + col + j, *reinterpret_cast<float(*)[4]>(&xv[j]));
+        load4<TG>(reinterpret_cast<const TG*>(st + kXB) + col + j, *reinterpret_cast<float(*)[4]>(&gv[j]));
+        if (dres) load4<TDx>(reinterpret_cast<const TDx*>(st + kXB + kGB) + col + j, *reinterpret_cast<float(*)[4]>(&rv[j]));
+        else *reinterpret_cast<float4*>(&rv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {
+        *reinterpret_cast<float4*>(&xv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(&gv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(&rv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float xh = xv[j] * rstd;
+      s2 += wv[j] * gv[j] * xh;
+      acc[j] += gv[j] * xh;
+    }
+    s2 = warp_sum(s2);
+    if (lane == 0) red[(i & 1) * 8 + warp] = s2;
+    // Every thread has read its part of the stage (and written its partial sum);
+    // all leave together when any wait ran out.
+    if (!__syncthreads_and(ok)) break;
+    if (tid == 0 && issued < nrows) issue(issued++);
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += red[(i & 1) * 8 + k];
+    tot *= 1.0f / C;
+    float o[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) o[j] = rstd * (wv[j] * gv[j] - xv[j] * rstd * tot) + rv[j];
+    TDx* dxr = dx + row * C + col;
+#pragma unroll
+    for (int j = 0; j < V; j += 4) store4<TDx>(dxr + j, *reinterpret_cast<float(*)[4]>(&o[j]));
+    if (dx_lp) {
+      TG* lpr = dx_lp + row * C + col;
+#pragma unroll
+      for (int j = 0; j < V; j += 4) store4<TG>(lpr + j, *reinterpret_cast<float(*)[4]>(&o[j]));
+    }
+    ++done;
+  }
+  if (tid == 0) {
+    // After an abort, wait (bounded) for the copies still landing in this CTA's shared memory.
+    volatile int never = 0;
+    for (int i = done; i < issued; ++i)
+      if (!mbar_wait(&full[i % kRowStages], (uint32_t)(i / kRowStages) & 1u, &never, status, kStatusTimeoutDrain))
+        break;
+  }
+#pragma unroll
+  for (int j = 0; j < V; j += 4)
+    *reinterpret_cast<float4*>(dw_part + (long long)blockIdx.x * C + col + j) = *reinterpret_cast<const float4*>(&acc[j]);
+}
+
+template <typename TIn, typename TG, typename TDx>
+static constexpr int rms_staged_smem(int V) {
+  return kRowStages * 256 * V * (int)(sizeof(TIn) + sizeof(TG) + sizeof(TDx)) + kRowStages * 8 + 16 * 4 + 16;
+}
+
+static inline bool rms_bwd_staged(bool rms, int C) { return rms && (C == 2048 || C == 3072 || C == 4096); }
+
 static inline bool rms_bwd_wide(bool rms, int C) { return rms && C > 1024 && C % 256 == 0 && C <= 4096; }
 static inline int rms_bwd_wide_smem(int C) { return (kNormWarps + 1) * C * (int)sizeof(float); }
 
@@ -524,8 +653,44 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   if (has_res) KB_CHECK(dres->scalar_type() == dx.scalar_type() && dres->is_contiguous(), "dres must match dx");
   const int smem = norm_bwd_smem_bytes(C);
   const bool sacc = norm_bwd_smem_acc(C);
-  const bool wide = rms_bwd_wide(rms, C);
-  if (wide) {
+  bool wide = rms_bwd_wide(rms, C);
+  int reduce_rows = grid;  // rows of dw_part the column reduction sums
+  bool staged = false;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (rms_bwd_staged(rms, C) && a16(x.data_ptr()) && a16(dy.data_ptr()) && a16(dx.data_ptr()) &&
+      (!has_res || a16(dres->data_ptr())) && (!(dx_lp.has_value() && dx_lp->defined()) || a16(dx_lp->data_ptr())) &&
+      a16(w.data_ptr())) {
+    with_type(x.scalar_type(), [&](auto tin) {
+      using TIn = decltype(tin);
+      with_lp_type(dy.scalar_type(), [&](auto tg) {
+        using TG = decltype(tg);
+        using TDx = TIn;
+        TG* lp = nullptr;
+        if (dx_lp.has_value() && dx_lp->defined()) {
+          KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
+                   "dx_lp must be contiguous, of dy's dtype and dx's size");
+          lp = (TG*)dx_lp->data_ptr();
+        }
+        auto go = [&](auto vc) {
+          constexpr int V = decltype(vc)::value;
+          constexpr int sm = rms_staged_smem<TIn, TG, TDx>(V);
+          auto kern = rms_bwd_staged_kernel<V, TIn, TG, TDx>;
+          KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+          const int per_sm = std::max(1, std::min(2, (227 * 1024) / (sm + 1024)));
+          const int g = std::max(1, std::min({num_sms(dev) * per_sm, M, grid}));
+          kern<<<g, 256, sm, stream>>>((const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(),
+                                       rstd.data_ptr<float>(), has_res ? (const TDx*)dres->data_ptr() : nullptr,
+                                       (TDx*)dx.data_ptr(), lp, dw_part, M, device_status_ptr(dev));
+          reduce_rows = g;
+        };
+        if (C == 2048) go(std::integral_constant<int, 8>{});
+        else if (C == 3072) go(std::integral_constant<int, 12>{});
+        else go(std::integral_constant<int, 16>{});
+      });
+    });
+    staged = true;
+    wide = false;
+  } else if (wide) {
     with_type(x.scalar_type(), [&](auto tin) {
       using TIn = decltype(tin);
       with_lp_type(dy.scalar_type(), [&](auto tg) {
@@ -547,7 +712,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
       });
     });
   }
-  if (!wide) with_vpt(C, [&](auto vpt) {
+  if (!wide && !staged) with_vpt(C, [&](auto vpt) {
     constexpr int V = decltype(vpt)::value;
     with_type(x.scalar_type(), [&](auto tin) {
       using TIn = decltype(tin);
@@ -584,7 +749,7 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   });
   KB_LAUNCHED();
   KB_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == C, "dw must be fp32 [C]");
-  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), grid, C, accumulate);
+  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), reduce_rows, C, accumulate);
   KB_LAUNCHED();
   if (!rms && db.has_value() && db->defined()) {
     KB_CHECK(db->scalar_type() == at::kFloat && db->numel() == C, "db must be fp32 [C]");

@@ -33,6 +33,7 @@ enum StatusCode : int {
   kStatusTimeoutPeer = 5,       // cross-GPU flag wait ran out
   kStatusBadArgs = 6,
   kStatusDebugBounds = 7,       // KB_DEBUG_BOUNDS build: an index fell outside its declared extent
+  kStatusTimeoutRowStage = 8,   // a row-streaming kernel waited too long for a staged row
 };
 
 // Bounds checks of the KB_DEBUG_BOUNDS build. Kernels compare the last
@@ -159,6 +160,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ----------------------------------------------------------------- TMA
+
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned)
+// from global to this CTA's shared memory, completing on an mbarrier's
+// transaction count. No cluster multicast.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -9,6 +9,8 @@ _CODES = {
     4: "kernel drain at exit did not complete",
     5: "cross-GPU wait ran out (a peer did not arrive)",
     6: "kernel rejected its arguments (index out of range)",
+    7: "debug-bounds build: an index fell outside its declared extent",
+    8: "row-streaming kernel timed out waiting for a staged row",
 }
 
 

@@ -73,7 +73,7 @@ def test_gemm_epilogues_and_batch():
     assert _rel(c, ref) < 1e-4
 
 
-@pytest.mark.parametrize("C", [64, 768, 1000, 1280, 2048, 4096])
+@pytest.mark.parametrize("C", [64, 768, 1000, 1280, 2048, 3072, 4096])
 @pytest.mark.parametrize("rms", [False, True])
 def test_norm_forward_backward(C, rms):
     kf = _kf()
@@ -447,3 +447,27 @@ def test_gemm_grouped_tile_order(group):
             assert _rel(y, kf.gemm_ref(x, w)) < 1e-2, (M, N, K, bn)
     finally:
         native().gemm_set_group(-1)
+
+
+@pytest.mark.parametrize("C", [2048, 3072, 4096])
+@pytest.mark.parametrize("M", [5, 333, 4099])
+@pytest.mark.parametrize("xdtype,with_res", [(torch.float32, True), (torch.float32, False), (torch.bfloat16, True)])
+def test_rmsnorm_backward_staged_rows(C, M, xdtype, with_res):
+    """RMSNorm backward with rows staged by bulk copies (C = 2048/3072/4096): dx (+ residual), its bf16 copy and
+    dgamma against the fp32 autograd reference, for row counts below, near and far above the CTA count."""
+    kf = _kf()
+    torch.manual_seed(15)
+    x = torch.randn(M, C, device=DEV).to(xdtype)
+    w = torch.rand(C, device=DEV) + 0.5
+    _, _, rstd = kf.norm_forward(x, w, None, 1e-5, rms=True, out_dtype=torch.bfloat16)
+    dy = torch.randn(M, C, device=DEV).bfloat16()
+    dres = torch.randn(M, C, device=DEV).to(xdtype) if with_res else None
+    dx, dw, _, lp = kf.norm_backward(dy, x, w, None, rstd, rms=True, dres=dres, dx_dtype=xdtype, want_lp=True)
+    xr = x.float().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    kf.rms_norm_ref(xr, wr, 1e-5).backward(dy.float())
+    want = xr.grad + (dres.float() if with_res else 0.0)
+    tol = 1e-3 if xdtype == torch.float32 else 1e-2
+    assert _rel(dx, want) < tol
+    assert _rel(lp, want) < 1e-2
+    assert _rel(dw, wr.grad) < tol

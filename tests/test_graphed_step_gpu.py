@@ -104,9 +104,9 @@ def test_replayed_gradients_match_eager_gradients():
             noise = rel(_comparable(n, ref2[n]), want)
             err = rel(got, want)
             assert err < max(2e-2, 4 * noise), (i, n, err, noise)
-        with torch.no_grad():  # an optimizer-like in-place change of every weight
-            for _, p in named:
-                p.mul_(0.98).add_(0.01)
+        with torch.no_grad():  # an optimizer-like in-place change of every weight (small: the model stays well
+            for _, p in named:  # conditioned, so rounding noise is not amplified)
+                p.mul_(0.99).add_(torch.randn_like(p), alpha=1e-3)
     assert step.graph is not None and not step.disabled
 
 
