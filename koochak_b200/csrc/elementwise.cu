@@ -266,25 +266,42 @@ void cross_entropy_backward(at::Tensor& logits, const at::Tensor& target, const 
 
 // ------------------------------------------------------------ bias gradient
 
-// out[n] += sum_m g[m, n]. A CTA covers 256 columns (32 threads x 8 columns,
-// 16-byte loads) x 8 row groups over a slice of rows; one atomic per column per CTA.
+// out[n] = sum_m g[m, n] (or out[n] += it), in two deterministic passes:
+// CTAs of 256 columns (32 threads x 8 columns, 16-byte loads) x 8 row groups
+// sum a slice of rows each and write one partial row; a second kernel sums
+// the partial rows. No atomics, so no zero-fill launch before it and the same
+// result on every run; each thread keeps four row loads in flight.
 template <typename T>
-__global__ void __launch_bounds__(256) bias_grad_kernel(const T* __restrict__ g, float* __restrict__ out, int M,
-                                                        int N, int rows_per_cta) {
+__global__ void __launch_bounds__(256) bias_grad_partial_kernel(const T* __restrict__ g, float* __restrict__ part,
+                                                                int M, int N, int rows_per_cta) {
   const int cg = threadIdx.x & 31, rg = threadIdx.x >> 5;
   const int col0 = blockIdx.x * 256 + cg * 8;
   const int r0 = blockIdx.y * rows_per_cta;
   const int r1 = min(M, r0 + rows_per_cta);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   const bool vec = (col0 + 8 <= N) && (N % 8 == 0) && sizeof(T) == 2;
-  for (int r = r0 + rg; r < r1; r += 8) {
-    const T* p = g + (long long)r * N + col0;
-    if (vec) {
-      const uint4 q = *reinterpret_cast<const uint4*>(p);
+  if (vec) {
+    int r = r0 + rg;
+    for (; r + 24 < r1; r += 32) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = *reinterpret_cast<const uint4*>(g + (long long)(r + 8 * u) * N + col0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&q[u]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += to_f32<T>(e[j]);
+      }
+    }
+    for (; r < r1; r += 8) {
+      const uint4 q = *reinterpret_cast<const uint4*>(g + (long long)r * N + col0);
       const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] += to_f32<T>(e[j]);
-    } else {
+    }
+  } else {
+    for (int r = r0 + rg; r < r1; r += 8) {
+      const T* p = g + (long long)r * N + col0;
       for (int j = 0; j < 8; ++j)
         if (col0 + j < N) acc[j] += to_f32<T>(p[j]);
     }
@@ -297,14 +314,42 @@ __global__ void __launch_bounds__(256) bias_grad_kernel(const T* __restrict__ g,
   float t = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; ++k) t += red[k][c];
-  if (blockIdx.x * 256 + c < N) atomicAdd(out + blockIdx.x * 256 + c, t);
+  if (blockIdx.x * 256 + c < N) part[(long long)blockIdx.y * N + blockIdx.x * 256 + c] = t;
 }
 
-// out must be zeroed by the caller unless accumulating.
-void bias_grad(const at::Tensor& g, at::Tensor& out) {
+// out[n] (+)= sum_r part[r, n]: 32 columns per CTA, 16 warps over the rows, four loads in flight each.
+__global__ void __launch_bounds__(512) bias_grad_finish_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                               int R, int N, int accumulate) {
+  const int lane = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (col < N) {
+    int r = rg;
+    for (; r + 48 < R; r += 64) {
+      s0 += part[(long long)r * N + col];
+      s1 += part[(long long)(r + 16) * N + col];
+      s2 += part[(long long)(r + 32) * N + col];
+      s3 += part[(long long)(r + 48) * N + col];
+    }
+    for (; r < R; r += 16) s0 += part[(long long)r * N + col];
+  }
+  __shared__ float red[16][33];
+  red[rg][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (rg == 0 && col < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t += red[k][lane];
+    out[col] = accumulate ? out[col] + t : t;
+  }
+}
+
+// out = column sums of g (accumulate: out += them).
+void bias_grad(const at::Tensor& g, at::Tensor& out, bool accumulate) {
   KB_CHECK(g.is_contiguous() && out.scalar_type() == at::kFloat, "bias_grad: contiguous g, fp32 out");
   const int N = (int)g.size(-1);
   const int M = (int)(g.numel() / N);
+  KB_CHECK(out.numel() == N && out.is_contiguous(), "bias_grad: out must be fp32 [N]");
   const c10::cuda::CUDAGuard guard(g.device());
   cudaStream_t s = c10::cuda::getCurrentCUDAStream().stream();
   const int col_blocks = (N + 255) / 256;
@@ -312,13 +357,19 @@ void bias_grad(const at::Tensor& g, at::Tensor& out) {
   int row_blocks = std::max(1, std::min((M + 63) / 64, target_ctas / std::max(1, col_blocks)));
   const int rows_per = (M + row_blocks - 1) / row_blocks;
   row_blocks = (M + rows_per - 1) / rows_per;
+  at::Tensor part = at::empty({row_blocks, N}, g.options().dtype(at::kFloat));
   dim3 grid(col_blocks, row_blocks);
   if (g.scalar_type() == at::kBFloat16)
-    bias_grad_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)g.data_ptr(), out.data_ptr<float>(), M, N, rows_per);
+    bias_grad_partial_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)g.data_ptr(),
+                                                                 part.data_ptr<float>(), M, N, rows_per);
   else if (g.scalar_type() == at::kHalf)
-    bias_grad_kernel<__half><<<grid, 256, 0, s>>>((const __half*)g.data_ptr(), out.data_ptr<float>(), M, N, rows_per);
+    bias_grad_partial_kernel<__half><<<grid, 256, 0, s>>>((const __half*)g.data_ptr(), part.data_ptr<float>(), M, N,
+                                                          rows_per);
   else
-    bias_grad_kernel<float><<<grid, 256, 0, s>>>(g.data_ptr<float>(), out.data_ptr<float>(), M, N, rows_per);
+    bias_grad_partial_kernel<float><<<grid, 256, 0, s>>>(g.data_ptr<float>(), part.data_ptr<float>(), M, N, rows_per);
+  KB_LAUNCHED();
+  bias_grad_finish_kernel<<<(N + 31) / 32, 512, 0, s>>>(part.data_ptr<float>(), out.data_ptr<float>(), row_blocks, N,
+                                                        accumulate ? 1 : 0);
   KB_LAUNCHED();
 }
 
@@ -718,7 +769,8 @@ void register_elementwise_ops(pybind11::module& m) {
   m.def("embedding_backward", &embedding_backward);
   m.def("cross_entropy_forward", &cross_entropy_forward);
   m.def("cross_entropy_backward", &cross_entropy_backward);
-  m.def("bias_grad", &bias_grad);
+  m.def("bias_grad", &bias_grad, "out = column sums of g (accumulate: out += them); deterministic",
+        pybind11::arg("g"), pybind11::arg("out"), pybind11::arg("accumulate") = false);
   m.def("cast_multi", &cast_multi);
   m.def("swiglu_forward", &swiglu_forward);
   m.def("swiglu_backward", &swiglu_backward);

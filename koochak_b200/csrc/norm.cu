@@ -400,33 +400,36 @@ __global__ void __launch_bounds__(32 * kNormWarps, 3)
   }
 }
 
-// RMSNorm backward for rows of C = 256 * V (V = 8, 12, 16: C = 2048, 3072,
-// 4096), rows staged in shared memory by 1-D bulk copies.
+// LayerNorm / RMSNorm backward with rows staged in shared memory by 1-D bulk
+// copies, for rows of C = NT * V (NT threads per CTA, V consecutive columns
+// per thread): C = 768, 1024 (V = 4) and 2048, 3072, 4096 (NT = 256).
 //
 // The register/shared-memory kernels above issue their row loads from the
 // threads and wait for them before the reductions; at C = 2048 that left the
-// wide kernel latency bound at 37 % of DRAM bandwidth (ncu: 18 long-scoreboard
-// stalls per issued instruction). Here one thread per CTA keeps kRowStages
-// rows (x, dy and the incoming residual gradient) in flight as bulk copies
-// while all 256 threads work on the oldest staged row: each thread owns V
-// consecutive columns for the CTA's whole life, so its share of dgamma stays
-// in registers, and a row costs one block-wide sum (one barrier). x and dy are
-// read from DRAM once; dx (+ the residual gradient) and its 16-bit copy are
-// written once.
+// wide RMSNorm kernel latency bound at 37 % of DRAM bandwidth (ncu: 18
+// long-scoreboard stalls per issued instruction). Here one thread per CTA
+// keeps kRowStages rows (x, dy and the incoming residual gradient) in flight
+// as bulk copies while all NT threads work on the oldest staged row: each
+// thread owns V consecutive columns for the CTA's whole life, so its share of
+// dgamma (and dbeta) stays in registers, and a row costs one block-wide sum
+// (one barrier). x and dy are read from DRAM once; dx (+ the residual
+// gradient) and its 16-bit copy are written once.
 constexpr int kRowStages = 4;
 
-template <int V, typename TIn, typename TG, typename TDx>
-__global__ void __launch_bounds__(256, 2)
-    rms_bwd_staged_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
-                          const float* __restrict__ rstd_in, const TDx* __restrict__ dres, TDx* __restrict__ dx,
-                          TG* __restrict__ dx_lp, float* __restrict__ dw_part, int M, int* status) {
-  constexpr int C = 256 * V;
+template <int NT, int V, bool RMS, typename TIn, typename TG, typename TDx>
+__global__ void __launch_bounds__(NT, (NT <= 192 ? 4 : 2))
+    norm_bwd_staged_kernel(const TG* __restrict__ dy, const TIn* __restrict__ x, const float* __restrict__ w,
+                           const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                           const TDx* __restrict__ dres, TDx* __restrict__ dx, TG* __restrict__ dx_lp,
+                           float* __restrict__ dw_part, float* __restrict__ db_part, int M, int* status) {
+  constexpr int C = NT * V;
+  constexpr int NW = NT / 32;
   constexpr int kXB = C * (int)sizeof(TIn), kGB = C * (int)sizeof(TG), kRB = C * (int)sizeof(TDx);
   constexpr int kStage = kXB + kGB + kRB;
   extern __shared__ __align__(128) uint8_t smem_rows[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_rows + kRowStages * kStage);
-  float* red = reinterpret_cast<float*>(full + kRowStages);  // [2][8] per-warp partial sums, by row parity
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 16);
+  float2* red = reinterpret_cast<float2*>(full + kRowStages);  // [2][NW] per-warp partial sums, by row parity
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red + 2 * NW);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int col = tid * V;
   const int nrows = blockIdx.x < M ? (M - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -451,55 +454,71 @@ __global__ void __launch_bounds__(256, 2)
   if (tid == 0)
     for (; issued < min(kRowStages, nrows); ++issued) issue(issued);
 
-  float wv[V], acc[V];
+  float wv[V], acc[V], accb[V];
 #pragma unroll
   for (int j = 0; j < V; j += 4) {
     *reinterpret_cast<float4*>(&wv[j]) = *reinterpret_cast<const float4*>(w + col + j);
     *reinterpret_cast<float4*>(&acc[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(&accb[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   int done = 0;
-  float rstd_next = nrows > 0 ? rstd_in[blockIdx.x] : 0.f;  // one row ahead: its latency hides behind a row
+  // Statistics one row ahead: their load latency hides behind a row.
+  float rstd_next = nrows > 0 ? rstd_in[blockIdx.x] : 0.f;
+  float mean_next = (!RMS && nrows > 0) ? mean_in[blockIdx.x] : 0.f;
   for (int i = 0; i < nrows; ++i) {
     const long long row = (long long)blockIdx.x + (long long)i * gridDim.x;
-    const float rstd = rstd_next;
-    if (i + 1 < nrows) rstd_next = rstd_in[row + gridDim.x];
+    const float rstd = rstd_next, mean = mean_next;
+    if (i + 1 < nrows) {
+      rstd_next = rstd_in[row + gridDim.x];
+      if (!RMS) mean_next = mean_in[row + gridDim.x];
+    }
     const uint8_t* st = smem_rows + (i % kRowStages) * kStage;
     const bool ok = mbar_wait(&full[i % kRowStages], (uint32_t)(i / kRowStages) & 1u, abort_flag, status,
                               kStatusTimeoutRowStage);
-    float xv[V], gv[V], rv[V];
-    float s2 = 0.f;
+    float xh[V], gv[V], rv[V];
 #pragma unroll
     for (int j = 0; j < V; j += 4) {
       if (ok) {
-        load4<TIn>(reinterpret_cast<const TIn*>(st) + col + j, *reinterpret_cast<float(*)[4]>(&xv[j]));
+        load4<TIn>(reinterpret_cast<const TIn*>(st) + col + j, *reinterpret_cast<float(*)[4]>(&xh[j]));
         load4<TG>(reinterpret_cast<const TG*>(st + kXB) + col + j, *reinterpret_cast<float(*)[4]>(&gv[j]));
         if (dres) load4<TDx>(reinterpret_cast<const TDx*>(st + kXB + kGB) + col + j, *reinterpret_cast<float(*)[4]>(&rv[j]));
         else *reinterpret_cast<float4*>(&rv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
       } else {
-        *reinterpret_cast<float4*>(&xv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(&xh[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(&gv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(&rv[j]) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-      const float xh = xv[j] * rstd;
-      s2 += wv[j] * gv[j] * xh;
-      acc[j] += gv[j] * xh;
+      xh[j] = RMS ? xh[j] * rstd : (xh[j] - mean) * rstd;  // normalised x
+      const float dxh = wv[j] * gv[j];
+      s1 += dxh;
+      s2 += dxh * xh[j];
+      acc[j] += gv[j] * xh[j];
+      if (!RMS) accb[j] += gv[j];
     }
     s2 = warp_sum(s2);
-    if (lane == 0) red[(i & 1) * 8 + warp] = s2;
-    // Every thread has read its part of the stage (and written its partial sum);
+    if (!RMS) s1 = warp_sum(s1);
+    if (lane == 0) red[(i & 1) * NW + warp] = make_float2(s1, s2);
+    // Every thread has read its part of the stage (and written its partial sums);
     // all leave together when any wait ran out.
     if (!__syncthreads_and(ok)) break;
     if (tid == 0 && issued < nrows) issue(issued++);
-    float tot = 0.f;
+    float t1 = 0.f, t2 = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) tot += red[(i & 1) * 8 + k];
-    tot *= 1.0f / C;
+    for (int k = 0; k < NW; ++k) {
+      const float2 v = red[(i & 1) * NW + k];
+      t1 += v.x;
+      t2 += v.y;
+    }
+    t1 *= 1.0f / C;
+    t2 *= 1.0f / C;
     float o[V];
 #pragma unroll
-    for (int j = 0; j < V; ++j) o[j] = rstd * (wv[j] * gv[j] - xv[j] * rstd * tot) + rv[j];
+    for (int j = 0; j < V; ++j)
+      o[j] = rstd * (wv[j] * gv[j] - (RMS ? 0.f : t1) - xh[j] * t2) + rv[j];
     TDx* dxr = dx + row * C + col;
 #pragma unroll
     for (int j = 0; j < V; j += 4) store4<TDx>(dxr + j, *reinterpret_cast<float(*)[4]>(&o[j]));
@@ -518,16 +537,36 @@ __global__ void __launch_bounds__(256, 2)
         break;
   }
 #pragma unroll
-  for (int j = 0; j < V; j += 4)
+  for (int j = 0; j < V; j += 4) {
     *reinterpret_cast<float4*>(dw_part + (long long)blockIdx.x * C + col + j) = *reinterpret_cast<const float4*>(&acc[j]);
+    if (!RMS)
+      *reinterpret_cast<float4*>(db_part + (long long)blockIdx.x * C + col + j) =
+          *reinterpret_cast<const float4*>(&accb[j]);
+  }
 }
 
-template <typename TIn, typename TG, typename TDx>
-static constexpr int rms_staged_smem(int V) {
-  return kRowStages * 256 * V * (int)(sizeof(TIn) + sizeof(TG) + sizeof(TDx)) + kRowStages * 8 + 16 * 4 + 16;
+// Threads per CTA of the staged backward for a row width, or 0 where it does not apply.
+static inline int norm_bwd_staged_threads(int C) {
+  switch (C) {
+    case 768: return 192;
+    case 1024: case 2048: case 3072: case 4096: return 256;
+    default: return 0;
+  }
 }
 
-static inline bool rms_bwd_staged(bool rms, int C) { return rms && (C == 2048 || C == 3072 || C == 4096); }
+static inline int norm_bwd_staged_smem(int C, int in_bytes, int g_bytes) {
+  const int nw = norm_bwd_staged_threads(C) / 32;
+  return kRowStages * C * (2 * in_bytes + g_bytes) + kRowStages * 8 + 2 * nw * 8 + 16;
+}
+
+// CTAs of the staged backward (also sizes its share of the workspace).
+static inline int norm_bwd_staged_grid(int M, int C, int dev) {
+  if (!norm_bwd_staged_threads(C)) return 0;
+  const int smem = norm_bwd_staged_smem(C, 4, 2);  // the largest case: fp32 x and dx, 16-bit dy
+  const int cap = norm_bwd_staged_threads(C) <= 192 ? 4 : 2;
+  const int per_sm = std::max(1, std::min(cap, (227 * 1024) / (smem + 1024)));
+  return std::max(1, std::min(num_sms(dev) * per_sm, M));
+}
 
 static inline bool rms_bwd_wide(bool rms, int C) { return rms && C > 1024 && C % 256 == 0 && C <= 4096; }
 static inline int rms_bwd_wide_smem(int C) { return (kNormWarps + 1) * C * (int)sizeof(float); }
@@ -561,6 +600,40 @@ __global__ void __launch_bounds__(256) column_reduce_kernel(const float* __restr
     float t = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x & 31];
+    out[col] = accumulate ? out[col] + t : t;
+  }
+}
+
+// out[c] (+)= sum_r part[r, c] for one or two partial-sum buffers (blockIdx.y
+// picks dgamma or dbeta), used by norm_backward: a CTA owns 32 columns and
+// splits the rows over 16 warps, each keeping four independent loads in
+// flight (the reduction above, one warp per eight rows with one load at a
+// time, took about 20 us for 592 partial rows of 768 columns).
+__global__ void __launch_bounds__(512) column_sum_kernel(const float* __restrict__ part0, float* __restrict__ out0,
+                                                         const float* __restrict__ part1, float* __restrict__ out1,
+                                                         int R, int C, int accumulate) {
+  const float* part = blockIdx.y ? part1 : part0;
+  float* out = blockIdx.y ? out1 : out0;
+  const int lane = threadIdx.x & 31, rg = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (col < C) {
+    int r = rg;
+    for (; r + 48 < R; r += 64) {
+      s0 += part[(long long)r * C + col];
+      s1 += part[(long long)(r + 16) * C + col];
+      s2 += part[(long long)(r + 32) * C + col];
+      s3 += part[(long long)(r + 48) * C + col];
+    }
+    for (; r < R; r += 16) s0 += part[(long long)r * C + col];
+  }
+  __shared__ float red[16][33];
+  red[rg][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (rg == 0 && col < C) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t += red[k][lane];
     out[col] = accumulate ? out[col] + t : t;
   }
 }
@@ -643,9 +716,13 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream().stream();
   const int dev = x.get_device();
   const int grid = norm_bwd_grid(M, C, rms, dev);
-  KB_CHECK(workspace.scalar_type() == at::kFloat && workspace.numel() >= 2LL * grid * C, "norm bwd: workspace too small");
+  // Rows of partial sums the workspace holds for dgamma (and as many for dbeta).
+  const int ws_grid = std::max({norm_bwd_grid(M, C, true, dev), norm_bwd_grid(M, C, false, dev),
+                                norm_bwd_staged_grid(M, C, dev)});
+  KB_CHECK(workspace.scalar_type() == at::kFloat && workspace.numel() >= 2LL * ws_grid * C,
+           "norm bwd: workspace too small");
   float* dw_part = workspace.data_ptr<float>();
-  float* db_part = rms ? nullptr : dw_part + (long long)grid * C;
+  float* db_part = rms ? nullptr : dw_part + (long long)ws_grid * C;
   const float* mp = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
   KB_CHECK(rms || mp, "LayerNorm backward needs mean");
   const bool has_res = dres.has_value() && dres->defined();
@@ -657,8 +734,9 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   int reduce_rows = grid;  // rows of dw_part the column reduction sums
   bool staged = false;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  if (rms_bwd_staged(rms, C) && a16(x.data_ptr()) && a16(dy.data_ptr()) && a16(dx.data_ptr()) &&
-      (!has_res || a16(dres->data_ptr())) && (!(dx_lp.has_value() && dx_lp->defined()) || a16(dx_lp->data_ptr())) &&
+  const bool lp_given = dx_lp.has_value() && dx_lp->defined();
+  if (norm_bwd_staged_threads(C) && (rms || mp != nullptr) && a16(x.data_ptr()) && a16(dy.data_ptr()) &&
+      a16(dx.data_ptr()) && (!has_res || a16(dres->data_ptr())) && (!lp_given || a16(dx_lp->data_ptr())) &&
       a16(w.data_ptr())) {
     with_type(x.scalar_type(), [&](auto tin) {
       using TIn = decltype(tin);
@@ -666,26 +744,36 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
         using TG = decltype(tg);
         using TDx = TIn;
         TG* lp = nullptr;
-        if (dx_lp.has_value() && dx_lp->defined()) {
+        if (lp_given) {
           KB_CHECK(dx_lp->scalar_type() == dy.scalar_type() && dx_lp->is_contiguous() && dx_lp->numel() == dx.numel(),
                    "dx_lp must be contiguous, of dy's dtype and dx's size");
           lp = (TG*)dx_lp->data_ptr();
         }
-        auto go = [&](auto vc) {
-          constexpr int V = decltype(vc)::value;
-          constexpr int sm = rms_staged_smem<TIn, TG, TDx>(V);
-          auto kern = rms_bwd_staged_kernel<V, TIn, TG, TDx>;
+        const int g = std::min(norm_bwd_staged_grid(M, C, dev), ws_grid);
+        const int sm = norm_bwd_staged_smem(C, (int)sizeof(TIn), (int)sizeof(TG));
+        auto go = [&](auto nt_c, auto v_c, auto rms_c) {
+          constexpr int NT = decltype(nt_c)::value;
+          constexpr int V = decltype(v_c)::value;
+          constexpr bool R = decltype(rms_c)::value;
+          auto kern = norm_bwd_staged_kernel<NT, V, R, TIn, TG, TDx>;
           KB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-          const int per_sm = std::max(1, std::min(2, (227 * 1024) / (sm + 1024)));
-          const int g = std::max(1, std::min({num_sms(dev) * per_sm, M, grid}));
-          kern<<<g, 256, sm, stream>>>((const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(),
-                                       rstd.data_ptr<float>(), has_res ? (const TDx*)dres->data_ptr() : nullptr,
-                                       (TDx*)dx.data_ptr(), lp, dw_part, M, device_status_ptr(dev));
-          reduce_rows = g;
+          kern<<<g, NT, sm, stream>>>((const TG*)dy.data_ptr(), (const TIn*)x.data_ptr(), w.data_ptr<float>(),
+                                      R ? nullptr : mp, rstd.data_ptr<float>(),
+                                      has_res ? (const TDx*)dres->data_ptr() : nullptr, (TDx*)dx.data_ptr(), lp,
+                                      dw_part, R ? nullptr : db_part, M, device_status_ptr(dev));
         };
-        if (C == 2048) go(std::integral_constant<int, 8>{});
-        else if (C == 3072) go(std::integral_constant<int, 12>{});
-        else go(std::integral_constant<int, 16>{});
+        auto by_width = [&](auto rms_c) {
+          switch (C) {
+            case 768: go(std::integral_constant<int, 192>{}, std::integral_constant<int, 4>{}, rms_c); break;
+            case 1024: go(std::integral_constant<int, 256>{}, std::integral_constant<int, 4>{}, rms_c); break;
+            case 2048: go(std::integral_constant<int, 256>{}, std::integral_constant<int, 8>{}, rms_c); break;
+            case 3072: go(std::integral_constant<int, 256>{}, std::integral_constant<int, 12>{}, rms_c); break;
+            default: go(std::integral_constant<int, 256>{}, std::integral_constant<int, 16>{}, rms_c); break;
+          }
+        };
+        if (rms) by_width(std::true_type{});
+        else by_width(std::false_type{});
+        reduce_rows = g;
       });
     });
     staged = true;
@@ -749,19 +837,19 @@ void norm_backward(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   });
   KB_LAUNCHED();
   KB_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == C, "dw must be fp32 [C]");
-  column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(dw_part, dw.data_ptr<float>(), reduce_rows, C, accumulate);
+  const bool want_db = !rms && db.has_value() && db->defined();
+  if (want_db) KB_CHECK(db->scalar_type() == at::kFloat && db->numel() == C, "db must be fp32 [C]");
+  column_sum_kernel<<<dim3((C + 31) / 32, want_db ? 2 : 1), 512, 0, stream>>>(
+      dw_part, dw.data_ptr<float>(), want_db ? db_part : nullptr, want_db ? db->data_ptr<float>() : nullptr,
+      reduce_rows, C, accumulate);
   KB_LAUNCHED();
-  if (!rms && db.has_value() && db->defined()) {
-    KB_CHECK(db->scalar_type() == at::kFloat && db->numel() == C, "db must be fp32 [C]");
-    column_reduce_kernel<<<(C + 31) / 32, 256, 0, stream>>>(db_part, db->data_ptr<float>(), grid, C, accumulate);
-    KB_LAUNCHED();
-  }
 }
 
 int64_t norm_backward_workspace_elems(int64_t M, int64_t C, int64_t device) {
-  // Sized for the larger of the two grids (RMSNorm's wide kernel runs more CTAs).
-  const int grid = std::max(norm_bwd_grid((int)M, (int)C, true, (int)device),
-                            norm_bwd_grid((int)M, (int)C, false, (int)device));
+  // Sized for the largest grid of the backward kernels (dgamma and dbeta halves).
+  const int grid = std::max({norm_bwd_grid((int)M, (int)C, true, (int)device),
+                             norm_bwd_grid((int)M, (int)C, false, (int)device),
+                             norm_bwd_staged_grid((int)M, (int)C, (int)device)});
   return 2LL * grid * C;
 }
 

@@ -189,8 +189,10 @@ def cross_entropy_backward_(logits, target, lse, gscale, vocab, ignore_index=-10
 
 
 def bias_grad(g: torch.Tensor) -> torch.Tensor:
-    out = torch.zeros(g.shape[-1], device=g.device, dtype=torch.float32)
-    native().bias_grad(g, out)
+    """Column sums of ``g`` in fp32 (the bias gradient), deterministic (two passes, no atomics)."""
+
+    out = torch.empty(g.shape[-1], device=g.device, dtype=torch.float32)
+    native().bias_grad(g, out, False)
     return out
 
 

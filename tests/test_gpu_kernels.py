@@ -449,25 +449,50 @@ def test_gemm_grouped_tile_order(group):
         native().gemm_set_group(-1)
 
 
-@pytest.mark.parametrize("C", [2048, 3072, 4096])
+@pytest.mark.parametrize("C", [768, 1024, 2048, 3072, 4096])
 @pytest.mark.parametrize("M", [5, 333, 4099])
 @pytest.mark.parametrize("xdtype,with_res", [(torch.float32, True), (torch.float32, False), (torch.bfloat16, True)])
-def test_rmsnorm_backward_staged_rows(C, M, xdtype, with_res):
-    """RMSNorm backward with rows staged by bulk copies (C = 2048/3072/4096): dx (+ residual), its bf16 copy and
-    dgamma against the fp32 autograd reference, for row counts below, near and far above the CTA count."""
+@pytest.mark.parametrize("rms", [True, False])
+def test_norm_backward_staged_rows(C, M, xdtype, with_res, rms):
+    """LayerNorm / RMSNorm backward with rows staged by bulk copies (C = 768 ... 4096): dx (+ residual), its bf16
+    copy, dgamma and dbeta against the fp32 autograd reference, for row counts below, near and far above the
+    CTA count."""
     kf = _kf()
     torch.manual_seed(15)
     x = torch.randn(M, C, device=DEV).to(xdtype)
     w = torch.rand(C, device=DEV) + 0.5
-    _, _, rstd = kf.norm_forward(x, w, None, 1e-5, rms=True, out_dtype=torch.bfloat16)
+    b = None if rms else torch.randn(C, device=DEV)
+    _, mean, rstd = kf.norm_forward(x, w, b, 1e-5, rms=rms, out_dtype=torch.bfloat16)
     dy = torch.randn(M, C, device=DEV).bfloat16()
     dres = torch.randn(M, C, device=DEV).to(xdtype) if with_res else None
-    dx, dw, _, lp = kf.norm_backward(dy, x, w, None, rstd, rms=True, dres=dres, dx_dtype=xdtype, want_lp=True)
+    dx, dw, db, lp = kf.norm_backward(dy, x, w, mean, rstd, rms=rms, dres=dres, dx_dtype=xdtype, want_lp=True)
     xr = x.float().requires_grad_(True)
     wr = w.clone().requires_grad_(True)
-    kf.rms_norm_ref(xr, wr, 1e-5).backward(dy.float())
+    br = None if rms else b.clone().requires_grad_(True)
+    yr = kf.rms_norm_ref(xr, wr, 1e-5) if rms else kf.layer_norm_ref(xr, wr, br, 1e-5)
+    yr.backward(dy.float())
     want = xr.grad + (dres.float() if with_res else 0.0)
     tol = 1e-3 if xdtype == torch.float32 else 1e-2
     assert _rel(dx, want) < tol
     assert _rel(lp, want) < 1e-2
     assert _rel(dw, wr.grad) < tol
+    if not rms:
+        assert _rel(db, br.grad) < tol
+
+
+@pytest.mark.parametrize("M,N,dtype", [(16384, 768, torch.bfloat16), (16384, 3072, torch.bfloat16), (777, 300, torch.float16),
+                                       (1000, 2304, torch.float32), (5, 8, torch.bfloat16)])
+def test_bias_grad_two_pass(M, N, dtype):
+    """Column sums (bias gradient) against fp32 torch: written, accumulated, and bitwise equal on a repeat."""
+    kf = _kf()
+    from koochak_b200.ops import native
+
+    torch.manual_seed(16)
+    g = torch.randn(M, N, device=DEV).to(dtype)
+    ref = g.float().sum(0)
+    a = kf.bias_grad(g)
+    assert _rel(a, ref) < 1e-4
+    assert torch.equal(a, kf.bias_grad(g))  # no atomics: the same bits every run
+    acc = torch.ones(N, device=DEV)
+    native().bias_grad(g, acc, True)
+    assert _rel(acc, ref + 1.0) < 1e-4
