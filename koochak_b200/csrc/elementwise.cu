@@ -505,22 +505,36 @@ __global__ void swiglu_bwd_kernel(const T* __restrict__ gu, const T* __restrict_
 // and 16-byte aligned rows), so every access is 16 bytes wide and the index
 // arithmetic runs once per 8 values. The arithmetic per value is the scalar
 // kernels'.
+// Vectorised forms: a thread owns eight consecutive columns of the gate and
+// up halves (16-byte loads for 16-bit types) at column j = 8 * (x index) and
+// walks rows m = blockIdx.y, += gridDim.y, two rows per step with every load
+// issued first. The 2-D grid needs no 64-bit division per element group, and
+// the sigmoid uses the fast reciprocal (__fdividef, __expf): the kernels were
+// instruction bound before at these byte counts.
 template <typename T>
 __global__ void __launch_bounds__(256)
     swiglu_fwd_vec_kernel(const T* __restrict__ gu, T* __restrict__ h, long long M, int F) {
-  const int F8 = F >> 3;
-  const long long total = M * F8;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
-       v += (long long)gridDim.x * blockDim.x) {
-    const long long m = v / F8;
-    const int j = (int)(v - m * F8) << 3;
-    const T* row = gu + m * 2 * F;
-    float g[8], u[8], o[8];
-    load8<T>(row + j, g);
-    load8<T>(row + F + j, u);
+  const int j = (blockIdx.x * 256 + threadIdx.x) * 8;
+  if (j >= F) return;
+  const long long step = gridDim.y;
+  for (long long m = blockIdx.y; m < M; m += 2 * step) {
+    const bool two = m + step < M;
+    float g[2][8], u[2][8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) o[t] = g[t] / (1.f + __expf(-g[t])) * u[t];
-    store8<T>(h + m * F + j, o);
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && !two) break;
+      const T* row = gu + (m + q * step) * 2 * F;
+      load8<T>(row + j, g[q]);
+      load8<T>(row + F + j, u[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && !two) break;
+      float o[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) o[t] = __fdividef(g[q][t], 1.f + __expf(-g[q][t])) * u[q][t];
+      store8<T>(h + (m + q * step) * F + j, o);
+    }
   }
 }
 
@@ -528,28 +542,43 @@ template <typename T>
 __global__ void __launch_bounds__(256)
     swiglu_bwd_vec_kernel(const T* __restrict__ gu, const T* __restrict__ dh, T* __restrict__ dgu, long long M,
                           int F) {
-  const int F8 = F >> 3;
-  const long long total = M * F8;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
-       v += (long long)gridDim.x * blockDim.x) {
-    const long long m = v / F8;
-    const int j = (int)(v - m * F8) << 3;
-    const T* row = gu + m * 2 * F;
-    float g[8], u[8], d[8], dg[8], du[8];
-    load8<T>(row + j, g);
-    load8<T>(row + F + j, u);
-    load8<T>(dh + m * F + j, d);
+  const int j = (blockIdx.x * 256 + threadIdx.x) * 8;
+  if (j >= F) return;
+  const long long step = gridDim.y;
+  for (long long m = blockIdx.y; m < M; m += 2 * step) {
+    const bool two = m + step < M;
+    float g[2][8], u[2][8], d[2][8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const float sig = 1.f / (1.f + __expf(-g[t]));
-      const float silu = g[t] * sig;
-      dg[t] = d[t] * u[t] * (sig + silu * (1.f - sig));
-      du[t] = d[t] * silu;
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && !two) break;
+      const T* row = gu + (m + q * step) * 2 * F;
+      load8<T>(row + j, g[q]);
+      load8<T>(row + F + j, u[q]);
+      load8<T>(dh + (m + q * step) * F + j, d[q]);
     }
-    T* out = dgu + m * 2 * F;
-    store8<T>(out + j, dg);
-    store8<T>(out + F + j, du);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && !two) break;
+      float dg[8], du[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const float sig = __fdividef(1.f, 1.f + __expf(-g[q][t]));
+        const float silu = g[q][t] * sig;
+        dg[t] = d[q][t] * u[q][t] * (sig + silu * (1.f - sig));
+        du[t] = d[q][t] * silu;
+      }
+      T* out = dgu + (m + q * step) * 2 * F;
+      store8<T>(out + j, dg);
+      store8<T>(out + F + j, du);
+    }
   }
+}
+
+// 2-D grid of the vectorised kernels: column blocks of 256 x 8 columns, rows spread over about 16 CTAs per SM.
+static dim3 swiglu_vec_grid(long long M, int F, int dev) {
+  const int xb = (F / 8 + 255) / 256;
+  const long long yb = std::max<long long>(1, std::min<long long>(M, (long long)num_sms(dev) * 16 / xb));
+  return dim3(xb, (unsigned)yb);
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -563,18 +592,19 @@ void swiglu_forward(const at::Tensor& gu, at::Tensor& h) {
   const bool vec = F % 8 == 0 && aligned16(gu.data_ptr()) && aligned16(h.data_ptr());
   const long long work = vec ? M * (F / 8) : M * F;
   const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, num_sms(gu.get_device()) * 16LL));
+  const dim3 vgrid = vec ? swiglu_vec_grid(M, F, gu.get_device()) : dim3(1);
   if (gu.scalar_type() == at::kBFloat16) {
     auto* in = (const __nv_bfloat16*)gu.data_ptr();
     auto* out = (__nv_bfloat16*)h.data_ptr();
-    if (vec) swiglu_fwd_vec_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+    if (vec) swiglu_fwd_vec_kernel<<<vgrid, 256, 0, s>>>(in, out, M, F);
     else swiglu_fwd_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
   } else if (gu.scalar_type() == at::kHalf) {
     auto* in = (const __half*)gu.data_ptr();
     auto* out = (__half*)h.data_ptr();
-    if (vec) swiglu_fwd_vec_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
+    if (vec) swiglu_fwd_vec_kernel<<<vgrid, 256, 0, s>>>(in, out, M, F);
     else swiglu_fwd_kernel<<<blocks, 256, 0, s>>>(in, out, M, F);
   } else {
-    if (vec) swiglu_fwd_vec_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
+    if (vec) swiglu_fwd_vec_kernel<float><<<vgrid, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
     else swiglu_fwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), h.data_ptr<float>(), M, F);
   }
   KB_LAUNCHED();
@@ -588,21 +618,22 @@ void swiglu_backward(const at::Tensor& gu, const at::Tensor& dh, at::Tensor& dgu
   const bool vec = F % 8 == 0 && aligned16(gu.data_ptr()) && aligned16(dh.data_ptr()) && aligned16(dgu.data_ptr());
   const long long work = vec ? M * (F / 8) : M * F;
   const int blocks = (int)std::max<long long>(1, std::min<long long>((work + 255) / 256, num_sms(gu.get_device()) * 16LL));
+  const dim3 vgrid = vec ? swiglu_vec_grid(M, F, gu.get_device()) : dim3(1);
   if (gu.scalar_type() == at::kBFloat16) {
     auto* g = (const __nv_bfloat16*)gu.data_ptr();
     auto* d = (const __nv_bfloat16*)dh.data_ptr();
     auto* o = (__nv_bfloat16*)dgu.data_ptr();
-    if (vec) swiglu_bwd_vec_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+    if (vec) swiglu_bwd_vec_kernel<<<vgrid, 256, 0, s>>>(g, d, o, M, F);
     else swiglu_bwd_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
   } else if (gu.scalar_type() == at::kHalf) {
     auto* g = (const __half*)gu.data_ptr();
     auto* d = (const __half*)dh.data_ptr();
     auto* o = (__half*)dgu.data_ptr();
-    if (vec) swiglu_bwd_vec_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
+    if (vec) swiglu_bwd_vec_kernel<<<vgrid, 256, 0, s>>>(g, d, o, M, F);
     else swiglu_bwd_kernel<<<blocks, 256, 0, s>>>(g, d, o, M, F);
   } else {
     if (vec)
-      swiglu_bwd_vec_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(),
+      swiglu_bwd_vec_kernel<float><<<vgrid, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(),
                                                           dgu.data_ptr<float>(), M, F);
     else
       swiglu_bwd_kernel<float><<<blocks, 256, 0, s>>>(gu.data_ptr<float>(), dh.data_ptr<float>(),

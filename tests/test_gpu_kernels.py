@@ -166,15 +166,17 @@ def test_cross_entropy_and_embedding():
 
 
 @pytest.mark.parametrize("F", [96, 100, 5504])
-def test_swiglu(F):
-    """Vectorised (F % 8 == 0) and scalar (F = 100) SwiGLU against the fp32 formula."""
+@pytest.mark.parametrize("M", [37, 5001])
+def test_swiglu(F, M):
+    """Vectorised (F % 8 == 0) and scalar (F = 100) SwiGLU against the fp32 formula; with 5001 rows the
+    vectorised kernels take two rows per step and an odd tail."""
 
     kf = _kf()
     torch.manual_seed(5)
-    gu = torch.randn(37, 2 * F, device=DEV).bfloat16()
+    gu = torch.randn(M, 2 * F, device=DEV).bfloat16()
     assert _rel(kf.swiglu_forward(gu), kf.swiglu_ref(gu)) < 1e-2
     gr = gu.float().requires_grad_(True)
-    dh = torch.randn(37, F, device=DEV).bfloat16()
+    dh = torch.randn(M, F, device=DEV).bfloat16()
     kf.swiglu_ref(gr).backward(dh.float())
     assert _rel(kf.swiglu_backward(gu, dh), gr.grad) < 2e-2
 
